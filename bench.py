@@ -1,0 +1,343 @@
+"""Benchmark: energy + forces throughput (atom-steps/s) of the uma-s-shaped model on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flash|reference] [--tf32]
+
+Workload: bulk fcc Cu 10x10x10 conventional supercell, 4,000
+atoms, displacements N(0, 0.05 A), cutoff 6 A, <= 30 neighbours (120,000 edges), random
+uma-s-shaped weights (lmax=mmax=2, C=128, 4 layers, B=64, seed 0). A step is one energy
++ forces evaluation (forward + backward of the whole backbone + energy head) on a new set
+of MD-like positions with the cached graph. Timing: CUDA events per step on the launching
+stream, L2 flushed (256 MB write) before every step outside the timed events, max over
+ranks. ``value`` has the positions already in HBM; ``e2e`` copies them from pinned host
+memory and the energy and forces back inside the timed region, through the public API
+(``Predictor(ZeroAllocBackbone(backbone), head)``).
+
+With N > 1 GPUs every rank runs an independent replica (weak scaling; the partitioned
+multi-GPU path is not part of this benchmark yet). ``--impl reference`` times the CPU
+restatement of the reference implementation (the oracle) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "atom-steps/s (energy+forces) uma-s-shaped"
+UNIT = "atom-steps/s"
+
+# algorithmic HBM bytes of one call of each entry point (fp32, minimum traffic: every
+# per-edge / per-node tensor read or written once)
+def alg_bytes(name, N, E, C, B, M_rows=None, D=None):
+    f = 4
+    if name == "fuma_gather_fwd":
+        return E * (f * 34 + f * 12 * C + 8 + f * 18 * C) + N * f * 9 * C
+    if name == "fuma_gather_bwd":
+        return E * (f * 18 * C + f * 12 * C + f * 34 + 16 + f * 12 * C + f * 34) + N * f * 9 * C * 2
+    if name == "fuma_rotate_scatter_fwd":
+        return E * (f * 9 * C + f * 34 + f + 4) + N * 2 * f * 9 * C + 4 * (N + 1)
+    if name == "fuma_rotate_scatter_bwd":
+        return E * (f * 9 * C * 2 + f * 34 * 2 + f * 2 + 4) + N * f * 9 * C
+    if name == "fuma_gating_fwd":
+        return E * f * 20 * C
+    if name == "fuma_gating_bwd":
+        return E * f * 31 * C
+    if name == "fuma_init_scatter_fwd":
+        return E * (f * 3 * C + f * 34 + f + 4) + N * f * 9 * C
+    if name == "fuma_init_scatter_bwd":
+        return E * (f * 6 * C + f * 68 + f * 2 + 4) + N * f * 9 * C
+    if name == "fuma_geometry_fwd":
+        return E * (f * (B + 2 * C) + f * 34 + f + 12 + 16) + N * 20
+    if name == "fuma_geometry_bwd":
+        return E * (f * B + f * 34 + f + 12 + 16 + 12) + N * 12
+    if name == "fuma_edge_vec_to_nodes":
+        return E * (2 * 12 + 8) + N * 12
+    if name == "fuma_ln_silu_fwd":
+        return M_rows * (2 * f * D + 8)
+    if name == "fuma_ln_silu_bwd":
+        return M_rows * (3 * f * D + 8)
+    return None
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def build_problem(device, tf32: bool, system=None):
+    from flash_uma_b200.predict import Predictor
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
+    from flash_uma_b200.systems import config3_system, to_graph
+    from flash_uma_b200.wrapper import ZeroAllocBackbone
+    torch.backends.cuda.matmul.allow_tf32 = tf32
+    system = system or config3_system()
+    data = to_graph([system])
+    off = SyntheticESCNMDBackbone(seed=0).to(device)
+    head = make_energy_head(128, 128, seed=1).to(device)
+    pred = Predictor(ZeroAllocBackbone(off), head)
+    return system, data, pred
+
+
+def md_positions(pos0: torch.Tensor, count: int, seed: int = 0):
+    """MD-like position sequence: small random displacements (0.01 A rms) around pos0."""
+    g = torch.Generator().manual_seed(seed)
+    return [pos0 + 0.01 * torch.randn(pos0.shape, generator=g) for _ in range(count)]
+
+
+def run_flash(args, rank, world, device):
+    from flash_uma_b200 import _native
+    _native.load()
+    system, data_cpu, pred = build_problem(device, args.tf32)
+    N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
+    C, B, L = 128, 64, 4
+    data = data_cpu.to(device)
+    K, W = args.steps, args.warmup
+    pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=rank)]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    import dataclasses
+
+    def step(pos):
+        return pred(dataclasses.replace(data, pos=pos))
+
+    # ---- which of our kernels dominates: one probe pass with every entry point timed
+    probe = _native.LaunchProbe(timed=list(_native.KERNELS_PER_CALL))
+    for w in range(W):
+        step(pos_seq[w])
+    torch.cuda.synchronize()
+    _native.set_probe(probe)
+    step(pos_seq[0])
+    torch.cuda.synchronize()
+    _native.set_probe(None)
+    per_op = {n: sum(probe.times_ms(n)) for n in probe.events}
+    dominant = max(per_op, key=per_op.get)
+    launches_per_step = probe.launches
+
+    # ---- timed region 1: inputs resident in HBM
+    probe = _native.LaunchProbe(timed=[dominant])
+    sampler = ClockSampler(device.index if device.index is not None else 0)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    _native.set_probe(probe)
+    evs = []
+    for k in range(K):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        res = step(pos_seq[W + k])
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    _native.set_probe(None)
+    clocks = sampler.stop()
+    total_ms = sum(a.elapsed_time(b) for a, b in evs)
+    dom_ms = probe.times_ms(dominant)
+    gpu_launches = probe.launches
+
+    # ---- timed region 2: end to end from pinned host buffers through the public API
+    host_pos = [p.cpu().pin_memory() for p in md_positions(data_cpu.pos, K, seed=100 + rank)]
+    f_host = torch.empty(N, 3).pin_memory()
+    e_host = torch.empty(1).pin_memory()
+    pos_dev = torch.empty(N, 3, device=device)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    evs2 = []
+    for k in range(K):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        pos_dev.copy_(host_pos[k], non_blocking=True)
+        res = step(pos_dev)
+        f_host.copy_(res["forces"], non_blocking=True)
+        e_host.copy_(res["energy"], non_blocking=True)
+        e1.record()
+        evs2.append((e0, e1))
+    torch.cuda.synchronize()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in evs2)
+
+    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    total_ms, e2e_ms = t.tolist()
+
+    hbm, _, peak_kind = load_peaks()
+    nbytes = alg_bytes(dominant, N, E, C, B, M_rows=E, D=128)
+    avg_ms = sum(dom_ms) / max(1, len(dom_ms))
+    achieved = nbytes / (avg_ms * 1e-3) / 1e9 if nbytes and avg_ms > 0 else None
+    out = {
+        "metric": METRIC, "value": world * N * K / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded bulk Cu positions, random-init weights)",
+        "config": {"workload": "bulk_cu_4000 (BASELINE config 3): 4000 atoms, %d edges, E+F per step" % E,
+                   "atoms": N, "edges": E, "sphere_channels": C, "layers": L, "num_distance_basis": B,
+                   "cutoff": 6.0, "max_neighbors": 30, "gemm": "tf32" if args.tf32 else "fp32 (cuBLAS, TF32 off)",
+                   "l2": "flushed (256 MB write) before every step, outside the timed events",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "e2e": {"value": world * N * K / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4,
+                "d2h_bytes_per_step": N * 3 * 4 + 4},
+        "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind,
+                     "traffic": None, "alg_bytes_per_launch": nbytes, "avg_launch_ms": avg_ms,
+                     "launches_timed": len(dom_ms),
+                     "share_of_step": (sum(dom_ms) / total_ms) if world == 1 else None},
+        "gpu_launches": gpu_launches,
+        "per_kernel_ms_one_step": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
+        "clocks": clocks,
+    }
+    return out
+
+
+def cpu_oracle_rate(atoms_sample: int = 256, min_seconds: float = 8.0, max_steps: int = 4):
+    """Time the CPU oracle (PyTorch restatement of the reference) on a bulk-Cu sample."""
+    from flash_uma_b200.predict import Predictor
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
+    from flash_uma_b200.systems import bulk_fcc, to_graph
+    from oracle.model import OracleBackbone
+    n = {256: 4, 500: 5, 864: 6}[atoms_sample]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    data = to_graph([bulk_fcc(n, n, n, jitter=0.05, seed=0)])
+    off = SyntheticESCNMDBackbone(seed=0)
+    pred = Predictor(OracleBackbone(off), make_energy_head(128, 128, seed=1))
+    pred(data)  # warm-up
+    t0 = time.perf_counter()
+    steps = 0
+    while steps < max_steps and (time.perf_counter() - t0 < min_seconds or steps == 0):
+        pred(data)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": atoms_sample * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"bulk fcc Cu {n}x{n}x{n} ({atoms_sample} atoms, same per-atom work as config 3), "
+                      f"{steps} E+F step(s), {dt:.1f} s"}
+
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (its restatement, ``oracle/``) on the host."""
+    from flash_uma_b200.predict import Predictor
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
+    from flash_uma_b200.systems import bulk_fcc, to_graph
+    from oracle.model import OracleBackbone
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n = 4
+    data = to_graph([bulk_fcc(n, n, n, jitter=0.05, seed=0)])
+    atoms = data.pos.shape[0]
+    pred = Predictor(OracleBackbone(SyntheticESCNMDBackbone(seed=0)), make_energy_head(128, 128, seed=1))
+    for _ in range(args.warmup):
+        pred(data)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        pred(data)
+    dt = time.perf_counter() - t0
+    v = atoms * args.steps / dt
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded bulk Cu positions, random-init weights)",
+            "config": {"workload": "bulk_cu_4000 (BASELINE config 3), each step a bounded sample: bulk Cu 4x4x4 "
+                                   f"({atoms} atoms, same per-atom work), E+F, CPU",
+                       "atoms_per_step": atoms, "sphere_channels": 128, "layers": 4, "num_distance_basis": 64},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"bulk fcc Cu 4x4x4 ({atoms} atoms) per step, {args.steps} steps"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="flash", choices=["flash", "reference"])
+    ap.add_argument("--tf32", action="store_true", help="TF32 dense contractions (the reference's published setup)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    try:
+        out = run_flash(args, rank, world, device)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                out["cpu_baseline"] = cpu_oracle_rate()
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

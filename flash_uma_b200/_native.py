@@ -1,0 +1,147 @@
+"""ctypes binding of the C ABI in ``include/flash_uma_b200.h``.
+
+There is no CPU fallback: if the library has not been built, or there is no CUDA
+device, the first call raises. Tensors are passed as raw device pointers; the
+stream is PyTorch's current stream on the tensors' device.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from . import build as _build
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_F32 = ctypes.c_float
+
+# name -> argument types (return type is int for all compute entry points)
+_SIGS = {
+    "fuma_geometry_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _F32, _F32, _I64, _I64, _I32, _I32, _P, _P, _P, _P],
+    "fuma_geometry_bwd": [_P, _P, _P, _P, _P, _F32, _F32, _P, _I64, _P, _P, _I64, _I32, _P, _P],
+    "fuma_edge_vec_to_nodes": [_P, _P, _P, _P, _P, _I64, _P, _P],
+    "fuma_ln_silu_fwd": [_P, _P, _P, _F32, _I64, _I32, _P, _P, _P, _P],
+    "fuma_ln_silu_bwd": [_P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P],
+    "fuma_gather_fwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P],
+    "fuma_gather_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P],
+    "fuma_gating_fwd": [_P, _P, _P, _I64, _I32, _P, _P, _P, _P],
+    "fuma_gating_bwd": [_P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P, _P],
+    "fuma_rotate_scatter_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P],
+    "fuma_rotate_scatter_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P],
+    "fuma_init_scatter_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P],
+    "fuma_init_scatter_bwd": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P],
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib_path() -> str:
+    return _build.lib_path()
+
+
+def load(allow_build: bool = False) -> ctypes.CDLL:
+    """Load the shared library (building it first if ``allow_build`` and it is missing/stale)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = lib_path()
+        if allow_build and _build.needs_build():
+            _build.build()
+        if not os.path.exists(path):
+            raise RuntimeError(f"flash_uma_b200: CUDA library not built ({path}); run `python -m flash_uma_b200.build`")
+        lib = ctypes.CDLL(path)
+        for name, args in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        lib.fuma_version.restype = ctypes.c_int
+        lib.fuma_last_error.restype = ctypes.c_char_p
+        _lib = lib
+        return lib
+
+
+def exported_symbols():
+    return ["fuma_version", "fuma_last_error", *_SIGS.keys()]
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+# kernels each entry point launches (used by launch accounting)
+KERNELS_PER_CALL = {name: 1 for name in _SIGS}
+KERNELS_PER_CALL["fuma_gather_bwd"] = 2
+
+
+class LaunchProbe:
+    """Optional per-call instrumentation: counts kernel launches per entry point and, for the
+    names in ``timed``, brackets each call with CUDA events on the current stream so the
+    kernel's device time can be measured inside a larger timed region."""
+
+    def __init__(self, timed=()):
+        self.timed = set(timed)
+        self.counts: dict[str, int] = {}
+        self.launches = 0
+        self.events: dict[str, list] = {}
+        self.meta: dict[str, list] = {}
+
+    def before(self, name, args):
+        self.counts[name] = self.counts.get(name, 0) + 1
+        self.launches += KERNELS_PER_CALL.get(name, 1)
+        if name in self.timed:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            return ev0
+        return None
+
+    def after(self, name, ev0, args):
+        if ev0 is None:
+            return
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev1.record()
+        self.events.setdefault(name, []).append((ev0, ev1))
+        self.meta.setdefault(name, []).append(args)
+
+    def times_ms(self, name):
+        return [a.elapsed_time(b) for a, b in self.events.get(name, [])]
+
+
+_probe: LaunchProbe | None = None
+
+
+def set_probe(p: LaunchProbe | None) -> None:
+    global _probe
+    _probe = p
+
+
+def call(name: str, *args) -> None:
+    lib = load()
+    p = _probe
+    ev = p.before(name, args) if p is not None else None
+    rc = getattr(lib, name)(*args)
+    if p is not None:
+        p.after(name, ev, args)
+    if rc != 0:
+        msg = lib.fuma_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name} failed (code {rc}): {msg}")
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("flash_uma_b200 ops run on CUDA tensors only (no CPU fallback); "
+                               f"got a tensor on {t.device}")

@@ -1,0 +1,237 @@
+// extern "C" entry points: argument validation, launch configuration, error reporting.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/flash_uma_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace fuma;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int launched(const char* what) {
+  const cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return fail((int)st, "%s: launch failed: %s", what, cudaGetErrorString(st));
+  g_err[0] = '\0';
+  return FUMA_OK;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+#define REQUIRE(cond, ...)                                  \
+  do {                                                      \
+    if (!(cond)) return fail(FUMA_E_INVALID, __VA_ARGS__);  \
+  } while (0)
+#define REQUIRE_ALIGNED(p, name)                                                     \
+  do {                                                                               \
+    if (!al16(p)) return fail(FUMA_E_ALIGN, "%s must be 16-byte aligned", name);     \
+  } while (0)
+
+int check_C(int32_t C) {
+  if (C <= 0 || (C & 3) != 0 || C > 512) return fail(FUMA_E_INVALID, "C=%d must be a positive multiple of 4, <= 512", C);
+  return FUMA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fuma_version(void) { return 100; }
+const char* fuma_last_error(void) { return g_err; }
+
+int fuma_geometry_fwd(const float* pos, const int64_t* Z, const int64_t* idx_i, const int64_t* idx_j,
+                      const float* shifts, const float* W_src, const float* W_tgt, const float* offset_g,
+                      float coeff_g, float cutoff, int64_t N, int64_t E, int32_t B, int32_t C, float* x_edge_raw,
+                      float* wigner, float* env, void* stream) {
+  REQUIRE(N >= 0 && E >= 0 && B > 0 && C > 0, "geometry_fwd: bad sizes N=%lld E=%lld B=%d C=%d", (long long)N,
+          (long long)E, B, C);
+  REQUIRE(cutoff > 0.f, "geometry_fwd: cutoff must be > 0");
+  if (E == 0) return FUMA_OK;
+  REQUIRE(pos && Z && idx_i && idx_j && shifts && W_src && W_tgt && offset_g && x_edge_raw && wigner && env,
+          "geometry_fwd: null pointer");
+  if (((B | C) & 3) == 0) {
+    REQUIRE_ALIGNED(x_edge_raw, "x_edge_raw"); REQUIRE_ALIGNED(W_src, "W_src"); REQUIRE_ALIGNED(W_tgt, "W_tgt");
+  }
+  launch_geom_fwd(pos, Z, idx_i, idx_j, shifts, W_src, W_tgt, offset_g, x_edge_raw, wigner, env, E, B, C, cutoff,
+                  coeff_g, (cudaStream_t)stream);
+  return launched("geometry_fwd");
+}
+
+int fuma_geometry_bwd(const float* pos, const int64_t* idx_i, const int64_t* idx_j, const float* shifts,
+                      const float* offset_g, float coeff_g, float cutoff, const float* g_x_edge,
+                      int64_t g_x_edge_stride, const float* g_wigner, const float* g_env, int64_t E, int32_t B,
+                      float* g_shifts, void* stream) {
+  REQUIRE(E >= 0 && B > 0 && g_x_edge_stride >= B, "geometry_bwd: bad sizes");
+  if (E == 0) return FUMA_OK;
+  REQUIRE(pos && idx_i && idx_j && shifts && offset_g && g_x_edge && g_wigner && g_env && g_shifts,
+          "geometry_bwd: null pointer");
+  launch_geom_bwd(pos, idx_i, idx_j, shifts, offset_g, g_x_edge, g_x_edge_stride, g_wigner, g_env, g_shifts, E, B,
+                  cutoff, coeff_g, (cudaStream_t)stream);
+  return launched("geometry_bwd");
+}
+
+int fuma_edge_vec_to_nodes(const int32_t* src_row_ptr, const int32_t* src_col, const int32_t* dst_row_ptr,
+                           const int32_t* dst_col, const float* g_vec, int64_t N, float* g_pos, void* stream) {
+  REQUIRE(N >= 0, "edge_vec_to_nodes: bad N");
+  if (N == 0) return FUMA_OK;
+  REQUIRE(src_row_ptr && src_col && dst_row_ptr && dst_col && g_vec && g_pos, "edge_vec_to_nodes: null pointer");
+  launch_node_vec3_segment(src_row_ptr, src_col, dst_row_ptr, dst_col, g_vec, g_pos, N, (cudaStream_t)stream);
+  return launched("edge_vec_to_nodes");
+}
+
+int fuma_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
+                     float* out, float* mean, float* rstd, void* stream) {
+  REQUIRE(M >= 0 && D > 0 && (D & 3) == 0 && D <= 2048, "ln_silu_fwd: D=%d must be a multiple of 4, <= 2048", D);
+  if (M == 0) return FUMA_OK;
+  REQUIRE(x && gamma && beta && out && mean && rstd, "ln_silu_fwd: null pointer");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(out, "out"); REQUIRE_ALIGNED(gamma, "gamma"); REQUIRE_ALIGNED(beta, "beta");
+  launch_ln_silu_fwd(x, gamma, beta, out, mean, rstd, M, D, eps, (cudaStream_t)stream);
+  return launched("ln_silu_fwd");
+}
+
+int fuma_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
+                     const float* g_out, int64_t M, int32_t D, float* g_x, void* stream) {
+  REQUIRE(M >= 0 && D > 0 && (D & 3) == 0 && D <= 2048, "ln_silu_bwd: D=%d must be a multiple of 4, <= 2048", D);
+  if (M == 0) return FUMA_OK;
+  REQUIRE(x && gamma && beta && mean && rstd && g_out && g_x, "ln_silu_bwd: null pointer");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(g_x, "g_x");
+  launch_ln_silu_bwd(x, gamma, beta, mean, rstd, g_out, g_x, M, D, (cudaStream_t)stream);
+  return launched("ln_silu_bwd");
+}
+
+int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
+                    const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
+                    float* X_m0, float* X_m1, float* X_m2, void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(N >= 0 && E >= 0, "gather_fwd: bad sizes");
+  if (E == 0) return FUMA_OK;
+  REQUIRE(x && idx_i && idx_j && wigner && rad && csd && batch && X_m0 && X_m1 && X_m2, "gather_fwd: null pointer");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(csd, "csd");
+  REQUIRE_ALIGNED(X_m0, "X_m0"); REQUIRE_ALIGNED(X_m1, "X_m1"); REQUIRE_ALIGNED(X_m2, "X_m2");
+  launch_gather_fwd(x, idx_i, idx_j, wigner, rad, csd, batch, X_m0, X_m1, X_m2, E, C, (cudaStream_t)stream);
+  return launched("gather_fwd");
+}
+
+int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
+                    const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
+                    const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
+                    const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
+                    float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
+                    void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(N >= 0 && E >= 0, "gather_bwd: bad sizes");
+  if (N == 0) return FUMA_OK;
+  REQUIRE(x && idx_i && wigner && rad && csd && batch && dst_row_ptr && dst_col && src_row_ptr && src_col && g_x &&
+              g_wigner && g_rad && g_X_m0 && g_X_m1 && g_X_m2,
+          "gather_bwd: null pointer");
+  REQUIRE(E == 0 || (scratch && scratch_floats >= E * 9 * (int64_t)C),
+          "gather_bwd: scratch must hold E*9*C = %lld floats", (long long)(E * 9 * (int64_t)C));
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(csd, "csd"); REQUIRE_ALIGNED(g_x, "g_x");
+  REQUIRE_ALIGNED(g_rad, "g_rad"); REQUIRE_ALIGNED(g_X_m0, "g_X_m0"); REQUIRE_ALIGNED(g_X_m1, "g_X_m1");
+  REQUIRE_ALIGNED(g_X_m2, "g_X_m2");
+  if (E > 0) REQUIRE_ALIGNED(scratch, "scratch");
+  launch_gather_bwd(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
+                    src_col, g_x, g_wigner, g_rad, scratch, N, C, (cudaStream_t)stream);
+  return launched("gather_bwd");
+}
+
+int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
+                    float* Z_m1, float* Z_m2, void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(E >= 0, "gating_fwd: bad E");
+  if (E == 0) return FUMA_OK;
+  REQUIRE(Y_m0 && Y_m1 && Y_m2 && Z_m0 && Z_m1 && Z_m2, "gating_fwd: null pointer");
+  REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
+  REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1"); REQUIRE_ALIGNED(Z_m2, "Z_m2");
+  launch_gating_fwd(Y_m0, Y_m1, Y_m2, Z_m0, Z_m1, Z_m2, E, C, (cudaStream_t)stream);
+  return launched("gating_fwd");
+}
+
+int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
+                    const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
+                    float* g_Y_m2, void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(E >= 0, "gating_bwd: bad E");
+  if (E == 0) return FUMA_OK;
+  REQUIRE(g_Z_m0 && g_Z_m1 && g_Z_m2 && Y_m0 && Y_m1 && Y_m2 && g_Y_m0 && g_Y_m1 && g_Y_m2, "gating_bwd: null pointer");
+  REQUIRE_ALIGNED(g_Z_m0, "g_Z_m0"); REQUIRE_ALIGNED(g_Z_m1, "g_Z_m1"); REQUIRE_ALIGNED(g_Z_m2, "g_Z_m2");
+  REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
+  REQUIRE_ALIGNED(g_Y_m0, "g_Y_m0"); REQUIRE_ALIGNED(g_Y_m1, "g_Y_m1"); REQUIRE_ALIGNED(g_Y_m2, "g_Y_m2");
+  launch_gating_bwd(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, g_Y_m0, g_Y_m1, g_Y_m2, E, C, (cudaStream_t)stream);
+  return launched("gating_bwd");
+}
+
+int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
+                            const float* env, const float* x_res, const int32_t* row_ptr, const int32_t* col_idx,
+                            int64_t N, int64_t E, int32_t C, float* x_out, void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(N >= 0 && E >= 0, "rotate_scatter_fwd: bad sizes");
+  if (N == 0) return FUMA_OK;
+  REQUIRE(x_res && row_ptr && x_out && (E == 0 || (Z_m0 && Z_m1 && Z_m2 && wigner && env && col_idx)),
+          "rotate_scatter_fwd: null pointer");
+  REQUIRE_ALIGNED(x_res, "x_res"); REQUIRE_ALIGNED(x_out, "x_out");
+  if (E > 0) { REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1"); REQUIRE_ALIGNED(Z_m2, "Z_m2"); }
+  launch_rotate_scatter_fwd(row_ptr, col_idx, Z_m0, Z_m1, Z_m2, wigner, env, x_res, x_out, N, C, (cudaStream_t)stream);
+  return launched("rotate_scatter_fwd");
+}
+
+int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
+                            const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
+                            int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
+                            float* g_wigner, float* g_env, void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(N >= 0 && E >= 0, "rotate_scatter_bwd: bad sizes");
+  if (E == 0 || N == 0) return FUMA_OK;
+  REQUIRE(g_out && Z_m0 && Z_m1 && Z_m2 && wigner && env && row_ptr && col_idx && g_Z_m0 && g_Z_m1 && g_Z_m2 &&
+              g_wigner && g_env,
+          "rotate_scatter_bwd: null pointer");
+  REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1");
+  REQUIRE_ALIGNED(Z_m2, "Z_m2"); REQUIRE_ALIGNED(g_Z_m0, "g_Z_m0"); REQUIRE_ALIGNED(g_Z_m1, "g_Z_m1");
+  REQUIRE_ALIGNED(g_Z_m2, "g_Z_m2");
+  launch_rotate_scatter_bwd(row_ptr, col_idx, g_out, Z_m0, Z_m1, Z_m2, wigner, env, g_Z_m0, g_Z_m1, g_Z_m2, g_wigner,
+                            g_env, N, C, (cudaStream_t)stream);
+  return launched("rotate_scatter_bwd");
+}
+
+int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* env, const int64_t* Z,
+                          const int64_t* batch, const float* W_sphere, const float* csd, const int32_t* row_ptr,
+                          const int32_t* col_idx, int64_t N, int64_t E, int32_t C, float* x_out, void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(N >= 0 && E >= 0, "init_scatter_fwd: bad sizes");
+  if (N == 0) return FUMA_OK;
+  REQUIRE(Z && batch && W_sphere && csd && row_ptr && x_out && (E == 0 || (rad && wigner && env && col_idx)),
+          "init_scatter_fwd: null pointer");
+  REQUIRE_ALIGNED(W_sphere, "W_sphere"); REQUIRE_ALIGNED(csd, "csd"); REQUIRE_ALIGNED(x_out, "x_out");
+  if (E > 0) REQUIRE_ALIGNED(rad, "rad");
+  launch_init_scatter_fwd(row_ptr, col_idx, rad, wigner, env, Z, batch, W_sphere, csd, x_out, N, C,
+                          (cudaStream_t)stream);
+  return launched("init_scatter_fwd");
+}
+
+int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wigner, const float* env,
+                          const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
+                          float* g_rad, float* g_wigner, float* g_env, void* stream) {
+  if (int r = check_C(C)) return r;
+  REQUIRE(N >= 0 && E >= 0, "init_scatter_bwd: bad sizes");
+  if (E == 0 || N == 0) return FUMA_OK;
+  REQUIRE(g_out && rad && wigner && env && row_ptr && col_idx && g_rad && g_wigner && g_env,
+          "init_scatter_bwd: null pointer");
+  REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(g_rad, "g_rad");
+  launch_init_scatter_bwd(row_ptr, col_idx, g_out, rad, wigner, env, g_rad, g_wigner, g_env, N, C,
+                          (cudaStream_t)stream);
+  return launched("init_scatter_bwd");
+}
+
+}  // extern "C"

@@ -1,0 +1,207 @@
+// Streaming kernels: split gating (forward/backward) and fused LayerNorm + SiLU.
+//
+// Gating reference: ops/gating.py:32-103 (forward), :109-185 (backward).
+//   g0 = sigmoid(Y0[0]), g1 = sigmoid(Y0[1])
+//   Z_m0 = [silu(Y0[2]), Y0[3] g0, Y0[4] g1]; Z_m1 = [Y1[0] g0, Y1[1] g1, Y1[2] g0, Y1[3] g1];
+//   Z_m2 = [Y2[0] g1, Y2[1] g1]                        (C-wide slots, per edge)
+// LayerNorm + SiLU reference: ops/ln_silu.py:29-72 (forward), :77-123 (backward, dx only):
+//   y = (x - mean) * rstd * gamma + beta, rstd = 1/sqrt(var + eps) (biased variance), out = y sigmoid(y)
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fuma {
+
+namespace {
+__device__ __forceinline__ float4 sig4(float4 a) {
+  return make_float4(sigmoidf_(a.x), sigmoidf_(a.y), sigmoidf_(a.z), sigmoidf_(a.w));
+}
+}  // namespace
+
+// One thread per (edge, 4 channels).
+__global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict__ Y0, const float* __restrict__ Y1,
+                                                         const float* __restrict__ Y2, float* __restrict__ Z0,
+                                                         float* __restrict__ Z1, float* __restrict__ Z2, int64_t E,
+                                                         int C) {
+  const int C4 = C >> 2;
+  const int64_t total = E * C4;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = t / C4;
+    const int co = (int)(t - e * C4) * 4;
+    const float* y0 = Y0 + e * 5 * (int64_t)C + co;
+    const float* y1 = Y1 + e * 4 * (int64_t)C + co;
+    const float* y2 = Y2 + e * 2 * (int64_t)C + co;
+    const float4 g0 = sig4(ld4_stream(y0)), g1 = sig4(ld4_stream(y0 + C));
+    const float4 a = ld4_stream(y0 + 2 * C);
+    float* z0 = Z0 + e * 3 * (int64_t)C + co;
+    float* z1 = Z1 + e * 4 * (int64_t)C + co;
+    float* z2 = Z2 + e * 2 * (int64_t)C + co;
+    st4_stream(z0, a * sig4(a));
+    st4_stream(z0 + C, ld4_stream(y0 + 3 * C) * g0);
+    st4_stream(z0 + 2 * C, ld4_stream(y0 + 4 * C) * g1);
+    st4_stream(z1, ld4_stream(y1) * g0);
+    st4_stream(z1 + C, ld4_stream(y1 + C) * g1);
+    st4_stream(z1 + 2 * C, ld4_stream(y1 + 2 * C) * g0);
+    st4_stream(z1 + 3 * C, ld4_stream(y1 + 3 * C) * g1);
+    st4_stream(z2, ld4_stream(y2) * g1);
+    st4_stream(z2 + C, ld4_stream(y2 + C) * g1);
+  }
+}
+
+__global__ void __launch_bounds__(256) gating_bwd_kernel(
+    const float* __restrict__ gZ0, const float* __restrict__ gZ1, const float* __restrict__ gZ2,
+    const float* __restrict__ Y0, const float* __restrict__ Y1, const float* __restrict__ Y2,
+    float* __restrict__ gY0, float* __restrict__ gY1, float* __restrict__ gY2, int64_t E, int C) {
+  const int C4 = C >> 2;
+  const int64_t total = E * C4;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = t / C4;
+    const int co = (int)(t - e * C4) * 4;
+    const float* y0 = Y0 + e * 5 * (int64_t)C + co;
+    const float* y1 = Y1 + e * 4 * (int64_t)C + co;
+    const float* y2 = Y2 + e * 2 * (int64_t)C + co;
+    const float* q0 = gZ0 + e * 3 * (int64_t)C + co;
+    const float* q1 = gZ1 + e * 4 * (int64_t)C + co;
+    const float* q2 = gZ2 + e * 2 * (int64_t)C + co;
+    const float4 g0 = sig4(ld4_stream(y0)), g1 = sig4(ld4_stream(y0 + C));
+    const float4 a = ld4_stream(y0 + 2 * C), sa = sig4(a);
+    const float4 y3 = ld4_stream(y0 + 3 * C), y4 = ld4_stream(y0 + 4 * C);
+    const float4 u0 = ld4_stream(y1), u1 = ld4_stream(y1 + C), u2 = ld4_stream(y1 + 2 * C), u3 = ld4_stream(y1 + 3 * C);
+    const float4 w0 = ld4_stream(y2), w1 = ld4_stream(y2 + C);
+    const float4 ga = ld4_stream(q0), g3 = ld4_stream(q0 + C), g4 = ld4_stream(q0 + 2 * C);
+    const float4 h0 = ld4_stream(q1), h1 = ld4_stream(q1 + C), h2 = ld4_stream(q1 + 2 * C), h3 = ld4_stream(q1 + 3 * C);
+    const float4 k0 = ld4_stream(q2), k1 = ld4_stream(q2 + C);
+    const float4 one = f4(1.f);
+    const float4 dg0 = g0 * (one - g0), dg1 = g1 * (one - g1);
+    float* p0 = gY0 + e * 5 * (int64_t)C + co;
+    float* p1 = gY1 + e * 4 * (int64_t)C + co;
+    float* p2 = gY2 + e * 2 * (int64_t)C + co;
+    st4_stream(p0, dg0 * (g3 * y3 + h0 * u0 + h2 * u2));
+    st4_stream(p0 + C, dg1 * (g4 * y4 + h1 * u1 + h3 * u3 + k0 * w0 + k1 * w1));
+    st4_stream(p0 + 2 * C, ga * (sa + a * (sa * (one - sa))));
+    st4_stream(p0 + 3 * C, g3 * g0);
+    st4_stream(p0 + 4 * C, g4 * g1);
+    st4_stream(p1, h0 * g0);
+    st4_stream(p1 + C, h1 * g1);
+    st4_stream(p1 + 2 * C, h2 * g0);
+    st4_stream(p1 + 3 * C, h3 * g1);
+    st4_stream(p2, k0 * g1);
+    st4_stream(p2 + C, k1 * g1);
+  }
+}
+
+// One warp per row; VPL float4 per lane (D <= 128 * VPL), row kept in registers.
+template <int VPL>
+__global__ void __launch_bounds__(256) ln_silu_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                          const float* __restrict__ beta, float* __restrict__ out,
+                                                          float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                          int64_t M, int D, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int D4 = D >> 2;
+  for (int64_t r = (int64_t)blockIdx.x * wpb + warp; r < M; r += (int64_t)gridDim.x * wpb) {
+    const float* xr = x + r * D;
+    float4 v[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int d4 = lane + 32 * q;
+      v[q] = d4 < D4 ? ld4_stream(xr + d4 * 4) : f4(0.f);
+      s += (v[q].x + v[q].y) + (v[q].z + v[q].w);
+    }
+    const float mean = warp_sum(s) / (float)D;
+    float ss = 0.f;
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int d4 = lane + 32 * q;
+      if (d4 < D4) {
+        const float4 c = v[q] - f4(mean);
+        ss += dot4(c, c);
+      }
+    }
+    const float var = warp_sum(ss) / (float)D;
+    const float rstd = 1.0f / sqrtf(var + eps);
+    if (lane == 0) { mean_out[r] = mean; rstd_out[r] = rstd; }
+    float* orow = out + r * D;
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int d4 = lane + 32 * q;
+      if (d4 < D4) {
+        const float4 y = (v[q] - f4(mean)) * rstd * ld4_keep(gamma + d4 * 4) + ld4_keep(beta + d4 * 4);
+        st4(orow + d4 * 4, y * sig4(y));
+      }
+    }
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                          const float* __restrict__ beta, const float* __restrict__ mean,
+                                                          const float* __restrict__ rstd, const float* __restrict__ g_out,
+                                                          float* __restrict__ g_x, int64_t M, int D) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int D4 = D >> 2;
+  for (int64_t r = (int64_t)blockIdx.x * wpb + warp; r < M; r += (int64_t)gridDim.x * wpb) {
+    const float mu = mean[r], rs = rstd[r];
+    float4 xh[VPL], gxh[VPL];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int d4 = lane + 32 * q;
+      if (d4 < D4) {
+        xh[q] = (ld4_stream(x + r * D + d4 * 4) - f4(mu)) * rs;
+        const float4 gm = ld4_keep(gamma + d4 * 4);
+        const float4 y = xh[q] * gm + ld4_keep(beta + d4 * 4);
+        const float4 sg = sig4(y);
+        const float4 ds = sg + y * (sg * (f4(1.f) - sg));
+        gxh[q] = ld4_stream(g_out + r * D + d4 * 4) * ds * gm;
+        s1 += (gxh[q].x + gxh[q].y) + (gxh[q].z + gxh[q].w);
+        s2 += dot4(gxh[q], xh[q]);
+      } else {
+        xh[q] = f4(0.f); gxh[q] = f4(0.f);
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float invD = 1.0f / (float)D;
+#pragma unroll
+    for (int q = 0; q < VPL; ++q) {
+      const int d4 = lane + 32 * q;
+      if (d4 < D4) st4(g_x + r * D + d4 * 4, (gxh[q] - (f4(s1) + xh[q] * s2) * invD) * rs);
+    }
+  }
+}
+
+void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,
+                       int C, cudaStream_t s) {
+  gating_fwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(Y0, Y1, Y2, Z0, Z1, Z2, E, C);
+}
+
+void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, const float* Y0, const float* Y1,
+                       const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, cudaStream_t s) {
+  gating_bwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C);
+}
+
+void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float* out, float* mean, float* rstd,
+                        int64_t M, int D, float eps, cudaStream_t s) {
+  const unsigned g = grid_for(M, 8, 8);
+  const int d4 = D / 4;
+  if (d4 <= 32) ln_silu_fwd_kernel<1><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
+  else if (d4 <= 64) ln_silu_fwd_kernel<2><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
+  else if (d4 <= 128) ln_silu_fwd_kernel<4><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
+  else if (d4 <= 256) ln_silu_fwd_kernel<8><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
+  else ln_silu_fwd_kernel<16><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
+}
+
+void launch_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
+                        const float* g_out, float* g_x, int64_t M, int D, cudaStream_t s) {
+  const unsigned g = grid_for(M, 8, 8);
+  const int d4 = D / 4;
+  if (d4 <= 32) ln_silu_bwd_kernel<1><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
+  else if (d4 <= 64) ln_silu_bwd_kernel<2><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
+  else if (d4 <= 128) ln_silu_bwd_kernel<4><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
+  else if (d4 <= 256) ln_silu_bwd_kernel<8><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
+  else ln_silu_bwd_kernel<16><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
+}
+
+}  // namespace fuma

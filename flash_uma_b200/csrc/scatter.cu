@@ -1,0 +1,331 @@
+// Inverse rotation out of the edge frame + envelope + deterministic FP64 segment sum
+// over the destination CSR (+ residual), and the initial edge-degree node embedding.
+//
+// Reference: ops/scatter.py:45-140 (rotate-scatter forward), :146-292 (backward),
+//            :360-423 (init scatter forward), :426-481 (init backward).
+//
+// Per edge e, channel c (C-wide slots):
+//   Z_m0 [E,3C] = [l0, l1(m=0), l2(m=0)]; Z_m1 [E,4C] = [R_l1, R_l2, I_l1, I_l2]; Z_m2 [E,2C] = [R_l2, I_l2]
+//   edge-frame rows  m1 = (I_l1, l1(m=0), R_l1),  m2 = (I_m2, I_l2, l2(m=0), R_l2, R_m2)
+//   message = env_e * [Z_m0[0]; D1^T m1; D2^T m2]
+// x_out[j] = x_res[j] + sum_{e in CSR row j} message_e, summed in fp64 in CSR order
+// (products in fp32), then rounded to fp32 once. Deterministic run to run.
+//
+// One warp per destination node; lane l owns channels [4l, 4l+4) (+128 per
+// extra group), 16-byte coalesced accesses; the per-edge scalars (34 Wigner
+// values + env) are staged once per edge in shared memory and broadcast.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fuma {
+
+namespace {
+
+__device__ __forceinline__ void stage_edge(float* sw, const float* __restrict__ wig, const float* __restrict__ env,
+                                           int64_t e, int lane) {
+  sw[lane] = __ldg(wig + e * kWig + lane);
+  if (lane < 2) sw[32 + lane] = __ldg(wig + e * kWig + 32 + lane);
+  if (lane == 2) sw[34] = __ldg(env + e);
+}
+
+}  // namespace
+
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) rotate_scatter_fwd_kernel(
+    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ Z0,
+    const float* __restrict__ Z1, const float* __restrict__ Z2, const float* __restrict__ wig,
+    const float* __restrict__ env, const float* __restrict__ x_res, float* __restrict__ x_out, int64_t N, int C) {
+  __shared__ float s_w[WARPS][36];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C4 = C >> 2;
+  float* sw = s_w[warp];
+  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+    const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
+    for (int c0 = 0; c0 < C4; c0 += 32) {
+      const int c4 = c0 + lane;
+      const bool act = c4 < C4;
+      const int co = c4 * 4;
+      d4 acc[9];
+      if (act) {
+        const float* xr = x_res + jn * 9 * (int64_t)C + co;
+#pragma unroll
+        for (int l = 0; l < 9; ++l) acc[l] = d4_of(ld4(xr + l * C));
+      }
+      for (int k = kb; k < ke; ++k) {
+        const int64_t e = col_idx[k];
+        stage_edge(sw, wig, env, e, lane);
+        __syncwarp();
+        if (act) {
+          const float* D1 = sw;
+          const float* D2 = sw + 9;
+          const float ev = sw[34];
+          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+          const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
+          const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
+                                ld4_stream(z1 + C), ld4_stream(z2)};
+          acc[0] += ld4_stream(z0) * ev;
+#pragma unroll
+          for (int kk = 0; kk < 3; ++kk) {
+            float4 a = D1[kk] * m1[0];
+            fma4(a, D1[3 + kk], m1[1]);
+            fma4(a, D1[6 + kk], m1[2]);
+            acc[1 + kk] += a * ev;
+          }
+#pragma unroll
+          for (int kk = 0; kk < 5; ++kk) {
+            float4 a = D2[kk] * m2[0];
+#pragma unroll
+            for (int r = 1; r < 5; ++r) fma4(a, D2[r * 5 + kk], m2[r]);
+            acc[4 + kk] += a * ev;
+          }
+        }
+        __syncwarp();
+      }
+      if (act) {
+        float* xo = x_out + jn * 9 * (int64_t)C + co;
+#pragma unroll
+        for (int l = 0; l < 9; ++l) st4(xo + l * C, f4_of(acc[l]));
+      }
+    }
+  }
+}
+
+// Backward, grouped by destination so g_out[j] is read once per node:
+//   g_Z = env * (rows of D applied to g_out[j]); g_wigner[e] = env * sum_c g_out[j] (x) m;
+//   g_env[e] = sum_c g_out[j] . (unscaled message).  (g_x_res = g_out is returned by the host.)
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) rotate_scatter_bwd_kernel(
+    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
+    const float* __restrict__ Z0, const float* __restrict__ Z1, const float* __restrict__ Z2,
+    const float* __restrict__ wig, const float* __restrict__ env, float* __restrict__ gZ0, float* __restrict__ gZ1,
+    float* __restrict__ gZ2, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C) {
+  __shared__ float s_w[WARPS][36];
+  __shared__ float s_red[WARPS][36];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C4 = C >> 2;
+  float* sw = s_w[warp];
+  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+    const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
+    for (int k = kb; k < ke; ++k) {
+      const int64_t e = col_idx[k];
+      stage_edge(sw, wig, env, e, lane);
+      __syncwarp();
+      const float* D1 = sw;
+      const float* D2 = sw + 9;
+      const float ev = sw[34];
+      float part[35];
+#pragma unroll
+      for (int m = 0; m < 35; ++m) part[m] = 0.f;
+      for (int c4 = lane; c4 < C4; c4 += 32) {
+        const int co = c4 * 4;
+        const float* go = g_out + jn * 9 * (int64_t)C + co;
+        float4 g[9];
+#pragma unroll
+        for (int l = 0; l < 9; ++l) g[l] = ld4_keep(go + l * C);
+        const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+        const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+        const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+        const float4 zl0 = ld4_stream(z0);
+        const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
+        const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
+                              ld4_stream(z1 + C), ld4_stream(z2)};
+        // g_Z: row r of the edge frame receives env * sum_k D[r][k] g[k]
+        float4 t1[3], t2[5];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+          float4 a = D1[r * 3] * g[1];
+          fma4(a, D1[r * 3 + 1], g[2]);
+          fma4(a, D1[r * 3 + 2], g[3]);
+          t1[r] = a * ev;
+        }
+#pragma unroll
+        for (int r = 0; r < 5; ++r) {
+          float4 a = D2[r * 5] * g[4];
+#pragma unroll
+          for (int kk = 1; kk < 5; ++kk) fma4(a, D2[r * 5 + kk], g[4 + kk]);
+          t2[r] = a * ev;
+        }
+        float* q0 = gZ0 + e * 3 * (int64_t)C + co;
+        float* q1 = gZ1 + e * 4 * (int64_t)C + co;
+        float* q2 = gZ2 + e * 2 * (int64_t)C + co;
+        st4_stream(q0, g[0] * ev);
+        st4_stream(q0 + C, t1[1]);
+        st4_stream(q0 + 2 * C, t2[2]);
+        st4_stream(q1, t1[2]);
+        st4_stream(q1 + C, t2[3]);
+        st4_stream(q1 + 2 * C, t1[0]);
+        st4_stream(q1 + 3 * C, t2[1]);
+        st4_stream(q2, t2[4]);
+        st4_stream(q2 + C, t2[0]);
+        // Wigner-gradient partials (before env): d/dD1[r][k] = sum_c g[1+k] m1[r]
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+          for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] += dot4(g[1 + kk], m1[r]);
+#pragma unroll
+        for (int r = 0; r < 5; ++r)
+#pragma unroll
+          for (int kk = 0; kk < 5; ++kk) part[9 + r * 5 + kk] += dot4(g[4 + kk], m2[r]);
+        part[34] += dot4(g[0], zl0);
+      }
+#pragma unroll
+      for (int m = 0; m < 35; ++m) {
+        const float t = warp_sum(part[m]);
+        if (lane == 0) s_red[warp][m] = t;
+      }
+      __syncwarp();
+      // g_env = sum_c g0 z0 + sum_{r,k} D[r][k] * raw[r][k]
+      float genv = (lane < 32) ? sw[lane] * s_red[warp][lane] : 0.f;
+      if (lane < 2) genv += sw[32 + lane] * s_red[warp][32 + lane];
+      genv = warp_sum(genv);
+      g_wig[e * kWig + lane] = s_red[warp][lane] * ev;
+      if (lane < 2) g_wig[e * kWig + 32 + lane] = s_red[warp][32 + lane] * ev;
+      if (lane == 0) g_env[e] = genv + s_red[warp][34];
+      __syncwarp();
+    }
+  }
+}
+
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) init_scatter_fwd_kernel(
+    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ rad,
+    const float* __restrict__ wig, const float* __restrict__ env, const int64_t* __restrict__ Z,
+    const int64_t* __restrict__ batch, const float* __restrict__ W_sphere, const float* __restrict__ csd,
+    float* __restrict__ x_out, int64_t N, int C) {
+  __shared__ float s_w[WARPS][36];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C4 = C >> 2;
+  float* sw = s_w[warp];
+  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+    const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
+    const int64_t z = Z[jn], b = batch[jn];
+    for (int c0 = 0; c0 < C4; c0 += 32) {
+      const int c4 = c0 + lane;
+      const bool act = c4 < C4;
+      const int co = c4 * 4;
+      d4 acc[9];
+      if (act) {
+        acc[0] = d4_of(ld4_keep(W_sphere + z * C + co) + ld4_keep(csd + b * C + co));
+#pragma unroll
+        for (int l = 1; l < 9; ++l) acc[l] = d4{0.0, 0.0, 0.0, 0.0};
+      }
+      for (int k = kb; k < ke; ++k) {
+        const int64_t e = col_idx[k];
+        stage_edge(sw, wig, env, e, lane);
+        __syncwarp();
+        if (act) {
+          const float ev = sw[34];
+          const float* rr = rad + e * 3 * (int64_t)C + co;
+          const float4 r0 = ld4_stream(rr), r1 = ld4_stream(rr + C), r2 = ld4_stream(rr + 2 * C);
+          acc[0] += div4(r0 * ev, 5.f);
+#pragma unroll
+          for (int kk = 0; kk < 3; ++kk) acc[1 + kk] += div4((r1 * sw[3 + kk]) * ev, 5.f);
+#pragma unroll
+          for (int kk = 0; kk < 5; ++kk) acc[4 + kk] += div4((r2 * sw[9 + 10 + kk]) * ev, 5.f);
+        }
+        __syncwarp();
+      }
+      if (act) {
+        float* xo = x_out + jn * 9 * (int64_t)C + co;
+#pragma unroll
+        for (int l = 0; l < 9; ++l) st4(xo + l * C, f4_of(acc[l]));
+      }
+    }
+  }
+}
+
+// Init-scatter backward (destination-grouped): g_rad = [g0, D1[1,:].g_l1, D2[2,:].g_l2] * env / 5,
+// g_wigner (m=0 rows only, other entries zero) = env * sum_c g (x) r / 5, g_env = sum_c g . contrib / env.
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
+    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
+    const float* __restrict__ rad, const float* __restrict__ wig, const float* __restrict__ env,
+    float* __restrict__ g_rad, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C) {
+  __shared__ float s_w[WARPS][36];
+  __shared__ float s_red[WARPS][12];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C4 = C >> 2;
+  float* sw = s_w[warp];
+  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+    const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
+    for (int k = kb; k < ke; ++k) {
+      const int64_t e = col_idx[k];
+      stage_edge(sw, wig, env, e, lane);
+      __syncwarp();
+      const float ev = sw[34];
+      float part[9];
+#pragma unroll
+      for (int m = 0; m < 9; ++m) part[m] = 0.f;
+      for (int c4 = lane; c4 < C4; c4 += 32) {
+        const int co = c4 * 4;
+        const float* go = g_out + jn * 9 * (int64_t)C + co;
+        float4 g[9];
+#pragma unroll
+        for (int l = 0; l < 9; ++l) g[l] = div4(ld4_keep(go + l * C), 5.f);
+        const float* rr = rad + e * 3 * (int64_t)C + co;
+        const float4 r0 = ld4_stream(rr), r1 = ld4_stream(rr + C), r2 = ld4_stream(rr + 2 * C);
+        float4 s1 = g[1] * sw[3];
+        fma4(s1, sw[4], g[2]);
+        fma4(s1, sw[5], g[3]);
+        float4 s2 = g[4] * sw[19];
+#pragma unroll
+        for (int kk = 1; kk < 5; ++kk) fma4(s2, sw[19 + kk], g[4 + kk]);
+        float* gr = g_rad + e * 3 * (int64_t)C + co;
+        st4_stream(gr, g[0] * ev);
+        st4_stream(gr + C, s1 * ev);
+        st4_stream(gr + 2 * C, s2 * ev);
+#pragma unroll
+        for (int kk = 0; kk < 3; ++kk) part[kk] += dot4(g[1 + kk], r1);
+#pragma unroll
+        for (int kk = 0; kk < 5; ++kk) part[3 + kk] += dot4(g[4 + kk], r2);
+        part[8] += dot4(g[0], r0) + dot4(s1, r1) + dot4(s2, r2);
+      }
+#pragma unroll
+      for (int m = 0; m < 9; ++m) {
+        const float t = warp_sum(part[m]);
+        if (lane == 0) s_red[warp][m] = t;
+      }
+      __syncwarp();
+      // full 34-wide row: D1 row 1 -> entries 3..5, D2 row 2 -> entries 19..23, zeros elsewhere
+      float v = 0.f;
+      if (lane >= 3 && lane < 6) v = s_red[warp][lane - 3] * ev;
+      if (lane >= 19 && lane < 24) v = s_red[warp][3 + lane - 19] * ev;
+      g_wig[e * kWig + lane] = v;
+      if (lane < 2) g_wig[e * kWig + 32 + lane] = 0.f;
+      if (lane == 0) g_env[e] = s_red[warp][8];
+      __syncwarp();
+    }
+  }
+}
+
+void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* Z0, const float* Z1,
+                               const float* Z2, const float* wig, const float* env, const float* x_res, float* x_out,
+                               int64_t N, int C, cudaStream_t s) {
+  rotate_scatter_fwd_kernel<8><<<grid_for(N, 8, 8), 256, 0, s>>>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out,
+                                                                 N, C);
+}
+
+void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* Z0,
+                               const float* Z1, const float* Z2, const float* wig, const float* env, float* gZ0,
+                               float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, cudaStream_t s) {
+  rotate_scatter_bwd_kernel<4><<<grid_for(N, 4, 16), 128, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0,
+                                                                  gZ1, gZ2, g_wig, g_env, N, C);
+}
+
+void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,
+                             const float* env, const int64_t* Z, const int64_t* batch, const float* W_sphere,
+                             const float* csd, float* x_out, int64_t N, int C, cudaStream_t s) {
+  init_scatter_fwd_kernel<8><<<grid_for(N, 8, 8), 256, 0, s>>>(row_ptr, col_idx, rad, wig, env, Z, batch, W_sphere,
+                                                               csd, x_out, N, C);
+}
+
+void launch_init_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* rad,
+                             const float* wig, const float* env, float* g_rad, float* g_wig, float* g_env, int64_t N,
+                             int C, cudaStream_t s) {
+  init_scatter_bwd_kernel<4><<<grid_for(N, 4, 16), 128, 0, s>>>(row_ptr, col_idx, g_out, rad, wig, env, g_rad, g_wig,
+                                                                 g_env, N, C);
+}
+
+}  // namespace fuma

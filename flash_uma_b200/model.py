@@ -1,0 +1,175 @@
+"""Model graph of the hot path: Morton reorder, cached CSRs, geometry, radial MLPs and the
+message-passing layers, driving the CUDA ops of :mod:`flash_uma_b200.ops`.
+
+Mirrors the reference ``model.py`` (``reorder_graph_morton`` :56-74, ``build_csr_cached``
+:28-44, ``Packed_eSCN_Layer`` :81-157, ``eSCN_Inference_Model`` :160-221). The dense
+contractions (radial MLP and SO(2) convolutions) are ``F.linear`` calls, as in the
+reference; TF32 follows PyTorch's global ``torch.backends.cuda.matmul`` setting.
+"""
+from __future__ import annotations
+
+from collections import OrderedDict
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .nodewise import balance_channels_batched
+
+# ---- graph preparation ---------------------------------------------------------------------
+
+_GRAPH_CACHE_CAPACITY = 8
+_graph_cache: "OrderedDict[tuple, ops.GraphCSR]" = OrderedDict()
+
+
+def _cache_key(idx_i: torch.Tensor, idx_j: torch.Tensor, N: int) -> tuple:
+    # same invalidation rule as model.py:28-44: storage pointer, in-place version, size, device
+    dev = idx_j.device.index if idx_j.device.type == "cuda" else -1
+    return (idx_i.data_ptr(), idx_i._version, idx_j.data_ptr(), idx_j._version, idx_j.numel(), N, dev)
+
+
+def build_graph_cached(idx_i: torch.Tensor, idx_j: torch.Tensor, N: int) -> ops.GraphCSR:
+    """Destination + source CSR of the edges, LRU-cached on the index tensors (``model.py:28-44``)."""
+    key = _cache_key(idx_i, idx_j, N)
+    hit = _graph_cache.get(key)
+    if hit is not None:
+        _graph_cache.move_to_end(key)
+        return hit
+    g = ops.build_graph_csr(idx_i, idx_j, N)
+    # keep the index tensors alive so their storage (and the key) cannot be recycled
+    g.keepalive = (idx_i, idx_j)
+    _graph_cache[key] = g
+    if len(_graph_cache) > _GRAPH_CACHE_CAPACITY:
+        _graph_cache.popitem(last=False)
+    return g
+
+
+def clear_graph_cache() -> None:
+    _graph_cache.clear()
+
+
+def _expand_bits(v: torch.Tensor) -> torch.Tensor:
+    v = (v | (v << 16)) & 0x030000FF
+    v = (v | (v << 8)) & 0x0300F00F
+    v = (v | (v << 4)) & 0x030C30C3
+    v = (v | (v << 2)) & 0x09249249
+    return v
+
+
+def reorder_graph_morton(pos, Z, batch, idx_i, idx_j):
+    """Sort atoms by (system, 30-bit Morton code of the position quantised to 10 bits per
+    axis over the bounding box) and remap the edges (``model.py:47-74``); stable sort."""
+    pos_min = pos.min(dim=0, keepdim=True)[0]
+    pos_max = pos.max(dim=0, keepdim=True)[0]
+    scale = 1023.0 / torch.clamp(pos_max - pos_min, min=1e-5)
+    q = ((pos - pos_min) * scale).to(torch.int32)
+    code = _expand_bits(q[:, 0]) | (_expand_bits(q[:, 1]) << 1) | (_expand_bits(q[:, 2]) << 2)
+    keys = code.to(torch.int64) | (batch.to(torch.int64) << 32)
+    perm = torch.argsort(keys, stable=True)
+    inv_perm = torch.empty_like(perm)
+    inv_perm[perm] = torch.arange(len(perm), device=pos.device)
+    return pos[perm], Z[perm], batch[perm], inv_perm[idx_i], inv_perm[idx_j], perm, inv_perm
+
+
+# ---- layers ------------------------------------------------------------------------------------
+
+def pack_complex(R: torch.Tensor, I: torch.Tensor) -> torch.Tensor:
+    """Real block form [[R, -I], [I, R]] of the complex SO(2) map R + iI (``model.py:101-138``)."""
+    return torch.cat([torch.cat([R, -I], 1), torch.cat([I, R], 1)], 0)
+
+
+class RadialMLP(nn.Module):
+    """Linear -> LN-SiLU -> Linear -> LN-SiLU -> Linear (``model.py:147-149``, ``:203-205``)."""
+
+    def __init__(self, net):
+        super().__init__()
+        g = lambda t: t.detach().clone().float()
+        self.register_buffer("W1", g(net[0].weight)); self.register_buffer("b1", g(net[0].bias))
+        self.register_buffer("g1", g(net[1].weight)); self.register_buffer("be1", g(net[1].bias))
+        self.register_buffer("W2", g(net[3].weight)); self.register_buffer("b2", g(net[3].bias))
+        self.register_buffer("g2", g(net[4].weight)); self.register_buffer("be2", g(net[4].bias))
+        self.register_buffer("W3", g(net[6].weight)); self.register_buffer("b3", g(net[6].bias))
+
+    def forward(self, x_edge):
+        h1 = ops.layer_norm_silu(F.linear(x_edge, self.W1, self.b1), self.g1, self.be1)
+        h2 = ops.layer_norm_silu(F.linear(h1, self.W2, self.b2), self.g2, self.be2)
+        return F.linear(h2, self.W3, self.b3)
+
+
+class PackedLayer(nn.Module):
+    """One eSCN message-passing block (``Packed_eSCN_Layer``, ``model.py:81-157``)."""
+
+    def __init__(self, blk, C: int):
+        super().__init__()
+        c1, c2 = blk.edge_wise.so2_conv_1, blk.edge_wise.so2_conv_2
+        g = lambda t: t.detach().clone().float()
+        self.C = C
+        self.rad = RadialMLP(c1.rad_func.net)
+        self.register_buffer("W_conv1_m0", g(c1.fc_m0.weight)); self.register_buffer("b_conv1_m0", g(c1.fc_m0.bias))
+        w = g(c1.so2_m_conv[0].fc.weight); self.register_buffer("W_conv1_m1", pack_complex(w[:2 * C], w[2 * C:]))
+        w = g(c1.so2_m_conv[1].fc.weight); self.register_buffer("W_conv1_m2", pack_complex(w[:C], w[C:]))
+        self.register_buffer("W_conv2_m0", g(c2.fc_m0.weight)); self.register_buffer("b_conv2_m0", g(c2.fc_m0.bias))
+        w = g(c2.so2_m_conv[0].fc.weight); self.register_buffer("W_conv2_m1", pack_complex(w[:2 * C], w[2 * C:]))
+        w = g(c2.so2_m_conv[1].fc.weight); self.register_buffer("W_conv2_m2", pack_complex(w[:C], w[C:]))
+        self.norm_1, self.norm_2, self.atom_wise = blk.norm_1, blk.norm_2, blk.atom_wise
+        for m in (self.norm_1, self.norm_2, self.atom_wise):
+            for p in m.parameters():
+                p.requires_grad_(False)
+
+    def forward(self, x_in, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch):
+        x_norm = self.norm_1(x_in)
+        rad_out = self.rad(x_edge)
+        X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch, graph=graph)
+        Y0 = F.linear(X0, self.W_conv1_m0, self.b_conv1_m0)
+        Y1 = F.linear(X1, self.W_conv1_m1)
+        Y2 = F.linear(X2, self.W_conv1_m2)
+        Z0, Z1, Z2 = ops.fused_gating_split(Y0, Y1, Y2, self.C)
+        O0 = F.linear(Z0, self.W_conv2_m0, self.b_conv2_m0)
+        O1 = F.linear(Z1, self.W_conv2_m1)
+        O2 = F.linear(Z2, self.W_conv2_m2)
+        x_mid = ops.rotate_scatter_split(O0, O1, O2, wigner, env, x_in, idx_j, graph.dst_row_ptr, graph.dst_col,
+                                         x_in.shape[0])
+        return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
+
+
+class ESCNInferenceModel(nn.Module):
+    """``eSCN_Inference_Model`` (``model.py:160-221``) built from a FAIRChem-layout backbone."""
+
+    def __init__(self, off_bb):
+        super().__init__()
+        self.C = int(off_bb.sphere_channels)
+        self.B = int(off_bb.num_distance_basis)
+        self.cutoff = float(off_bb.cutoff)
+        offset = torch.linspace(0.0, self.cutoff, self.B)
+        self.coeff_g = float(-0.5 / (2.0 * (offset[1] - offset[0])) ** 2)  # wrapper.py:122-125
+        g = lambda t: t.detach().clone().float()
+        self.register_buffer("offset_g", offset)
+        self.register_buffer("W_sphere", g(off_bb.sphere_embedding.weight))
+        self.register_buffer("W_src", g(off_bb.source_embedding.weight))
+        self.register_buffer("W_tgt", g(off_bb.target_embedding.weight))
+        self.rad_init = RadialMLP(off_bb.edge_degree_embedding.rad_func.net)
+        self.layers = nn.ModuleList([PackedLayer(b, self.C) for b in off_bb.blocks])
+        self.final_norm = off_bb.norm
+        for p in self.final_norm.parameters():
+            p.requires_grad_(False)
+        self.charge_start, self.charge_end = off_bb.charge_channel_start, off_bb.charge_channel_end
+        self.spin_start, self.spin_end = off_bb.spin_channel_start, off_bb.spin_channel_end
+
+    def forward(self, pos, Z, batch, edge_index, shifts, csd_emb, charge=None, spin=None, natoms=None):
+        pos_s, Z_s, batch_s, ii, jj, perm, inv_perm = reorder_graph_morton(pos, Z, batch, edge_index[0], edge_index[1])
+        N = pos_s.shape[0]
+        graph = build_graph_cached(ii, jj, N)
+        x_edge, wigner, env = ops.precompute_geometry(pos_s, Z_s, ii, jj, shifts, self.W_src, self.W_tgt,
+                                                      self.offset_g, self.coeff_g, self.cutoff, graph=graph)
+        rad0 = self.rad_init(x_edge)
+        x = ops.init_node_scatter(rad0, wigner, env, Z_s, batch_s, self.W_sphere, csd_emb, jj, graph.dst_row_ptr,
+                                  graph.dst_col, N)
+        for layer in self.layers:
+            x = layer(x, x_edge, wigner, env, ii, jj, graph, csd_emb, batch_s)
+            if self.charge_end > self.charge_start:
+                x = balance_channels_batched(x, charge, natoms, batch_s, self.charge_start, self.charge_end, 0.0)
+            if self.spin_end > self.spin_start:
+                x = balance_channels_batched(x, spin, natoms, batch_s, self.spin_start, self.spin_end, 1.0)
+        x = self.final_norm(x)
+        return x[inv_perm]

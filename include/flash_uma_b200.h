@@ -1,0 +1,120 @@
+/*
+ * flash_uma_b200 - C ABI of the B200 (sm_100a) eSCN/UMA message-passing hot path.
+ *
+ * Every entry point launches its kernels asynchronously on `stream` (a cudaStream_t
+ * passed as void*, NULL = legacy default stream) and returns 0 on success, a
+ * negative FUMA_E_* code for an invalid argument (nothing is launched), or a
+ * positive CUDA error code if the launch failed. fuma_last_error() describes the
+ * last failure of the calling thread.
+ *
+ * Conventions: all pointers are device pointers to contiguous row-major arrays;
+ * features are fp32; atom/edge indices, atomic numbers and system ids are int64
+ * (as the reference passes them); CSR arrays are int32. Vector-accessed feature
+ * arrays must be 16-byte aligned and C (channels) a multiple of 4, C <= 512.
+ * Outputs are written in full (no zero-initialised buffers are required) unless
+ * a comment says otherwise. No entry point allocates memory, synchronises the
+ * device or keeps state between calls.
+ *
+ * Each function replaces one reference op; the citation is the reference
+ * interface (path:line in the FlashUMA source tree) whose semantics it implements.
+ */
+#ifndef FLASH_UMA_B200_H
+#define FLASH_UMA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FUMA_OK 0
+#define FUMA_E_INVALID (-1)     /* bad size / null pointer / unsupported shape */
+#define FUMA_E_ALIGN (-2)       /* pointer not 16-byte aligned */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fuma_version(void);
+/* Message for the last failure on the calling thread ("" if none). */
+const char* fuma_last_error(void);
+
+/* ---- geometry ---------------------------------------------------------------------------
+ * Replaces PrecomputeGeometry.forward (ops/geom.py:496-531, kernel :36-214).
+ * pos[N,3], Z[N], idx_i/idx_j[E] (edge source i -> destination j), shifts[E,3],
+ * W_src/W_tgt[num_z,C], offset_g[B]  ->  x_edge_raw[E,B+2C], wigner[E,34], env[E]. */
+int fuma_geometry_fwd(const float* pos, const int64_t* Z, const int64_t* idx_i, const int64_t* idx_j,
+                      const float* shifts, const float* W_src, const float* W_tgt, const float* offset_g,
+                      float coeff_g, float cutoff, int64_t N, int64_t E, int32_t B, int32_t C,
+                      float* x_edge_raw, float* wigner, float* env, void* stream);
+
+/* Replaces PrecomputeGeometry.backward (ops/geom.py:533-589, kernel :220-493), split in two:
+ * per-edge gradient w.r.t. the edge vector (= g_shifts[E,3]); only the first B columns of
+ * g_x_edge (row stride g_x_edge_stride floats) are read. */
+int fuma_geometry_bwd(const float* pos, const int64_t* idx_i, const int64_t* idx_j, const float* shifts,
+                      const float* offset_g, float coeff_g, float cutoff, const float* g_x_edge,
+                      int64_t g_x_edge_stride, const float* g_wigner, const float* g_env, int64_t E, int32_t B,
+                      float* g_shifts, void* stream);
+/* ...and the deterministic per-atom reduction that replaces the reference's fp32 atomics
+ * (ops/geom.py:483-488): g_pos[n] = sum_{src CSR n} g_vec - sum_{dst CSR n} g_vec (fp64 sums). */
+int fuma_edge_vec_to_nodes(const int32_t* src_row_ptr, const int32_t* src_col, const int32_t* dst_row_ptr,
+                           const int32_t* dst_col, const float* g_vec, int64_t N, float* g_pos, void* stream);
+
+/* ---- fused LayerNorm + SiLU -------------------------------------------------------------
+ * Replaces _LayerNormSiLUFn (ops/ln_silu.py:126-185): x[M,D] -> out[M,D], mean[M], rstd[M].
+ * D a multiple of 4, D <= 2048. */
+int fuma_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
+                     float* out, float* mean, float* rstd, void* stream);
+/* dx only (gamma/beta are frozen), ops/ln_silu.py:156-177. */
+int fuma_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
+                     const float* g_out, int64_t M, int32_t D, float* g_x, void* stream);
+
+/* ---- gather + rotate into the edge frame ------------------------------------------------
+ * Replaces GatherWignerSplit.forward (ops/gather.py:408-433, kernel :34-154).
+ * x[N,9,C], wigner[E,34], rad[E,12C], csd[nsys,C], batch[N] -> X_m0[E,6C], X_m1[E,8C], X_m2[E,4C]. */
+int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
+                    const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
+                    float* X_m0, float* X_m1, float* X_m2, void* stream);
+/* Replaces GatherWignerSplit.backward (ops/gather.py:435-514) without atomics: needs the
+ * destination CSR (dst_row_ptr[N+1], dst_col[E]) and source CSR of the same edges, and a
+ * caller-provided scratch buffer of E*9*C floats. Writes g_x[N,9,C], g_wigner[E,34], g_rad[E,12C]. */
+int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
+                    const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
+                    const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
+                    const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
+                    float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad, void* stream);
+
+/* ---- split gating -----------------------------------------------------------------------
+ * Replaces FusedGatingSplit (ops/gating.py:188-236): Y_m0[E,5C], Y_m1[E,4C], Y_m2[E,2C] ->
+ * Z_m0[E,3C], Z_m1[E,4C], Z_m2[E,2C]. */
+int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
+                    float* Z_m1, float* Z_m2, void* stream);
+int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
+                    const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
+                    float* g_Y_m2, void* stream);
+
+/* ---- rotate back + envelope + FP64 CSR segment sum + residual ----------------------------
+ * Replaces RotateScatterSplit.forward (ops/scatter.py:295-315, kernel :45-140).
+ * Z_m0[E,3C], Z_m1[E,4C], Z_m2[E,2C], wigner, env, x_res[N,9,C], dst CSR -> x_out[N,9,C]. */
+int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
+                            const float* env, const float* x_res, const int32_t* row_ptr, const int32_t* col_idx,
+                            int64_t N, int64_t E, int32_t C, float* x_out, void* stream);
+/* Replaces RotateScatterSplit.backward (ops/scatter.py:317-352); g_x_res equals g_out. */
+int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
+                            const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
+                            int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
+                            float* g_wigner, float* g_env, void* stream);
+
+/* ---- initial (edge-degree) node embedding -----------------------------------------------
+ * Replaces InitNodeScatter.forward (ops/scatter.py:484-501, kernel :360-423).
+ * rad[E,3C], wigner, env, Z[N], batch[N], W_sphere[num_z,C], csd[nsys,C], dst CSR -> x[N,9,C]. */
+int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* env, const int64_t* Z,
+                          const int64_t* batch, const float* W_sphere, const float* csd, const int32_t* row_ptr,
+                          const int32_t* col_idx, int64_t N, int64_t E, int32_t C, float* x_out, void* stream);
+/* Replaces InitNodeScatter.backward (ops/scatter.py:503-525, kernel :426-481) for g_rad,
+ * g_wigner (full 34-wide rows, zeros outside the m=0 rows) and g_env. */
+int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wigner, const float* env,
+                          const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
+                          float* g_rad, float* g_wigner, float* g_env, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASH_UMA_B200_H */
