@@ -23,7 +23,7 @@ _F32 = ctypes.c_float
 _SIGS = {
     "fuma_geometry_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _F32, _F32, _I64, _I64, _I32, _I32, _P, _P, _P, _P],
     "fuma_geometry_bwd": [_P, _P, _P, _P, _P, _F32, _F32, _P, _I64, _P, _P, _I64, _I32, _P, _P],
-    "fuma_edge_vec_to_nodes": [_P, _P, _P, _P, _P, _I64, _P, _P],
+    "fuma_edge_vec_to_nodes": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P],
     "fuma_ln_silu_fwd": [_P, _P, _P, _F32, _I64, _I32, _P, _P, _P, _P],
     "fuma_ln_silu_bwd": [_P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P],
     "fuma_gather_fwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P],

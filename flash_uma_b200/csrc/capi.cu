@@ -83,10 +83,12 @@ int fuma_geometry_bwd(const float* pos, const int64_t* idx_i, const int64_t* idx
 }
 
 int fuma_edge_vec_to_nodes(const int32_t* src_row_ptr, const int32_t* src_col, const int32_t* dst_row_ptr,
-                           const int32_t* dst_col, const float* g_vec, int64_t N, float* g_pos, void* stream) {
-  REQUIRE(N >= 0, "edge_vec_to_nodes: bad N");
+                           const int32_t* dst_col, const float* g_vec, int64_t N, int64_t E, float* g_pos,
+                           void* stream) {
+  REQUIRE(N >= 0 && E >= 0, "edge_vec_to_nodes: bad sizes");
   if (N == 0) return FUMA_OK;
-  REQUIRE(src_row_ptr && src_col && dst_row_ptr && dst_col && g_vec && g_pos, "edge_vec_to_nodes: null pointer");
+  REQUIRE(src_row_ptr && dst_row_ptr && g_pos, "edge_vec_to_nodes: null pointer");
+  REQUIRE(E == 0 || (src_col && dst_col && g_vec), "edge_vec_to_nodes: null per-edge pointer");
   launch_node_vec3_segment(src_row_ptr, src_col, dst_row_ptr, dst_col, g_vec, g_pos, N, (cudaStream_t)stream);
   return launched("edge_vec_to_nodes");
 }
@@ -133,15 +135,16 @@ int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "gather_bwd: bad sizes");
   if (N == 0) return FUMA_OK;
-  REQUIRE(x && idx_i && wigner && rad && csd && batch && dst_row_ptr && dst_col && src_row_ptr && src_col && g_x &&
-              g_wigner && g_rad && g_X_m0 && g_X_m1 && g_X_m2,
-          "gather_bwd: null pointer");
+  REQUIRE(x && csd && batch && dst_row_ptr && src_row_ptr && g_x, "gather_bwd: null pointer");
+  REQUIRE(E == 0 || (idx_i && wigner && rad && dst_col && src_col && g_wigner && g_rad && g_X_m0 && g_X_m1 && g_X_m2),
+          "gather_bwd: null per-edge pointer");
   REQUIRE(E == 0 || (scratch && scratch_floats >= E * 9 * (int64_t)C),
           "gather_bwd: scratch must hold E*9*C = %lld floats", (long long)(E * 9 * (int64_t)C));
-  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(csd, "csd"); REQUIRE_ALIGNED(g_x, "g_x");
-  REQUIRE_ALIGNED(g_rad, "g_rad"); REQUIRE_ALIGNED(g_X_m0, "g_X_m0"); REQUIRE_ALIGNED(g_X_m1, "g_X_m1");
-  REQUIRE_ALIGNED(g_X_m2, "g_X_m2");
-  if (E > 0) REQUIRE_ALIGNED(scratch, "scratch");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(csd, "csd"); REQUIRE_ALIGNED(g_x, "g_x");
+  if (E > 0) {
+    REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(g_rad, "g_rad"); REQUIRE_ALIGNED(g_X_m0, "g_X_m0");
+    REQUIRE_ALIGNED(g_X_m1, "g_X_m1"); REQUIRE_ALIGNED(g_X_m2, "g_X_m2"); REQUIRE_ALIGNED(scratch, "scratch");
+  }
   launch_gather_bwd(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
                     src_col, g_x, g_wigner, g_rad, scratch, N, C, (cudaStream_t)stream);
   return launched("gather_bwd");

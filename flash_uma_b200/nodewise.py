@@ -114,8 +114,10 @@ class EnergyHead(nn.Module):
 
     def forward(self, node_embedding: torch.Tensor, batch: torch.Tensor, num_systems: int) -> torch.Tensor:
         e_atom = self.energy_block(node_embedding[:, 0]).squeeze(-1)
-        energy = torch.zeros(num_systems, dtype=e_atom.dtype, device=e_atom.device)
-        return energy.index_add(0, batch, e_atom)
+        # per-system sum as a one-hot contraction: fixed reduction order (index_add on a
+        # GPU uses atomics and is not run-to-run reproducible)
+        onehot = F.one_hot(batch, num_systems).to(e_atom.dtype)
+        return onehot.t() @ e_atom
 
 
 def balance_channels_batched(emb, target, natoms, batch, start_idx, end_idx, target_offset=0.0):

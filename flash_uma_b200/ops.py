@@ -107,7 +107,7 @@ class _PrecomputeGeometry(torch.autograd.Function):
             g = ctx.graph if ctx.graph is not None else build_graph_csr(idx_i, idx_j, N)
             g_pos = torch.empty_like(pos)
             nat.call("fuma_edge_vec_to_nodes", ptr(g.src_row_ptr), ptr(g.src_col), ptr(g.dst_row_ptr), ptr(g.dst_col),
-                     ptr(g_vec), N, ptr(g_pos), stream_of(pos))
+                     ptr(g_vec), N, E, ptr(g_pos), stream_of(pos))
         g_shifts = g_vec if ctx.needs_input_grad[4] else None
         return g_pos, None, None, None, g_shifts, None, None, None, None, None, None
 

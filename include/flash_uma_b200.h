@@ -12,7 +12,8 @@
  * (as the reference passes them); CSR arrays are int32. Vector-accessed feature
  * arrays must be 16-byte aligned and C (channels) a multiple of 4, C <= 512.
  * Outputs are written in full (no zero-initialised buffers are required) unless
- * a comment says otherwise. No entry point allocates memory, synchronises the
+ * a comment says otherwise. With E == 0 the per-edge pointers may be NULL (the
+ * data pointer of an empty tensor). No entry point allocates memory, synchronises the
  * device or keeps state between calls.
  *
  * Each function replaces one reference op; the citation is the reference
@@ -55,7 +56,8 @@ int fuma_geometry_bwd(const float* pos, const int64_t* idx_i, const int64_t* idx
 /* ...and the deterministic per-atom reduction that replaces the reference's fp32 atomics
  * (ops/geom.py:483-488): g_pos[n] = sum_{src CSR n} g_vec - sum_{dst CSR n} g_vec (fp64 sums). */
 int fuma_edge_vec_to_nodes(const int32_t* src_row_ptr, const int32_t* src_col, const int32_t* dst_row_ptr,
-                           const int32_t* dst_col, const float* g_vec, int64_t N, float* g_pos, void* stream);
+                           const int32_t* dst_col, const float* g_vec, int64_t N, int64_t E, float* g_pos,
+                           void* stream);
 
 /* ---- fused LayerNorm + SiLU -------------------------------------------------------------
  * Replaces _LayerNormSiLUFn (ops/ln_silu.py:126-185): x[M,D] -> out[M,D], mean[M], rstd[M].
