@@ -68,6 +68,29 @@ def alg_bytes(name, N, E, C, B, M_rows=None, D=None):
     return None
 
 
+# dense FLOPs of the model's GEMMs per edge and layer (forward; the input-gradient GEMMs of the
+# backward have the same count): radial 2*(K_in*H + H*H + H*12C), conv1 2*70C^2, conv2 2*29C^2
+def gemm_flops_per_step(E, C, B, L, H=None):
+    H = H or C
+    rad_layer = 2 * ((B + 2 * C) * H + H * H + H * 12 * C)
+    rad_init = 2 * ((B + 2 * C) * H + H * H + H * 3 * C)
+    so2 = 2 * 70 * C * C + 2 * 29 * C * C
+    fwd = E * (L * (rad_layer + so2) + rad_init)
+    return 2 * fwd
+
+
+def gemm_summary(per_op, E, C, B, L, tf32):
+    """Dense-contraction share of one step (from the probe pass): fp32-equivalent FLOP rate and the
+    tensor-pipe rate (3 TF32 products per fp32 product in the 3xTF32 mode)."""
+    ms = per_op.get("fuma_linear")
+    if not ms:
+        return None
+    flops = gemm_flops_per_step(E, C, B, L)
+    passes = 1 if tf32 else 3
+    return {"flops_per_step": flops, "ms_per_step": ms, "tflops_fp32_equiv": flops / (ms * 1e-3) / 1e12,
+            "tflops_tf32_pipe": passes * flops / (ms * 1e-3) / 1e12, "tf32_passes": passes}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -128,12 +151,11 @@ def build_problem(device, tf32: bool, system=None):
     from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
     from flash_uma_b200.systems import config3_system, to_graph
     from flash_uma_b200.wrapper import ZeroAllocBackbone
-    torch.backends.cuda.matmul.allow_tf32 = tf32
     system = system or config3_system()
     data = to_graph([system])
     off = SyntheticESCNMDBackbone(seed=0).to(device)
     head = make_energy_head(128, 128, seed=1).to(device)
-    pred = Predictor(ZeroAllocBackbone(off), head)
+    pred = Predictor(ZeroAllocBackbone(off, gemm="tf32" if tf32 else "tf32x3"), head)
     return system, data, pred
 
 
@@ -232,7 +254,7 @@ def run_flash(args, rank, world, device):
         "dtype": "f32", "data": "synthetic (seeded bulk Cu positions, random-init weights)",
         "config": {"workload": "bulk_cu_4000 (BASELINE config 3): 4000 atoms, %d edges, E+F per step" % E,
                    "atoms": N, "edges": E, "sphere_channels": C, "layers": L, "num_distance_basis": B,
-                   "cutoff": 6.0, "max_neighbors": 30, "gemm": "tf32" if args.tf32 else "fp32 (cuBLAS, TF32 off)",
+                   "cutoff": 6.0, "max_neighbors": 30, "gemm": "tcgen05 TF32 (single pass)" if args.tf32 else "tcgen05 3xTF32 (fp32-level)",
                    "l2": "flushed (256 MB write) before every step, outside the timed events",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "e2e": {"value": world * N * K / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4,
@@ -242,6 +264,7 @@ def run_flash(args, rank, world, device):
                      "traffic": None, "alg_bytes_per_launch": nbytes, "avg_launch_ms": avg_ms,
                      "launches_timed": len(dom_ms),
                      "share_of_step": (sum(dom_ms) / total_ms) if world == 1 else None},
+        "gemm": gemm_summary(per_op, E, C, B, L, args.tf32),
         "gpu_launches": gpu_launches,
         "per_kernel_ms_one_step": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
         "clocks": clocks,
@@ -310,7 +333,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="flash", choices=["flash", "reference"])
-    ap.add_argument("--tf32", action="store_true", help="TF32 dense contractions (the reference's published setup)")
+    ap.add_argument("--tf32", action="store_true",
+                    help="single-pass TF32 dense contractions (the reference's published setup) instead of 3xTF32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -34,6 +34,8 @@ _SIGS = {
     "fuma_rotate_scatter_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P],
     "fuma_init_scatter_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P],
     "fuma_init_scatter_bwd": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P],
+    "fuma_linear": [_P, _I64, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _P],
+    "fuma_split_tf32": [_P, _I64, _P, _P, _P],
 }
 
 _lib = None

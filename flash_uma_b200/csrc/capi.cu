@@ -30,6 +30,27 @@ int launched(const char* what) {
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Make the device that owns `p` current on the calling thread (and its primary context
+// current for driver-API calls). Callers such as PyTorch's autograd worker threads may
+// have no current context, or a different current device, when they call in.
+int bind_device(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FUMA_E_INVALID, "pointer %p is not a CUDA allocation", p);
+  }
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+    return fail(FUMA_E_INVALID, "pointer %p is not device memory", p);
+  const cudaError_t st = cudaSetDevice(a.device);
+  if (st != cudaSuccess) return fail((int)st, "cudaSetDevice(%d): %s", a.device, cudaGetErrorString(st));
+  return FUMA_OK;
+}
+
+#define BIND(p)                            \
+  do {                                     \
+    if (int rc_ = bind_device(p)) return rc_; \
+  } while (0)
+
 #define REQUIRE(cond, ...)                                  \
   do {                                                      \
     if (!(cond)) return fail(FUMA_E_INVALID, __VA_ARGS__);  \
@@ -64,6 +85,7 @@ int fuma_geometry_fwd(const float* pos, const int64_t* Z, const int64_t* idx_i, 
   if (((B | C) & 3) == 0) {
     REQUIRE_ALIGNED(x_edge_raw, "x_edge_raw"); REQUIRE_ALIGNED(W_src, "W_src"); REQUIRE_ALIGNED(W_tgt, "W_tgt");
   }
+  BIND(pos);
   launch_geom_fwd(pos, Z, idx_i, idx_j, shifts, W_src, W_tgt, offset_g, x_edge_raw, wigner, env, E, B, C, cutoff,
                   coeff_g, (cudaStream_t)stream);
   return launched("geometry_fwd");
@@ -77,6 +99,7 @@ int fuma_geometry_bwd(const float* pos, const int64_t* idx_i, const int64_t* idx
   if (E == 0) return FUMA_OK;
   REQUIRE(pos && idx_i && idx_j && shifts && offset_g && g_x_edge && g_wigner && g_env && g_shifts,
           "geometry_bwd: null pointer");
+  BIND(pos);
   launch_geom_bwd(pos, idx_i, idx_j, shifts, offset_g, g_x_edge, g_x_edge_stride, g_wigner, g_env, g_shifts, E, B,
                   cutoff, coeff_g, (cudaStream_t)stream);
   return launched("geometry_bwd");
@@ -89,6 +112,7 @@ int fuma_edge_vec_to_nodes(const int32_t* src_row_ptr, const int32_t* src_col, c
   if (N == 0) return FUMA_OK;
   REQUIRE(src_row_ptr && dst_row_ptr && g_pos, "edge_vec_to_nodes: null pointer");
   REQUIRE(E == 0 || (src_col && dst_col && g_vec), "edge_vec_to_nodes: null per-edge pointer");
+  BIND(g_pos);
   launch_node_vec3_segment(src_row_ptr, src_col, dst_row_ptr, dst_col, g_vec, g_pos, N, (cudaStream_t)stream);
   return launched("edge_vec_to_nodes");
 }
@@ -99,6 +123,7 @@ int fuma_ln_silu_fwd(const float* x, const float* gamma, const float* beta, floa
   if (M == 0) return FUMA_OK;
   REQUIRE(x && gamma && beta && out && mean && rstd, "ln_silu_fwd: null pointer");
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(out, "out"); REQUIRE_ALIGNED(gamma, "gamma"); REQUIRE_ALIGNED(beta, "beta");
+  BIND(x);
   launch_ln_silu_fwd(x, gamma, beta, out, mean, rstd, M, D, eps, (cudaStream_t)stream);
   return launched("ln_silu_fwd");
 }
@@ -109,6 +134,7 @@ int fuma_ln_silu_bwd(const float* x, const float* gamma, const float* beta, cons
   if (M == 0) return FUMA_OK;
   REQUIRE(x && gamma && beta && mean && rstd && g_out && g_x, "ln_silu_bwd: null pointer");
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(g_x, "g_x");
+  BIND(x);
   launch_ln_silu_bwd(x, gamma, beta, mean, rstd, g_out, g_x, M, D, (cudaStream_t)stream);
   return launched("ln_silu_bwd");
 }
@@ -122,6 +148,7 @@ int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, 
   REQUIRE(x && idx_i && idx_j && wigner && rad && csd && batch && X_m0 && X_m1 && X_m2, "gather_fwd: null pointer");
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(csd, "csd");
   REQUIRE_ALIGNED(X_m0, "X_m0"); REQUIRE_ALIGNED(X_m1, "X_m1"); REQUIRE_ALIGNED(X_m2, "X_m2");
+  BIND(x);
   launch_gather_fwd(x, idx_i, idx_j, wigner, rad, csd, batch, X_m0, X_m1, X_m2, E, C, (cudaStream_t)stream);
   return launched("gather_fwd");
 }
@@ -145,6 +172,7 @@ int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m
     REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(g_rad, "g_rad"); REQUIRE_ALIGNED(g_X_m0, "g_X_m0");
     REQUIRE_ALIGNED(g_X_m1, "g_X_m1"); REQUIRE_ALIGNED(g_X_m2, "g_X_m2"); REQUIRE_ALIGNED(scratch, "scratch");
   }
+  BIND(x);
   launch_gather_bwd(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
                     src_col, g_x, g_wigner, g_rad, scratch, N, C, (cudaStream_t)stream);
   return launched("gather_bwd");
@@ -158,6 +186,7 @@ int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int
   REQUIRE(Y_m0 && Y_m1 && Y_m2 && Z_m0 && Z_m1 && Z_m2, "gating_fwd: null pointer");
   REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
   REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1"); REQUIRE_ALIGNED(Z_m2, "Z_m2");
+  BIND(Y_m0);
   launch_gating_fwd(Y_m0, Y_m1, Y_m2, Z_m0, Z_m1, Z_m2, E, C, (cudaStream_t)stream);
   return launched("gating_fwd");
 }
@@ -172,6 +201,7 @@ int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m
   REQUIRE_ALIGNED(g_Z_m0, "g_Z_m0"); REQUIRE_ALIGNED(g_Z_m1, "g_Z_m1"); REQUIRE_ALIGNED(g_Z_m2, "g_Z_m2");
   REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
   REQUIRE_ALIGNED(g_Y_m0, "g_Y_m0"); REQUIRE_ALIGNED(g_Y_m1, "g_Y_m1"); REQUIRE_ALIGNED(g_Y_m2, "g_Y_m2");
+  BIND(Y_m0);
   launch_gating_bwd(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, g_Y_m0, g_Y_m1, g_Y_m2, E, C, (cudaStream_t)stream);
   return launched("gating_bwd");
 }
@@ -186,6 +216,7 @@ int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z
           "rotate_scatter_fwd: null pointer");
   REQUIRE_ALIGNED(x_res, "x_res"); REQUIRE_ALIGNED(x_out, "x_out");
   if (E > 0) { REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1"); REQUIRE_ALIGNED(Z_m2, "Z_m2"); }
+  BIND(x_res);
   launch_rotate_scatter_fwd(row_ptr, col_idx, Z_m0, Z_m1, Z_m2, wigner, env, x_res, x_out, N, C, (cudaStream_t)stream);
   return launched("rotate_scatter_fwd");
 }
@@ -203,6 +234,7 @@ int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* 
   REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1");
   REQUIRE_ALIGNED(Z_m2, "Z_m2"); REQUIRE_ALIGNED(g_Z_m0, "g_Z_m0"); REQUIRE_ALIGNED(g_Z_m1, "g_Z_m1");
   REQUIRE_ALIGNED(g_Z_m2, "g_Z_m2");
+  BIND(g_out);
   launch_rotate_scatter_bwd(row_ptr, col_idx, g_out, Z_m0, Z_m1, Z_m2, wigner, env, g_Z_m0, g_Z_m1, g_Z_m2, g_wigner,
                             g_env, N, C, (cudaStream_t)stream);
   return launched("rotate_scatter_bwd");
@@ -218,6 +250,7 @@ int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* en
           "init_scatter_fwd: null pointer");
   REQUIRE_ALIGNED(W_sphere, "W_sphere"); REQUIRE_ALIGNED(csd, "csd"); REQUIRE_ALIGNED(x_out, "x_out");
   if (E > 0) REQUIRE_ALIGNED(rad, "rad");
+  BIND(x_out);
   launch_init_scatter_fwd(row_ptr, col_idx, rad, wigner, env, Z, batch, W_sphere, csd, x_out, N, C,
                           (cudaStream_t)stream);
   return launched("init_scatter_fwd");
@@ -232,9 +265,38 @@ int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wig
   REQUIRE(g_out && rad && wigner && env && row_ptr && col_idx && g_rad && g_wigner && g_env,
           "init_scatter_bwd: null pointer");
   REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(g_rad, "g_rad");
+  BIND(g_out);
   launch_init_scatter_bwd(row_ptr, col_idx, g_out, rad, wigner, env, g_rad, g_wigner, g_env, N, C,
                           (cudaStream_t)stream);
   return launched("init_scatter_bwd");
+}
+
+int fuma_linear(const float* A, int64_t lda, const float* W_hi, const float* W_lo, const float* bias, int64_t M,
+                int32_t N, int32_t K, int32_t split, float* C, int64_t ldc, int* err_flag, void* stream) {
+  REQUIRE(M >= 0 && M < (int64_t(1) << 31), "linear: M=%lld out of range", (long long)M);
+  REQUIRE(N > 0 && N % 16 == 0 && N <= 65536 * 16, "linear: N=%d must be a positive multiple of 16", N);
+  REQUIRE(K > 0 && K % 4 == 0, "linear: K=%d must be a positive multiple of 4", K);
+  REQUIRE(lda >= K && lda % 4 == 0 && ldc >= N && ldc % 4 == 0, "linear: bad leading dimensions");
+  if (M == 0) return FUMA_OK;
+  REQUIRE(A && W_hi && C && (!split || W_lo), "linear: null pointer");
+  REQUIRE_ALIGNED(A, "A"); REQUIRE_ALIGNED(W_hi, "W_hi"); REQUIRE_ALIGNED(C, "C");
+  if (split) REQUIRE_ALIGNED(W_lo, "W_lo");
+  if (bias) REQUIRE_ALIGNED(bias, "bias");
+  BIND(A);
+  const int r = launch_gemm_tf32(A, lda, W_hi, W_lo, bias, C, ldc, M, N, K, split != 0, err_flag,
+                                 (cudaStream_t)stream);
+  if (r == -1) return fail(FUMA_E_INVALID, "linear: could not encode the TMA tensor maps: %s", gemm_map_error());
+  if (r != 0) return fail(r, "linear: launch failed: %s", cudaGetErrorString((cudaError_t)r));
+  return launched("linear");
+}
+
+int fuma_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream) {
+  REQUIRE(n >= 0, "split_tf32: bad n");
+  if (n == 0) return FUMA_OK;
+  REQUIRE(x && hi && lo, "split_tf32: null pointer");
+  BIND(x);
+  launch_split_tf32(x, hi, lo, n, (cudaStream_t)stream);
+  return launched("split_tf32");
 }
 
 }  // extern "C"

@@ -1,0 +1,423 @@
+// Dense contraction C[M,N] = A[M,K] . W[N,K]^T (+ bias[N]) on the 5th-generation tensor
+// cores (tcgen05, kind::tf32) with fp32-level accuracy (3xTF32 split).
+//
+// This replaces the cuBLAS F.linear calls of the reference's radial MLP and SO(2)
+// convolutions (model.py:147-154, weights packed at :101-141) and their input-gradient
+// GEMMs in the backward pass.
+//
+// Precision: every fp32 operand x is split into hi = x rounded to nearest TF32 and
+// lo = (x - hi) rounded to nearest TF32. Three MMAs per K step, hi.hi + hi.lo + lo.hi,
+// accumulate in fp32 in tensor memory; the dropped lo.lo term and the rounding of lo are
+// ~2^-22 relative and unbiased (a truncating split biases every product the same way
+// and the error then grows like sqrt(K)), i.e. fp32-level results. The weight
+// halves are prepared once on the host side (weights are frozen); the activation
+// halves are produced in shared memory by the kernel itself. kSplit=false gives the
+// plain single-pass TF32 product (hi and lo not used).
+//
+// Structure (one 128 x BN output tile per CTA, 192 threads):
+//   warp 0      TMA producer: A tile [128 x 32] and W tiles [BN x 32] (128-byte
+//               swizzle, K-major) into a STAGES-deep ring, mbarrier complete_tx.
+//   warp 1      allocates BN TMEM columns; lane 0 issues tcgen05.mma (M=128, N=BN,
+//               K=8 per instruction) and tcgen05.commit to release ring slots.
+//   warps 2-5   split A in place into hi / lo (fence.proxy.async so the tensor core
+//               sees the generic-proxy writes), then drain the accumulator with
+//               tcgen05.ld (each warp owns TMEM lanes 32*(warp%4)..+32), add the bias
+//               and store.
+// Every mbarrier wait is bounded; on timeout the kernel records a code in *err, waits
+// (bounded) for its own in-flight copies and MMAs, releases TMEM and returns.
+#include <cstdio>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fuma {
+
+namespace {
+
+constexpr int kBM = 128;          // rows per tile (one tcgen05 M=128 MMA, cta_group::1)
+constexpr int kBK = 32;           // fp32 elements per K step = one 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr uint32_t kWaitLimit = 1u << 24;   // try_wait iterations before giving up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait. Returns false (and records `code`) if the phase did not complete, or if
+// another role of this CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  if (err) atomicCAS(err, 0, code);
+  return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);          // start address
+  d |= (uint64_t)1u << 16;                          // leading byte offset (unused for SW128 K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;                // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1u << 46;                          // descriptor version (sm100)
+  d |= (uint64_t)2u << 61;                          // layout: SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::tf32, fp32 accumulator, both operands K-major, M=128.
+template <int BN>
+__device__ __forceinline__ constexpr uint32_t instr_desc_tf32() {
+  return (1u << 4)               // D format F32
+         | (2u << 7)             // A format TF32
+         | (2u << 10)            // B format TF32
+         | ((uint32_t)(BN >> 3) << 17)
+         | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Round-to-nearest TF32 split of one fp32 value: hi = rn_tf32(x), lo = rn_tf32(x - hi). Rounding
+// (not truncation) keeps the residual errors unbiased, so they do not grow linearly with K.
+__device__ __forceinline__ uint32_t rn_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void split_rn(uint32_t xbits, uint32_t& hi, uint32_t& lo) {
+  const float x = __uint_as_float(xbits);
+  hi = rn_tf32(x);
+  lo = rn_tf32(x - __uint_as_float(hi));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+template <int BN, int STAGES, bool kSplit>
+struct GemmSmem {
+  static constexpr int kA = kBM * kBK * 4;                          // 16 KB
+  static constexpr int kB = BN * kBK * 4;
+  static constexpr int kStage = kSplit ? 2 * kA + 2 * kB : kA + kB;  // A, W_hi (+ A_lo, W_lo)
+  static constexpr int kBytes = STAGES * kStage + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+  static_assert(kBytes <= 227 * 1024, "shared memory plan exceeds 227 KB");
+};
+
+}  // namespace
+
+template <int BN, int STAGES, bool kSplit>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                const __grid_constant__ CUtensorMap tmWh,
+                                                                const __grid_constant__ CUtensorMap tmWl,
+                                                                float* __restrict__ C, const float* __restrict__ bias,
+                                                                int M, int N, int K, int64_t ldc, int* err) {
+  using L = GemmSmem<BN, STAGES, kSplit>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStage);
+  uint64_t* bar_split = bar_full + STAGES;
+  uint64_t* bar_empty = bar_split + STAGES;
+  uint64_t* bar_acc = bar_empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_acc + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * kBM;
+  const int num_k = (K + kBK - 1) / kBK;  // a ragged last K step reads zeros past K (TMA out-of-range fill)
+  // stage layout: [A | W_hi | A_lo | W_lo], every tile 1024-byte aligned (128-byte swizzle atoms)
+  auto stage_A = [&](int s) { return smem + s * L::kStage; };
+  auto stage_Wh = [&](int s) { return smem + s * L::kStage + L::kA; };
+  auto stage_Alo = [&](int s) { return smem + s * L::kStage + L::kA + L::kB; };
+  auto stage_Wl = [&](int s) { return smem + s * L::kStage + 2 * L::kA + L::kB; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_split[s], 128);
+      mbar_init(&bar_empty[s], 1);
+    }
+    mbar_init(bar_acc, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;  // allocation granule: power of 2, >= 32 columns
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      const uint32_t bytes = L::kA + (kSplit ? 2 : 1) * L::kB;
+      int issued = 0;
+      for (int kt = 0; kt < num_k; ++kt) {
+        const int s = kt % STAGES;
+        if (kt >= STAGES && !mbar_wait(&bar_empty[s], ((kt / STAGES) - 1) & 1, abort_flag, err, 1)) break;
+        mbar_expect_tx(&bar_full[s], bytes);
+        tma_load_2d(stage_A(s), &tmA, kt * kBK, m0, &bar_full[s]);
+        tma_load_2d(stage_Wh(s), &tmWh, kt * kBK, n0, &bar_full[s]);
+        if (kSplit) tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, n0, &bar_full[s]);
+        issued = kt + 1;
+      }
+      if (*abort_flag) {
+        // let the copies this thread started land before the CTA can exit
+        for (int kt = issued - 1; kt >= 0 && kt >= issued - STAGES; --kt) {
+          for (uint32_t i = 0; i < kWaitLimit && !mbar_try(&bar_full[kt % STAGES], (kt / STAGES) & 1); ++i) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc_tf32<BN>();
+      for (int kt = 0; kt < num_k; ++kt) {
+        const int s = kt % STAGES;
+        if (!mbar_wait(&bar_split[s], (kt / STAGES) & 1, abort_flag, err, 2)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_hi = smem_u32(stage_A(s)), a_lo = smem_u32(stage_Alo(s));
+        const uint32_t w_hi = smem_u32(stage_Wh(s)), w_lo = smem_u32(stage_Wl(s));
+#pragma unroll
+        for (int kk = 0; kk < kBK / 8; ++kk) {
+          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
+          const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+          mma_tf32(tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(w_hi + off), idesc, acc);
+          if (kSplit) {
+            mma_tf32(tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(w_lo + off), idesc, 1u);
+            mma_tf32(tmem, smem_desc_sw128(a_lo + off), smem_desc_sw128(w_hi + off), idesc, 1u);
+          }
+        }
+        mma_commit(&bar_empty[s]);
+      }
+      // completion of every MMA issued above (also on the abort path)
+      mma_commit(bar_acc);
+      if (*abort_flag) {
+        for (uint32_t i = 0; i < kWaitLimit && !mbar_try(bar_acc, 0); ++i) {
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- split (warps 2-5), then epilogue
+    const int t = threadIdx.x - 64;  // 0..127
+    for (int kt = 0; kt < num_k; ++kt) {
+      const int s = kt % STAGES;
+      if (!mbar_wait(&bar_full[s], (kt / STAGES) & 1, abort_flag, err, 3)) break;
+      if (kSplit) {
+        uint4* a = reinterpret_cast<uint4*>(stage_A(s));
+        uint4* alo = reinterpret_cast<uint4*>(stage_Alo(s));
+#pragma unroll
+        for (int i = 0; i < L::kA / 16 / 128; ++i) {
+          const int c = i * 128 + t;
+          const uint4 v = a[c];
+          uint4 h, l;
+          split_rn(v.x, h.x, l.x); split_rn(v.y, h.y, l.y); split_rn(v.z, h.z, l.z); split_rn(v.w, h.w, l.w);
+          a[c] = h;
+          alo[c] = l;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      mbar_arrive(&bar_split[s]);
+    }
+    // epilogue: TMEM -> registers -> (+bias) -> global
+    bool ok = mbar_wait(bar_acc, 0, abort_flag, err, 4);
+    ok = __all_sync(kFull, ok && !*abort_flag);  // tcgen05.ld is warp-collective: decide per warp
+    if (ok) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int q = warp & 3;             // TMEM lane quadrant of this warp
+      const int row = m0 + q * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr + (uint32_t)c0));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < M) {
+          float* out = C + (int64_t)row * ldc + n0 + c0;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                   __uint_as_float(r[j + 3]));
+            if (bias) v = v + ld4_keep(bias + n0 + c0 + j);
+            st4(out + j, v);
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---- host side ------------------------------------------------------------------------------
+
+namespace {
+
+thread_local char g_map_err[160] = "";
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    void* p = nullptr;
+    const cudaError_t st = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (st == cudaSuccess && q == cudaDriverEntryPointSuccess && p)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      snprintf(g_map_err, sizeof(g_map_err), "cuTensorMapEncodeTiled entry point not found (cuda %d, query %d)",
+               (int)st, (int)q);
+  }
+  return fn;
+}
+
+// 2-D fp32 tensor map over rows x cols (cols contiguous, row stride ld elements), box 32 x box_rows,
+// 128-byte swizzle; out-of-range rows read as zero.
+bool make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    snprintf(g_map_err, sizeof(g_map_err),
+             "cuTensorMapEncodeTiled failed (CUresult %d) for base=%p rows=%lld cols=%lld ld=%lld box=%dx%d", (int)r,
+             (const void*)base, (long long)rows, (long long)cols, (long long)ld, kBK, box_rows);
+    return false;
+  }
+  return true;
+}
+
+template <int BN, int STAGES, bool kSplit>
+cudaError_t launch(const CUtensorMap& a, const CUtensorMap& wh, const CUtensorMap& wl, float* C, const float* bias,
+                   int M, int N, int K, int64_t ldc, int* err, cudaStream_t s) {
+  using L = GemmSmem<BN, STAGES, kSplit>;
+  auto kern = gemm_tf32_kernel<BN, STAGES, kSplit>;
+  static thread_local uint64_t configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> (dev & 63) & 1)) {
+    cudaError_t st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (st != cudaSuccess) return st;
+    configured |= uint64_t(1) << (dev & 63);
+  }
+  dim3 grid(N / BN, (M + kBM - 1) / kBM);
+  kern<<<grid, kThreads, L::kBytes, s>>>(a, wh, wl, C, bias, M, N, K, ldc, err);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Returns 0 on success, -1 if the tensor maps could not be built, else a CUDA error code.
+int launch_gemm_tf32(const float* A, int64_t lda, const float* W_hi, const float* W_lo, const float* bias, float* C,
+                     int64_t ldc, int64_t M, int N, int K, bool split, int* err, cudaStream_t s) {
+  const int BN = (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : (N % 32 == 0) ? 32 : 16;
+  CUtensorMap ma, mh, ml;
+  if (!make_map(&ma, A, M, K, lda, kBM)) return -1;
+  if (!make_map(&mh, W_hi, N, K, K, BN)) return -1;
+  if (!make_map(&ml, split ? W_lo : W_hi, N, K, K, BN)) return -1;
+  cudaError_t st;
+  const int m = (int)M;
+  switch (BN) {
+    case 128:
+      st = split ? launch<128, 3, true>(ma, mh, ml, C, bias, m, N, K, ldc, err, s)
+                 : launch<128, 4, false>(ma, mh, ml, C, bias, m, N, K, ldc, err, s);
+      break;
+    case 64:
+      st = split ? launch<64, 4, true>(ma, mh, ml, C, bias, m, N, K, ldc, err, s)
+                 : launch<64, 4, false>(ma, mh, ml, C, bias, m, N, K, ldc, err, s);
+      break;
+    case 32:
+      st = split ? launch<32, 4, true>(ma, mh, ml, C, bias, m, N, K, ldc, err, s)
+                 : launch<32, 4, false>(ma, mh, ml, C, bias, m, N, K, ldc, err, s);
+      break;
+    default:
+      st = split ? launch<16, 4, true>(ma, mh, ml, C, bias, m, N, K, ldc, err, s)
+                 : launch<16, 4, false>(ma, mh, ml, C, bias, m, N, K, ldc, err, s);
+  }
+  return st == cudaSuccess ? 0 : (int)st;
+}
+
+// hi = x rounded to TF32, lo = (x - hi) rounded to TF32 (see split_rn).
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                                  int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t h, l;
+    split_rn(__float_as_uint(x[i]), h, l);
+    hi[i] = __uint_as_float(h);
+    lo[i] = __uint_as_float(l);
+  }
+}
+
+const char* gemm_map_error() { return g_map_err; }
+
+void launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s) {
+  split_tf32_kernel<<<grid_for(n, 256, 4), 256, 0, s>>>(x, hi, lo, n);
+}
+
+}  // namespace fuma

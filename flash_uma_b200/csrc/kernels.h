@@ -47,4 +47,9 @@ void launch_init_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, con
                              const float* wig, const float* env, float* g_rad, float* g_wig, float* g_env, int64_t N,
                              int C, cudaStream_t s);
 
+int launch_gemm_tf32(const float* A, int64_t lda, const float* W_hi, const float* W_lo, const float* bias, float* C,
+                     int64_t ldc, int64_t M, int N, int K, bool split, int* err, cudaStream_t s);
+void launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s);
+const char* gemm_map_error();
+
 }  // namespace fuma

@@ -3,8 +3,9 @@ message-passing layers, driving the CUDA ops of :mod:`flash_uma_b200.ops`.
 
 Mirrors the reference ``model.py`` (``reorder_graph_morton`` :56-74, ``build_csr_cached``
 :28-44, ``Packed_eSCN_Layer`` :81-157, ``eSCN_Inference_Model`` :160-221). The dense
-contractions (radial MLP and SO(2) convolutions) are ``F.linear`` calls, as in the
-reference; TF32 follows PyTorch's global ``torch.backends.cuda.matmul`` setting.
+contractions (radial MLP and SO(2) convolutions, ``F.linear`` / cuBLAS in the reference)
+run on this library's tcgen05 tensor-core GEMM (:class:`~flash_uma_b200.linear.FrozenLinear`),
+3xTF32 by default (``FUMA_GEMM=tf32`` selects single-pass TF32).
 """
 from __future__ import annotations
 
@@ -15,6 +16,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
+from .linear import FrozenLinear
 from .nodewise import balance_channels_batched
 
 # ---- graph preparation ---------------------------------------------------------------------
@@ -82,36 +84,36 @@ def pack_complex(R: torch.Tensor, I: torch.Tensor) -> torch.Tensor:
 class RadialMLP(nn.Module):
     """Linear -> LN-SiLU -> Linear -> LN-SiLU -> Linear (``model.py:147-149``, ``:203-205``)."""
 
-    def __init__(self, net):
+    def __init__(self, net, mode=None):
         super().__init__()
         g = lambda t: t.detach().clone().float()
-        self.register_buffer("W1", g(net[0].weight)); self.register_buffer("b1", g(net[0].bias))
+        self.l1 = FrozenLinear(net[0].weight, net[0].bias, mode)
         self.register_buffer("g1", g(net[1].weight)); self.register_buffer("be1", g(net[1].bias))
-        self.register_buffer("W2", g(net[3].weight)); self.register_buffer("b2", g(net[3].bias))
+        self.l2 = FrozenLinear(net[3].weight, net[3].bias, mode)
         self.register_buffer("g2", g(net[4].weight)); self.register_buffer("be2", g(net[4].bias))
-        self.register_buffer("W3", g(net[6].weight)); self.register_buffer("b3", g(net[6].bias))
+        self.l3 = FrozenLinear(net[6].weight, net[6].bias, mode)
 
     def forward(self, x_edge):
-        h1 = ops.layer_norm_silu(F.linear(x_edge, self.W1, self.b1), self.g1, self.be1)
-        h2 = ops.layer_norm_silu(F.linear(h1, self.W2, self.b2), self.g2, self.be2)
-        return F.linear(h2, self.W3, self.b3)
+        h1 = ops.layer_norm_silu(self.l1(x_edge), self.g1, self.be1)
+        h2 = ops.layer_norm_silu(self.l2(h1), self.g2, self.be2)
+        return self.l3(h2)
 
 
 class PackedLayer(nn.Module):
     """One eSCN message-passing block (``Packed_eSCN_Layer``, ``model.py:81-157``)."""
 
-    def __init__(self, blk, C: int):
+    def __init__(self, blk, C: int, mode=None):
         super().__init__()
         c1, c2 = blk.edge_wise.so2_conv_1, blk.edge_wise.so2_conv_2
         g = lambda t: t.detach().clone().float()
         self.C = C
-        self.rad = RadialMLP(c1.rad_func.net)
-        self.register_buffer("W_conv1_m0", g(c1.fc_m0.weight)); self.register_buffer("b_conv1_m0", g(c1.fc_m0.bias))
-        w = g(c1.so2_m_conv[0].fc.weight); self.register_buffer("W_conv1_m1", pack_complex(w[:2 * C], w[2 * C:]))
-        w = g(c1.so2_m_conv[1].fc.weight); self.register_buffer("W_conv1_m2", pack_complex(w[:C], w[C:]))
-        self.register_buffer("W_conv2_m0", g(c2.fc_m0.weight)); self.register_buffer("b_conv2_m0", g(c2.fc_m0.bias))
-        w = g(c2.so2_m_conv[0].fc.weight); self.register_buffer("W_conv2_m1", pack_complex(w[:2 * C], w[2 * C:]))
-        w = g(c2.so2_m_conv[1].fc.weight); self.register_buffer("W_conv2_m2", pack_complex(w[:C], w[C:]))
+        self.rad = RadialMLP(c1.rad_func.net, mode)
+        self.conv1_m0 = FrozenLinear(c1.fc_m0.weight, c1.fc_m0.bias, mode)
+        w = g(c1.so2_m_conv[0].fc.weight); self.conv1_m1 = FrozenLinear(pack_complex(w[:2 * C], w[2 * C:]), None, mode)
+        w = g(c1.so2_m_conv[1].fc.weight); self.conv1_m2 = FrozenLinear(pack_complex(w[:C], w[C:]), None, mode)
+        self.conv2_m0 = FrozenLinear(c2.fc_m0.weight, c2.fc_m0.bias, mode)
+        w = g(c2.so2_m_conv[0].fc.weight); self.conv2_m1 = FrozenLinear(pack_complex(w[:2 * C], w[2 * C:]), None, mode)
+        w = g(c2.so2_m_conv[1].fc.weight); self.conv2_m2 = FrozenLinear(pack_complex(w[:C], w[C:]), None, mode)
         self.norm_1, self.norm_2, self.atom_wise = blk.norm_1, blk.norm_2, blk.atom_wise
         for m in (self.norm_1, self.norm_2, self.atom_wise):
             for p in m.parameters():
@@ -121,13 +123,8 @@ class PackedLayer(nn.Module):
         x_norm = self.norm_1(x_in)
         rad_out = self.rad(x_edge)
         X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch, graph=graph)
-        Y0 = F.linear(X0, self.W_conv1_m0, self.b_conv1_m0)
-        Y1 = F.linear(X1, self.W_conv1_m1)
-        Y2 = F.linear(X2, self.W_conv1_m2)
-        Z0, Z1, Z2 = ops.fused_gating_split(Y0, Y1, Y2, self.C)
-        O0 = F.linear(Z0, self.W_conv2_m0, self.b_conv2_m0)
-        O1 = F.linear(Z1, self.W_conv2_m1)
-        O2 = F.linear(Z2, self.W_conv2_m2)
+        Z0, Z1, Z2 = ops.fused_gating_split(self.conv1_m0(X0), self.conv1_m1(X1), self.conv1_m2(X2), self.C)
+        O0, O1, O2 = self.conv2_m0(Z0), self.conv2_m1(Z1), self.conv2_m2(Z2)
         x_mid = ops.rotate_scatter_split(O0, O1, O2, wigner, env, x_in, idx_j, graph.dst_row_ptr, graph.dst_col,
                                          x_in.shape[0])
         return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
@@ -136,7 +133,7 @@ class PackedLayer(nn.Module):
 class ESCNInferenceModel(nn.Module):
     """``eSCN_Inference_Model`` (``model.py:160-221``) built from a FAIRChem-layout backbone."""
 
-    def __init__(self, off_bb):
+    def __init__(self, off_bb, mode=None):
         super().__init__()
         self.C = int(off_bb.sphere_channels)
         self.B = int(off_bb.num_distance_basis)
@@ -148,8 +145,8 @@ class ESCNInferenceModel(nn.Module):
         self.register_buffer("W_sphere", g(off_bb.sphere_embedding.weight))
         self.register_buffer("W_src", g(off_bb.source_embedding.weight))
         self.register_buffer("W_tgt", g(off_bb.target_embedding.weight))
-        self.rad_init = RadialMLP(off_bb.edge_degree_embedding.rad_func.net)
-        self.layers = nn.ModuleList([PackedLayer(b, self.C) for b in off_bb.blocks])
+        self.rad_init = RadialMLP(off_bb.edge_degree_embedding.rad_func.net, mode)
+        self.layers = nn.ModuleList([PackedLayer(b, self.C, mode) for b in off_bb.blocks])
         self.final_norm = off_bb.norm
         for p in self.final_norm.parameters():
             p.requires_grad_(False)

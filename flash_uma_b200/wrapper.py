@@ -29,7 +29,9 @@ def validate_atoms_data(self, atoms, task_name):
 
 
 class ZeroAllocBackbone(nn.Module):
-    def __init__(self, off_bb, dtype=torch.float32):
+    def __init__(self, off_bb, dtype=torch.float32, gemm: str | None = None):
+        """``gemm``: "tf32x3" (default, fp32-level accuracy) or "tf32" (single pass, as the
+        reference runs with TF32 enabled); default from the FUMA_GEMM environment variable."""
         super().__init__()
         lmax = getattr(off_bb, "lmax", None)
         if lmax is not None and lmax != 2:
@@ -44,7 +46,7 @@ class ZeroAllocBackbone(nn.Module):
             raise ValueError("sphere_channels must be a multiple of 4 and <= 512")
         device = next(off_bb.parameters()).device
         self.dtype = dtype
-        self.ce = ESCNInferenceModel(off_bb).to(device)
+        self.ce = ESCNInferenceModel(off_bb, gemm).to(device)
         self.charge_embedding = off_bb.charge_embedding
         self.spin_embedding = off_bb.spin_embedding
         self.dataset_embedding = getattr(off_bb, "dataset_embedding", None)

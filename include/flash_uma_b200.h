@@ -116,6 +116,20 @@ int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wig
                           const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
                           float* g_rad, float* g_wigner, float* g_env, void* stream);
 
+/* ---- dense contractions on tcgen05 tensor cores ------------------------------------------
+ * Replaces the F.linear (cuBLAS) calls of the radial MLP and SO(2) convolutions
+ * (model.py:147-154, weights packed at model.py:101-141) and their input gradients:
+ * C[M,N] = A[M,K] . W[N,K]^T (+ bias[N]); A rows lda floats apart, C rows ldc floats apart.
+ * split != 0: 3xTF32 (fp32-level accuracy); W_hi / W_lo come from fuma_split_tf32(W).
+ * split == 0: single-pass TF32 with W_hi = W (W_lo unused).
+ * N a multiple of 16, K a multiple of 4, lda and ldc multiples of 4.
+ * err_flag (device int, may be NULL) receives a non-zero code if a pipeline wait of the
+ * kernel timed out; the kernel then returns without writing C. */
+int fuma_linear(const float* A, int64_t lda, const float* W_hi, const float* W_lo, const float* bias, int64_t M,
+                int32_t N, int32_t K, int32_t split, float* C, int64_t ldc, int* err_flag, void* stream);
+/* hi = x rounded to nearest TF32, lo = (x - hi) rounded to nearest TF32 (3xTF32 weight split). */
+int fuma_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
