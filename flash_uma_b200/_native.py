@@ -36,6 +36,8 @@ _SIGS = {
     "fuma_init_scatter_bwd": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P],
     "fuma_linear": [_P, _I64, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _P],
     "fuma_split_tf32": [_P, _I64, _P, _P, _P],
+    "fuma_gather_bwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P,
+                                _P],
 }
 
 _lib = None
@@ -85,6 +87,7 @@ def stream_of(t: torch.Tensor) -> int:
 # kernels each entry point launches (used by launch accounting)
 KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 2
+KERNELS_PER_CALL["fuma_gather_bwd_noalloc"] = 2
 
 
 class LaunchProbe:

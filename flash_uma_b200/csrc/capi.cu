@@ -67,6 +67,14 @@ int check_C(int32_t C) {
 
 }  // namespace
 
+int fuma::report_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 extern "C" {
 
 int fuma_version(void) { return 100; }

@@ -52,4 +52,7 @@ int launch_gemm_tf32(const float* A, int64_t lda, const float* W_hi, const float
 void launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s);
 const char* gemm_map_error();
 
+// Record `fmt` as the calling thread's fuma_last_error() message and return `code`.
+int report_error(int code, const char* fmt, ...);
+
 }  // namespace fuma

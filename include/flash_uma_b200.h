@@ -130,6 +130,22 @@ int fuma_linear(const float* A, int64_t lda, const float* W_hi, const float* W_l
 /* hi = x rounded to nearest TF32, lo = (x - hi) rounded to nearest TF32 (3xTF32 weight split). */
 int fuma_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream);
 
+/* ---- allocation-free gather backward -----------------------------------------------------
+ * No counterpart in the reference. For callers that cannot let a library allocate device
+ * memory (frameworks that own the whole device memory budget, steps that must not pay for or
+ * be serialised by cudaMalloc/cudaFree): the same computation as fuma_gather_bwd, but its
+ * E*9*C-float scratch lives in a 32 MiB array built into the library (resident on every GPU
+ * that loads it), so only inputs and outputs are passed. Limit: E*9*C <= 8,388,608 floats,
+ * larger calls return FUMA_E_INVALID. The first call on a device looks up the array's
+ * address; make that first call before any stream capture. All calls share the array:
+ * calls that can overlap on the GPU race and must be serialised by the caller. Allocates
+ * nothing and needs no zero-initialised memory. */
+int fuma_gather_bwd_noalloc(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
+                            const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
+                            const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
+                            const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
+                            float* g_x, float* g_wigner, float* g_rad, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
