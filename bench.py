@@ -207,7 +207,9 @@ def run_flash(args, rank, world, device):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
+        torch.cuda.nvtx.range_push("fuma_step")
         res = step(pos_seq[W + k])
+        torch.cuda.nvtx.range_pop()
         e1.record()
         evs.append((e0, e1))
     torch.cuda.synchronize()
@@ -270,6 +272,87 @@ def run_flash(args, rank, world, device):
         "clocks": clocks,
     }
     return out
+
+
+def run_micro(args, device):
+    """one message-passing layer (radial MLP with LN-SiLU -> gather-rotate ->
+    SO(2) conv1 -> gating -> conv2 -> FP64 rotate-scatter), forward + backward, inputs resident.
+    Geometry is computed once from the synthetic edge vectors (uniform directions, lengths
+    U(0.8, 6) A) outside the timed region. Every C-ABI call is bracketed with CUDA events;
+    prints per-kernel time, algorithmic bytes and fraction of the measured HBM / tensor peaks."""
+    from flash_uma_b200 import _native, ops
+    from flash_uma_b200.model import PackedLayer
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone
+    from flash_uma_b200.systems import microbench_layer_inputs
+    _native.load()
+    N, E, C, B = args.nodes, args.edges, 128, 64
+    inp = microbench_layer_inputs(N=N, E=E, C=C, seed=0)
+    off = SyntheticESCNMDBackbone(num_layers=1, seed=0).to(device)
+    layer = PackedLayer(off.blocks[0], C, "tf32" if args.tf32 else None).to(device)
+    ii, jj = inp["idx_i"].to(device), inp["idx_j"].to(device)
+    graph = ops.build_graph_csr(ii, jj, N)
+    Z = torch.full((N,), 29, dtype=torch.long, device=device)
+    batch = torch.zeros(N, dtype=torch.long, device=device)
+    offset = torch.linspace(0, 6.0, B, device=device)
+    coeff = float(-0.5 / (2.0 * (6.0 / (B - 1))) ** 2)
+    xe, wig, env = ops.precompute_geometry(inp["pos"].to(device), Z, ii, jj, inp["shifts"].to(device),
+                                           off.source_embedding.weight.detach(), off.target_embedding.weight.detach(),
+                                           offset, coeff, 6.0, graph=graph)
+    csd = torch.randn(1, C, device=device)
+    x0 = inp["x"].to(device)
+    gout = torch.randn(N, 9, C, device=device)
+
+    def step():
+        x = x0.detach().requires_grad_(True)
+        rad = layer.rad(xe)
+        X0, X1, X2 = ops.gather_wigner_split(x, ii, jj, wig, rad, csd, batch, graph=graph)
+        Z0, Z1, Z2 = ops.fused_gating_split(layer.conv1_m0(X0), layer.conv1_m1(X1), layer.conv1_m2(X2), C)
+        out = ops.rotate_scatter_split(layer.conv2_m0(Z0), layer.conv2_m1(Z1), layer.conv2_m2(Z2), wig, env, x, jj,
+                                       graph.dst_row_ptr, graph.dst_col, N)
+        (gx,) = torch.autograd.grad(out, [x], gout)
+        return gx
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    probe = _native.LaunchProbe(timed=list(_native.KERNELS_PER_CALL))
+    _native.set_probe(probe)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        torch.cuda.nvtx.range_push("fuma_step")
+        step()
+        torch.cuda.nvtx.range_pop()
+    e1.record()
+    torch.cuda.synchronize()
+    _native.set_probe(None)
+    total = e0.elapsed_time(e1) / args.steps
+    hbm, bf16, kind = load_peaks()
+    kernels = {}
+    for name in probe.events:
+        t = probe.times_ms(name)
+        per_step = sum(t) / args.steps
+        launches = len(t) // args.steps
+        entry = {"ms_per_step": per_step, "launches_per_step": launches}
+        nb = alg_bytes(name, N, E, C, B, M_rows=E, D=128)
+        if nb:
+            gbs = nb * launches / (per_step * 1e-3) / 1e9
+            entry.update(alg_bytes_per_launch=nb, achieved_gbs=gbs, frac_hbm=gbs / hbm)
+        kernels[name] = entry
+    if "fuma_linear" in kernels:
+        H = C
+        so2 = 2 * 70 * C * C + 2 * 29 * C * C
+        rad = 2 * ((B + 2 * C) * H + H * H + H * 12 * C)
+        flops = 2 * E * (so2 + rad)
+        passes = 1 if args.tf32 else 3
+        ms = kernels["fuma_linear"]["ms_per_step"]
+        tf = passes * flops / (ms * 1e-3) / 1e12
+        kernels["fuma_linear"].update(flops_per_step=flops, tf32_passes=passes, tflops_tf32_pipe=tf,
+                                      frac_tf32_peak=tf / (bf16 / 2))
+    print(json.dumps({"metric": "one message-passing layer fwd+bwd (BASELINE config 2)", "nodes": N, "edges": E,
+                      "ms_per_layer": total, "peaks": {"hbm_gbs": hbm, "tf32_tflops": bf16 / 2, "kind": kind,
+                                                        "tf32_note": "dense TF32 taken as half the measured bf16 rate"},
+                      "kernels": dict(sorted(kernels.items(), key=lambda kv: -kv[1]["ms_per_step"]))}), flush=True)
 
 
 def cpu_oracle_rate(atoms_sample: int = 256, min_seconds: float = 8.0, max_steps: int = 4):
@@ -336,6 +419,9 @@ def main():
     ap.add_argument("--tf32", action="store_true",
                     help="single-pass TF32 dense contractions (the reference's published setup) instead of 3xTF32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", action="store_true", help="one-layer kernel microbench (BASELINE config 2)")
+    ap.add_argument("--nodes", type=int, default=20000)
+    ap.add_argument("--edges", type=int, default=600000)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -349,6 +435,10 @@ def main():
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.micro:
+        if rank == 0:
+            run_micro(args, device)
+        return
     if world > 1:
         import datetime
         torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))

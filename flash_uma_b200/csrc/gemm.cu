@@ -5,8 +5,10 @@
 // convolutions (model.py:147-154, weights packed at :101-141) and their input-gradient
 // GEMMs in the backward pass.
 //
-// Precision: every fp32 operand x is split into hi = x rounded to nearest TF32 and
-// lo = (x - hi) rounded to nearest TF32. Three MMAs per K step, hi.hi + hi.lo + lo.hi,
+// Precision: every fp32 operand x is split into hi and lo parts. Weights (prepared once):
+// hi = rn_tf32(x), lo = rn_tf32(x - hi). Activations: hi = the raw fp32 value, which the
+// tensor core reads as TF32 by truncation, and lo = rn_tf32(x - trunc_tf32(x)), written by
+// the kernel into shared memory. Three MMAs per K step, hi.hi + hi.lo + lo.hi,
 // accumulate in fp32 in tensor memory; the dropped lo.lo term and the rounding of lo are
 // ~2^-22 relative and unbiased (a truncating split biases every product the same way
 // and the error then grows like sqrt(K)), i.e. fp32-level results. The weight
@@ -14,15 +16,17 @@
 // halves are produced in shared memory by the kernel itself. kSplit=false gives the
 // plain single-pass TF32 product (hi and lo not used).
 //
-// Structure (one 128 x BN output tile per CTA, 192 threads):
+// Structure (persistent, one CTA per SM, 320 threads, 128 x BN output tiles):
 //   warp 0      TMA producer: A tile [128 x 32] and W tiles [BN x 32] (128-byte
 //               swizzle, K-major) into a STAGES-deep ring, mbarrier complete_tx.
-//   warp 1      allocates BN TMEM columns; lane 0 issues tcgen05.mma (M=128, N=BN,
-//               K=8 per instruction) and tcgen05.commit to release ring slots.
-//   warps 2-5   split A in place into hi / lo (fence.proxy.async so the tensor core
-//               sees the generic-proxy writes), then drain the accumulator with
-//               tcgen05.ld (each warp owns TMEM lanes 32*(warp%4)..+32), add the bias
-//               and store.
+//   warp 1      allocates 2 x BN TMEM columns (two accumulators); lane 0 issues
+//               tcgen05.mma (M=128, N=BN, K=8 per instruction), tcgen05.commit releases
+//               ring slots and hands a finished accumulator to the epilogue.
+//   warps 2-5   write A_lo next to the A tile (fence.proxy.async so the tensor core
+//               sees the generic-proxy writes).
+//   warps 6-9   drain the other accumulator with tcgen05.ld (each warp owns TMEM lanes
+//               32*(warp%4)..+32), add the bias and store, while the next tile's K loop
+//               runs.
 // Every mbarrier wait is bounded; on timeout the kernel records a code in *err, waits
 // (bounded) for its own in-flight copies and MMAs, releases TMEM and returns.
 #include <cstdio>
@@ -39,7 +43,7 @@ namespace {
 
 constexpr int kBM = 128;          // rows per tile (one tcgen05 M=128 MMA, cta_group::1)
 constexpr int kBK = 32;           // fp32 elements per K step = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA, 4 split warps, 4 epilogue warps
 constexpr uint32_t kWaitLimit = 1u << 24;   // try_wait iterations before giving up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -134,6 +138,14 @@ __device__ __forceinline__ void split_rn(uint32_t xbits, uint32_t& hi, uint32_t&
   lo = rn_tf32(x - __uint_as_float(hi));
 }
 
+// Low part of the 3xTF32 split for an operand the tensor core truncates to TF32 itself:
+// rn_tf32(x - trunc_tf32(x)) (exact difference, rounded to nearest so the residual is unbiased).
+__device__ __forceinline__ uint32_t lo_part(uint32_t xbits) {
+  const float x = __uint_as_float(xbits);
+  const float t = __uint_as_float(xbits & 0xFFFFE000u);
+  return rn_tf32(x - t);
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -148,8 +160,14 @@ struct GemmSmem {
   static_assert(kBytes <= 227 * 1024, "shared memory plan exceeds 227 KB");
 };
 
+constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpSplit0 = 2, kWarpEpi0 = 6;
+
 }  // namespace
 
+// Persistent: CTA b owns tiles b, b + gridDim.x, ...; tile t covers rows (t / num_n) * 128 and
+// columns (t % num_n) * BN. The smem ring and the two TMEM accumulators are shared by all the
+// CTA's tiles, so the epilogue of one tile runs while the next tile's K loop is in the tensor
+// cores.
 template <int BN, int STAGES, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                 const __grid_constant__ CUtensorMap tmWh,
@@ -162,19 +180,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
   uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStage);
   uint64_t* bar_split = bar_full + STAGES;
   uint64_t* bar_empty = bar_split + STAGES;
-  uint64_t* bar_acc = bar_empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_acc + 1);
+  uint64_t* bar_acc_full = bar_empty + STAGES;   // [2]
+  uint64_t* bar_acc_empty = bar_acc_full + 2;    // [2]
+  uint64_t* bar_done = bar_acc_empty + 2;        // MMA completion on the abort path
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * kBM;
+  const int num_n = N / BN;
+  const int num_tiles = ((M + kBM - 1) / kBM) * num_n;
   const int num_k = (K + kBK - 1) / kBK;  // a ragged last K step reads zeros past K (TMA out-of-range fill)
   // stage layout: [A | W_hi | A_lo | W_lo], every tile 1024-byte aligned (128-byte swizzle atoms)
   auto stage_A = [&](int s) { return smem + s * L::kStage; };
   auto stage_Wh = [&](int s) { return smem + s * L::kStage + L::kA; };
   auto stage_Alo = [&](int s) { return smem + s * L::kStage + L::kA + L::kB; };
   auto stage_Wl = [&](int s) { return smem + s * L::kStage + 2 * L::kA + L::kB; };
+  constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;       // one accumulator
+  constexpr uint32_t kTmemCols = 2 * kAccCols;             // double buffered (power of 2, >= 32)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -182,12 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
       mbar_init(&bar_split[s], 128);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(bar_acc, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_acc_full[b], 1);
+      mbar_init(&bar_acc_empty[b], 128);
+    }
+    mbar_init(bar_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;  // allocation granule: power of 2, >= 32 columns
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
@@ -198,89 +223,111 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == kWarpProducer) {
     // ---------------- TMA producer
     if (lane == 0) {
       const uint32_t bytes = L::kA + (kSplit ? 2 : 1) * L::kB;
-      int issued = 0;
-      for (int kt = 0; kt < num_k; ++kt) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES && !mbar_wait(&bar_empty[s], ((kt / STAGES) - 1) & 1, abort_flag, err, 1)) break;
-        mbar_expect_tx(&bar_full[s], bytes);
-        tma_load_2d(stage_A(s), &tmA, kt * kBK, m0, &bar_full[s]);
-        tma_load_2d(stage_Wh(s), &tmWh, kt * kBK, n0, &bar_full[s]);
-        if (kSplit) tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, n0, &bar_full[s]);
-        issued = kt + 1;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * kBM, n0 = (tile % num_n) * BN;
+        for (int kt = 0; kt < num_k; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&bar_empty[s], ((it / STAGES) - 1) & 1, abort_flag, err, 1)) break;
+          mbar_expect_tx(&bar_full[s], bytes);
+          tma_load_2d(stage_A(s), &tmA, kt * kBK, m0, &bar_full[s]);
+          tma_load_2d(stage_Wh(s), &tmWh, kt * kBK, n0, &bar_full[s]);
+          if (kSplit) tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, n0, &bar_full[s]);
+        }
       }
       if (*abort_flag) {
         // let the copies this thread started land before the CTA can exit
-        for (int kt = issued - 1; kt >= 0 && kt >= issued - STAGES; --kt) {
-          for (uint32_t i = 0; i < kWaitLimit && !mbar_try(&bar_full[kt % STAGES], (kt / STAGES) & 1); ++i) {
+        for (int j = it - 1; j >= 0 && j >= it - STAGES; --j) {
+          for (uint32_t i = 0; i < kWaitLimit && !mbar_try(&bar_full[j % STAGES], (j / STAGES) & 1); ++i) {
           }
         }
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---------------- MMA issuer
+  } else if (warp == kWarpMma) {
+    // ---------------- MMA issuer (one thread)
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc_tf32<BN>();
-      for (int kt = 0; kt < num_k; ++kt) {
-        const int s = kt % STAGES;
-        if (!mbar_wait(&bar_split[s], (kt / STAGES) & 1, abort_flag, err, 2)) break;
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++lt) {
+        const int b = lt & 1;
+        if (lt >= 2 && !mbar_wait(&bar_acc_empty[b], ((lt >> 1) - 1) & 1, abort_flag, err, 5)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_hi = smem_u32(stage_A(s)), a_lo = smem_u32(stage_Alo(s));
-        const uint32_t w_hi = smem_u32(stage_Wh(s)), w_lo = smem_u32(stage_Wl(s));
-#pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk) {
-          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
-          const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
-          mma_tf32(tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(w_hi + off), idesc, acc);
-          if (kSplit) {
-            mma_tf32(tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(w_lo + off), idesc, 1u);
-            mma_tf32(tmem, smem_desc_sw128(a_lo + off), smem_desc_sw128(w_hi + off), idesc, 1u);
+        const uint32_t acc_tmem = tmem + (uint32_t)(b * kAccCols);
+        for (int kt = 0; kt < num_k; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(kSplit ? &bar_split[s] : &bar_full[s], (it / STAGES) & 1, abort_flag, err, 2)) {
+            ok = false;
+            break;
           }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_hi = smem_u32(stage_A(s)), a_lo = smem_u32(stage_Alo(s));
+          const uint32_t w_hi = smem_u32(stage_Wh(s)), w_lo = smem_u32(stage_Wl(s));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
+            const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+            mma_tf32(acc_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(w_hi + off), idesc, acc);
+            if (kSplit) {
+              mma_tf32(acc_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(w_lo + off), idesc, 1u);
+              mma_tf32(acc_tmem, smem_desc_sw128(a_lo + off), smem_desc_sw128(w_hi + off), idesc, 1u);
+            }
+          }
+          mma_commit(&bar_empty[s]);
         }
-        mma_commit(&bar_empty[s]);
+        if (ok) mma_commit(&bar_acc_full[b]);
       }
-      // completion of every MMA issued above (also on the abort path)
-      mma_commit(bar_acc);
-      if (*abort_flag) {
-        for (uint32_t i = 0; i < kWaitLimit && !mbar_try(bar_acc, 0); ++i) {
-        }
+      // completion of every MMA issued above (also on the abort path) before TMEM is released
+      mma_commit(bar_done);
+      for (uint32_t i = 0; i < kWaitLimit && !mbar_try(bar_done, 0); ++i) {
       }
     }
     __syncwarp();
-  } else {
-    // ---------------- split (warps 2-5), then epilogue
-    const int t = threadIdx.x - 64;  // 0..127
-    for (int kt = 0; kt < num_k; ++kt) {
-      const int s = kt % STAGES;
-      if (!mbar_wait(&bar_full[s], (kt / STAGES) & 1, abort_flag, err, 3)) break;
-      if (kSplit) {
-        uint4* a = reinterpret_cast<uint4*>(stage_A(s));
-        uint4* alo = reinterpret_cast<uint4*>(stage_Alo(s));
+  } else if (warp < kWarpEpi0) {
+    // ---------------- split (warps 2-5): A_lo = rn_tf32(a - trunc_tf32(a)). The tensor core reads
+    // the raw fp32 A tile as TF32 by truncation, so the hi part needs no rewrite.
+    if (kSplit) {
+      const int t = threadIdx.x - kWarpSplit0 * 32;  // 0..127
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        for (int kt = 0; kt < num_k; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&bar_full[s], (it / STAGES) & 1, abort_flag, err, 3)) {
+            ok = false;
+            break;
+          }
+          const uint4* a = reinterpret_cast<const uint4*>(stage_A(s));
+          uint4* alo = reinterpret_cast<uint4*>(stage_Alo(s));
 #pragma unroll
-        for (int i = 0; i < L::kA / 16 / 128; ++i) {
-          const int c = i * 128 + t;
-          const uint4 v = a[c];
-          uint4 h, l;
-          split_rn(v.x, h.x, l.x); split_rn(v.y, h.y, l.y); split_rn(v.z, h.z, l.z); split_rn(v.w, h.w, l.w);
-          a[c] = h;
-          alo[c] = l;
+          for (int i = 0; i < L::kA / 16 / 128; ++i) {
+            const int c = i * 128 + t;
+            const uint4 v = a[c];
+            alo[c] = make_uint4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive(&bar_split[s]);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
-      mbar_arrive(&bar_split[s]);
     }
-    // epilogue: TMEM -> registers -> (+bias) -> global
-    bool ok = mbar_wait(bar_acc, 0, abort_flag, err, 4);
-    ok = __all_sync(kFull, ok && !*abort_flag);  // tcgen05.ld is warp-collective: decide per warp
-    if (ok) {
+  } else {
+    // ---------------- epilogue (warps 6-9): TMEM -> registers -> (+bias) -> global
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+      const int b = lt & 1;
+      bool ok = mbar_wait(&bar_acc_full[b], (lt >> 1) & 1, abort_flag, err, 4);
+      ok = __all_sync(kFull, ok && !*abort_flag);  // tcgen05.ld is warp-collective: decide per warp
+      if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int q = warp & 3;             // TMEM lane quadrant of this warp
+      const int m0 = (tile / num_n) * kBM, n0 = (tile % num_n) * BN;
       const int row = m0 + q * 32 + lane;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t taddr = tmem + (uint32_t)(b * kAccCols) + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
@@ -301,11 +348,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
           }
         }
       }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&bar_acc_empty[b]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
@@ -366,7 +415,8 @@ cudaError_t launch(const CUtensorMap& a, const CUtensorMap& wh, const CUtensorMa
     if (st != cudaSuccess) return st;
     configured |= uint64_t(1) << (dev & 63);
   }
-  dim3 grid(N / BN, (M + kBM - 1) / kBM);
+  const int tiles = ((M + kBM - 1) / kBM) * (N / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
   kern<<<grid, kThreads, L::kBytes, s>>>(a, wh, wl, C, bias, M, N, K, ldc, err);
   return cudaGetLastError();
 }
