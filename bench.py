@@ -12,8 +12,9 @@ ranks. ``value`` has the positions already in HBM; ``e2e`` copies them from pinn
 memory and the energy and forces back inside the timed region, through the public API
 (``Predictor(ZeroAllocBackbone(backbone), head)``).
 
-With N > 1 GPUs every rank runs an independent replica (weak scaling; the partitioned
-multi-GPU path is not part of this benchmark yet). ``--impl reference`` times the CPU
+With N > 1 GPUs (torchrun, one process per GPU) the system is bulk Cu 10 x 10 x (10 N), 4,000
+atoms per GPU (weak scaling; N = 1 is config 3), split into N slabs with a per-layer halo
+exchange over NCCL (``flash_uma_b200.partition``). ``--impl reference`` times the CPU
 restatement of the reference implementation (the oracle) on the host cores instead.
 """
 from __future__ import annotations
@@ -165,21 +166,52 @@ def md_positions(pos0: torch.Tensor, count: int, seed: int = 0):
     return [pos0 + 0.01 * torch.randn(pos0.shape, generator=g) for _ in range(count)]
 
 
+def build_partitioned(device, tf32: bool, world: int, rank: int):
+    """Weak-scaling workload for N > 1 GPUs: bulk fcc Cu 10 x 10 x (10 N) (4,000 atoms per GPU,
+    so N = 1 is exactly config 3), split into N slabs along the long axis with a per-layer halo
+    exchange of node embeddings over NCCL (flash_uma_b200.partition)."""
+    from flash_uma_b200.partition import PartitionedModel, make_plan
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
+    from flash_uma_b200.systems import bulk_fcc, to_graph
+    from flash_uma_b200.wrapper import ZeroAllocBackbone
+    system = bulk_fcc(10, 10, 10 * world, jitter=0.05, seed=0, name=f"bulk_cu_{4000 * world}")
+    data = to_graph([system])
+    off = SyntheticESCNMDBackbone(seed=0).to(device)
+    head = make_energy_head(128, 128, seed=1).to(device)
+    bb = ZeroAllocBackbone(off, gemm="tf32" if tf32 else "tf32x3")
+    plan = make_plan(system.positions, system.cell, data.edge_index.numpy(), world, rank)
+    pm = PartitionedModel(bb.ce, plan, device)
+    d = data.to(device)
+    csd = bb.csd_embedding(d.charge, d.spin).float().detach()
+
+    def step(pos):
+        e, f = pm.energy_forces(head, pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd)
+        return {"energy": e, "forces": f}
+
+    return system, data, step, plan
+
+
 def run_flash(args, rank, world, device):
     from flash_uma_b200 import _native
     _native.load()
-    system, data_cpu, pred = build_problem(device, args.tf32)
-    N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
     C, B, L = 128, 64, 4
-    data = data_cpu.to(device)
     K, W = args.steps, args.warmup
-    pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=rank)]
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    if world > 1:
+        system, data_cpu, step, plan = build_partitioned(device, args.tf32, world, rank)
+        N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
+        pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=0)]
+    else:
+        plan = None
+        system, data_cpu, pred = build_problem(device, args.tf32)
+        N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
+        data = data_cpu.to(device)
+        pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=rank)]
 
-    import dataclasses
+        import dataclasses
 
-    def step(pos):
-        return pred(dataclasses.replace(data, pos=pos))
+        def step(pos):
+            return pred(dataclasses.replace(data, pos=pos))
 
     # ---- which of our kernels dominates: one probe pass with every entry point timed
     probe = _native.LaunchProbe(timed=list(_native.KERNELS_PER_CALL))
@@ -191,11 +223,15 @@ def run_flash(args, rank, world, device):
     torch.cuda.synchronize()
     _native.set_probe(None)
     per_op = {n: sum(probe.times_ms(n)) for n in probe.events}
+    probe_counts = dict(probe.counts)
     dominant = max(per_op, key=per_op.get)
     launches_per_step = probe.launches
 
-    # ---- timed region 1: inputs resident in HBM
-    probe = _native.LaunchProbe(timed=[dominant])
+    # ---- timed region 1: inputs resident in HBM. Launch counting covers every timed step; the
+    # dominant kernel's launches are bracketed with CUDA events in the last timed step only
+    # (pre-created events), so the instrumentation does not slow the other steps.
+    probe = _native.LaunchProbe(timed=[dominant], pool=4 * probe_counts.get(dominant, 1) + 8)
+    probe.timing = False
     sampler = ClockSampler(device.index if device.index is not None else 0)
     if world > 1:
         torch.distributed.barrier()
@@ -205,6 +241,7 @@ def run_flash(args, rank, world, device):
     evs = []
     for k in range(K):
         flush.zero_()
+        probe.timing = k == K - 1
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         torch.cuda.nvtx.range_push("fuma_step")
@@ -220,7 +257,7 @@ def run_flash(args, rank, world, device):
     gpu_launches = probe.launches
 
     # ---- timed region 2: end to end from pinned host buffers through the public API
-    host_pos = [p.cpu().pin_memory() for p in md_positions(data_cpu.pos, K, seed=100 + rank)]
+    host_pos = [p.cpu().pin_memory() for p in md_positions(data_cpu.pos, K, seed=100 + (0 if world > 1 else rank))]
     f_host = torch.empty(N, 3).pin_memory()
     e_host = torch.empty(1).pin_memory()
     pos_dev = torch.empty(N, 3, device=device)
@@ -246,27 +283,59 @@ def run_flash(args, rank, world, device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     total_ms, e2e_ms = t.tolist()
 
-    hbm, _, peak_kind = load_peaks()
-    nbytes = alg_bytes(dominant, N, E, C, B, M_rows=E, D=128)
+    hbm, bf16, peak_kind = load_peaks()
     avg_ms = sum(dom_ms) / max(1, len(dom_ms))
-    achieved = nbytes / (avg_ms * 1e-3) / 1e9 if nbytes and avg_ms > 0 else None
+    # per-launch sizes: this rank's local graph
+    Ek, Nk = (len(plan.edges), len(plan.local_ids)) if world > 1 else (E, N)
+    if dominant == "fuma_linear":
+        # tensor-bound: TF32-pipe FLOPs per launch (3 products per fp32 product in 3xTF32)
+        passes = 1 if args.tf32 else 3
+        launches = probe.counts.get(dominant, 1) // K
+        flops_launch = passes * gemm_flops_per_step(Ek, C, B, L) / max(1, launches)
+        achieved = flops_launch / (avg_ms * 1e-3) / 1e12
+        roof = {"kernel": "fuma_linear (gemm_tf32_kernel)", "bound": "tensor", "achieved": achieved,
+                "peak": bf16 / 2, "unit": "TFLOP/s", "frac": achieved / (bf16 / 2),
+                "peak_kind": f"{peak_kind} dense bf16 / 2 (TF32 rate; TF32 not measured separately)",
+                "traffic": None, "alg_flops_per_launch": flops_launch}
+    else:
+        nbytes = alg_bytes(dominant, Nk, Ek, C, B, M_rows=Ek, D=128)
+        achieved = nbytes / (avg_ms * 1e-3) / 1e9 if nbytes and avg_ms > 0 else None
+        roof = {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind, "traffic": None,
+                "alg_bytes_per_launch": nbytes}
+    roof.update(avg_launch_ms=avg_ms, launches_timed=len(dom_ms),
+                share_of_step=(sum(dom_ms) / total_ms) if world == 1 else None)
+    # the top HBM-bound kernel as well (device time from the probe pass)
+    mem_ops = {k: v for k, v in per_op.items() if k != "fuma_linear" and alg_bytes(k, Nk, Ek, C, B, Ek, 128)}
+    top_mem = max(mem_ops, key=mem_ops.get) if mem_ops else None
+    roof_mem = None
+    if top_mem:
+        launches = max(1, probe_counts.get(top_mem, 1))
+        ms_launch = per_op[top_mem] / launches
+        nb = alg_bytes(top_mem, Nk, Ek, C, B, M_rows=Ek, D=128)
+        gbs = nb / (ms_launch * 1e-3) / 1e9
+        roof_mem = {"kernel": top_mem, "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                    "frac": gbs / hbm, "alg_bytes_per_launch": nb, "avg_launch_ms": ms_launch}
+    atoms_total = N if world > 1 else world * N
     out = {
-        "metric": METRIC, "value": world * N * K / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "metric": METRIC, "value": atoms_total * K / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded bulk Cu positions, random-init weights)",
-        "config": {"workload": "bulk_cu_4000 (BASELINE config 3): 4000 atoms, %d edges, E+F per step" % E,
+        "config": {"workload": ("bulk_cu_4000 (BASELINE config 3): 4000 atoms, %d edges, E+F per step" % E
+                                if world == 1 else
+                                f"bulk Cu 10x10x{10 * world} ({N} atoms, {E} edges; 4000 atoms per GPU, weak "
+                                f"scaling of config 3), E+F per step, slab decomposition with per-layer halo "
+                                f"exchange (NCCL)"),
                    "atoms": N, "edges": E, "sphere_channels": C, "layers": L, "num_distance_basis": B,
                    "cutoff": 6.0, "max_neighbors": 30, "gemm": "tcgen05 TF32 (single pass)" if args.tf32 else "tcgen05 3xTF32 (fp32-level)",
                    "l2": "flushed (256 MB write) before every step, outside the timed events",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-        "e2e": {"value": world * N * K / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4,
+                   "parallelism": f"spatial slabs x{world} (halo atoms per rank: {len(plan.halo)} on rank 0)"
+                   if world > 1 else "single GPU"},
+        "e2e": {"value": atoms_total * K / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4,
                 "d2h_bytes_per_step": N * 3 * 4 + 4},
-        "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind,
-                     "traffic": None, "alg_bytes_per_launch": nbytes, "avg_launch_ms": avg_ms,
-                     "launches_timed": len(dom_ms),
-                     "share_of_step": (sum(dom_ms) / total_ms) if world == 1 else None},
-        "gemm": gemm_summary(per_op, E, C, B, L, args.tf32),
+        "roofline": roof,
+        "roofline_top_hbm_kernel": roof_mem,
+        "gemm": gemm_summary(per_op, Ek, C, B, L, args.tf32),
         "gpu_launches": gpu_launches,
         "per_kernel_ms_one_step": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
         "clocks": clocks,
@@ -441,7 +510,7 @@ def main():
         return
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     try:
         out = run_flash(args, rank, world, device)
         if rank == 0:

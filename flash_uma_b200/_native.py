@@ -86,8 +86,10 @@ def stream_of(t: torch.Tensor) -> int:
 
 # kernels each entry point launches (used by launch accounting)
 KERNELS_PER_CALL = {name: 1 for name in _SIGS}
-KERNELS_PER_CALL["fuma_gather_bwd"] = 2
-KERNELS_PER_CALL["fuma_gather_bwd_noalloc"] = 2
+KERNELS_PER_CALL["fuma_gather_bwd"] = 3
+KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
+KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2
+KERNELS_PER_CALL["fuma_gather_bwd_noalloc"] = 3
 
 
 class LaunchProbe:
@@ -95,18 +97,24 @@ class LaunchProbe:
     names in ``timed``, brackets each call with CUDA events on the current stream so the
     kernel's device time can be measured inside a larger timed region."""
 
-    def __init__(self, timed=()):
+    def __init__(self, timed=(), pool: int = 0):
         self.timed = set(timed)
         self.counts: dict[str, int] = {}
         self.launches = 0
         self.events: dict[str, list] = {}
         self.meta: dict[str, list] = {}
+        self.timing = True          # bracket calls of ``timed`` entry points with events
+        # pre-created events keep the per-call host cost to two cudaEventRecord calls
+        self._pool = [torch.cuda.Event(enable_timing=True) for _ in range(pool)]
+
+    def _event(self):
+        return self._pool.pop() if self._pool else torch.cuda.Event(enable_timing=True)
 
     def before(self, name, args):
         self.counts[name] = self.counts.get(name, 0) + 1
         self.launches += KERNELS_PER_CALL.get(name, 1)
-        if name in self.timed:
-            ev0 = torch.cuda.Event(enable_timing=True)
+        if self.timing and name in self.timed:
+            ev0 = self._event()
             ev0.record()
             return ev0
         return None
@@ -114,10 +122,9 @@ class LaunchProbe:
     def after(self, name, ev0, args):
         if ev0 is None:
             return
-        ev1 = torch.cuda.Event(enable_timing=True)
+        ev1 = self._event()
         ev1.record()
         self.events.setdefault(name, []).append((ev0, ev1))
-        self.meta.setdefault(name, []).append(args)
 
     def times_ms(self, name):
         return [a.elapsed_time(b) for a, b in self.events.get(name, [])]

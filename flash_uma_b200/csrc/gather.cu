@@ -18,11 +18,11 @@
 // processed on its own to keep the live register set small (these kernels are
 // bandwidth-bound and need occupancy, not ILP from a 200-register body).
 //
-// Backward without atomics: pass A walks the destination CSR, one warp per
-// destination node j; it writes g_rad[e] and g_wigner[e], accumulates the
-// target-side gradient of x[j] in shared memory and writes the source-side
-// contribution of every edge to a scratch row [9C]. Pass B walks the source CSR
-// and adds those rows to g_x[i] in a fixed order: run-to-run deterministic g_x.
+// Backward without atomics: pass A walks the destination CSR, two warps per
+// destination node j (l <= 1 and l = 2 coefficient blocks); it writes g_rad[e] and
+// g_wigner[e], accumulates the target-side gradient of x[j] in shared memory and writes
+// the source-side contribution of every edge to a scratch row [9C]. Pass B walks the
+// source CSR and adds those rows to g_x[i] in a fixed order: run-to-run deterministic g_x.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -61,7 +61,7 @@ __device__ __forceinline__ void rotT(const float* D, const float4* g, float4* ou
 }
 
 constexpr int kFwdWarps = 8;
-constexpr int kBwdWarps = 4;
+constexpr int kBwdWarps = 8;
 
 }  // namespace
 
@@ -124,144 +124,156 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
   }
 }
 
-// Pass A of the backward (see file comment). Dynamic shared memory: kBwdWarps * 9 * C floats.
-__global__ void __launch_bounds__(kBwdWarps * 32, 3) gather_bwd_dst_kernel(
+// Pass A of the backward (see file comment), one launch per coefficient block: PART 0 handles
+// the l <= 1 coefficients (rows 0-3, radial slots 0-3 and 6-7, Wigner D1), PART 1 the l = 2
+// coefficients (rows 4-8, radial slots 4-5 and 8-11, Wigner D2). Their outputs are disjoint.
+// The destination's CSR chunk (edge id, source atom, source system) is loaded once into the
+// lanes and broadcast with shuffles, so an edge iteration issues only independent loads.
+// Dynamic shared memory: kBwdWarps * 5 * C floats (target-side accumulator of this warp's rows).
+template <int PART>
+__global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
     const float* __restrict__ gX0, const float* __restrict__ gX1, const float* __restrict__ gX2,
     const float* __restrict__ x, const int64_t* __restrict__ idx_i, const float* __restrict__ wig,
     const float* __restrict__ rad, const float* __restrict__ csd, const int64_t* __restrict__ batch,
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, float* __restrict__ g_x,
     float* __restrict__ g_wig, float* __restrict__ g_rad, float* __restrict__ g_src_rows, int64_t N, int C) {
   extern __shared__ float4 s_acc4[];
-  __shared__ float s_w[kBwdWarps][36];
-  __shared__ float s_red[kBwdWarps][36];
+  __shared__ float s_w[kBwdWarps][28];
+  __shared__ float s_red[kBwdWarps][28];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   float* sw = s_w[warp];
-  const float* D1 = sw;
-  const float* D2 = sw + 9;
-  float4* acc = s_acc4 + (size_t)warp * 9 * C4;  // [9][C4]: target-side gradient of x[jn]
+  float4* acc = s_acc4 + (size_t)warp * 5 * C4;
+  constexpr int part = PART;
   for (int64_t jn = (int64_t)blockIdx.x * kBwdWarps + warp; jn < N; jn += (int64_t)gridDim.x * kBwdWarps) {
-    for (int t = lane; t < 9 * C4; t += 32) acc[t] = f4(0.f);
+    constexpr int nrows = part ? 5 : 4;       // target-side accumulator rows (l=0..1 -> 4, l=2 -> 5)
+    constexpr int nw = part ? 25 : 9;         // Wigner entries of this part
+    constexpr int woff = part ? 9 : 0;
+    for (int t = lane; t < nrows * C4; t += 32) acc[t] = f4(0.f);
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     const int64_t bj = batch[jn];
     const float* xj_base = x + jn * 9 * (int64_t)C;
-    for (int k = kb; k < ke; ++k) {
-      const int64_t e = col_idx[k];
-      stage_wigner(sw, wig, e, lane);
-      const int64_t in = idx_i[e];
-      const int64_t bi = batch[in];
-      const float* xi_base = x + in * 9 * (int64_t)C;
-      const float* g0b = gX0 + e * 6 * (int64_t)C;
-      const float* g1b = gX1 + e * 8 * (int64_t)C;
-      const float* g2b = gX2 + e * 4 * (int64_t)C;
-      const float* rrb = rad + e * 12 * (int64_t)C;
-      float* grb = g_rad + e * 12 * (int64_t)C;
-      float* gsb = g_src_rows + e * 9 * (int64_t)C;
-      __syncwarp();
-      // ---- l = 0 and l = 1 (9 Wigner partials)
-      float gw1[9];
+    for (int k0 = kb; k0 < ke; k0 += 32) {
+      // CSR chunk prefetch: lane l holds edge k0+l, its source atom and the source's system
+      int64_t e_l = 0, in_l = 0, bi_l = 0;
+      if (k0 + lane < ke) {
+        e_l = col_idx[k0 + lane];
+        in_l = idx_i[e_l];
+        bi_l = batch[in_l];
+      }
+      const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
+      for (int q = 0; q < cnt; ++q) {
+        const int64_t e = __shfl_sync(kFull, e_l, q);
+        const int64_t in = __shfl_sync(kFull, in_l, q);
+        const int64_t bi = __shfl_sync(kFull, bi_l, q);
+        if (lane < nw) sw[lane] = __ldg(wig + e * kWig + woff + lane);
+        __syncwarp();
+        const float* xi_base = x + in * 9 * (int64_t)C;
+        const float* g0b = gX0 + e * 6 * (int64_t)C;
+        const float* g1b = gX1 + e * 8 * (int64_t)C;
+        const float* g2b = gX2 + e * 4 * (int64_t)C;
+        const float* rrb = rad + e * 12 * (int64_t)C;
+        float* grb = g_rad + e * 12 * (int64_t)C;
+        float* gsb = g_src_rows + e * 9 * (int64_t)C;
+        float gw[nw];
 #pragma unroll
-      for (int m = 0; m < 9; ++m) gw1[m] = 0.f;
-      for (int c4 = lane; c4 < C4; c4 += 32) {
-        const int co = c4 * 4;
-        const float* rr = rrb + co; const float* g0 = g0b + co; const float* g1 = g1b + co;
-        const float* xi = xi_base + co; const float* xj = xj_base + co;
-        float* grr = grb + co; float* gsrc = gsb + co;
-        {
-          const float4 a0 = ld4_stream(g0), a1 = ld4_stream(g0 + C);
-          st4(grr, a0 * (ld4_keep(xi) + ld4_keep(csd + bi * C + co)));
-          st4(grr + C, a1 * (ld4_keep(xj) + ld4_keep(csd + bj * C + co)));
-          st4(gsrc, a0 * ld4_stream(rr));
-          acc[c4] += a1 * ld4_stream(rr + C);
+        for (int m = 0; m < nw; ++m) gw[m] = 0.f;
+        if constexpr (part == 0) {
+          const float* D1 = sw;
+          for (int c4 = lane; c4 < C4; c4 += 32) {
+            const int co = c4 * 4;
+            const float* rr = rrb + co; const float* g0 = g0b + co; const float* g1 = g1b + co;
+            const float* xi = xi_base + co; const float* xj = xj_base + co;
+            float* grr = grb + co; float* gsrc = gsb + co;
+            {
+              const float4 a0 = ld4_stream(g0), a1 = ld4_stream(g0 + C);
+              st4(grr, a0 * (ld4_keep(xi) + ld4_keep(csd + bi * C + co)));
+              st4(grr + C, a1 * (ld4_keep(xj) + ld4_keep(csd + bj * C + co)));
+              st4(gsrc, a0 * ld4_stream(rr));
+              acc[c4] += a1 * ld4_stream(rr + C);
+            }
+            float4 vi[3], vj[3], ri[3], rj[3];
+#pragma unroll
+            for (int m = 0; m < 3; ++m) { vi[m] = ld4_keep(xi + (1 + m) * C); vj[m] = ld4_keep(xj + (1 + m) * C); }
+            rot<3>(D1, vi, ri);
+            rot<3>(D1, vj, rj);
+            const float4 r2 = ld4_stream(rr + 2 * C), r3 = ld4_stream(rr + 3 * C);
+            const float4 r6 = ld4_stream(rr + 6 * C), r7 = ld4_stream(rr + 7 * C);
+            const float4 a2 = ld4_stream(g0 + 2 * C), a3 = ld4_stream(g0 + 3 * C);
+            const float4 b0 = ld4_stream(g1), b1 = ld4_stream(g1 + C);
+            const float4 b4 = ld4_stream(g1 + 4 * C), b5 = ld4_stream(g1 + 5 * C);
+            st4(grr + 2 * C, a2 * ri[1]);
+            st4(grr + 3 * C, a3 * rj[1]);
+            st4(grr + 6 * C, b0 * ri[2] + b4 * ri[0]);
+            st4(grr + 7 * C, b1 * rj[2] + b5 * rj[0]);
+            const float4 gi[3] = {b4 * r6, a2 * r2, b0 * r6};
+            const float4 gj[3] = {b5 * r7, a3 * r3, b1 * r7};
+            float4 t[3];
+            rotT<3>(D1, gi, t);
+#pragma unroll
+            for (int m = 0; m < 3; ++m) st4(gsrc + (1 + m) * C, t[m]);
+            rotT<3>(D1, gj, t);
+#pragma unroll
+            for (int m = 0; m < 3; ++m) acc[(1 + m) * C4 + c4] += t[m];
+#pragma unroll
+            for (int r = 0; r < 3; ++r)
+#pragma unroll
+              for (int m = 0; m < 3; ++m) gw[r * 3 + m] += dot4(gi[r], vi[m]) + dot4(gj[r], vj[m]);
+          }
+        } else {
+          const float* D2 = sw;
+          for (int c4 = lane; c4 < C4; c4 += 32) {
+            const int co = c4 * 4;
+            const float* rr = rrb + co; const float* g0 = g0b + co; const float* g1 = g1b + co;
+            const float* g2 = g2b + co;
+            const float* xi = xi_base + co; const float* xj = xj_base + co;
+            float* grr = grb + co; float* gsrc = gsb + co;
+#pragma unroll 1
+            for (int s = 0; s < 2; ++s) {   // s = 0: source side (even slots), s = 1: target side (odd slots)
+              const float* xs = s ? xj : xi;
+              float4 v[5], r[5];
+#pragma unroll
+              for (int m = 0; m < 5; ++m) v[m] = ld4_keep(xs + (4 + m) * C);
+              rot<5>(D2, v, r);
+              const float4 a4 = ld4_stream(g0 + (4 + s) * C);
+              const float4 b2 = ld4_stream(g1 + (2 + s) * C), b6 = ld4_stream(g1 + (6 + s) * C);
+              const float4 c0 = ld4_stream(g2 + s * C), c2 = ld4_stream(g2 + (2 + s) * C);
+              const float4 r4 = ld4_stream(rr + (4 + s) * C), r8 = ld4_stream(rr + (8 + s) * C);
+              const float4 r10 = ld4_stream(rr + (10 + s) * C);
+              st4(grr + (4 + s) * C, a4 * r[2]);
+              st4(grr + (8 + s) * C, b2 * r[3] + b6 * r[1]);
+              st4(grr + (10 + s) * C, c0 * r[4] + c2 * r[0]);
+              const float4 g[5] = {c2 * r10, b6 * r8, a4 * r4, b2 * r8, c0 * r10};
+              float4 t[5];
+              rotT<5>(D2, g, t);
+              if (s == 0) {
+#pragma unroll
+                for (int m = 0; m < 5; ++m) st4(gsrc + (4 + m) * C, t[m]);
+              } else {
+#pragma unroll
+                for (int m = 0; m < 5; ++m) acc[m * C4 + c4] += t[m];
+              }
+#pragma unroll
+              for (int rr2 = 0; rr2 < 5; ++rr2)
+#pragma unroll
+                for (int m = 0; m < 5; ++m) gw[rr2 * 5 + m] += dot4(g[rr2], v[m]);
+            }
+          }
         }
-        float4 vi[3], vj[3], ri[3], rj[3];
+        // reduce this part's Wigner-gradient partials across the warp
 #pragma unroll
-        for (int m = 0; m < 3; ++m) { vi[m] = ld4_keep(xi + (1 + m) * C); vj[m] = ld4_keep(xj + (1 + m) * C); }
-        rot<3>(D1, vi, ri);
-        rot<3>(D1, vj, rj);
-        const float4 r2 = ld4_stream(rr + 2 * C), r3 = ld4_stream(rr + 3 * C);
-        const float4 r6 = ld4_stream(rr + 6 * C), r7 = ld4_stream(rr + 7 * C);
-        const float4 a2 = ld4_stream(g0 + 2 * C), a3 = ld4_stream(g0 + 3 * C);
-        const float4 b0 = ld4_stream(g1), b1 = ld4_stream(g1 + C);
-        const float4 b4 = ld4_stream(g1 + 4 * C), b5 = ld4_stream(g1 + 5 * C);
-        st4(grr + 2 * C, a2 * ri[1]);
-        st4(grr + 3 * C, a3 * rj[1]);
-        st4(grr + 6 * C, b0 * ri[2] + b4 * ri[0]);
-        st4(grr + 7 * C, b1 * rj[2] + b5 * rj[0]);
-        const float4 gi[3] = {b4 * r6, a2 * r2, b0 * r6};
-        const float4 gj[3] = {b5 * r7, a3 * r3, b1 * r7};
-        float4 t[3];
-        rotT<3>(D1, gi, t);
-#pragma unroll
-        for (int m = 0; m < 3; ++m) st4(gsrc + (1 + m) * C, t[m]);
-        rotT<3>(D1, gj, t);
-#pragma unroll
-        for (int m = 0; m < 3; ++m) acc[(1 + m) * C4 + c4] += t[m];
-#pragma unroll
-        for (int r = 0; r < 3; ++r)
-#pragma unroll
-          for (int m = 0; m < 3; ++m) gw1[r * 3 + m] += dot4(gi[r], vi[m]) + dot4(gj[r], vj[m]);
+        for (int m = 0; m < nw; ++m) {
+          const float tsum = warp_sum(gw[m]);
+          if (lane == 0) s_red[warp][m] = tsum;
+        }
+        __syncwarp();
+        if (lane < nw) g_wig[e * kWig + woff + lane] = s_red[warp][lane];
+        __syncwarp();
       }
-#pragma unroll
-      for (int m = 0; m < 9; ++m) {
-        const float tsum = warp_sum(gw1[m]);
-        if (lane == 0) s_red[warp][m] = tsum;
-      }
-      // ---- l = 2 (25 Wigner partials)
-      float gw2[25];
-#pragma unroll
-      for (int m = 0; m < 25; ++m) gw2[m] = 0.f;
-      for (int c4 = lane; c4 < C4; c4 += 32) {
-        const int co = c4 * 4;
-        const float* rr = rrb + co; const float* g0 = g0b + co; const float* g1 = g1b + co;
-        const float* g2 = g2b + co;
-        const float* xi = xi_base + co; const float* xj = xj_base + co;
-        float* grr = grb + co; float* gsrc = gsb + co;
-        float4 vi[5], vj[5], ri[5], rj[5];
-#pragma unroll
-        for (int m = 0; m < 5; ++m) { vi[m] = ld4_keep(xi + (4 + m) * C); vj[m] = ld4_keep(xj + (4 + m) * C); }
-        rot<5>(D2, vi, ri);
-        rot<5>(D2, vj, rj);
-        const float4 a4 = ld4_stream(g0 + 4 * C), a5 = ld4_stream(g0 + 5 * C);
-        const float4 b2 = ld4_stream(g1 + 2 * C), b3 = ld4_stream(g1 + 3 * C);
-        const float4 b6 = ld4_stream(g1 + 6 * C), b7 = ld4_stream(g1 + 7 * C);
-        const float4 c0 = ld4_stream(g2), c1 = ld4_stream(g2 + C);
-        const float4 c2 = ld4_stream(g2 + 2 * C), c3 = ld4_stream(g2 + 3 * C);
-        st4(grr + 4 * C, a4 * ri[2]);
-        st4(grr + 5 * C, a5 * rj[2]);
-        st4(grr + 8 * C, b2 * ri[3] + b6 * ri[1]);
-        st4(grr + 9 * C, b3 * rj[3] + b7 * rj[1]);
-        st4(grr + 10 * C, c0 * ri[4] + c2 * ri[0]);
-        st4(grr + 11 * C, c1 * rj[4] + c3 * rj[0]);
-        const float4 r4 = ld4_stream(rr + 4 * C), r5 = ld4_stream(rr + 5 * C);
-        const float4 r8 = ld4_stream(rr + 8 * C), r9 = ld4_stream(rr + 9 * C);
-        const float4 r10 = ld4_stream(rr + 10 * C), r11 = ld4_stream(rr + 11 * C);
-        const float4 gi[5] = {c2 * r10, b6 * r8, a4 * r4, b2 * r8, c0 * r10};
-        const float4 gj[5] = {c3 * r11, b7 * r9, a5 * r5, b3 * r9, c1 * r11};
-        float4 t[5];
-        rotT<5>(D2, gi, t);
-#pragma unroll
-        for (int m = 0; m < 5; ++m) st4(gsrc + (4 + m) * C, t[m]);
-        rotT<5>(D2, gj, t);
-#pragma unroll
-        for (int m = 0; m < 5; ++m) acc[(4 + m) * C4 + c4] += t[m];
-#pragma unroll
-        for (int r = 0; r < 5; ++r)
-#pragma unroll
-          for (int m = 0; m < 5; ++m) gw2[r * 5 + m] += dot4(gi[r], vi[m]) + dot4(gj[r], vj[m]);
-      }
-#pragma unroll
-      for (int m = 0; m < 25; ++m) {
-        const float tsum = warp_sum(gw2[m]);
-        if (lane == 0) s_red[warp][9 + m] = tsum;
-      }
-      __syncwarp();
-      g_wig[e * kWig + lane] = s_red[warp][lane];
-      if (lane < 2) g_wig[e * kWig + 32 + lane] = s_red[warp][32 + lane];
-      __syncwarp();
     }
-    float* gx = g_x + jn * 9 * (int64_t)C;
-    for (int t = lane; t < 9 * C4; t += 32) {
+    // target-side gradient of x[jn] for this part's rows
+    float* gx = g_x + jn * 9 * (int64_t)C + (part ? 4 : 0) * C;
+    for (int t = lane; t < nrows * C4; t += 32) {
       const int l = t / C4, c4 = t - l * C4;
       st4(gx + l * C + c4 * 4, acc[t]);
     }
@@ -301,10 +313,14 @@ void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, con
                        const float* wig, const float* rad, const float* csd, const int64_t* batch,
                        const int32_t* dst_ptr, const int32_t* dst_col, const int32_t* src_ptr, const int32_t* src_col,
                        float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, cudaStream_t s) {
-  const size_t smem = (size_t)kBwdWarps * 9 * C * sizeof(float);
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(gather_bwd_dst_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  gather_bwd_dst_kernel<<<grid_for(N, kBwdWarps, 3), kBwdWarps * 32, smem, s>>>(
+  const size_t smem = (size_t)kBwdWarps * 5 * C * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaFuncSetAttribute(gather_bwd_dst_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gather_bwd_dst_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }
+  gather_bwd_dst_kernel<0><<<grid_for(N, kBwdWarps, 2), kBwdWarps * 32, smem, s>>>(
+      gX0, gX1, gX2, x, idx_i, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig, g_rad, scratch, N, C);
+  gather_bwd_dst_kernel<1><<<grid_for(N, kBwdWarps, 2), kBwdWarps * 32, smem, s>>>(
       gX0, gX1, gX2, x, idx_i, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig, g_rad, scratch, N, C);
   gather_bwd_src_kernel<<<grid_for(N, 8, 8), 256, 0, s>>>(src_ptr, src_col, scratch, g_x, N, C);
 }

@@ -11,9 +11,9 @@
 // x_out[j] = x_res[j] + sum_{e in CSR row j} message_e, summed in fp64 in CSR order
 // (products in fp32), then rounded to fp32 once. Deterministic run to run.
 //
-// One warp per destination node; lane l owns channels [4l, 4l+4) (+128 per
-// extra group), 16-byte coalesced accesses; the per-edge scalars (34 Wigner
-// values + env) are staged once per edge in shared memory and broadcast.
+// One warp per destination node and coefficient block; lane l owns channels [4l, 4l+4)
+// (+128 per extra group), 16-byte coalesced accesses; the per-edge Wigner values are staged
+// in shared memory and broadcast.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,160 +30,200 @@ __device__ __forceinline__ void stage_edge(float* sw, const float* __restrict__ 
 
 }  // namespace
 
-template <int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) rotate_scatter_fwd_kernel(
+// One launch per coefficient block: PART 0 accumulates rows 0-3 (l = 0, 1; D1), PART 1 rows 4-8
+// (l = 2; D2); the two write disjoint rows of x_out. The CSR chunk (edge ids and envelopes) is
+// loaded once into the lanes and broadcast with shuffles.
+template <int PART>
+__global__ void __launch_bounds__(256, 2) rotate_scatter_fwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ Z0,
     const float* __restrict__ Z1, const float* __restrict__ Z2, const float* __restrict__ wig,
     const float* __restrict__ env, const float* __restrict__ x_res, float* __restrict__ x_out, int64_t N, int C) {
-  __shared__ float s_w[WARPS][36];
+  constexpr int kRows = PART ? 5 : 4;
+  constexpr int kW = PART ? 25 : 9;
+  constexpr int kWoff = PART ? 9 : 0;
+  constexpr int kRow0 = PART ? 4 : 0;
+  __shared__ float s_w[8][28];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
   float* sw = s_w[warp];
-  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+  for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     for (int c0 = 0; c0 < C4; c0 += 32) {
       const int c4 = c0 + lane;
       const bool act = c4 < C4;
       const int co = c4 * 4;
-      d4 acc[9];
+      d4 acc[kRows];
       if (act) {
-        const float* xr = x_res + jn * 9 * (int64_t)C + co;
+        const float* xr = x_res + jn * 9 * (int64_t)C + kRow0 * C + co;
 #pragma unroll
-        for (int l = 0; l < 9; ++l) acc[l] = d4_of(ld4(xr + l * C));
+        for (int l = 0; l < kRows; ++l) acc[l] = d4_of(ld4(xr + l * C));
       }
-      for (int k = kb; k < ke; ++k) {
-        const int64_t e = col_idx[k];
-        stage_edge(sw, wig, env, e, lane);
-        __syncwarp();
-        if (act) {
-          const float* D1 = sw;
-          const float* D2 = sw + 9;
-          const float ev = sw[34];
-          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
-          const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
-          const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
-                                ld4_stream(z1 + C), ld4_stream(z2)};
-          acc[0] += ld4_stream(z0) * ev;
-#pragma unroll
-          for (int kk = 0; kk < 3; ++kk) {
-            float4 a = D1[kk] * m1[0];
-            fma4(a, D1[3 + kk], m1[1]);
-            fma4(a, D1[6 + kk], m1[2]);
-            acc[1 + kk] += a * ev;
-          }
-#pragma unroll
-          for (int kk = 0; kk < 5; ++kk) {
-            float4 a = D2[kk] * m2[0];
-#pragma unroll
-            for (int r = 1; r < 5; ++r) fma4(a, D2[r * 5 + kk], m2[r]);
-            acc[4 + kk] += a * ev;
-          }
+      for (int k0 = kb; k0 < ke; k0 += 32) {
+        int64_t e_l = 0;
+        float env_l = 0.f;
+        if (k0 + lane < ke) {
+          e_l = col_idx[k0 + lane];
+          env_l = __ldg(env + e_l);
         }
-        __syncwarp();
+        const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
+        for (int q = 0; q < cnt; ++q) {
+          const int64_t e = __shfl_sync(kFull, e_l, q);
+          const float ev = __shfl_sync(kFull, env_l, q);
+          if (lane < kW) sw[lane] = __ldg(wig + e * kWig + kWoff + lane);
+          __syncwarp();
+          if (act) {
+            const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+            const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+            const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+            if constexpr (PART == 0) {
+              const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
+              acc[0] += ld4_stream(z0) * ev;
+#pragma unroll
+              for (int kk = 0; kk < 3; ++kk) {
+                float4 a = sw[kk] * m1[0];
+                fma4(a, sw[3 + kk], m1[1]);
+                fma4(a, sw[6 + kk], m1[2]);
+                acc[1 + kk] += a * ev;
+              }
+            } else {
+              const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
+                                    ld4_stream(z1 + C), ld4_stream(z2)};
+#pragma unroll
+              for (int kk = 0; kk < 5; ++kk) {
+                float4 a = sw[kk] * m2[0];
+#pragma unroll
+                for (int r = 1; r < 5; ++r) fma4(a, sw[r * 5 + kk], m2[r]);
+                acc[kk] += a * ev;
+              }
+            }
+          }
+          __syncwarp();
+        }
       }
       if (act) {
-        float* xo = x_out + jn * 9 * (int64_t)C + co;
+        float* xo = x_out + jn * 9 * (int64_t)C + kRow0 * C + co;
 #pragma unroll
-        for (int l = 0; l < 9; ++l) st4(xo + l * C, f4_of(acc[l]));
+        for (int l = 0; l < kRows; ++l) st4(xo + l * C, f4_of(acc[l]));
       }
     }
   }
 }
 
-// Backward, grouped by destination so g_out[j] is read once per node:
+// Backward, grouped by destination so g_out[j] stays in L1 across the node's edges, one launch
+// per coefficient block (PART 0: rows 0-3 / Z slots of l <= 1 / Wigner 0-8; PART 1: rows 4-8 /
+// l = 2 slots / Wigner 9-33):
 //   g_Z = env * (rows of D applied to g_out[j]); g_wigner[e] = env * sum_c g_out[j] (x) m;
-//   g_env[e] = sum_c g_out[j] . (unscaled message).  (g_x_res = g_out is returned by the host.)
-template <int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) rotate_scatter_bwd_kernel(
+//   g_env[e] = sum_c g_out[j] . (unscaled message): PART 0 writes its share, PART 1 (launched
+//   after it on the same stream) adds the rest, so the sum has a fixed order.
+// (g_x_res = g_out is returned by the host.)
+template <int PART>
+__global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ Z0, const float* __restrict__ Z1, const float* __restrict__ Z2,
     const float* __restrict__ wig, const float* __restrict__ env, float* __restrict__ gZ0, float* __restrict__ gZ1,
     float* __restrict__ gZ2, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C) {
-  __shared__ float s_w[WARPS][36];
-  __shared__ float s_red[WARPS][36];
+  constexpr int kW = PART ? 25 : 9;
+  constexpr int kWoff = PART ? 9 : 0;
+  constexpr int kParts = kW + (PART ? 0 : 1);  // PART 0 also reduces g0 . Z0_0
+  __shared__ float s_w[8][28];
+  __shared__ float s_red[8][28];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
   float* sw = s_w[warp];
-  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+  for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
-    for (int k = kb; k < ke; ++k) {
-      const int64_t e = col_idx[k];
-      stage_edge(sw, wig, env, e, lane);
-      __syncwarp();
-      const float* D1 = sw;
-      const float* D2 = sw + 9;
-      const float ev = sw[34];
-      float part[35];
+    const float* go_base = g_out + jn * 9 * (int64_t)C;
+    for (int k0 = kb; k0 < ke; k0 += 32) {
+      int64_t e_l = 0;
+      float env_l = 0.f;
+      if (k0 + lane < ke) {
+        e_l = col_idx[k0 + lane];
+        env_l = __ldg(env + e_l);
+      }
+      const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
+      for (int q = 0; q < cnt; ++q) {
+        const int64_t e = __shfl_sync(kFull, e_l, q);
+        const float ev = __shfl_sync(kFull, env_l, q);
+        if (lane < kW) sw[lane] = __ldg(wig + e * kWig + kWoff + lane);
+        __syncwarp();
+        float part[kParts];
 #pragma unroll
-      for (int m = 0; m < 35; ++m) part[m] = 0.f;
-      for (int c4 = lane; c4 < C4; c4 += 32) {
-        const int co = c4 * 4;
-        const float* go = g_out + jn * 9 * (int64_t)C + co;
-        float4 g[9];
+        for (int m = 0; m < kParts; ++m) part[m] = 0.f;
+        for (int c4 = lane; c4 < C4; c4 += 32) {
+          const int co = c4 * 4;
+          const float* go = go_base + co;
+          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+          float* q0 = gZ0 + e * 3 * (int64_t)C + co;
+          float* q1 = gZ1 + e * 4 * (int64_t)C + co;
+          float* q2 = gZ2 + e * 2 * (int64_t)C + co;
+          if constexpr (PART == 0) {
+            float4 g[4];
 #pragma unroll
-        for (int l = 0; l < 9; ++l) g[l] = ld4_keep(go + l * C);
-        const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-        const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-        const float* z2 = Z2 + e * 2 * (int64_t)C + co;
-        const float4 zl0 = ld4_stream(z0);
-        const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
-        const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
-                              ld4_stream(z1 + C), ld4_stream(z2)};
-        // g_Z: row r of the edge frame receives env * sum_k D[r][k] g[k]
-        float4 t1[3], t2[5];
+            for (int l = 0; l < 4; ++l) g[l] = ld4_keep(go + l * C);
+            const float4 zl0 = ld4_stream(z0);
+            const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
+            float4 t1[3];
 #pragma unroll
-        for (int r = 0; r < 3; ++r) {
-          float4 a = D1[r * 3] * g[1];
-          fma4(a, D1[r * 3 + 1], g[2]);
-          fma4(a, D1[r * 3 + 2], g[3]);
-          t1[r] = a * ev;
+            for (int r = 0; r < 3; ++r) {
+              float4 a = sw[r * 3] * g[1];
+              fma4(a, sw[r * 3 + 1], g[2]);
+              fma4(a, sw[r * 3 + 2], g[3]);
+              t1[r] = a * ev;
+            }
+            st4_stream(q0, g[0] * ev);
+            st4_stream(q0 + C, t1[1]);
+            st4_stream(q1, t1[2]);
+            st4_stream(q1 + 2 * C, t1[0]);
+#pragma unroll
+            for (int r = 0; r < 3; ++r)
+#pragma unroll
+              for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] += dot4(g[1 + kk], m1[r]);
+            part[9] += dot4(g[0], zl0);
+          } else {
+            float4 g[5];
+#pragma unroll
+            for (int l = 0; l < 5; ++l) g[l] = ld4_keep(go + (4 + l) * C);
+            const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
+                                  ld4_stream(z1 + C), ld4_stream(z2)};
+            float4 t2[5];
+#pragma unroll
+            for (int r = 0; r < 5; ++r) {
+              float4 a = sw[r * 5] * g[0];
+#pragma unroll
+              for (int kk = 1; kk < 5; ++kk) fma4(a, sw[r * 5 + kk], g[kk]);
+              t2[r] = a * ev;
+            }
+            st4_stream(q0 + 2 * C, t2[2]);
+            st4_stream(q1 + C, t2[3]);
+            st4_stream(q1 + 3 * C, t2[1]);
+            st4_stream(q2, t2[4]);
+            st4_stream(q2 + C, t2[0]);
+#pragma unroll
+            for (int r = 0; r < 5; ++r)
+#pragma unroll
+              for (int kk = 0; kk < 5; ++kk) part[r * 5 + kk] += dot4(g[kk], m2[r]);
+          }
         }
 #pragma unroll
-        for (int r = 0; r < 5; ++r) {
-          float4 a = D2[r * 5] * g[4];
-#pragma unroll
-          for (int kk = 1; kk < 5; ++kk) fma4(a, D2[r * 5 + kk], g[4 + kk]);
-          t2[r] = a * ev;
+        for (int m = 0; m < kParts; ++m) {
+          const float t = warp_sum(part[m]);
+          if (lane == 0) s_red[warp][m] = t;
         }
-        float* q0 = gZ0 + e * 3 * (int64_t)C + co;
-        float* q1 = gZ1 + e * 4 * (int64_t)C + co;
-        float* q2 = gZ2 + e * 2 * (int64_t)C + co;
-        st4_stream(q0, g[0] * ev);
-        st4_stream(q0 + C, t1[1]);
-        st4_stream(q0 + 2 * C, t2[2]);
-        st4_stream(q1, t1[2]);
-        st4_stream(q1 + C, t2[3]);
-        st4_stream(q1 + 2 * C, t1[0]);
-        st4_stream(q1 + 3 * C, t2[1]);
-        st4_stream(q2, t2[4]);
-        st4_stream(q2 + C, t2[0]);
-        // Wigner-gradient partials (before env): d/dD1[r][k] = sum_c g[1+k] m1[r]
-#pragma unroll
-        for (int r = 0; r < 3; ++r)
-#pragma unroll
-          for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] += dot4(g[1 + kk], m1[r]);
-#pragma unroll
-        for (int r = 0; r < 5; ++r)
-#pragma unroll
-          for (int kk = 0; kk < 5; ++kk) part[9 + r * 5 + kk] += dot4(g[4 + kk], m2[r]);
-        part[34] += dot4(g[0], zl0);
+        __syncwarp();
+        // g_env share: sum_{r,k} D[r][k] raw[r][k] (+ g0 . Z0_0 in PART 0)
+        float genv = lane < kW ? sw[lane] * s_red[warp][lane] : 0.f;
+        genv = warp_sum(genv);
+        if (lane < kW) g_wig[e * kWig + kWoff + lane] = s_red[warp][lane] * ev;
+        if (lane == 0) {
+          if constexpr (PART == 0) g_env[e] = genv + s_red[warp][9];
+          else g_env[e] += genv;
+        }
+        __syncwarp();
       }
-#pragma unroll
-      for (int m = 0; m < 35; ++m) {
-        const float t = warp_sum(part[m]);
-        if (lane == 0) s_red[warp][m] = t;
-      }
-      __syncwarp();
-      // g_env = sum_c g0 z0 + sum_{r,k} D[r][k] * raw[r][k]
-      float genv = (lane < 32) ? sw[lane] * s_red[warp][lane] : 0.f;
-      if (lane < 2) genv += sw[32 + lane] * s_red[warp][32 + lane];
-      genv = warp_sum(genv);
-      g_wig[e * kWig + lane] = s_red[warp][lane] * ev;
-      if (lane < 2) g_wig[e * kWig + 32 + lane] = s_red[warp][32 + lane] * ev;
-      if (lane == 0) g_env[e] = genv + s_red[warp][34];
-      __syncwarp();
     }
   }
 }
@@ -303,15 +343,19 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
 void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* Z0, const float* Z1,
                                const float* Z2, const float* wig, const float* env, const float* x_res, float* x_out,
                                int64_t N, int C, cudaStream_t s) {
-  rotate_scatter_fwd_kernel<8><<<grid_for(N, 8, 8), 256, 0, s>>>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out,
-                                                                 N, C);
+  const unsigned g = grid_for(N, 8, 2);
+  rotate_scatter_fwd_kernel<0><<<g, 256, 0, s>>>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
+  rotate_scatter_fwd_kernel<1><<<g, 256, 0, s>>>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
 }
 
 void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* Z0,
                                const float* Z1, const float* Z2, const float* wig, const float* env, float* gZ0,
                                float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, cudaStream_t s) {
-  rotate_scatter_bwd_kernel<4><<<grid_for(N, 4, 16), 128, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0,
-                                                                  gZ1, gZ2, g_wig, g_env, N, C);
+  const unsigned g = grid_for(N, 8, 2);
+  rotate_scatter_bwd_kernel<0><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
+                                                 g_env, N, C);
+  rotate_scatter_bwd_kernel<1><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
+                                                 g_env, N, C);
 }
 
 void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,

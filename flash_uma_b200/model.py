@@ -153,20 +153,37 @@ class ESCNInferenceModel(nn.Module):
         self.charge_start, self.charge_end = off_bb.charge_channel_start, off_bb.charge_channel_end
         self.spin_start, self.spin_end = off_bb.spin_channel_start, off_bb.spin_channel_end
 
+    # ---- stages (also driven one by one by the spatially partitioned model, partition.py) ----
+    def build_graph(self, idx_i, idx_j, N):
+        return build_graph_cached(idx_i, idx_j, N)
+
+    def geometry(self, pos, Z, idx_i, idx_j, shifts, graph):
+        return ops.precompute_geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt, self.offset_g,
+                                       self.coeff_g, self.cutoff, graph=graph)
+
+    def init_embedding(self, x_edge, wigner, env, Z, batch, csd_emb, idx_j, graph, N):
+        rad0 = self.rad_init(x_edge)
+        return ops.init_node_scatter(rad0, wigner, env, Z, batch, self.W_sphere, csd_emb, idx_j, graph.dst_row_ptr,
+                                     graph.dst_col, N)
+
+    def layer_forward(self, k, x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, charge=None, spin=None,
+                      natoms=None):
+        x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch)
+        if self.charge_end > self.charge_start:
+            x = balance_channels_batched(x, charge, natoms, batch, self.charge_start, self.charge_end, 0.0)
+        if self.spin_end > self.spin_start:
+            x = balance_channels_batched(x, spin, natoms, batch, self.spin_start, self.spin_end, 1.0)
+        return x
+
+    def final(self, x):
+        return self.final_norm(x)
+
     def forward(self, pos, Z, batch, edge_index, shifts, csd_emb, charge=None, spin=None, natoms=None):
         pos_s, Z_s, batch_s, ii, jj, perm, inv_perm = reorder_graph_morton(pos, Z, batch, edge_index[0], edge_index[1])
         N = pos_s.shape[0]
-        graph = build_graph_cached(ii, jj, N)
-        x_edge, wigner, env = ops.precompute_geometry(pos_s, Z_s, ii, jj, shifts, self.W_src, self.W_tgt,
-                                                      self.offset_g, self.coeff_g, self.cutoff, graph=graph)
-        rad0 = self.rad_init(x_edge)
-        x = ops.init_node_scatter(rad0, wigner, env, Z_s, batch_s, self.W_sphere, csd_emb, jj, graph.dst_row_ptr,
-                                  graph.dst_col, N)
-        for layer in self.layers:
-            x = layer(x, x_edge, wigner, env, ii, jj, graph, csd_emb, batch_s)
-            if self.charge_end > self.charge_start:
-                x = balance_channels_batched(x, charge, natoms, batch_s, self.charge_start, self.charge_end, 0.0)
-            if self.spin_end > self.spin_start:
-                x = balance_channels_batched(x, spin, natoms, batch_s, self.spin_start, self.spin_end, 1.0)
-        x = self.final_norm(x)
-        return x[inv_perm]
+        graph = self.build_graph(ii, jj, N)
+        x_edge, wigner, env = self.geometry(pos_s, Z_s, ii, jj, shifts, graph)
+        x = self.init_embedding(x_edge, wigner, env, Z_s, batch_s, csd_emb, jj, graph, N)
+        for k in range(len(self.layers)):
+            x = self.layer_forward(k, x, x_edge, wigner, env, ii, jj, graph, csd_emb, batch_s, charge, spin, natoms)
+        return self.final(x)[inv_perm]

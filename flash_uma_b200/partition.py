@@ -1,0 +1,175 @@
+"""Spatial domain decomposition of one periodic system over several GPUs (one process per GPU).
+
+The reference is single-GPU. Here rank r owns the atoms whose fractional coordinate along
+the longest cell axis lies in slab r, and the edges whose destination it owns (a
+destination's messages come only from its own edges, so the per-destination FP64 scatter
+sums are the single-GPU sums). Sources owned by other ranks are halo atoms: before every
+message-passing layer each rank receives their current node embeddings from the owners
+(one ``all_to_all_single``, NCCL over NVLink on GPUs), and in the backward pass the
+gradients of those halo copies travel back to the owners and are added there in a fixed
+peer order. Positions are replicated (every rank holds the global ``pos``); each rank's
+partial position gradient is summed across ranks with one all-reduce, as is the energy.
+
+Every rank builds every rank's plan from the same global neighbour list, so the edge sets
+are exactly a partition of the single-GPU list and no setup communication is needed.
+
+The driver works with any model object exposing the stage protocol ``build_graph``,
+``geometry``, ``init_embedding``, ``layer_forward``, ``final`` (the CUDA model
+:class:`~flash_uma_b200.model.ESCNInferenceModel`; the CPU tests drive the oracle through
+the same protocol over gloo).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def slab_owner(positions: np.ndarray, cell: np.ndarray, world: int, axis: int | None = None) -> tuple[np.ndarray, int]:
+    """Owner rank of every atom: slab of the wrapped fractional coordinate along ``axis``
+    (default: the cell direction with the largest distance between opposite faces)."""
+    cell = np.asarray(cell, dtype=np.float64)
+    if axis is None:
+        vol = abs(np.linalg.det(cell))
+        face = [vol / np.linalg.norm(np.cross(cell[(k + 1) % 3], cell[(k + 2) % 3])) for k in range(3)]
+        axis = int(np.argmax(face))
+    frac = np.asarray(positions, dtype=np.float64) @ np.linalg.inv(cell)
+    f = frac[:, axis] - np.floor(frac[:, axis])
+    return np.minimum((f * world).astype(np.int64), world - 1), axis
+
+
+@dataclass
+class PartitionPlan:
+    world: int
+    rank: int
+    axis: int
+    owner: np.ndarray           # [N] owner rank of every atom
+    owned: np.ndarray           # global ids owned here, ascending
+    halo: np.ndarray            # global ids of halo atoms, ordered by (owner, id)
+    edges: np.ndarray           # global ids of the edges handled here (destination owned), ascending
+    edge_index: np.ndarray      # [2, E_r] local indices (owned atoms first, then halo)
+    send_idx: list              # per peer: positions in ``owned`` to send (peer's halo order)
+    recv_counts: list           # per peer: number of halo atoms received from it
+
+    @property
+    def local_ids(self) -> np.ndarray:
+        return np.concatenate([self.owned, self.halo])
+
+
+def _halo_of(p: int, owner: np.ndarray, src: np.ndarray, dst: np.ndarray) -> np.ndarray:
+    sel = (owner[dst] == p) & (owner[src] != p)
+    h = np.unique(src[sel])
+    return h[np.lexsort((h, owner[h]))]
+
+
+def make_plan(positions, cell, edge_index, world: int, rank: int, axis: int | None = None) -> PartitionPlan:
+    """Deterministic plan of ``rank`` for the global ``edge_index`` [2, E] (row 0 source, row 1
+    destination); identical on every rank for the same inputs."""
+    edge_index = np.asarray(edge_index)
+    src, dst = edge_index[0], edge_index[1]
+    owner, axis = slab_owner(positions, cell, world, axis)
+    N = owner.shape[0]
+    owned = np.nonzero(owner == rank)[0]
+    edges = np.nonzero(owner[dst] == rank)[0]
+    halos = [_halo_of(p, owner, src, dst) for p in range(world)]
+    halo = halos[rank]
+    local = np.concatenate([owned, halo])
+    g2l = np.full(N, -1, dtype=np.int64)
+    g2l[local] = np.arange(local.shape[0])
+    ei = g2l[edge_index[:, edges]]
+    assert (ei >= 0).all()
+    pos_in_owned = np.full(N, -1, dtype=np.int64)
+    pos_in_owned[owned] = np.arange(owned.shape[0])
+    send_idx = []
+    for p in range(world):
+        hp = halos[p]
+        mine = hp[owner[hp] == rank] if p != rank else hp[:0]
+        send_idx.append(pos_in_owned[mine])
+    recv_counts = [int((owner[halo] == p).sum()) for p in range(world)]
+    return PartitionPlan(world, rank, axis, owner, owned, halo, edges, ei, send_idx, recv_counts)
+
+
+class HaloExchanger:
+    """Device-side copy of a plan's exchange lists for one process group."""
+
+    def __init__(self, plan: PartitionPlan, device, group=None):
+        self.group = group
+        self.send_idx = [torch.as_tensor(s, dtype=torch.long, device=device) for s in plan.send_idx]
+        self.send_cat = torch.cat(self.send_idx) if self.send_idx else torch.zeros(0, dtype=torch.long, device=device)
+        self.send_splits = [int(s.shape[0]) for s in plan.send_idx]
+        self.recv_splits = list(plan.recv_counts)
+        self.n_send = sum(self.send_splits)
+        self.n_halo = sum(self.recv_splits)
+
+
+class _HaloExchange(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_owned, ex: HaloExchanger):
+        send = x_owned.index_select(0, ex.send_cat).contiguous()
+        recv = x_owned.new_empty((ex.n_halo,) + tuple(x_owned.shape[1:]))
+        dist.all_to_all_single(recv, send, ex.recv_splits, ex.send_splits, group=ex.group)
+        ctx.ex, ctx.n_owned = ex, x_owned.shape[0]
+        return recv
+
+    @staticmethod
+    def backward(ctx, g_recv):
+        ex = ctx.ex
+        g_send = g_recv.new_empty((ex.n_send,) + tuple(g_recv.shape[1:]))
+        dist.all_to_all_single(g_send, g_recv.contiguous(), ex.send_splits, ex.recv_splits, group=ex.group)
+        g_owned = g_recv.new_zeros((ctx.n_owned,) + tuple(g_recv.shape[1:]))
+        off = 0
+        for idx, n in zip(ex.send_idx, ex.send_splits):   # fixed peer order; indices unique per peer
+            if n:
+                g_owned.index_add_(0, idx, g_send[off: off + n])
+                off += n
+        return g_owned, None
+
+
+def halo_exchange(x_owned: torch.Tensor, ex: HaloExchanger) -> torch.Tensor:
+    """Node features of this rank's halo atoms, fetched from their owners (differentiable)."""
+    return _HaloExchange.apply(x_owned, ex)
+
+
+class PartitionedModel:
+    """Runs a stage-protocol model on this rank's part of one periodic system."""
+
+    def __init__(self, model, plan: PartitionPlan, device, group=None):
+        self.model, self.plan, self.device, self.group = model, plan, device, group
+        self.n_owned = int(plan.owned.shape[0])
+        self.local_ids = torch.as_tensor(plan.local_ids, dtype=torch.long, device=device)
+        self.edges = torch.as_tensor(plan.edges, dtype=torch.long, device=device)
+        ei = torch.as_tensor(plan.edge_index, dtype=torch.long, device=device)
+        self.idx_i, self.idx_j = ei[0].contiguous(), ei[1].contiguous()
+        self.n_local = int(self.local_ids.shape[0])
+        self.ex = HaloExchanger(plan, device, group)
+        self.graph = model.build_graph(self.idx_i, self.idx_j, self.n_local)
+
+    def node_embedding(self, pos, Z, batch, cell_offsets, cell, csd_emb):
+        """Final node embedding of the owned atoms. ``pos``, ``Z``, ``batch`` are global [N];
+        ``cell_offsets`` is the global [E, 3]; ``cell`` is [3, 3]."""
+        m = self.model
+        pos_l = pos.index_select(0, self.local_ids)
+        Z_l = Z.index_select(0, self.local_ids)
+        b_l = batch.index_select(0, self.local_ids)
+        shifts = cell_offsets.index_select(0, self.edges).to(cell.dtype) @ cell
+        xe, wig, env = m.geometry(pos_l, Z_l, self.idx_i, self.idx_j, shifts, self.graph)
+        x = m.init_embedding(xe, wig, env, Z_l, b_l, csd_emb, self.idx_j, self.graph, self.n_local)
+        for k in range(len(m.layers)):
+            x_owned = x[: self.n_owned]
+            x = torch.cat([x_owned, halo_exchange(x_owned, self.ex)], 0)
+            x = m.layer_forward(k, x, xe, wig, env, self.idx_i, self.idx_j, self.graph, csd_emb, b_l)
+        return m.final(x[: self.n_owned])
+
+    def energy_forces(self, head, pos, Z, batch, cell_offsets, cell, csd_emb, num_systems: int = 1):
+        """Global energy [num_systems] and forces [N, 3], identical on every rank."""
+        pos = pos.detach().requires_grad_(True)
+        x = self.node_embedding(pos, Z, batch, cell_offsets, cell, csd_emb)
+        b_owned = batch.index_select(0, self.local_ids[: self.n_owned])
+        e_local = head(x, b_owned, num_systems)
+        (g,) = torch.autograd.grad(e_local.sum(), [pos])
+        energy = e_local.detach().clone()
+        dist.all_reduce(energy, group=self.group)
+        dist.all_reduce(g, group=self.group)
+        return energy, -g

@@ -132,24 +132,42 @@ class OracleBackbone:
             return F.silu(bb.mix_csd(torch.cat((chg, sp, bb.dataset_embedding(dataset)), dim=1)))
         return F.silu(bb.mix_csd(torch.cat((chg, sp), dim=1)))
 
+    # ---- stages (the same protocol as the CUDA model; used by the partitioned driver) ----
+    def build_graph(self, idx_i, idx_j, N):
+        row_ptr, col_idx = build_csr(idx_j, N)
+        return (row_ptr, col_idx)
+
+    def geometry(self, pos, Z, idx_i, idx_j, shifts, graph):
+        return ops.precompute_geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt, self.offset_g,
+                                       self.coeff_g, self.cutoff)
+
+    def init_embedding(self, x_edge, wigner, env, Z, batch, csd_emb, idx_j, graph, N):
+        rad0 = self.rad_init(x_edge)
+        return ops.init_node_scatter(rad0, wigner, env, Z, batch, self.W_sphere, csd_emb, idx_j, graph[0], graph[1], N)
+
+    def layer_forward(self, k, x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, charge=None, spin=None,
+                      natoms=None):
+        from flash_uma_b200.nodewise import balance_channels_batched
+        x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph[0], graph[1], csd_emb, batch)
+        if self.charge_range[1] > self.charge_range[0]:
+            x = balance_channels_batched(x, charge, natoms, batch, *self.charge_range, target_offset=0.0)
+        if self.spin_range[1] > self.spin_range[0]:
+            x = balance_channels_batched(x, spin, natoms, batch, *self.spin_range, target_offset=1.0)
+        return x
+
+    def final(self, x):
+        return self.final_norm(x)
+
     def model_forward(self, pos, Z, batch, edge_index, shifts, csd_emb, charge=None, spin=None, natoms=None):
         """``model.py:187-221``."""
-        from flash_uma_b200.nodewise import balance_channels_batched
         pos_s, Z_s, batch_s, ii, jj, perm, inv_perm = reorder_graph_morton(pos, Z, batch, edge_index[0], edge_index[1])
         N = pos_s.shape[0]
-        row_ptr, col_idx = build_csr(jj, N)
-        x_edge, wigner, env = ops.precompute_geometry(pos_s, Z_s, ii, jj, shifts, self.W_src, self.W_tgt,
-                                                      self.offset_g, self.coeff_g, self.cutoff)
-        rad0 = self.rad_init(x_edge)
-        x = ops.init_node_scatter(rad0, wigner, env, Z_s, batch_s, self.W_sphere, csd_emb, jj, row_ptr, col_idx, N)
-        for layer in self.layers:
-            x = layer(x, x_edge, wigner, env, ii, jj, row_ptr, col_idx, csd_emb, batch_s)
-            if self.charge_range[1] > self.charge_range[0]:
-                x = balance_channels_batched(x, charge, natoms, batch_s, *self.charge_range, target_offset=0.0)
-            if self.spin_range[1] > self.spin_range[0]:
-                x = balance_channels_batched(x, spin, natoms, batch_s, *self.spin_range, target_offset=1.0)
-        x = self.final_norm(x)
-        return x[inv_perm]
+        graph = self.build_graph(ii, jj, N)
+        x_edge, wigner, env = self.geometry(pos_s, Z_s, ii, jj, shifts, graph)
+        x = self.init_embedding(x_edge, wigner, env, Z_s, batch_s, csd_emb, jj, graph, N)
+        for k in range(len(self.layers)):
+            x = self.layer_forward(k, x, x_edge, wigner, env, ii, jj, graph, csd_emb, batch_s, charge, spin, natoms)
+        return self.final(x)[inv_perm]
 
     def forward(self, data):
         """``wrapper.py:171-211``: enables pos/cell grads, builds csd embedding and shifts."""
