@@ -1,6 +1,6 @@
 """Benchmark: energy + forces throughput (atom-steps/s) of the uma-s-shaped model on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flash|reference] [--tf32]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flash|reference] [--gemm f16x3|tf32x3|tf32]
 
 Workload: bulk fcc Cu 10x10x10 conventional supercell, 4,000
 atoms, displacements N(0, 0.05 A), cutoff 6 A, <= 30 neighbours (120,000 edges), random
@@ -80,16 +80,31 @@ def gemm_flops_per_step(E, C, B, L, H=None):
     return 2 * fwd
 
 
-def gemm_summary(per_op, E, C, B, L, tf32):
+GEMM_OPS = ("fuma_linear_f16x3", "fuma_linear")
+
+
+def gemm_mode(mode, bf16):
+    """Tensor-pipe products per fp32 product, the pipe's peak (TF/s) and labels of a GEMM mode."""
+    if mode == "f16x3":
+        return {"passes": 3, "peak": bf16, "pipe": "fp16", "op": "fuma_linear_f16x3",
+                "kernel": "fuma_linear_f16x3 (gemm_f16x3_kernel)", "label": "tcgen05 f16x3 (fp16 split, fp32-level)",
+                "peak_note": "dense fp16 = measured dense bf16 rate"}
+    return {"passes": 3 if mode == "tf32x3" else 1, "peak": bf16 / 2, "pipe": "tf32", "op": "fuma_linear",
+            "kernel": "fuma_linear (gemm_tf32_kernel)",
+            "label": "tcgen05 3xTF32 (fp32-level)" if mode == "tf32x3" else "tcgen05 TF32 (single pass)",
+            "peak_note": "dense TF32 taken as half the measured dense bf16 rate"}
+
+
+def gemm_summary(per_op, E, C, B, L, mode):
     """Dense-contraction share of one step (from the probe pass): fp32-equivalent FLOP rate and the
-    tensor-pipe rate (3 TF32 products per fp32 product in the 3xTF32 mode)."""
-    ms = per_op.get("fuma_linear")
+    tensor-pipe rate (3 products per fp32 product in the split modes)."""
+    g = gemm_mode(mode, 0.0)
+    ms = per_op.get(g["op"])
     if not ms:
         return None
     flops = gemm_flops_per_step(E, C, B, L)
-    passes = 1 if tf32 else 3
     return {"flops_per_step": flops, "ms_per_step": ms, "tflops_fp32_equiv": flops / (ms * 1e-3) / 1e12,
-            "tflops_tf32_pipe": passes * flops / (ms * 1e-3) / 1e12, "tf32_passes": passes}
+            "tflops_pipe": g["passes"] * flops / (ms * 1e-3) / 1e12, "pipe": g["pipe"], "passes": g["passes"]}
 
 
 def load_peaks():
@@ -147,7 +162,7 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def build_problem(device, tf32: bool, system=None):
+def build_problem(device, gemm: str, system=None):
     from flash_uma_b200.predict import Predictor
     from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
     from flash_uma_b200.systems import config3_system, to_graph
@@ -156,7 +171,7 @@ def build_problem(device, tf32: bool, system=None):
     data = to_graph([system])
     off = SyntheticESCNMDBackbone(seed=0).to(device)
     head = make_energy_head(128, 128, seed=1).to(device)
-    pred = Predictor(ZeroAllocBackbone(off, gemm="tf32" if tf32 else "tf32x3"), head)
+    pred = Predictor(ZeroAllocBackbone(off, gemm=gemm), head)
     return system, data, pred
 
 
@@ -166,7 +181,7 @@ def md_positions(pos0: torch.Tensor, count: int, seed: int = 0):
     return [pos0 + 0.01 * torch.randn(pos0.shape, generator=g) for _ in range(count)]
 
 
-def build_partitioned(device, tf32: bool, world: int, rank: int):
+def build_partitioned(device, gemm: str, world: int, rank: int):
     """Weak-scaling workload for N > 1 GPUs: bulk fcc Cu 10 x 10 x (10 N) (4,000 atoms per GPU,
     so N = 1 is exactly config 3), split into N slabs along the long axis with a per-layer halo
     exchange of node embeddings over NCCL (flash_uma_b200.partition)."""
@@ -178,7 +193,7 @@ def build_partitioned(device, tf32: bool, world: int, rank: int):
     data = to_graph([system])
     off = SyntheticESCNMDBackbone(seed=0).to(device)
     head = make_energy_head(128, 128, seed=1).to(device)
-    bb = ZeroAllocBackbone(off, gemm="tf32" if tf32 else "tf32x3")
+    bb = ZeroAllocBackbone(off, gemm=gemm)
     plan = make_plan(system.positions, system.cell, data.edge_index.numpy(), world, rank)
     pm = PartitionedModel(bb.ce, plan, device)
     d = data.to(device)
@@ -198,12 +213,12 @@ def run_flash(args, rank, world, device):
     K, W = args.steps, args.warmup
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     if world > 1:
-        system, data_cpu, step, plan = build_partitioned(device, args.tf32, world, rank)
+        system, data_cpu, step, plan = build_partitioned(device, args.gemm, world, rank)
         N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
         pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=0)]
     else:
         plan = None
-        system, data_cpu, pred = build_problem(device, args.tf32)
+        system, data_cpu, pred = build_problem(device, args.gemm)
         N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
         data = data_cpu.to(device)
         pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=rank)]
@@ -287,15 +302,15 @@ def run_flash(args, rank, world, device):
     avg_ms = sum(dom_ms) / max(1, len(dom_ms))
     # per-launch sizes: this rank's local graph
     Ek, Nk = (len(plan.edges), len(plan.local_ids)) if world > 1 else (E, N)
-    if dominant == "fuma_linear":
-        # tensor-bound: TF32-pipe FLOPs per launch (3 products per fp32 product in 3xTF32)
-        passes = 1 if args.tf32 else 3
+    gm = gemm_mode(args.gemm, bf16)
+    if dominant in GEMM_OPS:
+        # tensor-bound: tensor-pipe FLOPs per launch (3 products per fp32 product in the split modes)
         launches = probe.counts.get(dominant, 1) // K
-        flops_launch = passes * gemm_flops_per_step(Ek, C, B, L) / max(1, launches)
+        flops_launch = gm["passes"] * gemm_flops_per_step(Ek, C, B, L) / max(1, launches)
         achieved = flops_launch / (avg_ms * 1e-3) / 1e12
-        roof = {"kernel": "fuma_linear (gemm_tf32_kernel)", "bound": "tensor", "achieved": achieved,
-                "peak": bf16 / 2, "unit": "TFLOP/s", "frac": achieved / (bf16 / 2),
-                "peak_kind": f"{peak_kind} dense bf16 / 2 (TF32 rate; TF32 not measured separately)",
+        roof = {"kernel": gm["kernel"], "bound": "tensor", "achieved": achieved,
+                "peak": gm["peak"], "unit": "TFLOP/s", "frac": achieved / gm["peak"],
+                "peak_kind": f"{peak_kind}: {gm['peak_note']}",
                 "traffic": None, "alg_flops_per_launch": flops_launch}
     else:
         nbytes = alg_bytes(dominant, Nk, Ek, C, B, M_rows=Ek, D=128)
@@ -306,7 +321,7 @@ def run_flash(args, rank, world, device):
     roof.update(avg_launch_ms=avg_ms, launches_timed=len(dom_ms),
                 share_of_step=(sum(dom_ms) / total_ms) if world == 1 else None)
     # the top HBM-bound kernel as well (device time from the probe pass)
-    mem_ops = {k: v for k, v in per_op.items() if k != "fuma_linear" and alg_bytes(k, Nk, Ek, C, B, Ek, 128)}
+    mem_ops = {k: v for k, v in per_op.items() if k not in GEMM_OPS and alg_bytes(k, Nk, Ek, C, B, Ek, 128)}
     top_mem = max(mem_ops, key=mem_ops.get) if mem_ops else None
     roof_mem = None
     if top_mem:
@@ -327,7 +342,7 @@ def run_flash(args, rank, world, device):
                                 f"scaling of config 3), E+F per step, slab decomposition with per-layer halo "
                                 f"exchange (NCCL)"),
                    "atoms": N, "edges": E, "sphere_channels": C, "layers": L, "num_distance_basis": B,
-                   "cutoff": 6.0, "max_neighbors": 30, "gemm": "tcgen05 TF32 (single pass)" if args.tf32 else "tcgen05 3xTF32 (fp32-level)",
+                   "cutoff": 6.0, "max_neighbors": 30, "gemm": gm["label"],
                    "l2": "flushed (256 MB write) before every step, outside the timed events",
                    "parallelism": f"spatial slabs x{world} (halo atoms per rank: {len(plan.halo)} on rank 0)"
                    if world > 1 else "single GPU"},
@@ -335,7 +350,7 @@ def run_flash(args, rank, world, device):
                 "d2h_bytes_per_step": N * 3 * 4 + 4},
         "roofline": roof,
         "roofline_top_hbm_kernel": roof_mem,
-        "gemm": gemm_summary(per_op, Ek, C, B, L, args.tf32),
+        "gemm": gemm_summary(per_op, Ek, C, B, L, args.gemm),
         "gpu_launches": gpu_launches,
         "per_kernel_ms_one_step": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
         "clocks": clocks,
@@ -357,7 +372,7 @@ def run_micro(args, device):
     N, E, C, B = args.nodes, args.edges, 128, 64
     inp = microbench_layer_inputs(N=N, E=E, C=C, seed=0)
     off = SyntheticESCNMDBackbone(num_layers=1, seed=0).to(device)
-    layer = PackedLayer(off.blocks[0], C, "tf32" if args.tf32 else None).to(device)
+    layer = PackedLayer(off.blocks[0], C, args.gemm).to(device)
     ii, jj = inp["idx_i"].to(device), inp["idx_j"].to(device)
     graph = ops.build_graph_csr(ii, jj, N)
     Z = torch.full((N,), 29, dtype=torch.long, device=device)
@@ -408,19 +423,19 @@ def run_micro(args, device):
             gbs = nb * launches / (per_step * 1e-3) / 1e9
             entry.update(alg_bytes_per_launch=nb, achieved_gbs=gbs, frac_hbm=gbs / hbm)
         kernels[name] = entry
-    if "fuma_linear" in kernels:
+    gm = gemm_mode(args.gemm, bf16)
+    if gm["op"] in kernels:
         H = C
         so2 = 2 * 70 * C * C + 2 * 29 * C * C
         rad = 2 * ((B + 2 * C) * H + H * H + H * 12 * C)
         flops = 2 * E * (so2 + rad)
-        passes = 1 if args.tf32 else 3
-        ms = kernels["fuma_linear"]["ms_per_step"]
-        tf = passes * flops / (ms * 1e-3) / 1e12
-        kernels["fuma_linear"].update(flops_per_step=flops, tf32_passes=passes, tflops_tf32_pipe=tf,
-                                      frac_tf32_peak=tf / (bf16 / 2))
+        ms = kernels[gm["op"]]["ms_per_step"]
+        tf = gm["passes"] * flops / (ms * 1e-3) / 1e12
+        kernels[gm["op"]].update(flops_per_step=flops, passes=gm["passes"], pipe=gm["pipe"], tflops_pipe=tf,
+                                 frac_pipe_peak=tf / gm["peak"])
     print(json.dumps({"metric": "one message-passing layer fwd+bwd (BASELINE config 2)", "nodes": N, "edges": E,
-                      "ms_per_layer": total, "peaks": {"hbm_gbs": hbm, "tf32_tflops": bf16 / 2, "kind": kind,
-                                                        "tf32_note": "dense TF32 taken as half the measured bf16 rate"},
+                      "ms_per_layer": total, "gemm": gm["label"],
+                      "peaks": {"hbm_gbs": hbm, "pipe_tflops": gm["peak"], "kind": kind, "note": gm["peak_note"]},
                       "kernels": dict(sorted(kernels.items(), key=lambda kv: -kv[1]["ms_per_step"]))}), flush=True)
 
 
@@ -479,19 +494,62 @@ def run_reference(args):
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def summarize_launches(path):
+    """Kernels between the first two L2-flush fills of an ncu launch list of ``bench.py --steps 1``
+    (the one timed step of the device-resident region), grouped by kernel: launches, total
+    device time, share. ncu serialises launches and runs them with cold caches, so the shares
+    are what compares with the bench, not the absolute times."""
+    import collections
+    import csv
+    rows = list(csv.reader(open(path)))
+    hi = next(i for i, r in enumerate(rows) if "Kernel Name" in r)
+    h = rows[hi]
+    ki, vi, ui = h.index("Kernel Name"), h.index("Metric Value"), h.index("Metric Unit")
+    seq = []
+    for r in rows[hi + 1:]:
+        if len(r) <= vi:
+            continue
+        v = float(r[vi].replace(",", ""))
+        unit = r[ui]
+        v = v / 1e3 if unit.startswith("n") else v * 1e3 if unit.startswith("m") else v   # -> microseconds
+        seq.append((r[ki], v))
+    flush = [i for i, (n, v) in enumerate(seq) if "FillFunctor" in n and v > 20.0]
+    a, b = flush[0] + 1, flush[1]
+    tot, cnt = collections.defaultdict(float), collections.Counter()
+    for n, v in seq[a:b]:
+        k = n.split("(")[0].replace("void ", "")
+        k = k if len(k) < 80 else k[:77] + "..."
+        tot[k] += v
+        cnt[k] += 1
+    T = sum(tot.values())
+    own = sum(v for k, v in tot.items() if k.startswith("fuma::"))
+    print(f"one timed step: {b - a} launches, {T / 1e3:.2f} ms of kernel time (serialised, cold caches); "
+          f"this library's kernels {100 * own / T:.1f}%, others {100 * (T - own) / T:.1f}%")
+    print(f"{'ms':>9} {'share':>6} {'n':>4}  kernel")
+    for k, v in sorted(tot.items(), key=lambda kv: -kv[1]):
+        print(f"{v / 1e3:9.3f} {100 * v / T:5.1f}% {cnt[k]:4d}  {k}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="flash", choices=["flash", "reference"])
-    ap.add_argument("--tf32", action="store_true",
-                    help="single-pass TF32 dense contractions (the reference's published setup) instead of 3xTF32")
+    ap.add_argument("--gemm", default="f16x3", choices=["f16x3", "tf32x3", "tf32"],
+                    help="dense-contraction mode: f16x3 / tf32x3 (fp32-level) or tf32 (single pass, the "
+                         "reference's published setup)")
+    ap.add_argument("--summarize-launches", metavar="CSV",
+                    help="print the per-kernel table of one timed step from an ncu launch list "
+                         "(--metrics gpu__time_duration.sum --csv of 'bench.py --steps 1') and exit")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", action="store_true", help="one-layer kernel microbench (BASELINE config 2)")
     ap.add_argument("--nodes", type=int, default=20000)
     ap.add_argument("--edges", type=int, default=600000)
     args = ap.parse_args()
+    if args.summarize_launches:
+        summarize_launches(args.summarize_launches)
+        return
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -36,6 +36,9 @@ _SIGS = {
     "fuma_init_scatter_bwd": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P, _P],
     "fuma_linear": [_P, _I64, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _P],
     "fuma_split_tf32": [_P, _I64, _P, _P, _P],
+    "fuma_linear_f16x3": [_P, _I64, _I32, _P, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _P, _P],
+    "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
+    "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
     "fuma_gather_bwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P,
                                 _P],
 }
@@ -85,11 +88,19 @@ def stream_of(t: torch.Tensor) -> int:
 
 
 # kernels each entry point launches (used by launch accounting)
+# variants writing the GEMM-input outputs in the row-packed f16x3 split layout: same arguments
+# plus an error flag before the stream
+for _name in ("fuma_ln_silu_fwd", "fuma_ln_silu_bwd", "fuma_gather_fwd", "fuma_gather_bwd", "fuma_gating_fwd",
+              "fuma_gating_bwd", "fuma_rotate_scatter_bwd", "fuma_init_scatter_bwd"):
+    _SIGS[_name + "_f16x3"] = _SIGS[_name][:-1] + [_P, _P]
+
 KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3
 KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2
 KERNELS_PER_CALL["fuma_gather_bwd_noalloc"] = 3
+KERNELS_PER_CALL["fuma_gather_bwd_f16x3"] = 3
+KERNELS_PER_CALL["fuma_rotate_scatter_bwd_f16x3"] = 2
 
 
 class LaunchProbe:

@@ -125,31 +125,54 @@ int fuma_edge_vec_to_nodes(const int32_t* src_row_ptr, const int32_t* src_col, c
   return launched("edge_vec_to_nodes");
 }
 
-int fuma_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
-                     float* out, float* mean, float* rstd, void* stream) {
+static int ln_silu_fwd_impl(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
+                     float* out, float* mean, float* rstd, bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || D % 8 == 0, "ln_silu_fwd_f16x3: the split output needs D %% 8 == 0");
   REQUIRE(M >= 0 && D > 0 && (D & 3) == 0 && D <= 2048, "ln_silu_fwd: D=%d must be a multiple of 4, <= 2048", D);
   if (M == 0) return FUMA_OK;
   REQUIRE(x && gamma && beta && out && mean && rstd, "ln_silu_fwd: null pointer");
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(out, "out"); REQUIRE_ALIGNED(gamma, "gamma"); REQUIRE_ALIGNED(beta, "beta");
   BIND(x);
-  launch_ln_silu_fwd(x, gamma, beta, out, mean, rstd, M, D, eps, (cudaStream_t)stream);
+  launch_ln_silu_fwd(x, gamma, beta, out, mean, rstd, M, D, eps, split, err_flag, (cudaStream_t)stream);
   return launched("ln_silu_fwd");
 }
 
-int fuma_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
-                     const float* g_out, int64_t M, int32_t D, float* g_x, void* stream) {
+int fuma_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
+                     float* out, float* mean, float* rstd, void* stream) {
+  return ln_silu_fwd_impl(x, gamma, beta, eps, M, D, out, mean, rstd, false, nullptr, stream);
+}
+
+int fuma_ln_silu_fwd_f16x3(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
+                     float* out, float* mean, float* rstd, int* err_flag, void* stream) {
+  return ln_silu_fwd_impl(x, gamma, beta, eps, M, D, out, mean, rstd, true, err_flag, stream);
+}
+
+static int ln_silu_bwd_impl(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
+                     const float* g_out, int64_t M, int32_t D, float* g_x, bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || D % 8 == 0, "ln_silu_bwd_f16x3: the split output needs D %% 8 == 0");
   REQUIRE(M >= 0 && D > 0 && (D & 3) == 0 && D <= 2048, "ln_silu_bwd: D=%d must be a multiple of 4, <= 2048", D);
   if (M == 0) return FUMA_OK;
   REQUIRE(x && gamma && beta && mean && rstd && g_out && g_x, "ln_silu_bwd: null pointer");
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(g_x, "g_x");
   BIND(x);
-  launch_ln_silu_bwd(x, gamma, beta, mean, rstd, g_out, g_x, M, D, (cudaStream_t)stream);
+  launch_ln_silu_bwd(x, gamma, beta, mean, rstd, g_out, g_x, M, D, split, err_flag, (cudaStream_t)stream);
   return launched("ln_silu_bwd");
 }
 
-int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
+int fuma_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
+                     const float* g_out, int64_t M, int32_t D, float* g_x, void* stream) {
+  return ln_silu_bwd_impl(x, gamma, beta, mean, rstd, g_out, M, D, g_x, false, nullptr, stream);
+}
+
+int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
+                     const float* g_out, int64_t M, int32_t D, float* g_x, int* err_flag, void* stream) {
+  return ln_silu_bwd_impl(x, gamma, beta, mean, rstd, g_out, M, D, g_x, true, err_flag, stream);
+}
+
+static int gather_fwd_impl(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                     const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
-                    float* X_m0, float* X_m1, float* X_m2, void* stream) {
+                    float* X_m0, float* X_m1, float* X_m2, bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || C % 8 == 0, "gather_fwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "gather_fwd: bad sizes");
   if (E == 0) return FUMA_OK;
@@ -157,16 +180,29 @@ int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, 
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(csd, "csd");
   REQUIRE_ALIGNED(X_m0, "X_m0"); REQUIRE_ALIGNED(X_m1, "X_m1"); REQUIRE_ALIGNED(X_m2, "X_m2");
   BIND(x);
-  launch_gather_fwd(x, idx_i, idx_j, wigner, rad, csd, batch, X_m0, X_m1, X_m2, E, C, (cudaStream_t)stream);
+  launch_gather_fwd(x, idx_i, idx_j, wigner, rad, csd, batch, X_m0, X_m1, X_m2, E, C, split, err_flag, (cudaStream_t)stream);
   return launched("gather_fwd");
 }
 
-int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
+int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
+                    const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
+                    float* X_m0, float* X_m1, float* X_m2, void* stream) {
+  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, false, nullptr, stream);
+}
+
+int fuma_gather_fwd_f16x3(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
+                    const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
+                    float* X_m0, float* X_m1, float* X_m2, int* err_flag, void* stream) {
+  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, true, err_flag, stream);
+}
+
+static int gather_bwd_impl(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
                     const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
                     const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
                     const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
                     float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
-                    void* stream) {
+                    bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || C % 8 == 0, "gather_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "gather_bwd: bad sizes");
   if (N == 0) return FUMA_OK;
@@ -182,12 +218,33 @@ int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m
   }
   BIND(x);
   launch_gather_bwd(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
-                    src_col, g_x, g_wigner, g_rad, scratch, N, C, (cudaStream_t)stream);
+                    src_col, g_x, g_wigner, g_rad, scratch, N, C, split, err_flag, (cudaStream_t)stream);
   return launched("gather_bwd");
 }
 
-int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
-                    float* Z_m1, float* Z_m2, void* stream) {
+int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
+                    const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
+                    const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
+                    const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
+                    float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
+                    void* stream) {
+  return gather_bwd_impl(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
+                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, false, nullptr, stream);
+}
+
+int fuma_gather_bwd_f16x3(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
+                    const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
+                    const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
+                    const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
+                    float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
+                    int* err_flag, void* stream) {
+  return gather_bwd_impl(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
+                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, true, err_flag, stream);
+}
+
+static int gating_fwd_impl(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
+                    float* Z_m1, float* Z_m2, bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || C % 8 == 0, "gating_fwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(E >= 0, "gating_fwd: bad E");
   if (E == 0) return FUMA_OK;
@@ -195,13 +252,24 @@ int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int
   REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
   REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1"); REQUIRE_ALIGNED(Z_m2, "Z_m2");
   BIND(Y_m0);
-  launch_gating_fwd(Y_m0, Y_m1, Y_m2, Z_m0, Z_m1, Z_m2, E, C, (cudaStream_t)stream);
+  launch_gating_fwd(Y_m0, Y_m1, Y_m2, Z_m0, Z_m1, Z_m2, E, C, split, err_flag, (cudaStream_t)stream);
   return launched("gating_fwd");
 }
 
-int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
+int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
+                    float* Z_m1, float* Z_m2, void* stream) {
+  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, false, nullptr, stream);
+}
+
+int fuma_gating_fwd_f16x3(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
+                    float* Z_m1, float* Z_m2, int* err_flag, void* stream) {
+  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, true, err_flag, stream);
+}
+
+static int gating_bwd_impl(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                     const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
-                    float* g_Y_m2, void* stream) {
+                    float* g_Y_m2, bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || C % 8 == 0, "gating_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(E >= 0, "gating_bwd: bad E");
   if (E == 0) return FUMA_OK;
@@ -210,8 +278,20 @@ int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m
   REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
   REQUIRE_ALIGNED(g_Y_m0, "g_Y_m0"); REQUIRE_ALIGNED(g_Y_m1, "g_Y_m1"); REQUIRE_ALIGNED(g_Y_m2, "g_Y_m2");
   BIND(Y_m0);
-  launch_gating_bwd(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, g_Y_m0, g_Y_m1, g_Y_m2, E, C, (cudaStream_t)stream);
+  launch_gating_bwd(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, g_Y_m0, g_Y_m1, g_Y_m2, E, C, split, err_flag, (cudaStream_t)stream);
   return launched("gating_bwd");
+}
+
+int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
+                    const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
+                    float* g_Y_m2, void* stream) {
+  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, false, nullptr, stream);
+}
+
+int fuma_gating_bwd_f16x3(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
+                    const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
+                    float* g_Y_m2, int* err_flag, void* stream) {
+  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, true, err_flag, stream);
 }
 
 int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
@@ -229,10 +309,11 @@ int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z
   return launched("rotate_scatter_fwd");
 }
 
-int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
+static int rotate_scatter_bwd_impl(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
                             const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
                             int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
-                            float* g_wigner, float* g_env, void* stream) {
+                            float* g_wigner, float* g_env, bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || C % 8 == 0, "rotate_scatter_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "rotate_scatter_bwd: bad sizes");
   if (E == 0 || N == 0) return FUMA_OK;
@@ -244,8 +325,24 @@ int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* 
   REQUIRE_ALIGNED(g_Z_m2, "g_Z_m2");
   BIND(g_out);
   launch_rotate_scatter_bwd(row_ptr, col_idx, g_out, Z_m0, Z_m1, Z_m2, wigner, env, g_Z_m0, g_Z_m1, g_Z_m2, g_wigner,
-                            g_env, N, C, (cudaStream_t)stream);
+                            g_env, N, C, split, err_flag, (cudaStream_t)stream);
   return launched("rotate_scatter_bwd");
+}
+
+int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
+                            const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
+                            int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
+                            float* g_wigner, float* g_env, void* stream) {
+  return rotate_scatter_bwd_impl(g_out, Z_m0, Z_m1, Z_m2, wigner, env, row_ptr, col_idx, N, E, C, g_Z_m0, g_Z_m1,
+                                 g_Z_m2, g_wigner, g_env, false, nullptr, stream);
+}
+
+int fuma_rotate_scatter_bwd_f16x3(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
+                            const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
+                            int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
+                            float* g_wigner, float* g_env, int* err_flag, void* stream) {
+  return rotate_scatter_bwd_impl(g_out, Z_m0, Z_m1, Z_m2, wigner, env, row_ptr, col_idx, N, E, C, g_Z_m0, g_Z_m1,
+                                 g_Z_m2, g_wigner, g_env, true, err_flag, stream);
 }
 
 int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* env, const int64_t* Z,
@@ -264,9 +361,10 @@ int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* en
   return launched("init_scatter_fwd");
 }
 
-int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wigner, const float* env,
+static int init_scatter_bwd_impl(const float* g_out, const float* rad, const float* wigner, const float* env,
                           const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
-                          float* g_rad, float* g_wigner, float* g_env, void* stream) {
+                          float* g_rad, float* g_wigner, float* g_env, bool split, int* err_flag, void* stream) {
+  REQUIRE(!split || C % 8 == 0, "init_scatter_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "init_scatter_bwd: bad sizes");
   if (E == 0 || N == 0) return FUMA_OK;
@@ -275,8 +373,22 @@ int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wig
   REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(g_rad, "g_rad");
   BIND(g_out);
   launch_init_scatter_bwd(row_ptr, col_idx, g_out, rad, wigner, env, g_rad, g_wigner, g_env, N, C,
-                          (cudaStream_t)stream);
+                          split, err_flag, (cudaStream_t)stream);
   return launched("init_scatter_bwd");
+}
+
+int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wigner, const float* env,
+                          const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
+                          float* g_rad, float* g_wigner, float* g_env, void* stream) {
+  return init_scatter_bwd_impl(g_out, rad, wigner, env, row_ptr, col_idx, N, E, C, g_rad, g_wigner, g_env, false,
+                               nullptr, stream);
+}
+
+int fuma_init_scatter_bwd_f16x3(const float* g_out, const float* rad, const float* wigner, const float* env,
+                          const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
+                          float* g_rad, float* g_wigner, float* g_env, int* err_flag, void* stream) {
+  return init_scatter_bwd_impl(g_out, rad, wigner, env, row_ptr, col_idx, N, E, C, g_rad, g_wigner, g_env, true,
+                               err_flag, stream);
 }
 
 int fuma_linear(const float* A, int64_t lda, const float* W_hi, const float* W_lo, const float* bias, int64_t M,
@@ -305,6 +417,51 @@ int fuma_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* strea
   BIND(x);
   launch_split_tf32(x, hi, lo, n, (cudaStream_t)stream);
   return launched("split_tf32");
+}
+
+int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* W_hi, const void* W_lo, int64_t ldw,
+                      float w_scale_inv, const float* bias, int64_t M, int32_t N, int32_t K, float* C, int64_t ldc,
+                      int* err_flag, void* stream) {
+  REQUIRE(M >= 0 && M < (int64_t(1) << 31), "linear_f16x3: M=%lld out of range", (long long)M);
+  REQUIRE(N > 0 && N % 16 == 0 && N <= 65536 * 16, "linear_f16x3: N=%d must be a positive multiple of 16", N);
+  REQUIRE(K > 0 && K % 4 == 0, "linear_f16x3: K=%d must be a positive multiple of 4", K);
+  REQUIRE(lda >= K && lda % 4 == 0 && ldc >= N && ldc % 4 == 0, "linear_f16x3: bad leading dimensions of A or C");
+  REQUIRE(!a_split || lda % 8 == 0, "linear_f16x3: a row-packed split A needs lda %% 8 == 0 (lda=%lld)",
+          (long long)lda);
+  REQUIRE(ldw >= K && ldw % 8 == 0, "linear_f16x3: ldw=%lld must be >= K and a multiple of 8", (long long)ldw);
+  REQUIRE(w_scale_inv > 0.0f, "linear_f16x3: w_scale_inv must be positive");
+  if (M == 0) return FUMA_OK;
+  REQUIRE(A && W_hi && W_lo && C, "linear_f16x3: null pointer");
+  REQUIRE_ALIGNED(A, "A"); REQUIRE_ALIGNED(W_hi, "W_hi"); REQUIRE_ALIGNED(W_lo, "W_lo"); REQUIRE_ALIGNED(C, "C");
+  if (bias) REQUIRE_ALIGNED(bias, "bias");
+  BIND(A);
+  const int r = launch_gemm_f16x3(A, lda, a_split != 0, W_hi, W_lo, ldw, w_scale_inv, bias, C, ldc, M, N, K, err_flag,
+                                  (cudaStream_t)stream);
+  if (r == -1) return fail(FUMA_E_INVALID, "linear_f16x3: could not encode the TMA tensor maps: %s", gemm_map_error());
+  if (r != 0) return fail(r, "linear_f16x3: launch failed: %s", cudaGetErrorString((cudaError_t)r));
+  return launched("linear_f16x3");
+}
+
+int fuma_split_rows_f16(const float* x, int64_t lda, int64_t M, int32_t K, void* out, int64_t ldp, int* err_flag,
+                        void* stream) {
+  REQUIRE(M >= 0 && K > 0 && K % 4 == 0, "split_rows_f16: bad shape M=%lld K=%d", (long long)M, K);
+  REQUIRE(lda >= K && lda % 4 == 0 && ldp >= K && ldp % 8 == 0, "split_rows_f16: bad leading dimensions");
+  if (M == 0) return FUMA_OK;
+  REQUIRE(x && out, "split_rows_f16: null pointer");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(out, "out");
+  BIND(x);
+  launch_split_rows_f16(x, lda, M, K, out, ldp, err_flag, (cudaStream_t)stream);
+  return launched("split_rows_f16");
+}
+
+int fuma_split_f16(const float* x, int64_t n, float scale, void* hi, void* lo, void* stream) {
+  REQUIRE(n >= 0, "split_f16: bad n");
+  REQUIRE(scale > 0.0f, "split_f16: scale must be positive");
+  if (n == 0) return FUMA_OK;
+  REQUIRE(x && hi && lo, "split_f16: null pointer");
+  BIND(x);
+  launch_split_f16(x, hi, lo, scale, n, (cudaStream_t)stream);
+  return launched("split_f16");
 }
 
 }  // extern "C"

@@ -1,7 +1,9 @@
 // Shared device helpers for the flash_uma_b200 kernels (sm_100a).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 namespace fuma {
 
@@ -47,6 +49,54 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// ---- f16x3 split operands -------------------------------------------------------------------
+// The fp16 tensor-core GEMM takes each fp32 operand value x as hi + lo * 2^-11 with
+// hi = fp16_rn(x) and lo = fp16_rn((x - hi) * 2^11) (the residual, scaled so it stays a normal
+// fp16 number). Producers of GEMM inputs can write that split directly, "row-packed": an fp32
+// [rows, W] output keeps its 4W bytes per row, the fp16 hi values of the row in its first 2W
+// bytes and the fp16 lo values in the next 2W bytes (row slices stay valid).
+constexpr float kSplitLoScale = 2048.0f;
+constexpr int kErrSplitRange = 16;   // error code: a finite value at or beyond the fp16 limit
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) {
+  uint32_t u;
+  memcpy(&u, &h, 4);
+  return u;
+}
+
+// Split 4 values; `bad` is set if one of them is finite but rounds beyond the fp16 range.
+__device__ __forceinline__ void split_f16x4(float4 v, uint2& hi, uint2& lo, bool& bad) {
+  const __half2 h01 = __float22half2_rn(make_float2(v.x, v.y));
+  const __half2 h23 = __float22half2_rn(make_float2(v.z, v.w));
+  const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+  const __half2 l01 =
+      __float22half2_rn(make_float2((v.x - f01.x) * kSplitLoScale, (v.y - f01.y) * kSplitLoScale));
+  const __half2 l23 =
+      __float22half2_rn(make_float2((v.z - f23.x) * kSplitLoScale, (v.w - f23.y) * kSplitLoScale));
+  hi = make_uint2(h2_bits(h01), h2_bits(h23));
+  lo = make_uint2(h2_bits(l01), h2_bits(l23));
+  const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  bad |= (m >= 65520.0f) & (m <= 3.402823466e38f);
+}
+
+// Store 4 consecutive values at column `col` of the [*, W] output row starting at `row`:
+// plain fp32 (streaming), or the row-packed split when `split`.
+__device__ __forceinline__ void st_out4(float* row, int W, int col, float4 v, bool split, bool& bad) {
+  if (!split) {
+    st4_stream(row + col, v);
+    return;
+  }
+  uint2 hi, lo;
+  split_f16x4(v, hi, lo, bad);
+  uint8_t* rb = reinterpret_cast<uint8_t*>(row);
+  __stcs(reinterpret_cast<uint2*>(rb + 2 * col), hi);
+  __stcs(reinterpret_cast<uint2*>(rb + 2 * (W + col)), lo);
+}
+
+__device__ __forceinline__ void report_split_range(bool bad, int* err) {
+  if (bad && err) atomicCAS(err, 0, kErrSplitRange);
+}
 
 // ---- host-side launch helpers ------------------------------------------------------------
 inline int sm_count() {

@@ -69,8 +69,9 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
     const float* __restrict__ x, const int64_t* __restrict__ idx_i, const int64_t* __restrict__ idx_j,
     const float* __restrict__ wig, const float* __restrict__ rad, const float* __restrict__ csd,
     const int64_t* __restrict__ batch, float* __restrict__ X0, float* __restrict__ X1, float* __restrict__ X2,
-    int64_t E, int C) {
+    int64_t E, int C, bool split, int* err) {
   __shared__ float s_w[kFwdWarps][36];
+  bool bad = false;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   float* sw = s_w[warp];
@@ -84,16 +85,17 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
     for (int c4 = lane; c4 < C4; c4 += 32) {
       const int co = c4 * 4;
       const float* rr = rad + e * 12 * (int64_t)C + co;
-      float* x0 = X0 + e * 6 * (int64_t)C + co;
-      float* x1 = X1 + e * 8 * (int64_t)C + co;
-      float* x2 = X2 + e * 4 * (int64_t)C + co;
+      float* x0 = X0 + e * 6 * (int64_t)C;   // output rows; columns are co + slot * C
+      float* x1 = X1 + e * 8 * (int64_t)C;
+      float* x2 = X2 + e * 4 * (int64_t)C;
 #pragma unroll 1
       for (int s = 0; s < 2; ++s) {
         const int64_t node = s ? nj : ni;
         const int64_t bsys = s ? bj : bi;
         const float* xr = x + node * 9 * (int64_t)C + co;
         // l = 0
-        st4_stream(x0 + s * C, (ld4_keep(xr) + ld4_keep(csd + bsys * C + co)) * ld4_stream(rr + s * C));
+        st_out4(x0, 6 * C, s * C + co, (ld4_keep(xr) + ld4_keep(csd + bsys * C + co)) * ld4_stream(rr + s * C), split,
+                bad);
         // l = 1
         {
           float4 v[3], r1[3];
@@ -101,9 +103,9 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
           for (int m = 0; m < 3; ++m) v[m] = ld4_keep(xr + (1 + m) * C);
           rot<3>(D1, v, r1);
           const float4 r6 = ld4_stream(rr + (6 + s) * C);
-          st4_stream(x0 + (2 + s) * C, r1[1] * ld4_stream(rr + (2 + s) * C));
-          st4_stream(x1 + (0 + s) * C, r1[2] * r6);
-          st4_stream(x1 + (4 + s) * C, r1[0] * r6);
+          st_out4(x0, 6 * C, (2 + s) * C + co, r1[1] * ld4_stream(rr + (2 + s) * C), split, bad);
+          st_out4(x1, 8 * C, (0 + s) * C + co, r1[2] * r6, split, bad);
+          st_out4(x1, 8 * C, (4 + s) * C + co, r1[0] * r6, split, bad);
         }
         // l = 2
         {
@@ -112,16 +114,17 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
           for (int m = 0; m < 5; ++m) v[m] = ld4_keep(xr + (4 + m) * C);
           rot<5>(D2, v, r2);
           const float4 r8 = ld4_stream(rr + (8 + s) * C), r10 = ld4_stream(rr + (10 + s) * C);
-          st4_stream(x0 + (4 + s) * C, r2[2] * ld4_stream(rr + (4 + s) * C));
-          st4_stream(x1 + (2 + s) * C, r2[3] * r8);
-          st4_stream(x1 + (6 + s) * C, r2[1] * r8);
-          st4_stream(x2 + (0 + s) * C, r2[4] * r10);
-          st4_stream(x2 + (2 + s) * C, r2[0] * r10);
+          st_out4(x0, 6 * C, (4 + s) * C + co, r2[2] * ld4_stream(rr + (4 + s) * C), split, bad);
+          st_out4(x1, 8 * C, (2 + s) * C + co, r2[3] * r8, split, bad);
+          st_out4(x1, 8 * C, (6 + s) * C + co, r2[1] * r8, split, bad);
+          st_out4(x2, 4 * C, (0 + s) * C + co, r2[4] * r10, split, bad);
+          st_out4(x2, 4 * C, (2 + s) * C + co, r2[0] * r10, split, bad);
         }
       }
     }
     __syncwarp();
   }
+  report_split_range(bad, err);
 }
 
 // Pass A of the backward (see file comment), one launch per coefficient block: PART 0 handles
@@ -136,8 +139,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
     const float* __restrict__ x, const int64_t* __restrict__ idx_i, const float* __restrict__ wig,
     const float* __restrict__ rad, const float* __restrict__ csd, const int64_t* __restrict__ batch,
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, float* __restrict__ g_x,
-    float* __restrict__ g_wig, float* __restrict__ g_rad, float* __restrict__ g_src_rows, int64_t N, int C) {
+    float* __restrict__ g_wig, float* __restrict__ g_rad, float* __restrict__ g_src_rows, int64_t N, int C,
+    bool split, int* err) {
   extern __shared__ float4 s_acc4[];
+  bool bad = false;
   __shared__ float s_w[kBwdWarps][28];
   __shared__ float s_red[kBwdWarps][28];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -173,7 +178,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
         const float* g1b = gX1 + e * 8 * (int64_t)C;
         const float* g2b = gX2 + e * 4 * (int64_t)C;
         const float* rrb = rad + e * 12 * (int64_t)C;
-        float* grb = g_rad + e * 12 * (int64_t)C;
+        float* grb = g_rad + e * 12 * (int64_t)C;   // g_rad row (12C wide), columns slot * C + co
         float* gsb = g_src_rows + e * 9 * (int64_t)C;
         float gw[nw];
 #pragma unroll
@@ -184,11 +189,12 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
             const int co = c4 * 4;
             const float* rr = rrb + co; const float* g0 = g0b + co; const float* g1 = g1b + co;
             const float* xi = xi_base + co; const float* xj = xj_base + co;
-            float* grr = grb + co; float* gsrc = gsb + co;
+            float* gsrc = gsb + co;
+            const int W = 12 * C;
             {
               const float4 a0 = ld4_stream(g0), a1 = ld4_stream(g0 + C);
-              st4(grr, a0 * (ld4_keep(xi) + ld4_keep(csd + bi * C + co)));
-              st4(grr + C, a1 * (ld4_keep(xj) + ld4_keep(csd + bj * C + co)));
+              st_out4(grb, W, co, a0 * (ld4_keep(xi) + ld4_keep(csd + bi * C + co)), split, bad);
+              st_out4(grb, W, C + co, a1 * (ld4_keep(xj) + ld4_keep(csd + bj * C + co)), split, bad);
               st4(gsrc, a0 * ld4_stream(rr));
               acc[c4] += a1 * ld4_stream(rr + C);
             }
@@ -202,10 +208,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
             const float4 a2 = ld4_stream(g0 + 2 * C), a3 = ld4_stream(g0 + 3 * C);
             const float4 b0 = ld4_stream(g1), b1 = ld4_stream(g1 + C);
             const float4 b4 = ld4_stream(g1 + 4 * C), b5 = ld4_stream(g1 + 5 * C);
-            st4(grr + 2 * C, a2 * ri[1]);
-            st4(grr + 3 * C, a3 * rj[1]);
-            st4(grr + 6 * C, b0 * ri[2] + b4 * ri[0]);
-            st4(grr + 7 * C, b1 * rj[2] + b5 * rj[0]);
+            st_out4(grb, W, 2 * C + co, a2 * ri[1], split, bad);
+            st_out4(grb, W, 3 * C + co, a3 * rj[1], split, bad);
+            st_out4(grb, W, 6 * C + co, b0 * ri[2] + b4 * ri[0], split, bad);
+            st_out4(grb, W, 7 * C + co, b1 * rj[2] + b5 * rj[0], split, bad);
             const float4 gi[3] = {b4 * r6, a2 * r2, b0 * r6};
             const float4 gj[3] = {b5 * r7, a3 * r3, b1 * r7};
             float4 t[3];
@@ -227,7 +233,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
             const float* rr = rrb + co; const float* g0 = g0b + co; const float* g1 = g1b + co;
             const float* g2 = g2b + co;
             const float* xi = xi_base + co; const float* xj = xj_base + co;
-            float* grr = grb + co; float* gsrc = gsb + co;
+            float* gsrc = gsb + co;
+            const int W = 12 * C;
 #pragma unroll 1
             for (int s = 0; s < 2; ++s) {   // s = 0: source side (even slots), s = 1: target side (odd slots)
               const float* xs = s ? xj : xi;
@@ -240,9 +247,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
               const float4 c0 = ld4_stream(g2 + s * C), c2 = ld4_stream(g2 + (2 + s) * C);
               const float4 r4 = ld4_stream(rr + (4 + s) * C), r8 = ld4_stream(rr + (8 + s) * C);
               const float4 r10 = ld4_stream(rr + (10 + s) * C);
-              st4(grr + (4 + s) * C, a4 * r[2]);
-              st4(grr + (8 + s) * C, b2 * r[3] + b6 * r[1]);
-              st4(grr + (10 + s) * C, c0 * r[4] + c2 * r[0]);
+              st_out4(grb, W, (4 + s) * C + co, a4 * r[2], split, bad);
+              st_out4(grb, W, (8 + s) * C + co, b2 * r[3] + b6 * r[1], split, bad);
+              st_out4(grb, W, (10 + s) * C + co, c0 * r[4] + c2 * r[0], split, bad);
               const float4 g[5] = {c2 * r10, b6 * r8, a4 * r4, b2 * r8, c0 * r10};
               float4 t[5];
               rotT<5>(D2, g, t);
@@ -279,6 +286,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_dst_kernel(
     }
     __syncwarp();
   }
+  report_split_range(bad, err);
 }
 
 // Pass B: g_x[n] += sum over edges with source n (source CSR order) of the scratch rows.
@@ -304,24 +312,25 @@ __global__ void __launch_bounds__(256) gather_bwd_src_kernel(const int32_t* __re
 
 void launch_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wig, const float* rad,
                        const float* csd, const int64_t* batch, float* X0, float* X1, float* X2, int64_t E, int C,
-                       cudaStream_t s) {
+                       bool split, int* err, cudaStream_t s) {
   gather_fwd_kernel<<<grid_for(E, kFwdWarps, 3), kFwdWarps * 32, 0, s>>>(x, idx_i, idx_j, wig, rad, csd, batch, X0,
-                                                                         X1, X2, E, C);
+                                                                         X1, X2, E, C, split, err);
 }
 
 void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, const float* x, const int64_t* idx_i,
                        const float* wig, const float* rad, const float* csd, const int64_t* batch,
                        const int32_t* dst_ptr, const int32_t* dst_col, const int32_t* src_ptr, const int32_t* src_col,
-                       float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, cudaStream_t s) {
+                       float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, bool split, int* err,
+                       cudaStream_t s) {
   const size_t smem = (size_t)kBwdWarps * 5 * C * sizeof(float);
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(gather_bwd_dst_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(gather_bwd_dst_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
   gather_bwd_dst_kernel<0><<<grid_for(N, kBwdWarps, 2), kBwdWarps * 32, smem, s>>>(
-      gX0, gX1, gX2, x, idx_i, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig, g_rad, scratch, N, C);
+      gX0, gX1, gX2, x, idx_i, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig, g_rad, scratch, N, C, split, err);
   gather_bwd_dst_kernel<1><<<grid_for(N, kBwdWarps, 2), kBwdWarps * 32, smem, s>>>(
-      gX0, gX1, gX2, x, idx_i, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig, g_rad, scratch, N, C);
+      gX0, gX1, gX2, x, idx_i, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig, g_rad, scratch, N, C, split, err);
   gather_bwd_src_kernel<<<grid_for(N, 8, 8), 256, 0, s>>>(src_ptr, src_col, scratch, g_x, N, C);
 }
 

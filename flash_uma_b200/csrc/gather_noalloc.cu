@@ -86,7 +86,7 @@ int fuma_gather_bwd_noalloc(const float* g_X_m0, const float* g_X_m1, const floa
   st = noalloc_scratch(&scratch);
   if (st != cudaSuccess) return reject((int)st, "cudaGetSymbolAddress of the scratch array failed");
   launch_gather_bwd(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
-                    src_col, g_x, g_wigner, g_rad, scratch, N, C, (cudaStream_t)stream);
+                    src_col, g_x, g_wigner, g_rad, scratch, N, C, false, nullptr, (cudaStream_t)stream);
   st = cudaGetLastError();
   if (st != cudaSuccess) return reject((int)st, "kernel launch failed");
   return report_error(FUMA_OK, "");

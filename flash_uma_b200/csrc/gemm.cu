@@ -36,6 +36,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace fuma {
 
@@ -44,67 +45,6 @@ namespace {
 constexpr int kBM = 128;          // rows per tile (one tcgen05 M=128 MMA, cta_group::1)
 constexpr int kBK = 32;           // fp32 elements per K step = one 128-byte swizzle row
 constexpr int kThreads = 320;  // producer, MMA, 4 split warps, 4 epilogue warps
-constexpr uint32_t kWaitLimit = 1u << 24;   // try_wait iterations before giving up
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait. Returns false (and records `code`) if the phase did not complete, or if
-// another role of this CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                          int code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *abort_flag) return false;
-  }
-  *abort_flag = 1;
-  if (err) atomicCAS(err, 0, code);
-  return false;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3FFFu);          // start address
-  d |= (uint64_t)1u << 16;                          // leading byte offset (unused for SW128 K-major)
-  d |= (uint64_t)(1024u >> 4) << 32;                // stride byte offset: 8 rows x 128 B
-  d |= (uint64_t)1u << 46;                          // descriptor version (sm100)
-  d |= (uint64_t)2u << 61;                          // layout: SWIZZLE_128B
-  return d;
-}
 
 // Instruction descriptor: kind::tf32, fp32 accumulator, both operands K-major, M=128.
 template <int BN>
@@ -146,10 +86,6 @@ __device__ __forceinline__ uint32_t lo_part(uint32_t xbits) {
   return rn_tf32(x - t);
 }
 
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
 
 template <int BN, int STAGES, bool kSplit>
 struct GemmSmem {
@@ -381,25 +317,35 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D fp32 tensor map over rows x cols (cols contiguous, row stride ld elements), box 32 x box_rows,
-// 128-byte swizzle; out-of-range rows read as zero.
-bool make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+}  // namespace
+
+// 2-D tensor map over rows x cols (cols contiguous, row stride ld_bytes), box box_cols x box_rows;
+// out-of-range elements read as zero.
+bool make_map_t(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int64_t rows, int64_t cols,
+                int64_t ld_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swz) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     snprintf(g_map_err, sizeof(g_map_err),
-             "cuTensorMapEncodeTiled failed (CUresult %d) for base=%p rows=%lld cols=%lld ld=%lld box=%dx%d", (int)r,
-             (const void*)base, (long long)rows, (long long)cols, (long long)ld, kBK, box_rows);
+             "cuTensorMapEncodeTiled failed (CUresult %d) for base=%p rows=%lld cols=%lld ld=%lldB box=%dx%d", (int)r,
+             base, (long long)rows, (long long)cols, (long long)ld_bytes, box_cols, box_rows);
     return false;
   }
   return true;
+}
+
+namespace {
+
+// fp32 operand: box 32 x box_rows (128-byte rows), 128-byte swizzle.
+bool make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  return make_map_t(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rows, cols, ld * 4, kBK, box_rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <int BN, int STAGES, bool kSplit>

@@ -21,8 +21,9 @@ __device__ __forceinline__ float4 sig4(float4 a) {
 __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict__ Y0, const float* __restrict__ Y1,
                                                          const float* __restrict__ Y2, float* __restrict__ Z0,
                                                          float* __restrict__ Z1, float* __restrict__ Z2, int64_t E,
-                                                         int C) {
+                                                         int C, bool split, int* err) {
   const int C4 = C >> 2;
+  bool bad = false;
   const int64_t total = E * C4;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = t / C4;
@@ -32,26 +33,29 @@ __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict
     const float* y2 = Y2 + e * 2 * (int64_t)C + co;
     const float4 g0 = sig4(ld4_stream(y0)), g1 = sig4(ld4_stream(y0 + C));
     const float4 a = ld4_stream(y0 + 2 * C);
-    float* z0 = Z0 + e * 3 * (int64_t)C + co;
-    float* z1 = Z1 + e * 4 * (int64_t)C + co;
-    float* z2 = Z2 + e * 2 * (int64_t)C + co;
-    st4_stream(z0, a * sig4(a));
-    st4_stream(z0 + C, ld4_stream(y0 + 3 * C) * g0);
-    st4_stream(z0 + 2 * C, ld4_stream(y0 + 4 * C) * g1);
-    st4_stream(z1, ld4_stream(y1) * g0);
-    st4_stream(z1 + C, ld4_stream(y1 + C) * g1);
-    st4_stream(z1 + 2 * C, ld4_stream(y1 + 2 * C) * g0);
-    st4_stream(z1 + 3 * C, ld4_stream(y1 + 3 * C) * g1);
-    st4_stream(z2, ld4_stream(y2) * g1);
-    st4_stream(z2 + C, ld4_stream(y2 + C) * g1);
+    float* z0 = Z0 + e * 3 * (int64_t)C;
+    float* z1 = Z1 + e * 4 * (int64_t)C;
+    float* z2 = Z2 + e * 2 * (int64_t)C;
+    st_out4(z0, 3 * C, co, a * sig4(a), split, bad);
+    st_out4(z0, 3 * C, C + co, ld4_stream(y0 + 3 * C) * g0, split, bad);
+    st_out4(z0, 3 * C, 2 * C + co, ld4_stream(y0 + 4 * C) * g1, split, bad);
+    st_out4(z1, 4 * C, co, ld4_stream(y1) * g0, split, bad);
+    st_out4(z1, 4 * C, C + co, ld4_stream(y1 + C) * g1, split, bad);
+    st_out4(z1, 4 * C, 2 * C + co, ld4_stream(y1 + 2 * C) * g0, split, bad);
+    st_out4(z1, 4 * C, 3 * C + co, ld4_stream(y1 + 3 * C) * g1, split, bad);
+    st_out4(z2, 2 * C, co, ld4_stream(y2) * g1, split, bad);
+    st_out4(z2, 2 * C, C + co, ld4_stream(y2 + C) * g1, split, bad);
   }
+  report_split_range(bad, err);
 }
 
 __global__ void __launch_bounds__(256) gating_bwd_kernel(
     const float* __restrict__ gZ0, const float* __restrict__ gZ1, const float* __restrict__ gZ2,
     const float* __restrict__ Y0, const float* __restrict__ Y1, const float* __restrict__ Y2,
-    float* __restrict__ gY0, float* __restrict__ gY1, float* __restrict__ gY2, int64_t E, int C) {
+    float* __restrict__ gY0, float* __restrict__ gY1, float* __restrict__ gY2, int64_t E, int C, bool split,
+    int* err) {
   const int C4 = C >> 2;
+  bool bad = false;
   const int64_t total = E * C4;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = t / C4;
@@ -72,21 +76,22 @@ __global__ void __launch_bounds__(256) gating_bwd_kernel(
     const float4 k0 = ld4_stream(q2), k1 = ld4_stream(q2 + C);
     const float4 one = f4(1.f);
     const float4 dg0 = g0 * (one - g0), dg1 = g1 * (one - g1);
-    float* p0 = gY0 + e * 5 * (int64_t)C + co;
-    float* p1 = gY1 + e * 4 * (int64_t)C + co;
-    float* p2 = gY2 + e * 2 * (int64_t)C + co;
-    st4_stream(p0, dg0 * (g3 * y3 + h0 * u0 + h2 * u2));
-    st4_stream(p0 + C, dg1 * (g4 * y4 + h1 * u1 + h3 * u3 + k0 * w0 + k1 * w1));
-    st4_stream(p0 + 2 * C, ga * (sa + a * (sa * (one - sa))));
-    st4_stream(p0 + 3 * C, g3 * g0);
-    st4_stream(p0 + 4 * C, g4 * g1);
-    st4_stream(p1, h0 * g0);
-    st4_stream(p1 + C, h1 * g1);
-    st4_stream(p1 + 2 * C, h2 * g0);
-    st4_stream(p1 + 3 * C, h3 * g1);
-    st4_stream(p2, k0 * g1);
-    st4_stream(p2 + C, k1 * g1);
+    float* p0 = gY0 + e * 5 * (int64_t)C;
+    float* p1 = gY1 + e * 4 * (int64_t)C;
+    float* p2 = gY2 + e * 2 * (int64_t)C;
+    st_out4(p0, 5 * C, co, dg0 * (g3 * y3 + h0 * u0 + h2 * u2), split, bad);
+    st_out4(p0, 5 * C, C + co, dg1 * (g4 * y4 + h1 * u1 + h3 * u3 + k0 * w0 + k1 * w1), split, bad);
+    st_out4(p0, 5 * C, 2 * C + co, ga * (sa + a * (sa * (one - sa))), split, bad);
+    st_out4(p0, 5 * C, 3 * C + co, g3 * g0, split, bad);
+    st_out4(p0, 5 * C, 4 * C + co, g4 * g1, split, bad);
+    st_out4(p1, 4 * C, co, h0 * g0, split, bad);
+    st_out4(p1, 4 * C, C + co, h1 * g1, split, bad);
+    st_out4(p1, 4 * C, 2 * C + co, h2 * g0, split, bad);
+    st_out4(p1, 4 * C, 3 * C + co, h3 * g1, split, bad);
+    st_out4(p2, 2 * C, co, k0 * g1, split, bad);
+    st_out4(p2, 2 * C, C + co, k1 * g1, split, bad);
   }
+  report_split_range(bad, err);
 }
 
 // One warp per row; VPL float4 per lane (D <= 128 * VPL), row kept in registers.
@@ -94,8 +99,9 @@ template <int VPL>
 __global__ void __launch_bounds__(256) ln_silu_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta, float* __restrict__ out,
                                                           float* __restrict__ mean_out, float* __restrict__ rstd_out,
-                                                          int64_t M, int D, float eps) {
+                                                          int64_t M, int D, float eps, bool split, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  bool bad = false;
   const int wpb = blockDim.x >> 5;
   const int D4 = D >> 2;
   for (int64_t r = (int64_t)blockIdx.x * wpb + warp; r < M; r += (int64_t)gridDim.x * wpb) {
@@ -127,18 +133,21 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_kernel(const float* __restric
       const int d4 = lane + 32 * q;
       if (d4 < D4) {
         const float4 y = (v[q] - f4(mean)) * rstd * ld4_keep(gamma + d4 * 4) + ld4_keep(beta + d4 * 4);
-        st4(orow + d4 * 4, y * sig4(y));
+        st_out4(orow, D, d4 * 4, y * sig4(y), split, bad);
       }
     }
   }
+  report_split_range(bad, err);
 }
 
 template <int VPL>
 __global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta, const float* __restrict__ mean,
                                                           const float* __restrict__ rstd, const float* __restrict__ g_out,
-                                                          float* __restrict__ g_x, int64_t M, int D) {
+                                                          float* __restrict__ g_x, int64_t M, int D, bool split,
+                                                          int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  bool bad = false;
   const int wpb = blockDim.x >> 5;
   const int D4 = D >> 2;
   for (int64_t r = (int64_t)blockIdx.x * wpb + warp; r < M; r += (int64_t)gridDim.x * wpb) {
@@ -167,41 +176,48 @@ __global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restric
 #pragma unroll
     for (int q = 0; q < VPL; ++q) {
       const int d4 = lane + 32 * q;
-      if (d4 < D4) st4(g_x + r * D + d4 * 4, (gxh[q] - (f4(s1) + xh[q] * s2) * invD) * rs);
+      if (d4 < D4) st_out4(g_x + r * D, D, d4 * 4, (gxh[q] - (f4(s1) + xh[q] * s2) * invD) * rs, split, bad);
     }
   }
+  report_split_range(bad, err);
 }
 
 void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,
-                       int C, cudaStream_t s) {
-  gating_fwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(Y0, Y1, Y2, Z0, Z1, Z2, E, C);
+                       int C, bool split, int* err, cudaStream_t s) {
+  gating_fwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(Y0, Y1, Y2, Z0, Z1, Z2, E, C, split, err);
 }
 
 void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, const float* Y0, const float* Y1,
-                       const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, cudaStream_t s) {
-  gating_bwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C);
+                       const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, bool split, int* err,
+                       cudaStream_t s) {
+  gating_bwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C,
+                                                                   split, err);
 }
 
 void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float* out, float* mean, float* rstd,
-                        int64_t M, int D, float eps, cudaStream_t s) {
+                        int64_t M, int D, float eps, bool split, int* err, cudaStream_t s) {
   const unsigned g = grid_for(M, 8, 8);
   const int d4 = D / 4;
-  if (d4 <= 32) ln_silu_fwd_kernel<1><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
-  else if (d4 <= 64) ln_silu_fwd_kernel<2><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
-  else if (d4 <= 128) ln_silu_fwd_kernel<4><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
-  else if (d4 <= 256) ln_silu_fwd_kernel<8><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
-  else ln_silu_fwd_kernel<16><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps);
+#define FWD(V) ln_silu_fwd_kernel<V><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps, split, err)
+  if (d4 <= 32) FWD(1);
+  else if (d4 <= 64) FWD(2);
+  else if (d4 <= 128) FWD(4);
+  else if (d4 <= 256) FWD(8);
+  else FWD(16);
+#undef FWD
 }
 
 void launch_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
-                        const float* g_out, float* g_x, int64_t M, int D, cudaStream_t s) {
+                        const float* g_out, float* g_x, int64_t M, int D, bool split, int* err, cudaStream_t s) {
   const unsigned g = grid_for(M, 8, 8);
   const int d4 = D / 4;
-  if (d4 <= 32) ln_silu_bwd_kernel<1><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
-  else if (d4 <= 64) ln_silu_bwd_kernel<2><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
-  else if (d4 <= 128) ln_silu_bwd_kernel<4><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
-  else if (d4 <= 256) ln_silu_bwd_kernel<8><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
-  else ln_silu_bwd_kernel<16><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D);
+#define BWD(V) ln_silu_bwd_kernel<V><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D, split, err)
+  if (d4 <= 32) BWD(1);
+  else if (d4 <= 64) BWD(2);
+  else if (d4 <= 128) BWD(4);
+  else if (d4 <= 256) BWD(8);
+  else BWD(16);
+#undef BWD
 }
 
 }  // namespace fuma

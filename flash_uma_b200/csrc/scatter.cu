@@ -122,8 +122,10 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ Z0, const float* __restrict__ Z1, const float* __restrict__ Z2,
     const float* __restrict__ wig, const float* __restrict__ env, float* __restrict__ gZ0, float* __restrict__ gZ1,
-    float* __restrict__ gZ2, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C) {
+    float* __restrict__ gZ2, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, bool split,
+    int* err) {
   constexpr int kW = PART ? 25 : 9;
+  bool bad = false;
   constexpr int kWoff = PART ? 9 : 0;
   constexpr int kParts = kW + (PART ? 0 : 1);  // PART 0 also reduces g0 . Z0_0
   __shared__ float s_w[8][28];
@@ -157,9 +159,9 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
           const float* z0 = Z0 + e * 3 * (int64_t)C + co;
           const float* z1 = Z1 + e * 4 * (int64_t)C + co;
           const float* z2 = Z2 + e * 2 * (int64_t)C + co;
-          float* q0 = gZ0 + e * 3 * (int64_t)C + co;
-          float* q1 = gZ1 + e * 4 * (int64_t)C + co;
-          float* q2 = gZ2 + e * 2 * (int64_t)C + co;
+          float* q0 = gZ0 + e * 3 * (int64_t)C;   // gradient rows; columns slot * C + co
+          float* q1 = gZ1 + e * 4 * (int64_t)C;
+          float* q2 = gZ2 + e * 2 * (int64_t)C;
           if constexpr (PART == 0) {
             float4 g[4];
 #pragma unroll
@@ -174,10 +176,10 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
               fma4(a, sw[r * 3 + 2], g[3]);
               t1[r] = a * ev;
             }
-            st4_stream(q0, g[0] * ev);
-            st4_stream(q0 + C, t1[1]);
-            st4_stream(q1, t1[2]);
-            st4_stream(q1 + 2 * C, t1[0]);
+            st_out4(q0, 3 * C, co, g[0] * ev, split, bad);
+            st_out4(q0, 3 * C, C + co, t1[1], split, bad);
+            st_out4(q1, 4 * C, co, t1[2], split, bad);
+            st_out4(q1, 4 * C, 2 * C + co, t1[0], split, bad);
 #pragma unroll
             for (int r = 0; r < 3; ++r)
 #pragma unroll
@@ -197,11 +199,11 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
               for (int kk = 1; kk < 5; ++kk) fma4(a, sw[r * 5 + kk], g[kk]);
               t2[r] = a * ev;
             }
-            st4_stream(q0 + 2 * C, t2[2]);
-            st4_stream(q1 + C, t2[3]);
-            st4_stream(q1 + 3 * C, t2[1]);
-            st4_stream(q2, t2[4]);
-            st4_stream(q2 + C, t2[0]);
+            st_out4(q0, 3 * C, 2 * C + co, t2[2], split, bad);
+            st_out4(q1, 4 * C, C + co, t2[3], split, bad);
+            st_out4(q1, 4 * C, 3 * C + co, t2[1], split, bad);
+            st_out4(q2, 2 * C, co, t2[4], split, bad);
+            st_out4(q2, 2 * C, C + co, t2[0], split, bad);
 #pragma unroll
             for (int r = 0; r < 5; ++r)
 #pragma unroll
@@ -226,6 +228,7 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
       }
     }
   }
+  report_split_range(bad, err);
 }
 
 template <int WARPS>
@@ -282,9 +285,11 @@ template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ rad, const float* __restrict__ wig, const float* __restrict__ env,
-    float* __restrict__ g_rad, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C) {
+    float* __restrict__ g_rad, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, bool split,
+    int* err) {
   __shared__ float s_w[WARPS][36];
   __shared__ float s_red[WARPS][12];
+  bool bad = false;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   float* sw = s_w[warp];
@@ -312,10 +317,10 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
         float4 s2 = g[4] * sw[19];
 #pragma unroll
         for (int kk = 1; kk < 5; ++kk) fma4(s2, sw[19 + kk], g[4 + kk]);
-        float* gr = g_rad + e * 3 * (int64_t)C + co;
-        st4_stream(gr, g[0] * ev);
-        st4_stream(gr + C, s1 * ev);
-        st4_stream(gr + 2 * C, s2 * ev);
+        float* gr = g_rad + e * 3 * (int64_t)C;
+        st_out4(gr, 3 * C, co, g[0] * ev, split, bad);
+        st_out4(gr, 3 * C, C + co, s1 * ev, split, bad);
+        st_out4(gr, 3 * C, 2 * C + co, s2 * ev, split, bad);
 #pragma unroll
         for (int kk = 0; kk < 3; ++kk) part[kk] += dot4(g[1 + kk], r1);
 #pragma unroll
@@ -338,6 +343,7 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
       __syncwarp();
     }
   }
+  report_split_range(bad, err);
 }
 
 void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* Z0, const float* Z1,
@@ -350,12 +356,13 @@ void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, c
 
 void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* Z0,
                                const float* Z1, const float* Z2, const float* wig, const float* env, float* gZ0,
-                               float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, cudaStream_t s) {
+                               float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, bool split,
+                               int* err, cudaStream_t s) {
   const unsigned g = grid_for(N, 8, 2);
   rotate_scatter_bwd_kernel<0><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
-                                                 g_env, N, C);
+                                                 g_env, N, C, split, err);
   rotate_scatter_bwd_kernel<1><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
-                                                 g_env, N, C);
+                                                 g_env, N, C, split, err);
 }
 
 void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,
@@ -367,9 +374,9 @@ void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, con
 
 void launch_init_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* rad,
                              const float* wig, const float* env, float* g_rad, float* g_wig, float* g_env, int64_t N,
-                             int C, cudaStream_t s) {
+                             int C, bool split, int* err, cudaStream_t s) {
   init_scatter_bwd_kernel<4><<<grid_for(N, 4, 16), 128, 0, s>>>(row_ptr, col_idx, g_out, rad, wig, env, g_rad, g_wig,
-                                                                 g_env, N, C);
+                                                                 g_env, N, C, split, err);
 }
 
 }  // namespace fuma

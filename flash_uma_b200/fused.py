@@ -1,0 +1,218 @@
+"""Fused message-passing blocks for the f16x3 GEMM mode.
+
+The edge-wise part of one layer of the reference (``Packed_eSCN_Layer.forward``,
+``model.py:143-157``: radial MLP, gather + rotate, SO(2) convolution 1, gating, SO(2)
+convolution 2, rotate back + scatter) and the initial edge-degree embedding
+(``model.py:203-206``) run here as ONE autograd Function each. Inside a block every dense
+contraction reads its input in the row-packed f16x3 split layout, written directly by the
+kernel that produces it (``*_f16x3`` entry points), so the fp16 tensor-core GEMM does no
+conversion work; at the block boundary all tensors (inputs, outputs and their gradients)
+are plain fp32, so autograd and the node-wise modules around the blocks see the same
+interface as the per-op path. The arithmetic per element is the per-op path's; only the
+GEMM operand format differs.
+
+The blocks need every GEMM width to be a multiple of 16 (C, the radial hidden width and the
+edge-feature width B + 2C); :func:`fusable` checks a model, which otherwise runs per op.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+from ._native import ptr, stream_of
+from .linear import _gemm16, error_flag
+
+_EPS_LN = 1e-7   # LayerNorm epsilon of the radial MLPs (ops/ln_silu.py:180)
+
+
+def _empty(shape, like):
+    return torch.empty(shape, device=like.device, dtype=torch.float32)
+
+
+class _SplitRowsFn(torch.autograd.Function):
+    """x [M, K] fp32 -> its row-packed split (same shape, fp32-typed); the gradient passes through."""
+
+    @staticmethod
+    def forward(ctx, x):
+        M, K = x.shape
+        out = _empty((M, K), x)
+        nat.call("fuma_split_rows_f16", ptr(x), x.stride(0), M, K, ptr(out), K, ptr(error_flag(x.device)),
+                 stream_of(x))
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        return g
+
+
+def split_rows(x: torch.Tensor) -> torch.Tensor:
+    """Differentiable row-packed split of a contiguous [M, K] fp32 tensor (K a multiple of 8)."""
+    return _SplitRowsFn.apply(x.contiguous())
+
+
+# ---- radial MLP on split operands ------------------------------------------------------------
+
+def _ln_silu_split(y, gamma, beta, err):
+    M, D = y.shape
+    out, mean, rstd = _empty((M, D), y), _empty((M,), y), _empty((M,), y)
+    nat.call("fuma_ln_silu_fwd_f16x3", ptr(y), ptr(gamma), ptr(beta), _EPS_LN, M, D, ptr(out), ptr(mean), ptr(rstd),
+             ptr(err), stream_of(y))
+    return out, mean, rstd
+
+
+def _ln_silu_bwd_split(y, gamma, beta, mean, rstd, g, err):
+    M, D = y.shape
+    gx = _empty((M, D), y)
+    nat.call("fuma_ln_silu_bwd_f16x3", ptr(y), ptr(gamma), ptr(beta), ptr(mean), ptr(rstd), ptr(g), M, D, ptr(gx),
+             ptr(err), stream_of(y))
+    return gx
+
+
+def radial_fwd(rad, xe_p, err):
+    """Linear -> LN-SiLU -> Linear -> LN-SiLU -> Linear on the split edge features; returns the
+    fp32 radial output and what the backward needs."""
+    Kx = xe_p.shape[1]
+    y1 = _gemm16(xe_p, rad.l1.w16, rad.l1.bias_p, Kx)
+    h1, m1, r1 = _ln_silu_split(y1, rad.g1, rad.be1, err)
+    y2 = _gemm16(h1, rad.l2.w16, rad.l2.bias_p, h1.shape[1])
+    del h1
+    h2, m2, r2 = _ln_silu_split(y2, rad.g2, rad.be2, err)
+    out = _gemm16(h2, rad.l3.w16, rad.l3.bias_p, h2.shape[1])
+    return out, (y1, m1, r1, y2, m2, r2)
+
+
+def radial_bwd(rad, saved, g_out_p, err):
+    """Input gradient of :func:`radial_fwd` from the split gradient of its output."""
+    y1, m1, r1, y2, m2, r2 = saved
+    g_h2 = _gemm16(g_out_p, rad.l3.wt16, None, g_out_p.shape[1])
+    g_y2 = _ln_silu_bwd_split(y2, rad.g2, rad.be2, m2, r2, g_h2, err)
+    del g_h2
+    g_h1 = _gemm16(g_y2, rad.l2.wt16, None, g_y2.shape[1])
+    del g_y2
+    g_y1 = _ln_silu_bwd_split(y1, rad.g1, rad.be1, m1, r1, g_h1, err)
+    del g_h1
+    return _gemm16(g_y1, rad.l1.wt16, None, g_y1.shape[1])
+
+
+# ---- one message-passing block ---------------------------------------------------------------
+
+class _MessageBlockFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_norm, x_in, xe_p, wigner, env, csd, layer, idx_i, idx_j, batch, graph):
+        N, _, C = x_in.shape
+        E = idx_i.shape[0]
+        err = error_flag(x_in.device)
+        s = stream_of(x_in)
+        rad, rsaved = radial_fwd(layer.rad, xe_p, err)
+        X0, X1, X2 = _empty((E, 6 * C), x_in), _empty((E, 8 * C), x_in), _empty((E, 4 * C), x_in)
+        nat.call("fuma_gather_fwd_f16x3", ptr(x_norm), ptr(idx_i), ptr(idx_j), ptr(wigner), ptr(rad), ptr(csd),
+                 ptr(batch), N, E, C, ptr(X0), ptr(X1), ptr(X2), ptr(err), s)
+        Y0 = _gemm16(X0, layer.conv1_m0.w16, layer.conv1_m0.bias_p, 6 * C)
+        Y1 = _gemm16(X1, layer.conv1_m1.w16, None, 8 * C)
+        Y2 = _gemm16(X2, layer.conv1_m2.w16, None, 4 * C)
+        del X0, X1, X2
+        Z0, Z1, Z2 = _empty((E, 3 * C), x_in), _empty((E, 4 * C), x_in), _empty((E, 2 * C), x_in)
+        nat.call("fuma_gating_fwd_f16x3", ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(Z0), ptr(Z1), ptr(Z2), ptr(err), s)
+        O0 = _gemm16(Z0, layer.conv2_m0.w16, layer.conv2_m0.bias_p, 3 * C)
+        O1 = _gemm16(Z1, layer.conv2_m1.w16, None, 4 * C)
+        O2 = _gemm16(Z2, layer.conv2_m2.w16, None, 2 * C)
+        del Z0, Z1, Z2
+        x_mid = _empty((N, 9, C), x_in)
+        nat.call("fuma_rotate_scatter_fwd", ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env), ptr(x_in),
+                 ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(x_mid), s)
+        ctx.save_for_backward(x_norm, wigner, env, csd, rad, Y0, Y1, Y2, O0, O1, O2, idx_i, batch, *rsaved)
+        ctx.layer, ctx.graph = layer, graph
+        return x_mid
+
+    @staticmethod
+    def backward(ctx, g_mid):
+        (x_norm, wigner, env, csd, rad, Y0, Y1, Y2, O0, O1, O2, idx_i, batch, *rsaved) = ctx.saved_tensors
+        layer, graph = ctx.layer, ctx.graph
+        g_mid = g_mid.contiguous()
+        N, _, C = x_norm.shape
+        E = idx_i.shape[0]
+        err = error_flag(x_norm.device)
+        s = stream_of(x_norm)
+        gO0, gO1, gO2 = _empty((E, 3 * C), rad), _empty((E, 4 * C), rad), _empty((E, 2 * C), rad)
+        g_w = _empty((E, 34), rad)
+        g_env = _empty((E,), rad)
+        nat.call("fuma_rotate_scatter_bwd_f16x3", ptr(g_mid), ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env),
+                 ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(gO0), ptr(gO1), ptr(gO2), ptr(g_w),
+                 ptr(g_env), ptr(err), s)
+        gZ0 = _gemm16(gO0, layer.conv2_m0.wt16, None, 3 * C)
+        gZ1 = _gemm16(gO1, layer.conv2_m1.wt16, None, 4 * C)
+        gZ2 = _gemm16(gO2, layer.conv2_m2.wt16, None, 2 * C)
+        del gO0, gO1, gO2
+        gY0, gY1, gY2 = _empty((E, 5 * C), rad), _empty((E, 4 * C), rad), _empty((E, 2 * C), rad)
+        nat.call("fuma_gating_bwd_f16x3", ptr(gZ0), ptr(gZ1), ptr(gZ2), ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(gY0),
+                 ptr(gY1), ptr(gY2), ptr(err), s)
+        del gZ0, gZ1, gZ2
+        gX0 = _gemm16(gY0, layer.conv1_m0.wt16, None, 5 * C)
+        gX1 = _gemm16(gY1, layer.conv1_m1.wt16, None, 4 * C)
+        gX2 = _gemm16(gY2, layer.conv1_m2.wt16, None, 2 * C)
+        del gY0, gY1, gY2
+        g_x = torch.empty_like(x_norm)
+        g_w2 = _empty((E, 34), rad)
+        g_rad = torch.empty_like(rad)
+        scratch = _empty((E * 9 * C,), rad)
+        nat.call("fuma_gather_bwd_f16x3", ptr(gX0), ptr(gX1), ptr(gX2), ptr(x_norm), ptr(idx_i), ptr(wigner), ptr(rad),
+                 ptr(csd), ptr(batch), ptr(graph.dst_row_ptr), ptr(graph.dst_col), ptr(graph.src_row_ptr),
+                 ptr(graph.src_col), N, E, C, ptr(scratch), scratch.numel(), ptr(g_x), ptr(g_w2), ptr(g_rad),
+                 ptr(err), s)
+        del gX0, gX1, gX2, scratch
+        g_xe = radial_bwd(layer.rad, rsaved, g_rad, err)
+        g_w += g_w2
+        return g_x, g_mid, g_xe, g_w, g_env, None, None, None, None, None, None
+
+
+def message_block(layer, x_norm, x_in, xe_p, wigner, env, csd, idx_i, idx_j, batch, graph):
+    """x_mid = x_in + scatter(SO(2) message of every edge) for one layer (fp32 in and out)."""
+    return _MessageBlockFn.apply(x_norm.contiguous(), x_in.contiguous(), xe_p, wigner, env, csd.contiguous(), layer,
+                                 idx_i, idx_j, batch, graph)
+
+
+# ---- initial edge-degree embedding -----------------------------------------------------------
+
+class _InitBlockFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xe_p, wigner, env, Z, batch, model, csd, graph, N):
+        E = xe_p.shape[0]
+        C = model.C
+        err = error_flag(xe_p.device)
+        rad, rsaved = radial_fwd(model.rad_init, xe_p, err)
+        x = _empty((N, 9, C), xe_p)
+        nat.call("fuma_init_scatter_fwd", ptr(rad), ptr(wigner), ptr(env), ptr(Z), ptr(batch), ptr(model.W_sphere),
+                 ptr(csd), ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(x), stream_of(xe_p))
+        ctx.save_for_backward(rad, wigner, env, *rsaved)
+        ctx.model, ctx.graph, ctx.N = model, graph, N
+        return x
+
+    @staticmethod
+    def backward(ctx, g_out):
+        rad, wigner, env, *rsaved = ctx.saved_tensors
+        model, graph, N = ctx.model, ctx.graph, ctx.N
+        g_out = g_out.contiguous()
+        E, C = rad.shape[0], model.C
+        err = error_flag(rad.device)
+        g_rad = torch.empty_like(rad)
+        g_w, g_env = _empty((E, 34), rad), _empty((E,), rad)
+        nat.call("fuma_init_scatter_bwd_f16x3", ptr(g_out), ptr(rad), ptr(wigner), ptr(env), ptr(graph.dst_row_ptr),
+                 ptr(graph.dst_col), N, E, C, ptr(g_rad), ptr(g_w), ptr(g_env), ptr(err), stream_of(rad))
+        g_xe = radial_bwd(model.rad_init, rsaved, g_rad, err)
+        return g_xe, g_w, g_env, None, None, None, None, None, None
+
+
+def init_block(model, xe_p, wigner, env, Z, batch, csd, graph, N):
+    """Initial node embedding from the split edge features (fp32 out)."""
+    return _InitBlockFn.apply(xe_p, wigner, env, Z.long().contiguous(), batch.long().contiguous(), model,
+                              csd.contiguous(), graph, int(N))
+
+
+def fusable(model) -> bool:
+    """True if every dense contraction of ``model`` (an ESCNInferenceModel in f16x3 mode) has
+    widths that are multiples of 16, so the fused blocks apply."""
+    lins = [model.rad_init.l1, model.rad_init.l2, model.rad_init.l3]
+    for lay in model.layers:
+        lins += [lay.rad.l1, lay.rad.l2, lay.rad.l3, lay.conv1_m0, lay.conv1_m1, lay.conv1_m2, lay.conv2_m0,
+                 lay.conv2_m1, lay.conv2_m2]
+    return all(l.mode == "f16x3" and l.N % 16 == 0 and l.K % 16 == 0 for l in lins) and model.C % 16 == 0

@@ -4,8 +4,8 @@ message-passing layers, driving the CUDA ops of :mod:`flash_uma_b200.ops`.
 Mirrors the reference ``model.py`` (``reorder_graph_morton`` :56-74, ``build_csr_cached``
 :28-44, ``Packed_eSCN_Layer`` :81-157, ``eSCN_Inference_Model`` :160-221). The dense
 contractions (radial MLP and SO(2) convolutions, ``F.linear`` / cuBLAS in the reference)
-run on this library's tcgen05 tensor-core GEMM (:class:`~flash_uma_b200.linear.FrozenLinear`),
-3xTF32 by default (``FUMA_GEMM=tf32`` selects single-pass TF32).
+run on this library's tcgen05 tensor-core GEMMs (:class:`~flash_uma_b200.linear.FrozenLinear`),
+f16x3 by default (``FUMA_GEMM=tf32x3`` / ``tf32`` select the TF32 kernels).
 """
 from __future__ import annotations
 
@@ -15,7 +15,9 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import ops
+import os
+
+from . import fused, ops
 from .linear import FrozenLinear
 from .nodewise import balance_channels_batched
 
@@ -119,8 +121,13 @@ class PackedLayer(nn.Module):
             for p in m.parameters():
                 p.requires_grad_(False)
 
+    fused = False   # set by ESCNInferenceModel: x_edge is then the row-packed split of the edge features
+
     def forward(self, x_in, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch):
         x_norm = self.norm_1(x_in)
+        if self.fused:
+            x_mid = fused.message_block(self, x_norm, x_in, x_edge, wigner, env, csd_emb, idx_i, idx_j, batch, graph)
+            return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
         rad_out = self.rad(x_edge)
         X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch, graph=graph)
         Z0, Z1, Z2 = ops.fused_gating_split(self.conv1_m0(X0), self.conv1_m1(X1), self.conv1_m2(X2), self.C)
@@ -152,16 +159,37 @@ class ESCNInferenceModel(nn.Module):
             p.requires_grad_(False)
         self.charge_start, self.charge_end = off_bb.charge_channel_start, off_bb.charge_channel_end
         self.spin_start, self.spin_end = off_bb.spin_channel_start, off_bb.spin_channel_end
+        # f16x3 with GEMM widths that are multiples of 16: fused blocks on split operands
+        # (FUMA_FUSED=0 keeps the per-op path, for comparisons)
+        self.set_fused(os.environ.get("FUMA_FUSED", "1") != "0")
+
+    def set_fused(self, enable: bool) -> bool:
+        """Use the fused f16x3 blocks when possible (``enable``) or the per-op path; returns the mode."""
+        self.fused = bool(enable) and fused.fusable(self)
+        for lay in self.layers:
+            lay.fused = self.fused
+        return self.fused
+
+    def _linears(self):
+        return [m for m in self.modules() if isinstance(m, FrozenLinear)]
 
     # ---- stages (also driven one by one by the spatially partitioned model, partition.py) ----
     def build_graph(self, idx_i, idx_j, N):
         return build_graph_cached(idx_i, idx_j, N)
 
     def geometry(self, pos, Z, idx_i, idx_j, shifts, graph):
-        return ops.precompute_geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt, self.offset_g,
-                                       self.coeff_g, self.cutoff, graph=graph)
+        """(x_edge, wigner, env); in the fused mode x_edge comes back as its row-packed split."""
+        x_edge, wigner, env = ops.precompute_geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt,
+                                                      self.offset_g, self.coeff_g, self.cutoff, graph=graph)
+        if self.fused:
+            for lin in self._linears():
+                lin.prepare()
+            x_edge = fused.split_rows(x_edge)
+        return x_edge, wigner, env
 
     def init_embedding(self, x_edge, wigner, env, Z, batch, csd_emb, idx_j, graph, N):
+        if self.fused:
+            return fused.init_block(self, x_edge, wigner, env, Z, batch, csd_emb, graph, N)
         rad0 = self.rad_init(x_edge)
         return ops.init_node_scatter(rad0, wigner, env, Z, batch, self.W_sphere, csd_emb, idx_j, graph.dst_row_ptr,
                                      graph.dst_col, N)

@@ -136,6 +136,13 @@ class PartitionedModel:
     """Runs a stage-protocol model on this rank's part of one periodic system."""
 
     def __init__(self, model, plan: PartitionPlan, device, group=None):
+        charge = getattr(model, "charge_end", 0) > getattr(model, "charge_start", 0) or \
+            getattr(model, "charge_range", (0, 0))[1] > getattr(model, "charge_range", (0, 0))[0]
+        spin = getattr(model, "spin_end", 0) > getattr(model, "spin_start", 0) or \
+            getattr(model, "spin_range", (0, 0))[1] > getattr(model, "spin_range", (0, 0))[0]
+        if charge or spin:
+            raise NotImplementedError("charge/spin channel balancing needs per-system sums across ranks; "
+                                      "not supported by the partitioned model")
         self.model, self.plan, self.device, self.group = model, plan, device, group
         self.n_owned = int(plan.owned.shape[0])
         self.local_ids = torch.as_tensor(plan.local_ids, dtype=torch.long, device=device)

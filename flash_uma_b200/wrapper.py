@@ -17,6 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import linear
 from .model import ESCNInferenceModel
 
 
@@ -30,8 +31,10 @@ def validate_atoms_data(self, atoms, task_name):
 
 class ZeroAllocBackbone(nn.Module):
     def __init__(self, off_bb, dtype=torch.float32, gemm: str | None = None):
-        """``gemm``: "tf32x3" (default, fp32-level accuracy) or "tf32" (single pass, as the
-        reference runs with TF32 enabled); default from the FUMA_GEMM environment variable."""
+        """``gemm``: "f16x3" (default; fp16 tensor cores with fp32-level accuracy, inputs of the
+        dense layers inside the fp16 range), "tf32x3" (fp32-level accuracy, full fp32 range) or
+        "tf32" (single pass, as the reference runs with TF32 enabled); default from the
+        FUMA_GEMM environment variable."""
         super().__init__()
         lmax = getattr(off_bb, "lmax", None)
         if lmax is not None and lmax != 2:
@@ -74,6 +77,9 @@ class ZeroAllocBackbone(nn.Module):
         return F.silu(self.mix_csd(torch.cat((chg_emb, spin_emb), dim=1)))
 
     def forward(self, data):
+        # errors recorded by earlier GEMMs (pipeline timeouts, f16x3 range) surface here, one
+        # call late, without a synchronisation
+        linear.poll_errors()
         data.atomic_numbers = data.atomic_numbers.long()
         data.atomic_numbers_full = data.atomic_numbers
         data.batch_full = data.batch
@@ -92,4 +98,5 @@ class ZeroAllocBackbone(nn.Module):
             shifts = torch.einsum("ij,ijk->ik", data.cell_offsets.to(cell_per_edge.dtype), cell_per_edge)
         x_node = self.ce(pos=data.pos, Z=data.atomic_numbers, batch=data.batch, edge_index=data.edge_index,
                          shifts=shifts, csd_emb=csd.float(), charge=data.charge, spin=data.spin, natoms=data.natoms)
+        linear.snapshot_errors()
         return {"node_embedding": x_node, "batch": data.batch}

@@ -129,6 +129,66 @@ int fuma_linear(const float* A, int64_t lda, const float* W_hi, const float* W_l
                 int32_t N, int32_t K, int32_t split, float* C, int64_t ldc, int* err_flag, void* stream);
 /* hi = x rounded to nearest TF32, lo = (x - hi) rounded to nearest TF32 (3xTF32 weight split). */
 int fuma_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream);
+/* Same contraction as fuma_linear (same reference call sites) in the f16x3 mode: fp16 tensor
+ * cores with fp32-level accuracy. Both operands are split as x = hi + lo * 2^-11 with
+ * hi = fp16(x), lo = fp16((x - hi) * 2^11). The weight split (W_hi, W_lo: fp16 [N, ldw] of
+ * W * scale) comes from fuma_split_f16 and w_scale_inv = 1 / scale is applied in the epilogue.
+ * a_split == 0: A is fp32 [M, lda] and the kernel splits it in shared memory.
+ * a_split == 1: A is the row-packed split from fuma_split_rows_f16 (lda = its ldp, a multiple
+ *               of 8), the fast path: no conversion inside the GEMM.
+ * K a multiple of 4, ldw >= K a multiple of 8. err_flag additionally receives 16 when an
+ * activation is finite in fp32 but beyond the fp16 range (|x| >= 65520); use fuma_linear for
+ * such data. */
+int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* W_hi, const void* W_lo, int64_t ldw,
+                      float w_scale_inv, const float* bias, int64_t M, int32_t N, int32_t K, float* C, int64_t ldc,
+                      int* err_flag, void* stream);
+/* Row-packed f16x3 split of an activation matrix x [M, K] (rows lda floats apart) into out,
+ * whose row r spans 4 * ldp bytes: fp16 hi values of x[r, :K] at byte 0, the scaled fp16 lo
+ * values at byte 2 * ldp (the same footprint as fp32 [M, ldp]). ldp >= K, a multiple of 8.
+ * err_flag receives 16 on an out-of-range value. */
+int fuma_split_rows_f16(const float* x, int64_t lda, int64_t M, int32_t K, void* out, int64_t ldp, int* err_flag,
+                        void* stream);
+/* hi = fp16_rn(x * scale), lo = fp16_rn((x * scale - hi) * 2^11), n elements (f16x3 weight split). */
+int fuma_split_f16(const float* x, int64_t n, float scale, void* hi, void* lo, void* stream);
+
+/* ---- split-output variants for the f16x3 GEMM -----------------------------------------------
+ * No counterpart in the reference (its GEMM inputs are plain fp32 tensors). Each takes the
+ * arguments of the entry point without the suffix plus err_flag, and writes the outputs that
+ * feed a dense contraction in the row-packed f16x3 split layout of fuma_split_rows_f16
+ * (ldp = the output's row width) instead of fp32, so fuma_linear_f16x3 (a_split = 1) reads
+ * them without a conversion pass:
+ *   ln_silu_fwd: out          ln_silu_bwd: g_x              gather_fwd: X_m0, X_m1, X_m2
+ *   gather_bwd: g_rad         gating_fwd: Z_m0, Z_m1, Z_m2  gating_bwd: g_Y_m0, g_Y_m1, g_Y_m2
+ *   rotate_scatter_bwd: g_Z_m0, g_Z_m1, g_Z_m2              init_scatter_bwd: g_rad
+ * All other outputs are unchanged. C (D for ln_silu) must be a multiple of 8. err_flag (device
+ * int, may be NULL) receives 16 if a finite value is at or beyond the fp16 limit (65520). */
+int fuma_ln_silu_fwd_f16x3(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
+                           float* out, float* mean, float* rstd, int* err_flag, void* stream);
+int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta, const float* mean,
+                           const float* rstd, const float* g_out, int64_t M, int32_t D, float* g_x, int* err_flag,
+                           void* stream);
+int fuma_gather_fwd_f16x3(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
+                          const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
+                          float* X_m0, float* X_m1, float* X_m2, int* err_flag, void* stream);
+int fuma_gather_bwd_f16x3(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
+                          const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
+                          const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
+                          const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
+                          float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
+                          int* err_flag, void* stream);
+int fuma_gating_fwd_f16x3(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
+                          float* Z_m1, float* Z_m2, int* err_flag, void* stream);
+int fuma_gating_bwd_f16x3(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
+                          const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
+                          float* g_Y_m2, int* err_flag, void* stream);
+int fuma_rotate_scatter_bwd_f16x3(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
+                                  const float* wigner, const float* env, const int32_t* row_ptr,
+                                  const int32_t* col_idx, int64_t N, int64_t E, int32_t C, float* g_Z_m0,
+                                  float* g_Z_m1, float* g_Z_m2, float* g_wigner, float* g_env, int* err_flag,
+                                  void* stream);
+int fuma_init_scatter_bwd_f16x3(const float* g_out, const float* rad, const float* wigner, const float* env,
+                                const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
+                                float* g_rad, float* g_wigner, float* g_env, int* err_flag, void* stream);
 
 /* ---- allocation-free gather backward -----------------------------------------------------
  * No counterpart in the reference. For callers that cannot let a library allocate device

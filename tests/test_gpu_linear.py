@@ -1,8 +1,10 @@
-"""tcgen05 GEMM (``fuma_linear``) vs fp64 torch matmul: forward and input gradient.
+"""tcgen05 GEMMs (``fuma_linear_f16x3``, ``fuma_linear``) vs fp64 torch matmul: forward and
+input gradient.
 
-3xTF32 bound: max error <= (2e-6 + 1e-8 K) of the output's max magnitude. The K term is
-the tensor core's fp32 accumulation, which truncates (~0.4 ulp toward zero per MMA
-instruction of K=8, measured on B200: 1.1e-6 at K=128, 8e-6 at K=1024). Single-pass
+f16x3 and 3xTF32 bound: max error <= (2e-6 + 1e-8 K) of the output's max magnitude. The K
+term is the tensor core's fp32 accumulation, which truncates (~0.4 ulp toward zero per MMA
+instruction, measured on B200 for 3xTF32: 1.1e-6 at K=128, 8e-6 at K=1024; f16x3 has one
+truncating add per K=16 on the full-size accumulator instead of three per K=8). Single-pass
 TF32 must be within TF32 rounding (2e-3)."""
 import pytest
 import torch
@@ -29,10 +31,11 @@ def _lin(N, K, bias, mode, seed):
     return W, b, FrozenLinear(W, b, mode=mode).to(DEV)
 
 
+@pytest.mark.parametrize("mode", ["f16x3", "tf32x3"])
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_linear_tf32x3_forward_backward(M, N, K):
+def test_linear_split_forward_backward(M, N, K, mode):
     from flash_uma_b200.linear import check_errors
-    W, b, lin = _lin(N, K, True, "tf32x3", M + N + K)
+    W, b, lin = _lin(N, K, True, mode, M + N + K)
     g = torch.Generator().manual_seed(K)
     x = torch.randn(M, K, generator=g)
     gy = torch.randn(M, N, generator=g)
@@ -58,8 +61,9 @@ def test_linear_tf32(M, N, K):
     assert err >= 1e-7   # it really is a reduced-precision product
 
 
-def test_linear_strided_input_and_empty():
-    W, b, lin = _lin(128, 64, True, "tf32x3", 3)
+@pytest.mark.parametrize("mode", ["f16x3", "tf32x3"])
+def test_linear_strided_input_and_empty(mode):
+    W, b, lin = _lin(128, 64, True, mode, 3)
     x = torch.randn(300, 320, generator=torch.Generator().manual_seed(2))
     xs = x.to(DEV)[:, :64]                      # row stride 320, view of a wider tensor
     y = lin(xs)
@@ -68,7 +72,49 @@ def test_linear_strided_input_and_empty():
     assert lin(torch.empty(0, 64, device=DEV)).shape == (0, 128)
 
 
-def test_linear_deterministic():
-    W, b, lin = _lin(512, 1024, False, "tf32x3", 4)
+@pytest.mark.parametrize("mode", ["f16x3", "tf32x3"])
+def test_linear_deterministic(mode):
+    W, b, lin = _lin(512, 1024, False, mode, 4)
     x = torch.randn(5000, 1024, device=DEV)
     assert torch.equal(lin(x), lin(x))
+
+
+def test_f16x3_wide_dynamic_range():
+    """Activations across eight decades, and weights far beyond the fp16 range (taken care of by
+    the power-of-two weight scale), keep fp32-level relative accuracy row by row. Below ~1e-4
+    the split has an absolute floor instead (2^-36 per activation, from fp16 subnormals in the
+    scaled residual), checked on rows down to 1e-9."""
+    from flash_uma_b200.linear import FrozenLinear, check_errors
+    g = torch.Generator().manual_seed(9)
+    K = 512
+    W = torch.randn(256, K, generator=g) * 1e5
+    scales = torch.cat([torch.logspace(-4, 4, 600), torch.logspace(-9, -4, 100)])
+    x = torch.randn(700, K, generator=g) * scales[:, None]
+    lin = FrozenLinear(W, None, mode="f16x3").to(DEV)
+    y = lin(x.to(DEV))
+    torch.cuda.synchronize()
+    check_errors()
+    y_ref = x.double() @ W.double().t()
+    err = (y.cpu().double() - y_ref).abs().max(1).values
+    rel = err / y_ref.abs().max(1).values
+    assert rel[:600].max() <= tol(K)
+    floor = K * 2.0 ** -36 * W.abs().max().item()
+    assert (err[600:] <= tol(K) * y_ref[600:].abs().max(1).values + floor).all()
+
+
+def test_f16x3_out_of_range_input_is_reported():
+    """A finite activation beyond the fp16 range cannot be split: the kernel records it and
+    the error check raises (the tf32x3 mode handles such data)."""
+    from flash_uma_b200.linear import FrozenLinear, check_errors, poll_errors, snapshot_errors
+    W = torch.randn(128, 64, generator=torch.Generator().manual_seed(5))
+    lin = FrozenLinear(W, None, mode="f16x3").to(DEV)
+    x = torch.randn(300, 64, device=DEV)
+    x[17, 3] = 1.0e5
+    lin(x)
+    snapshot_errors()
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="fp16 range"):
+        poll_errors()
+    check_errors()                       # the flag was cleared by the raise
+    lin(torch.randn(300, 64, device=DEV))
+    check_errors()

@@ -24,7 +24,7 @@ def _no_tf32():
     torch.backends.cuda.matmul.allow_tf32 = old
 
 
-def _run(systems, C, L, B, stress=True, seed=0):
+def _run(systems, C, L, B, stress=True, seed=0, gemm=None, fused=True):
     from flash_uma_b200.predict import Predictor
     from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
     from flash_uma_b200.systems import to_graph
@@ -33,7 +33,8 @@ def _run(systems, C, L, B, stress=True, seed=0):
     off = SyntheticESCNMDBackbone(num_layers=L, sphere_channels=C, hidden_channels=C, num_distance_basis=B,
                                   seed=seed, stress=stress).to(DEV)
     head = make_energy_head(C, C, seed=1).to(DEV)
-    bb = ZeroAllocBackbone(off)
+    bb = ZeroAllocBackbone(off, gemm=gemm)
+    bb.ce.set_fused(fused)
     return data, Predictor(bb, head)(data.to(DEV), forces=True, stress=stress)
 
 
@@ -47,10 +48,14 @@ def _check(res, g, stress=True):
                                    atol=1e-4 * max(1.0, np.abs(g["stress"]).max()))
 
 
-def test_config1_matches_reference():
+@pytest.mark.parametrize("gemm,fused", [("f16x3", True), ("f16x3", False), ("tf32x3", False)])
+def test_config1_matches_reference(gemm, fused):
+    """Every dense-contraction path: fused f16x3 blocks (the default), f16x3 per op, 3xTF32."""
     from flash_uma_b200.systems import config1_system
     g = dict(np.load(os.path.join(GOLD, "e2e_config1.npz")))
-    data, res = _run([config1_system()], int(g["C"]), int(g["layers"]), int(g["B"]))
+    data, res = _run([config1_system()], int(g["C"]), int(g["layers"]), int(g["B"]), gemm=gemm, fused=fused)
+    from flash_uma_b200.linear import check_errors
+    check_errors()
     np.testing.assert_array_equal(data.edge_index.numpy(), g["edge_index"])
     _check(res, g)
     np.testing.assert_allclose(res["node_embedding"].cpu().numpy(), g["node_embedding"], atol=2e-4, rtol=1e-4)
