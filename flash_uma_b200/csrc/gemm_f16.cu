@@ -60,7 +60,10 @@ struct F16Smem {
   static constexpr int kA16 = kBM * kBK * 2;   // 8 KB fp16 A half, 64-byte swizzle
   static constexpr int kW16 = BN * kBK * 2;    // fp16 W half, 64-byte swizzle
   static constexpr int kStage = kRaw + 2 * kA16 + 2 * kW16;
-  static constexpr int kBytes = STAGES * kStage + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+  // epilogue staging for the TMA store: per epilogue warp two [32 rows x 32 fp32] boxes
+  static constexpr bool kTmaStore = BN >= 32;
+  static constexpr int kStaging = kTmaStore ? 4 * 2 * 4096 : 0;
+  static constexpr int kBytes = STAGES * kStage + kStaging + 1024 /*barriers*/ + 1024 /*alignment slack*/;
   static_assert(kBytes <= 227 * 1024, "shared memory plan exceeds 227 KB");
   static_assert(kW16 % 512 == 0, "fp16 tiles must stay aligned to the 512-byte swizzle atom");
 };
@@ -91,6 +94,25 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b,
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// TMA tile store shared -> global (bulk async-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -106,13 +128,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
                                                                  const __grid_constant__ CUtensorMap tmAl,
                                                                  const __grid_constant__ CUtensorMap tmWh,
                                                                  const __grid_constant__ CUtensorMap tmWl,
+                                                                 const __grid_constant__ CUtensorMap tmC,
                                                                  float* __restrict__ C, const float* __restrict__ bias,
                                                                  float w_scale_inv, int M, int N, int K, int64_t ldc,
                                                                  int* err) {
   using L = F16Smem<BN, STAGES, kPre>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStage);
+  uint8_t* smem_c = smem + STAGES * L::kStage;   // epilogue staging (TMA store path)
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem_c + L::kStaging);
   uint64_t* bar_split = bar_full + STAGES;
   uint64_t* bar_empty = bar_split + STAGES;
   uint64_t* bar_acc_full = bar_empty + STAGES;   // [2]
@@ -264,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
   } else {
     // ---------------- epilogue (warps 6-9)
     const int q = warp & 3;
-    int lt = 0;
+    int lt = 0, nbox = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
       const int b = lt & 1;
       bool ok = mbar_wait(&bar_acc_full[b], (lt >> 1) & 1, abort_flag, err, kErrWaitAcc);
@@ -272,30 +296,70 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int m0 = (tile / num_n) * kBM, n0 = (tile % num_n) * BN;
-      const int row = m0 + q * 32 + lane;
       const uint32_t taddr = tmem + (uint32_t)(b * kBufCols) + ((uint32_t)(q * 32) << 16);
+      if constexpr (L::kTmaStore) {
+        // 32-column chunks, lane = row of this warp's 32-row quadrant. The row's 32 results go
+        // to a [32 x 32] fp32 staging box (128-byte swizzle: 16-byte chunk j of row r at
+        // j ^ (r & 7), conflict-free) that one TMA store writes out; rows beyond M are clipped
+        // by the tensor map. Two boxes per warp alternate, so the next chunk's TMEM loads and
+        // arithmetic overlap the previous store.
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t rm[16], rc[16];
-        tmem_ld16(taddr + (uint32_t)c0, rm);
-        tmem_ld16(taddr + (uint32_t)(BN + c0), rc);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row < M) {
-          float* out = C + (int64_t)row * ldc + n0 + c0;
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t rm[32], rc[32];
+          tmem_ld32(taddr + (uint32_t)c0, rm);
+          tmem_ld32(taddr + (uint32_t)(BN + c0), rc);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          uint8_t* box = smem_c + (q * 2 + (nbox & 1)) * 4096;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
 #pragma unroll
-          for (int jj = 0; jj < 16; jj += 4) {
+          for (int jj = 0; jj < 8; ++jj) {
             float o[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              o[u] = fmaf(__uint_as_float(rc[jj + u]), kLoScaleInv, __uint_as_float(rm[jj + u])) * w_scale_inv;
+              o[u] = fmaf(__uint_as_float(rc[4 * jj + u]), kLoScaleInv, __uint_as_float(rm[4 * jj + u])) * w_scale_inv;
             float4 v = make_float4(o[0], o[1], o[2], o[3]);
-            if (bias) v = v + ld4_keep(bias + n0 + c0 + jj);
-            st4(out + jj, v);
+            if (bias) v = v + ld4_keep(bias + n0 + c0 + 4 * jj);
+            *reinterpret_cast<float4*>(box + lane * 128 + ((jj ^ (lane & 7)) << 4)) = v;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, box, n0 + c0, m0 + q * 32);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          ++nbox;
+        }
+      } else {
+        const int row = m0 + q * 32 + lane;
+  #pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t rm[16], rc[16];
+          tmem_ld16(taddr + (uint32_t)c0, rm);
+          tmem_ld16(taddr + (uint32_t)(BN + c0), rc);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (row < M) {
+            float* out = C + (int64_t)row * ldc + n0 + c0;
+  #pragma unroll
+            for (int jj = 0; jj < 16; jj += 4) {
+              float o[4];
+  #pragma unroll
+              for (int u = 0; u < 4; ++u)
+                o[u] = fmaf(__uint_as_float(rc[jj + u]), kLoScaleInv, __uint_as_float(rm[jj + u])) * w_scale_inv;
+              float4 v = make_float4(o[0], o[1], o[2], o[3]);
+              if (bias) v = v + ld4_keep(bias + n0 + c0 + jj);
+              st4(out + jj, v);
+            }
           }
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&bar_acc_empty[b]);
+    }
+    if constexpr (L::kTmaStore) {
+      // the staging boxes must stay alive (and the results land) before the CTA exits
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      __syncwarp();
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -310,7 +374,7 @@ namespace {
 
 template <int BN, int STAGES, bool kPre>
 cudaError_t launch_f16(const CUtensorMap& a, const CUtensorMap& al, const CUtensorMap& wh, const CUtensorMap& wl,
-                       float* C, const float* bias, float w_scale_inv, int M, int N, int K, int64_t ldc, int* err,
+                       const CUtensorMap& mc, float* C, const float* bias, float w_scale_inv, int M, int N, int K, int64_t ldc, int* err,
                        cudaStream_t s) {
   using L = F16Smem<BN, STAGES, kPre>;
   auto kern = gemm_f16x3_kernel<BN, STAGES, kPre>;
@@ -324,19 +388,19 @@ cudaError_t launch_f16(const CUtensorMap& a, const CUtensorMap& al, const CUtens
   }
   const int tiles = ((M + kBM - 1) / kBM) * (N / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, kThreads, L::kBytes, s>>>(a, al, wh, wl, C, bias, w_scale_inv, M, N, K, ldc, err);
+  kern<<<grid, kThreads, L::kBytes, s>>>(a, al, wh, wl, mc, C, bias, w_scale_inv, M, N, K, ldc, err);
   return cudaGetLastError();
 }
 
 template <bool kPre>
 cudaError_t launch_bn(int BN, const CUtensorMap& a, const CUtensorMap& al, const CUtensorMap& wh,
-                      const CUtensorMap& wl, float* C, const float* bias, float inv, int M, int N, int K,
+                      const CUtensorMap& wl, const CUtensorMap& mc, float* C, const float* bias, float inv, int M, int N, int K,
                       int64_t ldc, int* err, cudaStream_t s) {
   switch (BN) {
-    case 128: return launch_f16<128, kPre ? 6 : 4, kPre>(a, al, wh, wl, C, bias, inv, M, N, K, ldc, err, s);
-    case 64: return launch_f16<64, kPre ? 8 : 5, kPre>(a, al, wh, wl, C, bias, inv, M, N, K, ldc, err, s);
-    case 32: return launch_f16<32, kPre ? 8 : 6, kPre>(a, al, wh, wl, C, bias, inv, M, N, K, ldc, err, s);
-    default: return launch_f16<16, kPre ? 8 : 6, kPre>(a, al, wh, wl, C, bias, inv, M, N, K, ldc, err, s);
+    case 128: return launch_f16<128, kPre ? 5 : 4, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 64: return launch_f16<64, kPre ? 6 : 4, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 32: return launch_f16<32, kPre ? 8 : 5, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    default: return launch_f16<16, kPre ? 8 : 6, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
   }
 }
 
@@ -365,9 +429,15 @@ int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_h
     return -1;
   if (!make_map_t(&ml, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, W_lo, N, K, ldw * 2, kBK, BN, CU_TENSOR_MAP_SWIZZLE_64B))
     return -1;
+  // output: fp32 [M, N] rows ldc apart, [32 x 32] boxes with 128-byte swizzle (unused for BN = 16)
+  CUtensorMap mc = ma;
+  if (BN >= 32 &&
+      !make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, ldc * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+    return -1;
   const int m = (int)M;
-  const cudaError_t st = a_split ? launch_bn<true>(BN, ma, mal, mh, ml, C, bias, w_scale_inv, m, N, K, ldc, err, s)
-                                 : launch_bn<false>(BN, ma, mal, mh, ml, C, bias, w_scale_inv, m, N, K, ldc, err, s);
+  const cudaError_t st =
+      a_split ? launch_bn<true>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s)
+              : launch_bn<false>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s);
   return st == cudaSuccess ? 0 : (int)st;
 }
 
