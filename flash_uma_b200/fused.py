@@ -29,25 +29,59 @@ def _empty(shape, like):
     return torch.empty(shape, device=like.device, dtype=torch.float32)
 
 
-class _SplitRowsFn(torch.autograd.Function):
-    """x [M, K] fp32 -> its row-packed split (same shape, fp32-typed); the gradient passes through."""
+class _GeometryFn(torch.autograd.Function):
+    """Edge geometry for the fused blocks: the edge features come back as their row-packed
+    split (a constant for autograd) plus ``x_gauss``, the Gaussian-basis columns [E, B] that
+    carry the only position dependence of the edge features. The blocks return gradients for
+    ``x_gauss`` alone: the embedding columns depend on the atomic numbers only."""
 
     @staticmethod
-    def forward(ctx, x):
-        M, K = x.shape
-        out = _empty((M, K), x)
-        nat.call("fuma_split_rows_f16", ptr(x), x.stride(0), M, K, ptr(out), K, ptr(error_flag(x.device)),
-                 stream_of(x))
-        return out
+    def forward(ctx, pos, Z, idx_i, idx_j, shifts, W_src, W_tgt, offset_g, coeff_g, cutoff, graph):
+        N, E = pos.shape[0], idx_i.shape[0]
+        B, C = offset_g.shape[0], W_src.shape[1]
+        x_edge = _empty((E, B + 2 * C), pos)
+        wigner, env = _empty((E, 34), pos), _empty((E,), pos)
+        s = stream_of(pos)
+        nat.call("fuma_geometry_fwd", ptr(pos), ptr(Z), ptr(idx_i), ptr(idx_j), ptr(shifts), ptr(W_src), ptr(W_tgt),
+                 ptr(offset_g), float(coeff_g), float(cutoff), N, E, B, C, ptr(x_edge), ptr(wigner), ptr(env), s)
+        xe_p = _empty((E, B + 2 * C), pos)
+        nat.call("fuma_split_rows_f16", ptr(x_edge), B + 2 * C, E, B + 2 * C, ptr(xe_p), B + 2 * C,
+                 ptr(error_flag(pos.device)), s)
+        ctx.mark_non_differentiable(xe_p)
+        ctx.save_for_backward(pos, idx_i, idx_j, shifts, offset_g)
+        ctx.coeff_g, ctx.cutoff, ctx.graph = float(coeff_g), float(cutoff), graph
+        return xe_p, x_edge[:, :B], wigner, env
 
     @staticmethod
-    def backward(ctx, g):
-        return g
+    def backward(ctx, g_xe_p, g_gauss, g_wigner, g_env):
+        pos, idx_i, idx_j, shifts, offset_g = ctx.saved_tensors
+        E, B, N = idx_i.shape[0], offset_g.shape[0], pos.shape[0]
+        g_gauss = g_gauss.contiguous() if g_gauss is not None else _empty((E, B), pos).zero_()
+        g_wigner = g_wigner.contiguous() if g_wigner is not None else _empty((E, 34), pos).zero_()
+        g_env = g_env.contiguous() if g_env is not None else _empty((E,), pos).zero_()
+        g_vec = _empty((E, 3), pos)
+        s = stream_of(pos)
+        nat.call("fuma_geometry_bwd", ptr(pos), ptr(idx_i), ptr(idx_j), ptr(shifts), ptr(offset_g), ctx.coeff_g,
+                 ctx.cutoff, ptr(g_gauss), g_gauss.shape[1], ptr(g_wigner), ptr(g_env), E, B, ptr(g_vec), s)
+        g_pos = None
+        if ctx.needs_input_grad[0]:
+            g = ctx.graph
+            g_pos = torch.empty_like(pos)
+            nat.call("fuma_edge_vec_to_nodes", ptr(g.src_row_ptr), ptr(g.src_col), ptr(g.dst_row_ptr), ptr(g.dst_col),
+                     ptr(g_vec), N, E, ptr(g_pos), s)
+        g_shifts = g_vec if ctx.needs_input_grad[4] else None
+        return g_pos, None, None, None, g_shifts, None, None, None, None, None, None
 
 
-def split_rows(x: torch.Tensor) -> torch.Tensor:
-    """Differentiable row-packed split of a contiguous [M, K] fp32 tensor (K a multiple of 8)."""
-    return _SplitRowsFn.apply(x.contiguous())
+def geometry(pos, Z, idx_i, idx_j, shifts, W_src, W_tgt, offset_g, coeff_g, cutoff, graph):
+    """(edge features as ((split [E, B+2C]), x_gauss [E, B]), wigner [E, 34], env [E]) for the
+    fused blocks; same kernels and arguments as ``ops.precompute_geometry``."""
+    nat.require_cuda(pos, Z, idx_i, idx_j, shifts, W_src, W_tgt, offset_g)
+    f32 = lambda t: t.float().contiguous()
+    i64 = lambda t: t.long().contiguous()
+    xe_p, x_gauss, wigner, env = _GeometryFn.apply(f32(pos), i64(Z), i64(idx_i), i64(idx_j), f32(shifts), f32(W_src),
+                                                   f32(W_tgt), f32(offset_g), coeff_g, cutoff, graph)
+    return (xe_p, x_gauss), wigner, env
 
 
 # ---- radial MLP on split operands ------------------------------------------------------------
@@ -91,14 +125,17 @@ def radial_bwd(rad, saved, g_out_p, err):
     del g_y2
     g_y1 = _ln_silu_bwd_split(y1, rad.g1, rad.be1, m1, r1, g_h1, err)
     del g_h1
-    return _gemm16(g_y1, rad.l1.wt16, None, g_y1.shape[1])
+    # only the Gaussian-basis columns of the edge features depend on positions: rows :B of W1^T
+    B = rad.n_gauss
+    hi, lo, inv = rad.l1.wt16
+    return _gemm16(g_y1, (hi[:B], lo[:B], inv), None, g_y1.shape[1])
 
 
 # ---- one message-passing block ---------------------------------------------------------------
 
 class _MessageBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_norm, x_in, xe_p, wigner, env, csd, layer, idx_i, idx_j, batch, graph):
+    def forward(ctx, x_norm, x_in, xe_p, x_gauss, wigner, env, csd, layer, idx_i, idx_j, batch, graph):
         N, _, C = x_in.shape
         E = idx_i.shape[0]
         err = error_flag(x_in.device)
@@ -162,20 +199,22 @@ class _MessageBlockFn(torch.autograd.Function):
         del gX0, gX1, gX2, scratch
         g_xe = radial_bwd(layer.rad, rsaved, g_rad, err)
         g_w += g_w2
-        return g_x, g_mid, g_xe, g_w, g_env, None, None, None, None, None, None
+        return g_x, g_mid, None, g_xe, g_w, g_env, None, None, None, None, None, None
 
 
-def message_block(layer, x_norm, x_in, xe_p, wigner, env, csd, idx_i, idx_j, batch, graph):
-    """x_mid = x_in + scatter(SO(2) message of every edge) for one layer (fp32 in and out)."""
-    return _MessageBlockFn.apply(x_norm.contiguous(), x_in.contiguous(), xe_p, wigner, env, csd.contiguous(), layer,
-                                 idx_i, idx_j, batch, graph)
+def message_block(layer, x_norm, x_in, xe, wigner, env, csd, idx_i, idx_j, batch, graph):
+    """x_mid = x_in + scatter(SO(2) message of every edge) for one layer (fp32 in and out);
+    ``xe`` = (split edge features, x_gauss) from :func:`geometry`."""
+    xe_p, x_gauss = xe
+    return _MessageBlockFn.apply(x_norm.contiguous(), x_in.contiguous(), xe_p, x_gauss, wigner, env,
+                                 csd.contiguous(), layer, idx_i, idx_j, batch, graph)
 
 
 # ---- initial edge-degree embedding -----------------------------------------------------------
 
 class _InitBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, xe_p, wigner, env, Z, batch, model, csd, graph, N):
+    def forward(ctx, xe_p, x_gauss, wigner, env, Z, batch, model, csd, graph, N):
         E = xe_p.shape[0]
         C = model.C
         err = error_flag(xe_p.device)
@@ -199,12 +238,13 @@ class _InitBlockFn(torch.autograd.Function):
         nat.call("fuma_init_scatter_bwd_f16x3", ptr(g_out), ptr(rad), ptr(wigner), ptr(env), ptr(graph.dst_row_ptr),
                  ptr(graph.dst_col), N, E, C, ptr(g_rad), ptr(g_w), ptr(g_env), ptr(err), stream_of(rad))
         g_xe = radial_bwd(model.rad_init, rsaved, g_rad, err)
-        return g_xe, g_w, g_env, None, None, None, None, None, None
+        return None, g_xe, g_w, g_env, None, None, None, None, None, None
 
 
-def init_block(model, xe_p, wigner, env, Z, batch, csd, graph, N):
+def init_block(model, xe, wigner, env, Z, batch, csd, graph, N):
     """Initial node embedding from the split edge features (fp32 out)."""
-    return _InitBlockFn.apply(xe_p, wigner, env, Z.long().contiguous(), batch.long().contiguous(), model,
+    xe_p, x_gauss = xe
+    return _InitBlockFn.apply(xe_p, x_gauss, wigner, env, Z.long().contiguous(), batch.long().contiguous(), model,
                               csd.contiguous(), graph, int(N))
 
 
@@ -215,4 +255,5 @@ def fusable(model) -> bool:
     for lay in model.layers:
         lins += [lay.rad.l1, lay.rad.l2, lay.rad.l3, lay.conv1_m0, lay.conv1_m1, lay.conv1_m2, lay.conv2_m0,
                  lay.conv2_m1, lay.conv2_m2]
-    return all(l.mode == "f16x3" and l.N % 16 == 0 and l.K % 16 == 0 for l in lins) and model.C % 16 == 0
+    return (all(l.mode == "f16x3" and l.N % 16 == 0 and l.K % 16 == 0 for l in lins) and model.C % 16 == 0
+            and model.B % 16 == 0)

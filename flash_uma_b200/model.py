@@ -154,6 +154,8 @@ class ESCNInferenceModel(nn.Module):
         self.register_buffer("W_tgt", g(off_bb.target_embedding.weight))
         self.rad_init = RadialMLP(off_bb.edge_degree_embedding.rad_func.net, mode)
         self.layers = nn.ModuleList([PackedLayer(b, self.C, mode) for b in off_bb.blocks])
+        for rad in [self.rad_init] + [lay.rad for lay in self.layers]:
+            rad.n_gauss = self.B   # leading edge-feature columns that depend on positions
         self.final_norm = off_bb.norm
         for p in self.final_norm.parameters():
             p.requires_grad_(False)
@@ -178,14 +180,15 @@ class ESCNInferenceModel(nn.Module):
         return build_graph_cached(idx_i, idx_j, N)
 
     def geometry(self, pos, Z, idx_i, idx_j, shifts, graph):
-        """(x_edge, wigner, env); in the fused mode x_edge comes back as its row-packed split."""
-        x_edge, wigner, env = ops.precompute_geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt,
-                                                      self.offset_g, self.coeff_g, self.cutoff, graph=graph)
+        """(x_edge, wigner, env); in the fused mode x_edge comes back as (its row-packed split,
+        its Gaussian-basis columns), see :func:`flash_uma_b200.fused.geometry`."""
         if self.fused:
             for lin in self._linears():
                 lin.prepare()
-            x_edge = fused.split_rows(x_edge)
-        return x_edge, wigner, env
+            return fused.geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt, self.offset_g, self.coeff_g,
+                                  self.cutoff, graph)
+        return ops.precompute_geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt, self.offset_g,
+                                       self.coeff_g, self.cutoff, graph=graph)
 
     def init_embedding(self, x_edge, wigner, env, Z, batch, csd_emb, idx_j, graph, N):
         if self.fused:

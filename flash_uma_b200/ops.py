@@ -42,10 +42,10 @@ class GraphCSR:
 
 
 def _csr(idx: torch.Tensor, N: int):
+    # stable sort + binary search of every row start: no device-to-host synchronisation
     order = torch.argsort(idx, stable=True)
-    counts = torch.bincount(idx, minlength=N)
-    row_ptr = torch.zeros(N + 1, dtype=torch.int32, device=idx.device)
-    row_ptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
+    bounds = torch.arange(N + 1, device=idx.device, dtype=idx.dtype)
+    row_ptr = torch.searchsorted(idx[order], bounds).to(torch.int32)
     return row_ptr, order.to(torch.int32)
 
 
