@@ -39,6 +39,8 @@ UNIT = "atom-steps/s"
 # algorithmic HBM bytes of one call of each entry point (fp32, minimum traffic: every
 # per-edge / per-node tensor read or written once)
 def alg_bytes(name, N, E, C, B, M_rows=None, D=None):
+    # the *_f16x3 variants move the same bytes (a split output has the fp32 footprint)
+    name = name[: -len("_f16x3")] if name.endswith("_f16x3") and name != "fuma_linear_f16x3" else name
     f = 4
     if name == "fuma_gather_fwd":
         return E * (f * 34 + f * 12 * C + 8 + f * 18 * C) + N * f * 9 * C
@@ -69,15 +71,18 @@ def alg_bytes(name, N, E, C, B, M_rows=None, D=None):
     return None
 
 
-# dense FLOPs of the model's GEMMs per edge and layer (forward; the input-gradient GEMMs of the
-# backward have the same count): radial 2*(K_in*H + H*H + H*12C), conv1 2*70C^2, conv2 2*29C^2
-def gemm_flops_per_step(E, C, B, L, H=None):
+# dense FLOPs of the model's GEMMs per edge and layer: radial 2*(K_in*H + H*H + H*12C), conv1
+# 2*70C^2, conv2 2*29C^2 in the forward; the input-gradient GEMMs of the backward have the same
+# count, except that with gauss_only the first radial layer's gradient covers only the B
+# Gaussian columns (the fused path: the embedding columns do not depend on positions)
+def gemm_flops_per_step(E, C, B, L, H=None, gauss_only=True):
     H = H or C
     rad_layer = 2 * ((B + 2 * C) * H + H * H + H * 12 * C)
     rad_init = 2 * ((B + 2 * C) * H + H * H + H * 3 * C)
     so2 = 2 * 70 * C * C + 2 * 29 * C * C
     fwd = E * (L * (rad_layer + so2) + rad_init)
-    return 2 * fwd
+    bwd = fwd - (E * (L + 1) * 2 * 2 * C * H if gauss_only else 0)
+    return fwd + bwd
 
 
 GEMM_OPS = ("fuma_linear_f16x3", "fuma_linear")
@@ -102,7 +107,7 @@ def gemm_summary(per_op, E, C, B, L, mode):
     ms = per_op.get(g["op"])
     if not ms:
         return None
-    flops = gemm_flops_per_step(E, C, B, L)
+    flops = gemm_flops_per_step(E, C, B, L, gauss_only=mode == "f16x3")
     return {"flops_per_step": flops, "ms_per_step": ms, "tflops_fp32_equiv": flops / (ms * 1e-3) / 1e12,
             "tflops_pipe": g["passes"] * flops / (ms * 1e-3) / 1e12, "pipe": g["pipe"], "passes": g["passes"]}
 
@@ -306,7 +311,8 @@ def run_flash(args, rank, world, device):
     if dominant in GEMM_OPS:
         # tensor-bound: tensor-pipe FLOPs per launch (3 products per fp32 product in the split modes)
         launches = probe.counts.get(dominant, 1) // K
-        flops_launch = gm["passes"] * gemm_flops_per_step(Ek, C, B, L) / max(1, launches)
+        flops = gemm_flops_per_step(Ek, C, B, L, gauss_only=args.gemm == "f16x3")
+        flops_launch = gm["passes"] * flops / max(1, launches)
         achieved = flops_launch / (avg_ms * 1e-3) / 1e12
         roof = {"kernel": gm["kernel"], "bound": "tensor", "achieved": achieved,
                 "peak": gm["peak"], "unit": "TFLOP/s", "frac": achieved / gm["peak"],
@@ -364,7 +370,10 @@ def run_micro(args, device):
     Geometry is computed once from the synthetic edge vectors (uniform directions, lengths
     U(0.8, 6) A) outside the timed region. Every C-ABI call is bracketed with CUDA events;
     prints per-kernel time, algorithmic bytes and fraction of the measured HBM / tensor peaks."""
-    from flash_uma_b200 import _native, ops
+    import functools
+
+    from flash_uma_b200 import _native, fused, ops
+    from flash_uma_b200.linear import FrozenLinear
     from flash_uma_b200.model import PackedLayer
     from flash_uma_b200.synthetic import SyntheticESCNMDBackbone
     from flash_uma_b200.systems import microbench_layer_inputs
@@ -379,15 +388,27 @@ def run_micro(args, device):
     batch = torch.zeros(N, dtype=torch.long, device=device)
     offset = torch.linspace(0, 6.0, B, device=device)
     coeff = float(-0.5 / (2.0 * (6.0 / (B - 1))) ** 2)
-    xe, wig, env = ops.precompute_geometry(inp["pos"].to(device), Z, ii, jj, inp["shifts"].to(device),
-                                           off.source_embedding.weight.detach(), off.target_embedding.weight.detach(),
-                                           offset, coeff, 6.0, graph=graph)
+    # f16x3: the production path, one fused message block (split operands, pre-split GEMMs)
+    use_fused = args.gemm == "f16x3"
+    geom = fused.geometry if use_fused else functools.partial(ops.precompute_geometry, graph=graph)
+    geom_args = (inp["pos"].to(device), Z, ii, jj, inp["shifts"].to(device), off.source_embedding.weight.detach(),
+                 off.target_embedding.weight.detach(), offset, coeff, 6.0) + ((graph,) if use_fused else ())
+    if use_fused:
+        layer.rad.n_gauss = B
+        for lin in layer.modules():
+            if isinstance(lin, FrozenLinear):
+                lin.prepare()
+    xe, wig, env = geom(*geom_args)
     csd = torch.randn(1, C, device=device)
     x0 = inp["x"].to(device)
     gout = torch.randn(N, 9, C, device=device)
 
     def step():
         x = x0.detach().requires_grad_(True)
+        if use_fused:
+            out = fused.message_block(layer, x, x, xe, wig, env, csd, ii, jj, batch, graph)
+            (gx,) = torch.autograd.grad(out, [x], gout)
+            return gx
         rad = layer.rad(xe)
         X0, X1, X2 = ops.gather_wigner_split(x, ii, jj, wig, rad, csd, batch, graph=graph)
         Z0, Z1, Z2 = ops.fused_gating_split(layer.conv1_m0(X0), layer.conv1_m1(X1), layer.conv1_m2(X2), C)
@@ -428,7 +449,7 @@ def run_micro(args, device):
         H = C
         so2 = 2 * 70 * C * C + 2 * 29 * C * C
         rad = 2 * ((B + 2 * C) * H + H * H + H * 12 * C)
-        flops = 2 * E * (so2 + rad)
+        flops = 2 * E * (so2 + rad) - (E * 2 * 2 * C * H if use_fused else 0)
         ms = kernels[gm["op"]]["ms_per_step"]
         tf = gm["passes"] * flops / (ms * 1e-3) / 1e12
         kernels[gm["op"]].update(flops_per_step=flops, passes=gm["passes"], pipe=gm["pipe"], tflops_pipe=tf,

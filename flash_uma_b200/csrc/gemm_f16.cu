@@ -34,6 +34,7 @@
 //   warps 6-9   epilogue of the other accumulator pair while the next tile's K loop runs.
 // Every mbarrier wait is bounded (the error protocol of gemm.cu).
 #include <cstdio>
+#include <cstdlib>
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -156,7 +157,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
   auto stage_Wh = [&](int s) { return smem + s * L::kStage + L::kRaw + 2 * L::kA16; };
   auto stage_Wl = [&](int s) { return smem + s * L::kStage + L::kRaw + 2 * L::kA16 + L::kW16; };
   constexpr uint32_t kBufCols = 2 * BN;            // main + cross of one buffer
-  constexpr uint32_t kTmemCols = 2 * kBufCols;     // double buffered: 64..512, a power of 2
+  constexpr int kAcc = BN <= 128 ? 2 : 1;          // accumulator buffers (BN = 256 fills TMEM with one)
+  constexpr uint32_t kTmemCols = kAcc * kBufCols;  // 64..512, a power of 2
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -218,8 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
       int it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++lt) {
-        const int b = lt & 1;
-        if (lt >= 2 && !mbar_wait(&bar_acc_empty[b], ((lt >> 1) - 1) & 1, abort_flag, err, kErrWaitAccEmpty)) break;
+        const int b = kAcc == 2 ? (lt & 1) : 0;
+        if (lt >= kAcc && !mbar_wait(&bar_acc_empty[b], ((lt / kAcc) - 1) & 1, abort_flag, err, kErrWaitAccEmpty))
+          break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t acc_main = tmem + (uint32_t)(b * kBufCols);
         const uint32_t acc_cross = acc_main + (uint32_t)BN;
@@ -290,8 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
     const int q = warp & 3;
     int lt = 0, nbox = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
-      const int b = lt & 1;
-      bool ok = mbar_wait(&bar_acc_full[b], (lt >> 1) & 1, abort_flag, err, kErrWaitAcc);
+      const int b = kAcc == 2 ? (lt & 1) : 0;
+      bool ok = mbar_wait(&bar_acc_full[b], (lt / kAcc) & 1, abort_flag, err, kErrWaitAcc);
       ok = __all_sync(kFull, ok && !*abort_flag);
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -397,6 +400,7 @@ cudaError_t launch_bn(int BN, const CUtensorMap& a, const CUtensorMap& al, const
                       const CUtensorMap& wl, const CUtensorMap& mc, float* C, const float* bias, float inv, int M, int N, int K,
                       int64_t ldc, int* err, cudaStream_t s) {
   switch (BN) {
+    case 256: return launch_f16<256, kPre ? 4 : 3, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
     case 128: return launch_f16<128, kPre ? 5 : 4, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
     case 64: return launch_f16<64, kPre ? 6 : 4, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
     case 32: return launch_f16<32, kPre ? 8 : 5, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
@@ -406,10 +410,21 @@ cudaError_t launch_bn(int BN, const CUtensorMap& a, const CUtensorMap& al, const
 
 }  // namespace
 
+// 256-wide tiles for N % 256 == 0 and K >= this. They hold one TMEM accumulator pair (the
+// epilogue is not overlapped with the next tile) but halve the A-operand traffic per FLOP:
+// measured on B200 with pre-split A, M = 120,000: K = 1024, N = 512: 0.356 -> 0.287 ms;
+// K = 512, N = 512: 0.189 -> 0.156 ms; K = 256, N = 256: 0.059 -> 0.066 ms (slower).
+// FUMA_BN256_MIN_K overrides the default.
+const int g_bn256_min_k = [] {
+  const char* e = getenv("FUMA_BN256_MIN_K");
+  return e ? atoi(e) : 512;
+}();
+
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,
                       float w_scale_inv, const float* bias, float* C, int64_t ldc, int64_t M, int N, int K, int* err,
                       cudaStream_t s) {
-  const int BN = (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : (N % 32 == 0) ? 32 : 16;
+  const int BN = (N % 256 == 0 && K >= g_bn256_min_k) ? 256
+                 : (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : (N % 32 == 0) ? 32 : 16;
   CUtensorMap ma, mal, mh, ml;
   if (a_split) {
     // row-packed split operand: row r holds K fp16 hi values at byte 4*lda*r and the K lo values
