@@ -209,12 +209,12 @@ static int gather_bwd_impl(const float* g_X_m0, const float* g_X_m1, const float
   REQUIRE(x && csd && batch && dst_row_ptr && src_row_ptr && g_x, "gather_bwd: null pointer");
   REQUIRE(E == 0 || (idx_i && wigner && rad && dst_col && src_col && g_wigner && g_rad && g_X_m0 && g_X_m1 && g_X_m2),
           "gather_bwd: null per-edge pointer");
-  REQUIRE(E == 0 || (scratch && scratch_floats >= E * 9 * (int64_t)C),
-          "gather_bwd: scratch must hold E*9*C = %lld floats", (long long)(E * 9 * (int64_t)C));
+  (void)scratch;
+  (void)scratch_floats;   // unused since the backward runs as two passes (source / target side)
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(csd, "csd"); REQUIRE_ALIGNED(g_x, "g_x");
   if (E > 0) {
     REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(g_rad, "g_rad"); REQUIRE_ALIGNED(g_X_m0, "g_X_m0");
-    REQUIRE_ALIGNED(g_X_m1, "g_X_m1"); REQUIRE_ALIGNED(g_X_m2, "g_X_m2"); REQUIRE_ALIGNED(scratch, "scratch");
+    REQUIRE_ALIGNED(g_X_m1, "g_X_m1"); REQUIRE_ALIGNED(g_X_m2, "g_X_m2");
   }
   BIND(x);
   launch_gather_bwd(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,

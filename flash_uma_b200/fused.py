@@ -191,12 +191,10 @@ class _MessageBlockFn(torch.autograd.Function):
         g_x = torch.empty_like(x_norm)
         g_w2 = _empty((E, 34), rad)
         g_rad = torch.empty_like(rad)
-        scratch = _empty((E * 9 * C,), rad)
         nat.call("fuma_gather_bwd_f16x3", ptr(gX0), ptr(gX1), ptr(gX2), ptr(x_norm), ptr(idx_i), ptr(wigner), ptr(rad),
                  ptr(csd), ptr(batch), ptr(graph.dst_row_ptr), ptr(graph.dst_col), ptr(graph.src_row_ptr),
-                 ptr(graph.src_col), N, E, C, ptr(scratch), scratch.numel(), ptr(g_x), ptr(g_w2), ptr(g_rad),
-                 ptr(err), s)
-        del gX0, gX1, gX2, scratch
+                 ptr(graph.src_col), N, E, C, None, 0, ptr(g_x), ptr(g_w2), ptr(g_rad), ptr(err), s)
+        del gX0, gX1, gX2
         g_xe = radial_bwd(layer.rad, rsaved, g_rad, err)
         g_w += g_w2
         return g_x, g_mid, None, g_xe, g_w, g_env, None, None, None, None, None, None

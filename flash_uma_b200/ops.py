@@ -181,10 +181,9 @@ class _GatherWignerSplit(torch.autograd.Function):
         g_x = torch.empty_like(x_in)
         g_w = torch.empty(E, 34, device=dev, dtype=torch.float32)
         g_r = torch.empty_like(rad_out)
-        scratch = torch.empty(E * 9 * C, device=dev, dtype=torch.float32)
         nat.call("fuma_gather_bwd", ptr(g0), ptr(g1), ptr(g2), ptr(x_in), ptr(idx_i), ptr(wigner), ptr(rad_out),
                  ptr(csd_emb), ptr(batch), ptr(g.dst_row_ptr), ptr(g.dst_col), ptr(g.src_row_ptr), ptr(g.src_col),
-                 N, E, C, ptr(scratch), scratch.numel(), ptr(g_x), ptr(g_w), ptr(g_r), stream_of(x_in))
+                 N, E, C, None, 0, ptr(g_x), ptr(g_w), ptr(g_r), stream_of(x_in))
         return g_x, None, None, g_w, g_r, None, None, None
 
 

@@ -75,8 +75,10 @@ int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, 
                     const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
                     float* X_m0, float* X_m1, float* X_m2, void* stream);
 /* Replaces GatherWignerSplit.backward (ops/gather.py:435-514) without atomics: needs the
- * destination CSR (dst_row_ptr[N+1], dst_col[E]) and source CSR of the same edges, and a
- * caller-provided scratch buffer of E*9*C floats. Writes g_x[N,9,C], g_wigner[E,34], g_rad[E,12C]. */
+ * destination CSR (dst_row_ptr[N+1], dst_col[E]) and source CSR of the same edges (a target-
+ * side pass over the first, a source-side pass over the second). Writes g_x[N,9,C],
+ * g_wigner[E,34], g_rad[E,12C]. scratch / scratch_floats are unused (may be NULL / 0); they
+ * stay in the signature for callers written against the earlier scratch-row version. */
 int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
                     const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
                     const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,

@@ -59,9 +59,9 @@ def test_invalid_arguments_rejected_before_any_launch(lib):
     g = lib.fuma_gather_bwd
     g.argtypes = _native._SIGS["fuma_gather_bwd"]
     g.restype = ctypes.c_int
-    # scratch too small is rejected
-    rc = g(*([1] * 13), 5, 7, 8, 1, 10, *([1] * 4))
-    assert rc == -1 and b"scratch" in lib.fuma_last_error()
+    # a misaligned per-edge pointer is rejected (the scratch arguments are unused: NULL / 0)
+    rc = g(*([16] * 3), 16, 16, 16, 16, 16, 16, 16, 16, 16, 16, 5, 7, 8, None, 0, 16, 16, 3, None)
+    assert rc == -2 and b"aligned" in lib.fuma_last_error()   # FUMA_E_ALIGN
 
 
 def test_ops_refuse_cpu_tensors():
