@@ -50,6 +50,33 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// One round of the recursive-halving warp reduction: lanes with bit OFF clear keep entries
+// [0, OFF), the others [OFF, 2 OFF) (moved down to [0, OFF)), each adding its partner's copy.
+template <int OFF, int NV>
+__device__ __forceinline__ void halve(float (&v)[NV], int lane) {
+  const bool upper = (lane & OFF) != 0;
+#pragma unroll
+  for (int k = 0; k < OFF; ++k) {
+    const float send = upper ? v[k] : v[k + OFF];
+    const float keep = upper ? v[k + OFF] : v[k];
+    v[k] = keep + __shfl_xor_sync(kFull, send, OFF);
+  }
+}
+
+// Warp reduction of NV per-lane partial sums (NV = 16 or 32): lane l receives the warp total
+// of v[l % NV], in NV - 1 (+1) shuffles instead of 5 per value.
+template <int NV>
+__device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
+  if constexpr (NV == 32) halve<16>(v, lane);
+  halve<8>(v, lane);
+  halve<4>(v, lane);
+  halve<2>(v, lane);
+  halve<1>(v, lane);
+  float r = v[0];
+  if constexpr (NV == 16) r += __shfl_xor_sync(kFull, r, 16);
+  return r;
+}
+
 // ---- f16x3 split operands -------------------------------------------------------------------
 // The fp16 tensor-core GEMM takes each fp32 operand value x as hi + lo * 2^-11 with
 // hi = fp16_rn(x) and lo = fp16_rn((x - hi) * 2^11) (the residual, scaled so it stays a normal

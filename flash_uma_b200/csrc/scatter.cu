@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_fwd_kernel(
   constexpr int kW = PART ? 25 : 9;
   constexpr int kWoff = PART ? 9 : 0;
   constexpr int kRow0 = PART ? 4 : 0;
-  __shared__ float s_w[8][28];
+  __shared__ float s_w[8][56];   // two edges' Wigner blocks
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
@@ -67,34 +67,65 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_fwd_kernel(
           env_l = __ldg(env + e_l);
         }
         const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
-        for (int q = 0; q < cnt; ++q) {
-          const int64_t e = __shfl_sync(kFull, e_l, q);
-          const float ev = __shfl_sync(kFull, env_l, q);
-          if (lane < kW) sw[lane] = __ldg(wig + e * kWig + kWoff + lane);
+        // two edges per iteration (their loads in flight together), accumulated in CSR order
+        for (int q = 0; q < cnt; q += 2) {
+          const bool two = q + 1 < cnt;
+          const int q1 = two ? q + 1 : q;
+          const int64_t e0 = __shfl_sync(kFull, e_l, q), e1 = __shfl_sync(kFull, e_l, q1);
+          const float ev0 = __shfl_sync(kFull, env_l, q), ev1 = __shfl_sync(kFull, env_l, q1);
+          if (lane < kW) {
+            sw[lane] = __ldg(wig + e0 * kWig + kWoff + lane);
+            sw[28 + lane] = __ldg(wig + e1 * kWig + kWoff + lane);
+          }
           __syncwarp();
           if (act) {
-            const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-            const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-            const float* z2 = Z2 + e * 2 * (int64_t)C + co;
             if constexpr (PART == 0) {
-              const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
-              acc[0] += ld4_stream(z0) * ev;
+              float4 m[2][3], z[2];
 #pragma unroll
-              for (int kk = 0; kk < 3; ++kk) {
-                float4 a = sw[kk] * m1[0];
-                fma4(a, sw[3 + kk], m1[1]);
-                fma4(a, sw[6 + kk], m1[2]);
-                acc[1 + kk] += a * ev;
+              for (int u = 0; u < 2; ++u) {
+                const int64_t e = u ? e1 : e0;
+                const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+                const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+                m[u][0] = ld4_stream(z1 + 2 * C); m[u][1] = ld4_stream(z0 + C); m[u][2] = ld4_stream(z1);
+                z[u] = ld4_stream(z0);
+              }
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                if (u == 1 && !two) break;
+                const float* D = sw + 28 * u;
+                const float ev = u ? ev1 : ev0;
+                acc[0] += z[u] * ev;
+#pragma unroll
+                for (int kk = 0; kk < 3; ++kk) {
+                  float4 a = D[kk] * m[u][0];
+                  fma4(a, D[3 + kk], m[u][1]);
+                  fma4(a, D[6 + kk], m[u][2]);
+                  acc[1 + kk] += a * ev;
+                }
               }
             } else {
-              const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
-                                    ld4_stream(z1 + C), ld4_stream(z2)};
+              float4 m[2][5];
 #pragma unroll
-              for (int kk = 0; kk < 5; ++kk) {
-                float4 a = sw[kk] * m2[0];
+              for (int u = 0; u < 2; ++u) {
+                const int64_t e = u ? e1 : e0;
+                const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+                const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+                const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+                m[u][0] = ld4_stream(z2 + C); m[u][1] = ld4_stream(z1 + 3 * C); m[u][2] = ld4_stream(z0 + 2 * C);
+                m[u][3] = ld4_stream(z1 + C); m[u][4] = ld4_stream(z2);
+              }
 #pragma unroll
-                for (int r = 1; r < 5; ++r) fma4(a, sw[r * 5 + kk], m2[r]);
-                acc[kk] += a * ev;
+              for (int u = 0; u < 2; ++u) {
+                if (u == 1 && !two) break;
+                const float* D = sw + 28 * u;
+                const float ev = u ? ev1 : ev0;
+#pragma unroll
+                for (int kk = 0; kk < 5; ++kk) {
+                  float4 a = D[kk] * m[u][0];
+#pragma unroll
+                  for (int r = 1; r < 5; ++r) fma4(a, D[r * 5 + kk], m[u][r]);
+                  acc[kk] += a * ev;
+                }
               }
             }
           }
@@ -125,49 +156,54 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
     float* __restrict__ gZ2, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, bool split,
     int* err) {
   constexpr int kW = PART ? 25 : 9;
-  bool bad = false;
   constexpr int kWoff = PART ? 9 : 0;
-  constexpr int kParts = kW + (PART ? 0 : 1);  // PART 0 also reduces g0 . Z0_0
+  constexpr int kRows = PART ? 5 : 4;
+  constexpr int kRow0 = PART ? 4 : 0;
+  constexpr int NV = PART ? 32 : 16;   // kW Wigner partials (+ g0 . Z0_0 at index 9 in PART 0), padded
   __shared__ float s_w[8][28];
-  __shared__ float s_red[8][28];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
   float* sw = s_w[warp];
+  bool bad = false;
   for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
-    const float* go_base = g_out + jn * 9 * (int64_t)C;
-    for (int k0 = kb; k0 < ke; k0 += 32) {
-      int64_t e_l = 0;
-      float env_l = 0.f;
-      if (k0 + lane < ke) {
-        e_l = col_idx[k0 + lane];
-        env_l = __ldg(env + e_l);
-      }
-      const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
-      for (int q = 0; q < cnt; ++q) {
-        const int64_t e = __shfl_sync(kFull, e_l, q);
-        const float ev = __shfl_sync(kFull, env_l, q);
-        if (lane < kW) sw[lane] = __ldg(wig + e * kWig + kWoff + lane);
-        __syncwarp();
-        float part[kParts];
+    for (int cb = 0; cb < C4; cb += 32) {
+      const int c4 = cb + lane;
+      const bool on = c4 < C4;
+      const int co = c4 * 4;
+      // this block's rows of g_out[j], loaded once per node
+      float4 g[kRows];
 #pragma unroll
-        for (int m = 0; m < kParts; ++m) part[m] = 0.f;
-        for (int c4 = lane; c4 < C4; c4 += 32) {
-          const int co = c4 * 4;
-          const float* go = go_base + co;
-          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+      for (int l = 0; l < kRows; ++l) g[l] = on ? ld4_keep(g_out + (jn * 9 + kRow0 + l) * (int64_t)C + co) : f4(0.f);
+      for (int k0 = kb; k0 < ke; k0 += 32) {
+        int e_l = 0;
+        float env_l = 0.f;
+        if (k0 + lane < ke) {
+          e_l = col_idx[k0 + lane];
+          env_l = __ldg(env + e_l);
+        }
+        const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
+        for (int q = 0; q < cnt; ++q) {
+          const int64_t e = __shfl_sync(kFull, e_l, q);
+          const float ev = __shfl_sync(kFull, env_l, q);
+          if (lane < kW) sw[lane] = __ldg(wig + e * kWig + kWoff + lane);
+          __syncwarp();
           float* q0 = gZ0 + e * 3 * (int64_t)C;   // gradient rows; columns slot * C + co
           float* q1 = gZ1 + e * 4 * (int64_t)C;
           float* q2 = gZ2 + e * 2 * (int64_t)C;
-          if constexpr (PART == 0) {
-            float4 g[4];
+          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+          float part[NV];
 #pragma unroll
-            for (int l = 0; l < 4; ++l) g[l] = ld4_keep(go + l * C);
-            const float4 zl0 = ld4_stream(z0);
-            const float4 m1[3] = {ld4_stream(z1 + 2 * C), ld4_stream(z0 + C), ld4_stream(z1)};
+          for (int m = 0; m < NV; ++m) part[m] = 0.f;
+          if constexpr (PART == 0) {
+            float4 zl0 = f4(0.f), m1[3] = {f4(0.f), f4(0.f), f4(0.f)};
+            if (on) {
+              zl0 = ld4_stream(z0);
+              m1[0] = ld4_stream(z1 + 2 * C); m1[1] = ld4_stream(z0 + C); m1[2] = ld4_stream(z1);
+            }
             float4 t1[3];
 #pragma unroll
             for (int r = 0; r < 3; ++r) {
@@ -176,21 +212,23 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
               fma4(a, sw[r * 3 + 2], g[3]);
               t1[r] = a * ev;
             }
-            st_out4(q0, 3 * C, co, g[0] * ev, split, bad);
-            st_out4(q0, 3 * C, C + co, t1[1], split, bad);
-            st_out4(q1, 4 * C, co, t1[2], split, bad);
-            st_out4(q1, 4 * C, 2 * C + co, t1[0], split, bad);
+            if (on) {
+              st_out4(q0, 3 * C, co, g[0] * ev, split, bad);
+              st_out4(q0, 3 * C, C + co, t1[1], split, bad);
+              st_out4(q1, 4 * C, co, t1[2], split, bad);
+              st_out4(q1, 4 * C, 2 * C + co, t1[0], split, bad);
+            }
 #pragma unroll
             for (int r = 0; r < 3; ++r)
 #pragma unroll
-              for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] += dot4(g[1 + kk], m1[r]);
-            part[9] += dot4(g[0], zl0);
+              for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] = dot4(g[1 + kk], m1[r]);
+            part[9] = dot4(g[0], zl0);
           } else {
-            float4 g[5];
-#pragma unroll
-            for (int l = 0; l < 5; ++l) g[l] = ld4_keep(go + (4 + l) * C);
-            const float4 m2[5] = {ld4_stream(z2 + C), ld4_stream(z1 + 3 * C), ld4_stream(z0 + 2 * C),
-                                  ld4_stream(z1 + C), ld4_stream(z2)};
+            float4 m2[5] = {f4(0.f), f4(0.f), f4(0.f), f4(0.f), f4(0.f)};
+            if (on) {
+              m2[0] = ld4_stream(z2 + C); m2[1] = ld4_stream(z1 + 3 * C); m2[2] = ld4_stream(z0 + 2 * C);
+              m2[3] = ld4_stream(z1 + C); m2[4] = ld4_stream(z2);
+            }
             float4 t2[5];
 #pragma unroll
             for (int r = 0; r < 5; ++r) {
@@ -199,32 +237,30 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
               for (int kk = 1; kk < 5; ++kk) fma4(a, sw[r * 5 + kk], g[kk]);
               t2[r] = a * ev;
             }
-            st_out4(q0, 3 * C, 2 * C + co, t2[2], split, bad);
-            st_out4(q1, 4 * C, C + co, t2[3], split, bad);
-            st_out4(q1, 4 * C, 3 * C + co, t2[1], split, bad);
-            st_out4(q2, 2 * C, co, t2[4], split, bad);
-            st_out4(q2, 2 * C, C + co, t2[0], split, bad);
+            if (on) {
+              st_out4(q0, 3 * C, 2 * C + co, t2[2], split, bad);
+              st_out4(q1, 4 * C, C + co, t2[3], split, bad);
+              st_out4(q1, 4 * C, 3 * C + co, t2[1], split, bad);
+              st_out4(q2, 2 * C, co, t2[4], split, bad);
+              st_out4(q2, 2 * C, C + co, t2[0], split, bad);
+            }
 #pragma unroll
             for (int r = 0; r < 5; ++r)
 #pragma unroll
-              for (int kk = 0; kk < 5; ++kk) part[r * 5 + kk] += dot4(g[kk], m2[r]);
+              for (int kk = 0; kk < 5; ++kk) part[r * 5 + kk] = dot4(g[kk], m2[r]);
           }
+          // lane l < kW: the channel sum of Wigner partial l (lane 9: g0 . Z0_0 in PART 0)
+          const float tot = warp_transpose_sum<NV>(part, lane);
+          // g_env share: sum_{r,k} D[r][k] raw[r][k] (+ g0 . Z0_0 in PART 0)
+          float genv = warp_sum(lane < kW ? sw[lane] * tot : 0.f);
+          if (PART == 0) genv += __shfl_sync(kFull, tot, 9);
+          if (lane < kW) {
+            float* dst = g_wig + e * kWig + kWoff + lane;
+            *dst = cb == 0 ? tot * ev : *dst + tot * ev;
+          }
+          if (lane == 0) g_env[e] = (PART == 0 && cb == 0) ? genv : g_env[e] + genv;
+          __syncwarp();
         }
-#pragma unroll
-        for (int m = 0; m < kParts; ++m) {
-          const float t = warp_sum(part[m]);
-          if (lane == 0) s_red[warp][m] = t;
-        }
-        __syncwarp();
-        // g_env share: sum_{r,k} D[r][k] raw[r][k] (+ g0 . Z0_0 in PART 0)
-        float genv = lane < kW ? sw[lane] * s_red[warp][lane] : 0.f;
-        genv = warp_sum(genv);
-        if (lane < kW) g_wig[e * kWig + kWoff + lane] = s_red[warp][lane] * ev;
-        if (lane == 0) {
-          if constexpr (PART == 0) g_env[e] = genv + s_red[warp][9];
-          else g_env[e] += genv;
-        }
-        __syncwarp();
       }
     }
   }
