@@ -232,6 +232,7 @@ def run_flash(args, rank, world, device):
 
         def step(pos):
             return pred(dataclasses.replace(data, pos=pos))
+        eager_step = step
 
     # ---- which of our kernels dominates: one probe pass with every entry point timed
     probe = _native.LaunchProbe(timed=list(_native.KERNELS_PER_CALL))
@@ -247,6 +248,17 @@ def run_flash(args, rank, world, device):
     dominant = max(per_op, key=per_op.get)
     launches_per_step = probe.launches
 
+    graphed = world == 1 and args.graph
+    if graphed:
+        # the whole step (graph build, forward, backward) as one CUDA graph. The probe is active
+        # during the capture: it counts the launches of one step and records event nodes around
+        # the dominant kernel's launches, whose elapsed times then read the last replay.
+        from flash_uma_b200.predict import GraphedStep
+        gprobe = _native.LaunchProbe(timed=[dominant], external=True)
+        gstep = GraphedStep(pred, dataclasses.replace(data, pos=pos_seq[0]),
+                            capture_hook=lambda on: _native.set_probe(gprobe if on else None))
+        graph_launches = gprobe.launches
+        step = gstep
     # ---- timed region 1: inputs resident in HBM. Launch counting covers every timed step; the
     # dominant kernel's launches are bracketed with CUDA events in the last timed step only
     # (pre-created events), so the instrumentation does not slow the other steps.
@@ -273,8 +285,8 @@ def run_flash(args, rank, world, device):
     _native.set_probe(None)
     clocks = sampler.stop()
     total_ms = sum(a.elapsed_time(b) for a, b in evs)
-    dom_ms = probe.times_ms(dominant)
-    gpu_launches = probe.launches
+    dom_ms = gprobe.times_ms(dominant) if graphed else probe.times_ms(dominant)
+    gpu_launches = graph_launches * K if graphed else probe.launches
 
     # ---- timed region 2: end to end from pinned host buffers through the public API
     host_pos = [p.cpu().pin_memory() for p in md_positions(data_cpu.pos, K, seed=100 + (0 if world > 1 else rank))]
@@ -310,7 +322,7 @@ def run_flash(args, rank, world, device):
     gm = gemm_mode(args.gemm, bf16)
     if dominant in GEMM_OPS:
         # tensor-bound: tensor-pipe FLOPs per launch (3 products per fp32 product in the split modes)
-        launches = probe.counts.get(dominant, 1) // K
+        launches = gprobe.counts.get(dominant, 1) if graphed else probe.counts.get(dominant, 1) // K
         flops = gemm_flops_per_step(Ek, C, B, L, gauss_only=args.gemm == "f16x3")
         flops_launch = gm["passes"] * flops / max(1, launches)
         achieved = flops_launch / (avg_ms * 1e-3) / 1e12
@@ -325,7 +337,7 @@ def run_flash(args, rank, world, device):
                 "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind, "traffic": None,
                 "alg_bytes_per_launch": nbytes}
     roof.update(avg_launch_ms=avg_ms, launches_timed=len(dom_ms),
-                share_of_step=(sum(dom_ms) / total_ms) if world == 1 else None)
+                share_of_step=(sum(dom_ms) / (total_ms / K)) if world == 1 else None)   # dom_ms: one step
     # the top HBM-bound kernel as well (device time from the probe pass)
     mem_ops = {k: v for k, v in per_op.items() if k not in GEMM_OPS and alg_bytes(k, Nk, Ek, C, B, Ek, 128)}
     top_mem = max(mem_ops, key=mem_ops.get) if mem_ops else None
@@ -350,6 +362,8 @@ def run_flash(args, rank, world, device):
                    "atoms": N, "edges": E, "sphere_channels": C, "layers": L, "num_distance_basis": B,
                    "cutoff": 6.0, "max_neighbors": 30, "gemm": gm["label"],
                    "l2": "flushed (256 MB write) before every step, outside the timed events",
+                   "launch": "one CUDA graph replay per step (graph build, forward, backward captured once)"
+                   if graphed else "eager (every kernel launched from the host)",
                    "parallelism": f"spatial slabs x{world} (halo atoms per rank: {len(plan.halo)} on rank 0)"
                    if world > 1 else "single GPU"},
         "e2e": {"value": atoms_total * K / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4,
@@ -564,6 +578,8 @@ def main():
                     help="print the per-kernel table of one timed step from an ncu launch list "
                          "(--metrics gpu__time_duration.sum --csv of 'bench.py --steps 1') and exit")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch every kernel from the host each step instead of replaying a CUDA graph")
     ap.add_argument("--micro", action="store_true", help="one-layer kernel microbench (BASELINE config 2)")
     ap.add_argument("--nodes", type=int, default=20000)
     ap.add_argument("--edges", type=int, default=600000)

@@ -108,7 +108,10 @@ class LaunchProbe:
     names in ``timed``, brackets each call with CUDA events on the current stream so the
     kernel's device time can be measured inside a larger timed region."""
 
-    def __init__(self, timed=(), pool: int = 0):
+    def __init__(self, timed=(), pool: int = 0, external: bool = False):
+        """``external``: events that record as nodes when the calls are captured in a CUDA graph
+        (their elapsed times then read the last replay)."""
+        self.external = external
         self.timed = set(timed)
         self.counts: dict[str, int] = {}
         self.launches = 0
@@ -116,10 +119,15 @@ class LaunchProbe:
         self.meta: dict[str, list] = {}
         self.timing = True          # bracket calls of ``timed`` entry points with events
         # pre-created events keep the per-call host cost to two cudaEventRecord calls
-        self._pool = [torch.cuda.Event(enable_timing=True) for _ in range(pool)]
+        self._pool = [self._new_event() for _ in range(pool)]
+
+    def _new_event(self):
+        if self.external:
+            return torch.cuda.Event(enable_timing=True, external=True)
+        return torch.cuda.Event(enable_timing=True)
 
     def _event(self):
-        return self._pool.pop() if self._pool else torch.cuda.Event(enable_timing=True)
+        return self._pool.pop() if self._pool else self._new_event()
 
     def before(self, name, args):
         self.counts[name] = self.counts.get(name, 0) + 1
