@@ -52,8 +52,10 @@ def build(verbose: bool = False, force: bool = False) -> str:
         return out
     os.makedirs(LIBDIR, exist_ok=True)
     tmp = out + ".tmp"
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--use_fast_math" if False else "-DFUMA_PRECISE",
-           "-Xcompiler", "-fPIC", "-shared", "-I", os.path.join(ROOT, "include"), "-o", tmp, *sources()]
+    # --no-undefined: a launcher declared but not defined fails the build instead of the first dlopen
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-DFUMA_PRECISE",
+           "-Xcompiler", "-fPIC", "-shared", "-Xlinker", "--no-undefined", "-I", os.path.join(ROOT, "include"),
+           "-o", tmp, *sources()]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -131,11 +131,31 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
   report_split_range(bad, err);
 }
 
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+template <int PART>
+struct BwdSlots {
+  static constexpr int n = PART ? 8 : 7;   // 16-byte loads per lane and edge: gX and rad slots of one side
+};
+
 // One side (SIDE 1: target pass over the destination CSR, SIDE 0: source pass over the source
 // CSR) and one coefficient block (PART 0: rows 0-3, radial slots 0-3 and 6-7, D1; PART 1:
 // rows 4-8, radial slots 4-5 and 8-11, D2) of the gather backward. Warp per node n, lane =
 // 4 channels (channel chunks of 128 in an outer loop); the node's rows stay in registers
-// and are rotated into every edge's frame.
+// and are rotated into every edge's frame. The next edge's gradient and radial slots and
+// Wigner block are copied into shared memory (cp.async, double-buffered per warp) while the
+// current edge is computed, so two edges' loads are in flight per warp.
+// Dynamic shared memory: kBwdWarps * 2 * BwdSlots<PART>::n * 512 bytes.
 template <int SIDE, int PART>
 __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
     const float* __restrict__ gX0, const float* __restrict__ gX1, const float* __restrict__ gX2,
@@ -149,11 +169,13 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
   constexpr int woff = PART ? 9 : 0;
   constexpr int row0 = PART ? 4 : 0;
   constexpr int NV = PART ? 32 : 16;
-  __shared__ float s_w[kBwdWarps][28];
+  constexpr int kS = BwdSlots<PART>::n;
+  extern __shared__ float4 s_stage[];
+  __shared__ float s_w[kBwdWarps][2][28];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   const int W = 12 * C;   // g_rad / rad row width
-  float* sw = s_w[warp];
+  float4* stage = s_stage + (size_t)warp * 2 * kS * 32;   // [buffer][slot][lane]
   bool bad = false;
   for (int64_t n = (int64_t)blockIdx.x * kBwdWarps + warp; n < N; n += (int64_t)gridDim.x * kBwdWarps) {
     const int kb = row_ptr[n], ke = row_ptr[n + 1];
@@ -162,6 +184,36 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
       const int c4 = cb + lane;
       const bool on = c4 < C4;
       const int co = c4 * 4;
+      // copies of edge e's slots (this side) and Wigner block into buffer b; one commit group
+      auto issue = [&](int64_t e, int b) {
+        float4* dst = stage + b * kS * 32 + lane;
+        if (on) {
+          const float* g0 = gX0 + e * 6 * (int64_t)C + co;
+          const float* g1 = gX1 + e * 8 * (int64_t)C + co;
+          const float* g2 = gX2 + e * 4 * (int64_t)C + co;
+          const float* rr = rad + e * (int64_t)W + co;
+          if constexpr (PART == 0) {
+            cp_async16(dst + 0 * 32, g0 + s * C);
+            cp_async16(dst + 1 * 32, g0 + (2 + s) * C);
+            cp_async16(dst + 2 * 32, g1 + s * C);
+            cp_async16(dst + 3 * 32, g1 + (4 + s) * C);
+            cp_async16(dst + 4 * 32, rr + s * C);
+            cp_async16(dst + 5 * 32, rr + (2 + s) * C);
+            cp_async16(dst + 6 * 32, rr + (6 + s) * C);
+          } else {
+            cp_async16(dst + 0 * 32, g0 + (4 + s) * C);
+            cp_async16(dst + 1 * 32, g1 + (2 + s) * C);
+            cp_async16(dst + 2 * 32, g1 + (6 + s) * C);
+            cp_async16(dst + 3 * 32, g2 + s * C);
+            cp_async16(dst + 4 * 32, g2 + (2 + s) * C);
+            cp_async16(dst + 5 * 32, rr + (4 + s) * C);
+            cp_async16(dst + 6 * 32, rr + (8 + s) * C);
+            cp_async16(dst + 7 * 32, rr + (10 + s) * C);
+          }
+        }
+        if (lane < nw) cp_async4(&s_w[warp][b][lane], wig + e * kWig + woff + lane);
+        cp_async_commit();
+      };
       // the node's rows of this block (l = 0 with the system embedding added)
       float4 v[nrows], acc[nrows];
 #pragma unroll
@@ -170,81 +222,84 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
         acc[r] = f4(0.f);
       }
       if (PART == 0 && on) v[0] = v[0] + ld4_keep(csd + bn * C + co);
-      for (int k0 = kb; k0 < ke; k0 += 32) {
-        const int e_l = (k0 + lane < ke) ? col_idx[k0 + lane] : 0;
-        const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
-        for (int q = 0; q < cnt; ++q) {
-          const int64_t e = __shfl_sync(kFull, e_l, q);
-          if (lane < nw) sw[lane] = __ldg(wig + e * kWig + woff + lane);
-          __syncwarp();
-          const float* g0 = gX0 + e * 6 * (int64_t)C + co;
-          const float* g1 = gX1 + e * 8 * (int64_t)C + co;
-          const float* g2 = gX2 + e * 4 * (int64_t)C + co;
-          const float* rr = rad + e * (int64_t)W + co;
-          float* grow = g_rad + e * (int64_t)W;
-          float gw[NV];
-#pragma unroll
-          for (int m = 0; m < NV; ++m) gw[m] = 0.f;
-          if constexpr (PART == 0) {
-            float4 a0 = f4(0.f), a2 = f4(0.f), b0 = f4(0.f), b4 = f4(0.f);
-            float4 r0 = f4(0.f), r2 = f4(0.f), r6 = f4(0.f);
-            if (on) {
-              a0 = ld4_stream(g0 + s * C); a2 = ld4_stream(g0 + (2 + s) * C);
-              b0 = ld4_stream(g1 + s * C); b4 = ld4_stream(g1 + (4 + s) * C);
-              r0 = ld4_stream(rr + s * C); r2 = ld4_stream(rr + (2 + s) * C); r6 = ld4_stream(rr + (6 + s) * C);
-            }
-            const float* D1 = sw;
-            float4 r1[3];
-            rot<3>(D1, v + 1, r1);
-            if (on) {
-              st_out4(grow, W, s * C + co, a0 * v[0], split, bad);
-              st_out4(grow, W, (2 + s) * C + co, a2 * r1[1], split, bad);
-              st_out4(grow, W, (6 + s) * C + co, b0 * r1[2] + b4 * r1[0], split, bad);
-            }
-            acc[0] += a0 * r0;
-            const float4 gi[3] = {b4 * r6, a2 * r2, b0 * r6};
-            float4 t[3];
-            rotT<3>(D1, gi, t);
-#pragma unroll
-            for (int m = 0; m < 3; ++m) acc[1 + m] += t[m];
-#pragma unroll
-            for (int r = 0; r < 3; ++r)
-#pragma unroll
-              for (int m = 0; m < 3; ++m) gw[r * 3 + m] = dot4(gi[r], v[1 + m]);
-          } else {
-            float4 a4 = f4(0.f), b2 = f4(0.f), b6 = f4(0.f), c0 = f4(0.f), c2 = f4(0.f);
-            float4 r4 = f4(0.f), r8 = f4(0.f), r10 = f4(0.f);
-            if (on) {
-              a4 = ld4_stream(g0 + (4 + s) * C); b2 = ld4_stream(g1 + (2 + s) * C); b6 = ld4_stream(g1 + (6 + s) * C);
-              c0 = ld4_stream(g2 + s * C); c2 = ld4_stream(g2 + (2 + s) * C);
-              r4 = ld4_stream(rr + (4 + s) * C); r8 = ld4_stream(rr + (8 + s) * C);
-              r10 = ld4_stream(rr + (10 + s) * C);
-            }
-            const float* D2 = sw;
-            float4 rv[5];
-            rot<5>(D2, v, rv);
-            if (on) {
-              st_out4(grow, W, (4 + s) * C + co, a4 * rv[2], split, bad);
-              st_out4(grow, W, (8 + s) * C + co, b2 * rv[3] + b6 * rv[1], split, bad);
-              st_out4(grow, W, (10 + s) * C + co, c0 * rv[4] + c2 * rv[0], split, bad);
-            }
-            const float4 g[5] = {c2 * r10, b6 * r8, a4 * r4, b2 * r8, c0 * r10};
-            float4 t[5];
-            rotT<5>(D2, g, t);
-#pragma unroll
-            for (int m = 0; m < 5; ++m) acc[m] += t[m];
-#pragma unroll
-            for (int r = 0; r < 5; ++r)
-#pragma unroll
-              for (int m = 0; m < 5; ++m) gw[r * 5 + m] = dot4(g[r], v[m]);
+      int base = kb;
+      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
+      int64_t e_cur = __shfl_sync(kFull, e_l, 0);
+      if (kb < ke) issue(e_cur, 0);
+      for (int k = kb; k < ke; ++k) {
+        const int b = (k - kb) & 1;
+        int64_t e_next = 0;
+        if (k + 1 < ke) {
+          if (k + 1 - base >= 32) {
+            base += 32;
+            e_l = (base + lane < ke) ? col_idx[base + lane] : 0;
           }
-          const float tot = warp_transpose_sum<NV>(gw, lane);
-          if (lane < nw) {
-            float* dst = g_wig + e * kWig + woff + lane;
-            *dst = (SIDE == 1 && cb == 0) ? tot : *dst + tot;
-          }
-          __syncwarp();
+          e_next = __shfl_sync(kFull, e_l, k + 1 - base);
+          issue(e_next, b ^ 1);
+        } else {
+          cp_async_commit();   // empty group: keeps "all but the newest group" = edge k
         }
+        cp_async_wait1();
+        __syncwarp();   // edge k's Wigner block, copied by lanes < nw, is visible to the warp
+        const int64_t e = e_cur;
+        const float4* src = stage + b * kS * 32 + lane;
+        const float* sw = s_w[warp][b];
+        float* grow = g_rad + e * (int64_t)W;
+        float gw[NV];
+#pragma unroll
+        for (int m = 0; m < NV; ++m) gw[m] = 0.f;
+        if constexpr (PART == 0) {
+          const float4 z = f4(0.f);
+          const float4 a0 = on ? src[0] : z, a2 = on ? src[32] : z, b0 = on ? src[64] : z, b4 = on ? src[96] : z;
+          const float4 r0 = on ? src[128] : z, r2 = on ? src[160] : z, r6 = on ? src[192] : z;
+          const float* D1 = sw;
+          float4 r1[3];
+          rot<3>(D1, v + 1, r1);
+          if (on) {
+            st_out4(grow, W, s * C + co, a0 * v[0], split, bad);
+            st_out4(grow, W, (2 + s) * C + co, a2 * r1[1], split, bad);
+            st_out4(grow, W, (6 + s) * C + co, b0 * r1[2] + b4 * r1[0], split, bad);
+          }
+          acc[0] += a0 * r0;
+          const float4 gi[3] = {b4 * r6, a2 * r2, b0 * r6};
+          float4 t[3];
+          rotT<3>(D1, gi, t);
+#pragma unroll
+          for (int m = 0; m < 3; ++m) acc[1 + m] += t[m];
+#pragma unroll
+          for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int m = 0; m < 3; ++m) gw[r * 3 + m] = dot4(gi[r], v[1 + m]);
+        } else {
+          const float4 z = f4(0.f);
+          const float4 a4 = on ? src[0] : z, b2 = on ? src[32] : z, b6 = on ? src[64] : z;
+          const float4 c0 = on ? src[96] : z, c2 = on ? src[128] : z;
+          const float4 r4 = on ? src[160] : z, r8 = on ? src[192] : z, r10 = on ? src[224] : z;
+          const float* D2 = sw;
+          float4 rv[5];
+          rot<5>(D2, v, rv);
+          if (on) {
+            st_out4(grow, W, (4 + s) * C + co, a4 * rv[2], split, bad);
+            st_out4(grow, W, (8 + s) * C + co, b2 * rv[3] + b6 * rv[1], split, bad);
+            st_out4(grow, W, (10 + s) * C + co, c0 * rv[4] + c2 * rv[0], split, bad);
+          }
+          const float4 g[5] = {c2 * r10, b6 * r8, a4 * r4, b2 * r8, c0 * r10};
+          float4 t[5];
+          rotT<5>(D2, g, t);
+#pragma unroll
+          for (int m = 0; m < 5; ++m) acc[m] += t[m];
+#pragma unroll
+          for (int r = 0; r < 5; ++r)
+#pragma unroll
+            for (int m = 0; m < 5; ++m) gw[r * 5 + m] = dot4(g[r], v[m]);
+        }
+        const float tot = warp_transpose_sum<NV>(gw, lane);
+        if (lane < nw) {
+          float* dst = g_wig + e * kWig + woff + lane;
+          *dst = (SIDE == 1 && cb == 0) ? tot : *dst + tot;
+        }
+        __syncwarp();   // buffer b is refilled by the next iteration's copies
+        e_cur = e_next;
       }
       if (on) {
         float* gx = g_x + (n * 9 + row0) * (int64_t)C + co;
@@ -272,15 +327,27 @@ void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, con
   (void)scratch;   // the two-pass backward needs no scratch rows
   const unsigned g = grid_for(N, kBwdWarps, 2);
   const int b = kBwdWarps * 32;
+  const size_t sm0 = (size_t)kBwdWarps * 2 * BwdSlots<0>::n * 32 * sizeof(float4);
+  const size_t sm1 = (size_t)kBwdWarps * 2 * BwdSlots<1>::n * 32 * sizeof(float4);
+  static thread_local uint64_t configured = 0;   // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> (dev & 63) & 1)) {
+    cudaFuncSetAttribute(gather_bwd_side_kernel<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm0);
+    cudaFuncSetAttribute(gather_bwd_side_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+    cudaFuncSetAttribute(gather_bwd_side_kernel<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm0);
+    cudaFuncSetAttribute(gather_bwd_side_kernel<0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+    configured |= uint64_t(1) << (dev & 63);
+  }
   // target pass (writes g_x, g_wigner), then source pass (adds to them)
-  gather_bwd_side_kernel<1, 0><<<g, b, 0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig,
-                                               g_rad, N, C, split, err);
-  gather_bwd_side_kernel<1, 1><<<g, b, 0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig,
-                                               g_rad, N, C, split, err);
-  gather_bwd_side_kernel<0, 0><<<g, b, 0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x, g_wig,
-                                               g_rad, N, C, split, err);
-  gather_bwd_side_kernel<0, 1><<<g, b, 0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x, g_wig,
-                                               g_rad, N, C, split, err);
+  gather_bwd_side_kernel<1, 0><<<g, b, sm0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig,
+                                                 g_rad, N, C, split, err);
+  gather_bwd_side_kernel<1, 1><<<g, b, sm1, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig,
+                                                 g_rad, N, C, split, err);
+  gather_bwd_side_kernel<0, 0><<<g, b, sm0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x, g_wig,
+                                                 g_rad, N, C, split, err);
+  gather_bwd_side_kernel<0, 1><<<g, b, sm1, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x, g_wig,
+                                                 g_rad, N, C, split, err);
 }
 
 }  // namespace fuma

@@ -94,89 +94,123 @@ __global__ void __launch_bounds__(256) gating_bwd_kernel(
   report_split_range(bad, err);
 }
 
-// One warp per row; VPL float4 per lane (D <= 128 * VPL), row kept in registers.
-template <int VPL>
+// One warp per group of ROWS rows (their loads in flight together); VPL float4 per lane
+// (D <= 128 * VPL), rows kept in registers.
+template <int VPL, int ROWS>
 __global__ void __launch_bounds__(256) ln_silu_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta, float* __restrict__ out,
                                                           float* __restrict__ mean_out, float* __restrict__ rstd_out,
                                                           int64_t M, int D, float eps, bool split, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  bool bad = false;
   const int wpb = blockDim.x >> 5;
   const int D4 = D >> 2;
-  for (int64_t r = (int64_t)blockIdx.x * wpb + warp; r < M; r += (int64_t)gridDim.x * wpb) {
-    const float* xr = x + r * D;
-    float4 v[VPL];
-    float s = 0.f;
+  bool bad = false;
+  for (int64_t r0 = ((int64_t)blockIdx.x * wpb + warp) * ROWS; r0 < M; r0 += (int64_t)gridDim.x * wpb * ROWS) {
+    float4 v[ROWS][VPL];
+    float s[ROWS];
 #pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int d4 = lane + 32 * q;
-      v[q] = d4 < D4 ? ld4_stream(xr + d4 * 4) : f4(0.f);
-      s += (v[q].x + v[q].y) + (v[q].z + v[q].w);
-    }
-    const float mean = warp_sum(s) / (float)D;
-    float ss = 0.f;
+    for (int i = 0; i < ROWS; ++i) {
+      s[i] = 0.f;
+      const bool row_ok = r0 + i < M;
 #pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int d4 = lane + 32 * q;
-      if (d4 < D4) {
-        const float4 c = v[q] - f4(mean);
-        ss += dot4(c, c);
+      for (int q = 0; q < VPL; ++q) {
+        const int d4 = lane + 32 * q;
+        v[i][q] = (row_ok && d4 < D4) ? ld4_stream(x + (r0 + i) * D + d4 * 4) : f4(0.f);
+        s[i] += (v[i][q].x + v[i][q].y) + (v[i][q].z + v[i][q].w);
       }
     }
-    const float var = warp_sum(ss) / (float)D;
-    const float rstd = 1.0f / sqrtf(var + eps);
-    if (lane == 0) { mean_out[r] = mean; rstd_out[r] = rstd; }
-    float* orow = out + r * D;
+    float mean[ROWS], rstd[ROWS];
 #pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int d4 = lane + 32 * q;
-      if (d4 < D4) {
-        const float4 y = (v[q] - f4(mean)) * rstd * ld4_keep(gamma + d4 * 4) + ld4_keep(beta + d4 * 4);
-        st_out4(orow, D, d4 * 4, y * sig4(y), split, bad);
+    for (int i = 0; i < ROWS; ++i) mean[i] = warp_sum(s[i]) / (float)D;
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) {
+      float ss = 0.f;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int d4 = lane + 32 * q;
+        if (d4 < D4) {
+          const float4 c = v[i][q] - f4(mean[i]);
+          ss += dot4(c, c);
+        }
+      }
+      s[i] = ss;
+    }
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) rstd[i] = 1.0f / sqrtf(warp_sum(s[i]) / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) {
+      const int64_t r = r0 + i;
+      if (r >= M) break;
+      if (lane == 0) { mean_out[r] = mean[i]; rstd_out[r] = rstd[i]; }
+      float* orow = out + r * D;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int d4 = lane + 32 * q;
+        if (d4 < D4) {
+          const float4 y = (v[i][q] - f4(mean[i])) * rstd[i] * ld4_keep(gamma + d4 * 4) + ld4_keep(beta + d4 * 4);
+          st_out4(orow, D, d4 * 4, y * sig4(y), split, bad);
+        }
       }
     }
   }
   report_split_range(bad, err);
 }
 
-template <int VPL>
+template <int VPL, int ROWS>
 __global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta, const float* __restrict__ mean,
                                                           const float* __restrict__ rstd, const float* __restrict__ g_out,
                                                           float* __restrict__ g_x, int64_t M, int D, bool split,
                                                           int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  bool bad = false;
   const int wpb = blockDim.x >> 5;
   const int D4 = D >> 2;
-  for (int64_t r = (int64_t)blockIdx.x * wpb + warp; r < M; r += (int64_t)gridDim.x * wpb) {
-    const float mu = mean[r], rs = rstd[r];
-    float4 xh[VPL], gxh[VPL];
-    float s1 = 0.f, s2 = 0.f;
+  bool bad = false;
+  for (int64_t r0 = ((int64_t)blockIdx.x * wpb + warp) * ROWS; r0 < M; r0 += (int64_t)gridDim.x * wpb * ROWS) {
+    float4 xh[ROWS][VPL], gxh[ROWS][VPL];
+    float s1[ROWS], s2[ROWS], rs[ROWS];
 #pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int d4 = lane + 32 * q;
-      if (d4 < D4) {
-        xh[q] = (ld4_stream(x + r * D + d4 * 4) - f4(mu)) * rs;
-        const float4 gm = ld4_keep(gamma + d4 * 4);
-        const float4 y = xh[q] * gm + ld4_keep(beta + d4 * 4);
-        const float4 sg = sig4(y);
-        const float4 ds = sg + y * (sg * (f4(1.f) - sg));
-        gxh[q] = ld4_stream(g_out + r * D + d4 * 4) * ds * gm;
-        s1 += (gxh[q].x + gxh[q].y) + (gxh[q].z + gxh[q].w);
-        s2 += dot4(gxh[q], xh[q]);
-      } else {
-        xh[q] = f4(0.f); gxh[q] = f4(0.f);
+    for (int i = 0; i < ROWS; ++i) {
+      const int64_t r = r0 + i;
+      const bool row_ok = r < M;
+      const float mu = row_ok ? mean[r] : 0.f;
+      rs[i] = row_ok ? rstd[r] : 0.f;
+      s1[i] = 0.f;
+      s2[i] = 0.f;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int d4 = lane + 32 * q;
+        if (row_ok && d4 < D4) {
+          xh[i][q] = (ld4_stream(x + r * D + d4 * 4) - f4(mu)) * rs[i];
+          const float4 gm = ld4_keep(gamma + d4 * 4);
+          const float4 y = xh[i][q] * gm + ld4_keep(beta + d4 * 4);
+          const float4 sg = sig4(y);
+          const float4 ds = sg + y * (sg * (f4(1.f) - sg));
+          gxh[i][q] = ld4_stream(g_out + r * D + d4 * 4) * ds * gm;
+          s1[i] += (gxh[i][q].x + gxh[i][q].y) + (gxh[i][q].z + gxh[i][q].w);
+          s2[i] += dot4(gxh[i][q], xh[i][q]);
+        } else {
+          xh[i][q] = f4(0.f);
+          gxh[i][q] = f4(0.f);
+        }
       }
     }
-    s1 = warp_sum(s1);
-    s2 = warp_sum(s2);
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) {
+      s1[i] = warp_sum(s1[i]);
+      s2[i] = warp_sum(s2[i]);
+    }
     const float invD = 1.0f / (float)D;
 #pragma unroll
-    for (int q = 0; q < VPL; ++q) {
-      const int d4 = lane + 32 * q;
-      if (d4 < D4) st_out4(g_x + r * D, D, d4 * 4, (gxh[q] - (f4(s1) + xh[q] * s2) * invD) * rs, split, bad);
+    for (int i = 0; i < ROWS; ++i) {
+      const int64_t r = r0 + i;
+      if (r >= M) break;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        const int d4 = lane + 32 * q;
+        if (d4 < D4)
+          st_out4(g_x + r * D, D, d4 * 4, (gxh[i][q] - (f4(s1[i]) + xh[i][q] * s2[i]) * invD) * rs[i], split, bad);
+      }
     }
   }
   report_split_range(bad, err);
@@ -196,27 +230,31 @@ void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, con
 
 void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float* out, float* mean, float* rstd,
                         int64_t M, int D, float eps, bool split, int* err, cudaStream_t s) {
-  const unsigned g = grid_for(M, 8, 8);
   const int d4 = D / 4;
-#define FWD(V) ln_silu_fwd_kernel<V><<<g, 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps, split, err)
-  if (d4 <= 32) FWD(1);
-  else if (d4 <= 64) FWD(2);
-  else if (d4 <= 128) FWD(4);
-  else if (d4 <= 256) FWD(8);
-  else FWD(16);
+  // one row per warp: several rows per warp (ROWS > 1) raise the register count and measured
+  // slower on B200 (occupancy loss outweighs the extra loads in flight)
+#define FWD(V, R) \
+  ln_silu_fwd_kernel<V, R><<<grid_for((M + R - 1) / R, 8, 8), 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps, \
+                                                                           split, err)
+  if (d4 <= 32) FWD(1, 1);
+  else if (d4 <= 64) FWD(2, 1);
+  else if (d4 <= 128) FWD(4, 1);
+  else if (d4 <= 256) FWD(8, 1);
+  else FWD(16, 1);
 #undef FWD
 }
 
 void launch_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
                         const float* g_out, float* g_x, int64_t M, int D, bool split, int* err, cudaStream_t s) {
-  const unsigned g = grid_for(M, 8, 8);
   const int d4 = D / 4;
-#define BWD(V) ln_silu_bwd_kernel<V><<<g, 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, D, split, err)
-  if (d4 <= 32) BWD(1);
-  else if (d4 <= 64) BWD(2);
-  else if (d4 <= 128) BWD(4);
-  else if (d4 <= 256) BWD(8);
-  else BWD(16);
+#define BWD(V, R)                                                                                                      \
+  ln_silu_bwd_kernel<V, R><<<grid_for((M + R - 1) / R, 8, 8), 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, \
+                                                                           D, split, err)
+  if (d4 <= 32) BWD(1, 1);
+  else if (d4 <= 64) BWD(2, 1);
+  else if (d4 <= 128) BWD(4, 1);
+  else if (d4 <= 256) BWD(8, 1);
+  else BWD(16, 1);
 #undef BWD
 }
 
