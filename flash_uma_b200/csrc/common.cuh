@@ -77,6 +77,19 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
   return r;
 }
 
+// ---- cp.async (global -> shared, per-thread groups) ------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 // ---- f16x3 split operands -------------------------------------------------------------------
 // The fp16 tensor-core GEMM takes each fp32 operand value x as hi + lo * 2^-11 with
 // hi = fp16_rn(x) and lo = fp16_rn((x - hi) * 2^11) (the residual, scaled so it stays a normal

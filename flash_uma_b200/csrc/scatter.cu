@@ -159,12 +159,13 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
   constexpr int kWoff = PART ? 9 : 0;
   constexpr int kRows = PART ? 5 : 4;
   constexpr int kRow0 = PART ? 4 : 0;
+  constexpr int kS = PART ? 5 : 4;     // Z slots per edge and lane (16-byte copies)
   constexpr int NV = PART ? 32 : 16;   // kW Wigner partials (+ g0 . Z0_0 at index 9 in PART 0), padded
-  __shared__ float s_w[8][28];
+  __shared__ float4 s_stage[8][2][kS][32];
+  __shared__ float s_w[8][2][28];      // Wigner block (0..kW-1) and envelope (27) of the staged edge
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
-  float* sw = s_w[warp];
   bool bad = false;
   for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
@@ -172,95 +173,122 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
       const int c4 = cb + lane;
       const bool on = c4 < C4;
       const int co = c4 * 4;
+      // copies of edge e's Z slots, Wigner block and envelope into buffer b (one commit group);
+      // the next edge's copies are in flight while the current edge is computed
+      auto issue = [&](int64_t e, int b) {
+        if (on) {
+          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+          float4* d = &s_stage[warp][b][0][lane];
+          if constexpr (PART == 0) {
+            cp_async16(d + 0 * 32, z0);
+            cp_async16(d + 1 * 32, z1 + 2 * C);
+            cp_async16(d + 2 * 32, z0 + C);
+            cp_async16(d + 3 * 32, z1);
+          } else {
+            cp_async16(d + 0 * 32, z2 + C);
+            cp_async16(d + 1 * 32, z1 + 3 * C);
+            cp_async16(d + 2 * 32, z0 + 2 * C);
+            cp_async16(d + 3 * 32, z1 + C);
+            cp_async16(d + 4 * 32, z2);
+          }
+        }
+        if (lane < kW) cp_async4(&s_w[warp][b][lane], wig + e * kWig + kWoff + lane);
+        if (lane == 31) cp_async4(&s_w[warp][b][27], env + e);
+        cp_async_commit();
+      };
       // this block's rows of g_out[j], loaded once per node
       float4 g[kRows];
 #pragma unroll
       for (int l = 0; l < kRows; ++l) g[l] = on ? ld4_keep(g_out + (jn * 9 + kRow0 + l) * (int64_t)C + co) : f4(0.f);
-      for (int k0 = kb; k0 < ke; k0 += 32) {
-        int e_l = 0;
-        float env_l = 0.f;
-        if (k0 + lane < ke) {
-          e_l = col_idx[k0 + lane];
-          env_l = __ldg(env + e_l);
-        }
-        const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
-        for (int q = 0; q < cnt; ++q) {
-          const int64_t e = __shfl_sync(kFull, e_l, q);
-          const float ev = __shfl_sync(kFull, env_l, q);
-          if (lane < kW) sw[lane] = __ldg(wig + e * kWig + kWoff + lane);
-          __syncwarp();
-          float* q0 = gZ0 + e * 3 * (int64_t)C;   // gradient rows; columns slot * C + co
-          float* q1 = gZ1 + e * 4 * (int64_t)C;
-          float* q2 = gZ2 + e * 2 * (int64_t)C;
-          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
-          float part[NV];
-#pragma unroll
-          for (int m = 0; m < NV; ++m) part[m] = 0.f;
-          if constexpr (PART == 0) {
-            float4 zl0 = f4(0.f), m1[3] = {f4(0.f), f4(0.f), f4(0.f)};
-            if (on) {
-              zl0 = ld4_stream(z0);
-              m1[0] = ld4_stream(z1 + 2 * C); m1[1] = ld4_stream(z0 + C); m1[2] = ld4_stream(z1);
-            }
-            float4 t1[3];
-#pragma unroll
-            for (int r = 0; r < 3; ++r) {
-              float4 a = sw[r * 3] * g[1];
-              fma4(a, sw[r * 3 + 1], g[2]);
-              fma4(a, sw[r * 3 + 2], g[3]);
-              t1[r] = a * ev;
-            }
-            if (on) {
-              st_out4(q0, 3 * C, co, g[0] * ev, split, bad);
-              st_out4(q0, 3 * C, C + co, t1[1], split, bad);
-              st_out4(q1, 4 * C, co, t1[2], split, bad);
-              st_out4(q1, 4 * C, 2 * C + co, t1[0], split, bad);
-            }
-#pragma unroll
-            for (int r = 0; r < 3; ++r)
-#pragma unroll
-              for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] = dot4(g[1 + kk], m1[r]);
-            part[9] = dot4(g[0], zl0);
-          } else {
-            float4 m2[5] = {f4(0.f), f4(0.f), f4(0.f), f4(0.f), f4(0.f)};
-            if (on) {
-              m2[0] = ld4_stream(z2 + C); m2[1] = ld4_stream(z1 + 3 * C); m2[2] = ld4_stream(z0 + 2 * C);
-              m2[3] = ld4_stream(z1 + C); m2[4] = ld4_stream(z2);
-            }
-            float4 t2[5];
-#pragma unroll
-            for (int r = 0; r < 5; ++r) {
-              float4 a = sw[r * 5] * g[0];
-#pragma unroll
-              for (int kk = 1; kk < 5; ++kk) fma4(a, sw[r * 5 + kk], g[kk]);
-              t2[r] = a * ev;
-            }
-            if (on) {
-              st_out4(q0, 3 * C, 2 * C + co, t2[2], split, bad);
-              st_out4(q1, 4 * C, C + co, t2[3], split, bad);
-              st_out4(q1, 4 * C, 3 * C + co, t2[1], split, bad);
-              st_out4(q2, 2 * C, co, t2[4], split, bad);
-              st_out4(q2, 2 * C, C + co, t2[0], split, bad);
-            }
-#pragma unroll
-            for (int r = 0; r < 5; ++r)
-#pragma unroll
-              for (int kk = 0; kk < 5; ++kk) part[r * 5 + kk] = dot4(g[kk], m2[r]);
+      int base = kb;
+      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
+      int64_t e_cur = __shfl_sync(kFull, e_l, 0);
+      if (kb < ke) issue(e_cur, 0);
+      for (int k = kb; k < ke; ++k) {
+        const int b = (k - kb) & 1;
+        int64_t e_next = 0;
+        if (k + 1 < ke) {
+          if (k + 1 - base >= 32) {
+            base += 32;
+            e_l = (base + lane < ke) ? col_idx[base + lane] : 0;
           }
-          // lane l < kW: the channel sum of Wigner partial l (lane 9: g0 . Z0_0 in PART 0)
-          const float tot = warp_transpose_sum<NV>(part, lane);
-          // g_env share: sum_{r,k} D[r][k] raw[r][k] (+ g0 . Z0_0 in PART 0)
-          float genv = warp_sum(lane < kW ? sw[lane] * tot : 0.f);
-          if (PART == 0) genv += __shfl_sync(kFull, tot, 9);
-          if (lane < kW) {
-            float* dst = g_wig + e * kWig + kWoff + lane;
-            *dst = cb == 0 ? tot * ev : *dst + tot * ev;
-          }
-          if (lane == 0) g_env[e] = (PART == 0 && cb == 0) ? genv : g_env[e] + genv;
-          __syncwarp();
+          e_next = __shfl_sync(kFull, e_l, k + 1 - base);
+          issue(e_next, b ^ 1);
+        } else {
+          cp_async_commit();   // empty group: "all but the newest group" is then edge k
         }
+        cp_async_wait1();
+        __syncwarp();
+        const int64_t e = e_cur;
+        const float* sw = s_w[warp][b];
+        const float ev = sw[27];
+        const float4* src = &s_stage[warp][b][0][lane];
+        const float4 zz = f4(0.f);
+        float* q0 = gZ0 + e * 3 * (int64_t)C;   // gradient rows; columns slot * C + co
+        float* q1 = gZ1 + e * 4 * (int64_t)C;
+        float* q2 = gZ2 + e * 2 * (int64_t)C;
+        float part[NV];
+#pragma unroll
+        for (int m = 0; m < NV; ++m) part[m] = 0.f;
+        if constexpr (PART == 0) {
+          const float4 zl0 = on ? src[0] : zz;
+          const float4 m1[3] = {on ? src[32] : zz, on ? src[64] : zz, on ? src[96] : zz};
+          float4 t1[3];
+#pragma unroll
+          for (int r = 0; r < 3; ++r) {
+            float4 a = sw[r * 3] * g[1];
+            fma4(a, sw[r * 3 + 1], g[2]);
+            fma4(a, sw[r * 3 + 2], g[3]);
+            t1[r] = a * ev;
+          }
+          if (on) {
+            st_out4(q0, 3 * C, co, g[0] * ev, split, bad);
+            st_out4(q0, 3 * C, C + co, t1[1], split, bad);
+            st_out4(q1, 4 * C, co, t1[2], split, bad);
+            st_out4(q1, 4 * C, 2 * C + co, t1[0], split, bad);
+          }
+#pragma unroll
+          for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] = dot4(g[1 + kk], m1[r]);
+          part[9] = dot4(g[0], zl0);
+        } else {
+          const float4 m2[5] = {on ? src[0] : zz, on ? src[32] : zz, on ? src[64] : zz, on ? src[96] : zz,
+                                on ? src[128] : zz};
+          float4 t2[5];
+#pragma unroll
+          for (int r = 0; r < 5; ++r) {
+            float4 a = sw[r * 5] * g[0];
+#pragma unroll
+            for (int kk = 1; kk < 5; ++kk) fma4(a, sw[r * 5 + kk], g[kk]);
+            t2[r] = a * ev;
+          }
+          if (on) {
+            st_out4(q0, 3 * C, 2 * C + co, t2[2], split, bad);
+            st_out4(q1, 4 * C, C + co, t2[3], split, bad);
+            st_out4(q1, 4 * C, 3 * C + co, t2[1], split, bad);
+            st_out4(q2, 2 * C, co, t2[4], split, bad);
+            st_out4(q2, 2 * C, C + co, t2[0], split, bad);
+          }
+#pragma unroll
+          for (int r = 0; r < 5; ++r)
+#pragma unroll
+            for (int kk = 0; kk < 5; ++kk) part[r * 5 + kk] = dot4(g[kk], m2[r]);
+        }
+        // lane l < kW: the channel sum of Wigner partial l (lane 9: g0 . Z0_0 in PART 0)
+        const float tot = warp_transpose_sum<NV>(part, lane);
+        // g_env share: sum_{r,k} D[r][k] raw[r][k] (+ g0 . Z0_0 in PART 0)
+        float genv = warp_sum(lane < kW ? sw[lane] * tot : 0.f);
+        if (PART == 0) genv += __shfl_sync(kFull, tot, 9);
+        if (lane < kW) {
+          float* dst = g_wig + e * kWig + kWoff + lane;
+          *dst = cb == 0 ? tot * ev : *dst + tot * ev;
+        }
+        if (lane == 0) g_env[e] = (PART == 0 && cb == 0) ? genv : g_env[e] + genv;
+        __syncwarp();   // buffer b is refilled by the next iteration's copies
+        e_cur = e_next;
       }
     }
   }
