@@ -186,15 +186,31 @@ def md_positions(pos0: torch.Tensor, count: int, seed: int = 0):
     return [pos0 + 0.01 * torch.randn(pos0.shape, generator=g) for _ in range(count)]
 
 
-def build_partitioned(device, gemm: str, world: int, rank: int):
-    """Weak-scaling workload for N > 1 GPUs: bulk fcc Cu 10 x 10 x (10 N) (4,000 atoms per GPU,
-    so N = 1 is exactly config 3), split into N slabs along the long axis with a per-layer halo
+def workload_system(workload: str, world: int):
+    """(system, stress, scaling, label) of a bench workload at ``world`` GPUs.
+
+    default: config 3 at N = 1, weak scaling beyond (bulk fcc Cu 10 x 10 x 10N, 4,000 atoms
+             per GPU, split into N slabs with per-layer halo exchange);
+    config4: the ~10k-atom water box with energy + forces + stress (1 and 2 GPUs);
+    config5: bulk fcc Cu 30 x 30 x 28 (100,800 atoms) at every N (strong scaling)."""
+    from flash_uma_b200.systems import bulk_fcc, config3_system, config4_system, config5_system
+    if workload == "config5":
+        return config5_system(), False, "strong", "bulk_cu_100800 (BASELINE config 5), E+F per step"
+    if workload == "config4":
+        return config4_system(), True, "strong", "water box 3,333 H2O (BASELINE config 4), E+F+S per step"
+    if world == 1:
+        return config3_system(), False, "weak", "bulk_cu_4000 (BASELINE config 3), E+F per step"
+    return (bulk_fcc(10, 10, 10 * world, jitter=0.05, seed=0, name=f"bulk_cu_{4000 * world}"), False, "weak",
+            f"bulk Cu 10x10x{10 * world} (4000 atoms per GPU, weak scaling of config 3), E+F per step")
+
+
+def build_partitioned(device, gemm: str, world: int, rank: int, system=None, stress: bool = False):
+    """N > 1 GPUs: the system split into N slabs along its long axis with a per-layer halo
     exchange of node embeddings over NCCL (flash_uma_b200.partition)."""
     from flash_uma_b200.partition import PartitionedModel, make_plan
     from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
-    from flash_uma_b200.systems import bulk_fcc, to_graph
+    from flash_uma_b200.systems import to_graph
     from flash_uma_b200.wrapper import ZeroAllocBackbone
-    system = bulk_fcc(10, 10, 10 * world, jitter=0.05, seed=0, name=f"bulk_cu_{4000 * world}")
     data = to_graph([system])
     off = SyntheticESCNMDBackbone(seed=0).to(device)
     head = make_energy_head(128, 128, seed=1).to(device)
@@ -205,8 +221,8 @@ def build_partitioned(device, gemm: str, world: int, rank: int):
     csd = bb.csd_embedding(d.charge, d.spin).float().detach()
 
     def step(pos):
-        e, f = pm.energy_forces(head, pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd)
-        return {"energy": e, "forces": f}
+        out = pm.energy_forces(head, pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd, stress=stress)
+        return dict(zip(("energy", "forces", "stress"), out))
 
     return system, data, step, plan
 
@@ -217,13 +233,14 @@ def run_flash(args, rank, world, device):
     C, B, L = 128, 64, 4
     K, W = args.steps, args.warmup
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    system, with_stress, scaling, label = workload_system(args.workload, world)
     if world > 1:
-        system, data_cpu, step, plan = build_partitioned(device, args.gemm, world, rank)
+        system, data_cpu, step, plan = build_partitioned(device, args.gemm, world, rank, system, with_stress)
         N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
         pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=0)]
     else:
         plan = None
-        system, data_cpu, pred = build_problem(device, args.gemm)
+        system, data_cpu, pred = build_problem(device, args.gemm, system)
         N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
         data = data_cpu.to(device)
         pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=rank)]
@@ -231,8 +248,7 @@ def run_flash(args, rank, world, device):
         import dataclasses
 
         def step(pos):
-            return pred(dataclasses.replace(data, pos=pos))
-        eager_step = step
+            return pred(dataclasses.replace(data, pos=pos), stress=with_stress)
 
     # ---- which of our kernels dominates: one probe pass with every entry point timed
     probe = _native.LaunchProbe(timed=list(_native.KERNELS_PER_CALL))
@@ -255,7 +271,7 @@ def run_flash(args, rank, world, device):
         # the dominant kernel's launches, whose elapsed times then read the last replay.
         from flash_uma_b200.predict import GraphedStep
         gprobe = _native.LaunchProbe(timed=[dominant], external=True)
-        gstep = GraphedStep(pred, dataclasses.replace(data, pos=pos_seq[0]),
+        gstep = GraphedStep(pred, dataclasses.replace(data, pos=pos_seq[0]), stress=with_stress,
                             capture_hook=lambda on: _native.set_probe(gprobe if on else None))
         graph_launches = gprobe.launches
         step = gstep
@@ -292,6 +308,7 @@ def run_flash(args, rank, world, device):
     host_pos = [p.cpu().pin_memory() for p in md_positions(data_cpu.pos, K, seed=100 + (0 if world > 1 else rank))]
     f_host = torch.empty(N, 3).pin_memory()
     e_host = torch.empty(1).pin_memory()
+    s_host = torch.empty(1, 3, 3).pin_memory()
     pos_dev = torch.empty(N, 3, device=device)
     if world > 1:
         torch.distributed.barrier()
@@ -305,6 +322,8 @@ def run_flash(args, rank, world, device):
         res = step(pos_dev)
         f_host.copy_(res["forces"], non_blocking=True)
         e_host.copy_(res["energy"], non_blocking=True)
+        if with_stress:
+            s_host.copy_(res["stress"], non_blocking=True)
         e1.record()
         evs2.append((e0, e1))
     torch.cuda.synchronize()
@@ -352,13 +371,10 @@ def run_flash(args, rank, world, device):
     atoms_total = N if world > 1 else world * N
     out = {
         "metric": METRIC, "value": atoms_total * K / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded bulk Cu positions, random-init weights)",
-        "config": {"workload": ("bulk_cu_4000 (BASELINE config 3): 4000 atoms, %d edges, E+F per step" % E
-                                if world == 1 else
-                                f"bulk Cu 10x10x{10 * world} ({N} atoms, {E} edges; 4000 atoms per GPU, weak "
-                                f"scaling of config 3), E+F per step, slab decomposition with per-layer halo "
-                                f"exchange (NCCL)"),
+        "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded positions, random-init weights)",
+        "config": {"workload": f"{label}: {N} atoms, {E} edges"
+                               + (", slab decomposition with per-layer halo exchange (NCCL)" if world > 1 else ""),
                    "atoms": N, "edges": E, "sphere_channels": C, "layers": L, "num_distance_basis": B,
                    "cutoff": 6.0, "max_neighbors": 30, "gemm": gm["label"],
                    "l2": "flushed (256 MB write) before every step, outside the timed events",
@@ -367,7 +383,8 @@ def run_flash(args, rank, world, device):
                    "parallelism": f"spatial slabs x{world} (halo atoms per rank: {len(plan.halo)} on rank 0)"
                    if world > 1 else "single GPU"},
         "e2e": {"value": atoms_total * K / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4,
-                "d2h_bytes_per_step": N * 3 * 4 + 4},
+                "d2h_bytes_per_step": N * 3 * 4 + 4 + (36 if with_stress else 0)},
+        "max_device_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
         "roofline": roof,
         "roofline_top_hbm_kernel": roof_mem,
         "gemm": gemm_summary(per_op, Ek, C, B, L, args.gemm),
@@ -571,6 +588,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="flash", choices=["flash", "reference"])
+    ap.add_argument("--workload", default="default", choices=["default", "config4", "config5"],
+                    help="default: config 3 (weak scaling of it for N > 1); config4: water box E+F+S; "
+                         "config5: 100,800-atom bulk Cu (strong scaling)")
     ap.add_argument("--gemm", default="f16x3", choices=["f16x3", "tf32x3", "tf32"],
                     help="dense-contraction mode: f16x3 / tf32x3 (fp32-level) or tf32 (single pass, the "
                          "reference's published setup)")
@@ -584,6 +604,10 @@ def main():
     ap.add_argument("--nodes", type=int, default=20000)
     ap.add_argument("--edges", type=int, default=600000)
     args = ap.parse_args()
+    if args.workload == "config5":
+        # ~150 GB of activations on one GPU: growable segments keep the caching allocator from
+        # stranding tens of GB in fragments (set before the first CUDA allocation)
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     if args.summarize_launches:
         summarize_launches(args.summarize_launches)
         return

@@ -50,7 +50,7 @@ class _GeometryFn(torch.autograd.Function):
         ctx.mark_non_differentiable(xe_p)
         ctx.save_for_backward(pos, idx_i, idx_j, shifts, offset_g)
         ctx.coeff_g, ctx.cutoff, ctx.graph = float(coeff_g), float(cutoff), graph
-        return xe_p, x_edge[:, :B], wigner, env
+        return xe_p, x_edge[:, :B].contiguous(), wigner, env   # x_edge itself is freed
 
     @staticmethod
     def backward(ctx, g_xe_p, g_gauss, g_wigner, g_env):
@@ -131,59 +131,90 @@ def radial_bwd(rad, saved, g_out_p, err):
     return _gemm16(g_y1, (hi[:B], lo[:B], inv), None, g_y1.shape[1])
 
 
+def _conv2(layer, Y0, Y1, Y2, C, err, s):
+    """Gating (split outputs) then the three conv2 GEMMs: O0, O1, O2 fp32."""
+    E = Y0.shape[0]
+    Z0, Z1, Z2 = _empty((E, 3 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
+    nat.call("fuma_gating_fwd_f16x3", ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(Z0), ptr(Z1), ptr(Z2), ptr(err), s)
+    O0 = _gemm16(Z0, layer.conv2_m0.w16, layer.conv2_m0.bias_p, 3 * C)
+    O1 = _gemm16(Z1, layer.conv2_m1.w16, None, 4 * C)
+    O2 = _gemm16(Z2, layer.conv2_m2.w16, None, 2 * C)
+    return O0, O1, O2
+
+
+def _edge_forward(layer, x_norm, xe_p, wigner, csd, idx_i, idx_j, batch, N, C, err, s):
+    """Radial MLP, gather, conv1, gating, conv2 of one block: (rad, radial saved, Y0..2, O0..2)."""
+    E = idx_i.shape[0]
+    rad, rsaved = radial_fwd(layer.rad, xe_p, err)
+    X0, X1, X2 = _empty((E, 6 * C), rad), _empty((E, 8 * C), rad), _empty((E, 4 * C), rad)
+    nat.call("fuma_gather_fwd_f16x3", ptr(x_norm), ptr(idx_i), ptr(idx_j), ptr(wigner), ptr(rad), ptr(csd),
+             ptr(batch), N, E, C, ptr(X0), ptr(X1), ptr(X2), ptr(err), s)
+    Y0 = _gemm16(X0, layer.conv1_m0.w16, layer.conv1_m0.bias_p, 6 * C)
+    Y1 = _gemm16(X1, layer.conv1_m1.w16, None, 8 * C)
+    Y2 = _gemm16(X2, layer.conv1_m2.w16, None, 4 * C)
+    del X0, X1, X2
+    O0, O1, O2 = _conv2(layer, Y0, Y1, Y2, C, err, s)
+    return rad, rsaved, (Y0, Y1, Y2), (O0, O1, O2)
+
+
 # ---- one message-passing block ---------------------------------------------------------------
+# Saved for the backward per edge and layer: the radial output (12C), pre-activations (2H), Y
+# (11C) and the conv2 outputs (9C), 17.4 KB at C = H = 128. With ``lean`` the block saves only
+# its inputs and the backward recomputes the edge forward first (block-level recomputation:
+# about 1.4x the step's work, for graphs whose activations would not fit in device memory).
 
 class _MessageBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_norm, x_in, xe_p, x_gauss, wigner, env, csd, layer, idx_i, idx_j, batch, graph):
+    def forward(ctx, x_norm, x_in, xe_p, x_gauss, wigner, env, csd, layer, idx_i, idx_j, batch, graph, lean):
         N, _, C = x_in.shape
         E = idx_i.shape[0]
         err = error_flag(x_in.device)
         s = stream_of(x_in)
-        rad, rsaved = radial_fwd(layer.rad, xe_p, err)
-        X0, X1, X2 = _empty((E, 6 * C), x_in), _empty((E, 8 * C), x_in), _empty((E, 4 * C), x_in)
-        nat.call("fuma_gather_fwd_f16x3", ptr(x_norm), ptr(idx_i), ptr(idx_j), ptr(wigner), ptr(rad), ptr(csd),
-                 ptr(batch), N, E, C, ptr(X0), ptr(X1), ptr(X2), ptr(err), s)
-        Y0 = _gemm16(X0, layer.conv1_m0.w16, layer.conv1_m0.bias_p, 6 * C)
-        Y1 = _gemm16(X1, layer.conv1_m1.w16, None, 8 * C)
-        Y2 = _gemm16(X2, layer.conv1_m2.w16, None, 4 * C)
-        del X0, X1, X2
-        Z0, Z1, Z2 = _empty((E, 3 * C), x_in), _empty((E, 4 * C), x_in), _empty((E, 2 * C), x_in)
-        nat.call("fuma_gating_fwd_f16x3", ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(Z0), ptr(Z1), ptr(Z2), ptr(err), s)
-        O0 = _gemm16(Z0, layer.conv2_m0.w16, layer.conv2_m0.bias_p, 3 * C)
-        O1 = _gemm16(Z1, layer.conv2_m1.w16, None, 4 * C)
-        O2 = _gemm16(Z2, layer.conv2_m2.w16, None, 2 * C)
-        del Z0, Z1, Z2
+        rad, rsaved, (Y0, Y1, Y2), (O0, O1, O2) = _edge_forward(layer, x_norm, xe_p, wigner, csd, idx_i, idx_j,
+                                                                 batch, N, C, err, s)
         x_mid = _empty((N, 9, C), x_in)
         nat.call("fuma_rotate_scatter_fwd", ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env), ptr(x_in),
                  ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(x_mid), s)
-        ctx.save_for_backward(x_norm, wigner, env, csd, rad, Y0, Y1, Y2, O0, O1, O2, idx_i, batch, *rsaved)
-        ctx.layer, ctx.graph = layer, graph
+        if lean:
+            ctx.save_for_backward(x_norm, wigner, env, csd, idx_i, batch, xe_p, idx_j)
+        else:
+            ctx.save_for_backward(x_norm, wigner, env, csd, idx_i, batch, rad, *rsaved, Y0, Y1, Y2, O0, O1, O2)
+        ctx.layer, ctx.graph, ctx.lean = layer, graph, lean
         return x_mid
 
     @staticmethod
     def backward(ctx, g_mid):
-        (x_norm, wigner, env, csd, rad, Y0, Y1, Y2, O0, O1, O2, idx_i, batch, *rsaved) = ctx.saved_tensors
+        saved = ctx.saved_tensors
+        x_norm, wigner, env, csd, idx_i, batch = saved[:6]
         layer, graph = ctx.layer, ctx.graph
         g_mid = g_mid.contiguous()
         N, _, C = x_norm.shape
         E = idx_i.shape[0]
         err = error_flag(x_norm.device)
         s = stream_of(x_norm)
-        gO0, gO1, gO2 = _empty((E, 3 * C), rad), _empty((E, 4 * C), rad), _empty((E, 2 * C), rad)
-        g_w = _empty((E, 34), rad)
-        g_env = _empty((E,), rad)
+        if ctx.lean:
+            xe_p, idx_j = saved[6:8]
+            rad, rsaved, (Y0, Y1, Y2), (O0, O1, O2) = _edge_forward(layer, x_norm, xe_p, wigner, csd, idx_i, idx_j,
+                                                                     batch, N, C, err, s)
+        else:
+            rad = saved[6]
+            rsaved = saved[7:13]
+            Y0, Y1, Y2, O0, O1, O2 = saved[13:19]
+        gO0, gO1, gO2 = _empty((E, 3 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
+        g_w = _empty((E, 34), Y0)
+        g_env = _empty((E,), Y0)
         nat.call("fuma_rotate_scatter_bwd_f16x3", ptr(g_mid), ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env),
                  ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(gO0), ptr(gO1), ptr(gO2), ptr(g_w),
                  ptr(g_env), ptr(err), s)
+        del O0, O1, O2
         gZ0 = _gemm16(gO0, layer.conv2_m0.wt16, None, 3 * C)
         gZ1 = _gemm16(gO1, layer.conv2_m1.wt16, None, 4 * C)
         gZ2 = _gemm16(gO2, layer.conv2_m2.wt16, None, 2 * C)
         del gO0, gO1, gO2
-        gY0, gY1, gY2 = _empty((E, 5 * C), rad), _empty((E, 4 * C), rad), _empty((E, 2 * C), rad)
+        gY0, gY1, gY2 = _empty((E, 5 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
         nat.call("fuma_gating_bwd_f16x3", ptr(gZ0), ptr(gZ1), ptr(gZ2), ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(gY0),
                  ptr(gY1), ptr(gY2), ptr(err), s)
-        del gZ0, gZ1, gZ2
+        del gZ0, gZ1, gZ2, Y0, Y1, Y2
         gX0 = _gemm16(gY0, layer.conv1_m0.wt16, None, 5 * C)
         gX1 = _gemm16(gY1, layer.conv1_m1.wt16, None, 4 * C)
         gX2 = _gemm16(gY2, layer.conv1_m2.wt16, None, 2 * C)
@@ -194,18 +225,31 @@ class _MessageBlockFn(torch.autograd.Function):
         nat.call("fuma_gather_bwd_f16x3", ptr(gX0), ptr(gX1), ptr(gX2), ptr(x_norm), ptr(idx_i), ptr(wigner), ptr(rad),
                  ptr(csd), ptr(batch), ptr(graph.dst_row_ptr), ptr(graph.dst_col), ptr(graph.src_row_ptr),
                  ptr(graph.src_col), N, E, C, None, 0, ptr(g_x), ptr(g_w2), ptr(g_rad), ptr(err), s)
-        del gX0, gX1, gX2
+        del gX0, gX1, gX2, rad
         g_xe = radial_bwd(layer.rad, rsaved, g_rad, err)
         g_w += g_w2
-        return g_x, g_mid, None, g_xe, g_w, g_env, None, None, None, None, None, None
+        return g_x, g_mid, None, g_xe, g_w, g_env, None, None, None, None, None, None, None
 
 
-def message_block(layer, x_norm, x_in, xe, wigner, env, csd, idx_i, idx_j, batch, graph):
+def message_block(layer, x_norm, x_in, xe, wigner, env, csd, idx_i, idx_j, batch, graph, lean: bool = False):
     """x_mid = x_in + scatter(SO(2) message of every edge) for one layer (fp32 in and out);
-    ``xe`` = (split edge features, x_gauss) from :func:`geometry`."""
+    ``xe`` = (split edge features, x_gauss) from :func:`geometry`; ``lean``: recompute instead
+    of saving the radial and conv2 outputs."""
     xe_p, x_gauss = xe
     return _MessageBlockFn.apply(x_norm.contiguous(), x_in.contiguous(), xe_p, x_gauss, wigner, env,
-                                 csd.contiguous(), layer, idx_i, idx_j, batch, graph)
+                                 csd.contiguous(), layer, idx_i, idx_j, batch, graph, bool(lean))
+
+
+def lean_needed(E: int, C: int, H: int, L: int, device) -> bool:
+    """Whether the saved activations of an L-layer step over E edges would crowd the device:
+    ~4 (L (32C + 2H) + 45C) bytes per edge in the default mode (92 KB at C = H = 128, L = 4;
+    measured: 139 GB for 1.51M edges), against 90% of the device memory. FUMA_LEAN=0/1 forces it."""
+    import os
+    force = os.environ.get("FUMA_LEAN")
+    if force is not None:
+        return force == "1"
+    per_edge = 4 * (L * (32 * C + 2 * H) + 45 * C)
+    return E * per_edge > 0.9 * torch.cuda.get_device_properties(device).total_memory
 
 
 # ---- initial edge-degree embedding -----------------------------------------------------------

@@ -122,11 +122,13 @@ class PackedLayer(nn.Module):
                 p.requires_grad_(False)
 
     fused = False   # set by ESCNInferenceModel: x_edge is then the row-packed split of the edge features
+    lean = False    # set per step by ESCNInferenceModel for graphs too large to keep every activation
 
     def forward(self, x_in, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch):
         x_norm = self.norm_1(x_in)
         if self.fused:
-            x_mid = fused.message_block(self, x_norm, x_in, x_edge, wigner, env, csd_emb, idx_i, idx_j, batch, graph)
+            x_mid = fused.message_block(self, x_norm, x_in, x_edge, wigner, env, csd_emb, idx_i, idx_j, batch, graph,
+                                        self.lean)
             return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
         rad_out = self.rad(x_edge)
         X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch, graph=graph)
@@ -185,6 +187,10 @@ class ESCNInferenceModel(nn.Module):
         if self.fused:
             for lin in self._linears():
                 lin.prepare()
+            lean = fused.lean_needed(int(idx_i.shape[0]), self.C, self.layers[0].rad.l1.N if len(self.layers) else 0,
+                                     len(self.layers), pos.device)
+            for lay in self.layers:
+                lay.lean = lean
             return fused.geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt, self.offset_g, self.coeff_g,
                                   self.cutoff, graph)
         return ops.precompute_geometry(pos, Z, idx_i, idx_j, shifts, self.W_src, self.W_tgt, self.offset_g,

@@ -169,14 +169,36 @@ class PartitionedModel:
             x = m.layer_forward(k, x, xe, wig, env, self.idx_i, self.idx_j, self.graph, csd_emb, b_l)
         return m.final(x[: self.n_owned])
 
-    def energy_forces(self, head, pos, Z, batch, cell_offsets, cell, csd_emb, num_systems: int = 1):
-        """Global energy [num_systems] and forces [N, 3], identical on every rank."""
+    def energy_forces(self, head, pos, Z, batch, cell_offsets, cell, csd_emb, num_systems: int = 1,
+                      stress: bool = False):
+        """Global energy [num_systems] and forces [N, 3] (and, with ``stress``, the virial stress
+        [1, 3, 3] of the one periodic system), identical on every rank.
+
+        Stress follows the strain-displacement construction of the single-GPU predictor: a
+        symmetric strain applied to the replicated positions and to the cell; every rank's
+        gradient with respect to it covers its own edges and atoms, and one all-reduce sums them."""
         pos = pos.detach().requires_grad_(True)
-        x = self.node_embedding(pos, Z, batch, cell_offsets, cell, csd_emb)
+        wrt = [pos]
+        p, c = pos, cell
+        if stress:
+            if num_systems != 1:
+                raise ValueError("the partitioned stress covers one periodic system")
+            disp = torch.zeros(3, 3, dtype=pos.dtype, device=pos.device, requires_grad=True)
+            sym = 0.5 * (disp + disp.t())
+            p = pos + pos @ sym
+            c = cell + cell @ sym
+            wrt.append(disp)
+        x = self.node_embedding(p, Z, batch, cell_offsets, c, csd_emb)
         b_owned = batch.index_select(0, self.local_ids[: self.n_owned])
         e_local = head(x, b_owned, num_systems)
-        (g,) = torch.autograd.grad(e_local.sum(), [pos])
+        grads = torch.autograd.grad(e_local.sum(), wrt)
         energy = e_local.detach().clone()
         dist.all_reduce(energy, group=self.group)
+        g = grads[0]
         dist.all_reduce(g, group=self.group)
-        return energy, -g
+        if not stress:
+            return energy, -g
+        g_disp = grads[1].contiguous()
+        dist.all_reduce(g_disp, group=self.group)
+        vol = torch.linalg.det(cell.detach()).abs()
+        return energy, -g, (g_disp / vol)[None]

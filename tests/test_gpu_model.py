@@ -115,3 +115,22 @@ def test_gpu_matches_oracle_on_water():
     assert ((e - er).abs() / er.abs().clamp(min=1)).max() < 1e-5
     assert (res["forces"].cpu().double() - ref["forces"]).abs().max() < 1e-4
     assert (res["stress"].cpu().double() - ref["stress"]).abs().max() < 1e-4 * max(1.0, ref["stress"].abs().max())
+
+
+def test_lean_mode_is_bitwise_identical(monkeypatch):
+    """The memory-lean backward (radial and conv2 outputs recomputed instead of saved) gives
+    exactly the default mode's energy and forces: the recomputation runs the same kernels."""
+    from flash_uma_b200.predict import Predictor
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
+    from flash_uma_b200.systems import bulk_fcc, to_graph
+    from flash_uma_b200.wrapper import ZeroAllocBackbone
+    data = to_graph([bulk_fcc(3, 3, 3, jitter=0.05, seed=6)]).to(DEV)
+    off = SyntheticESCNMDBackbone(num_layers=2, sphere_channels=64, hidden_channels=64, seed=7).to(DEV)
+    pred = Predictor(ZeroAllocBackbone(off), make_energy_head(64, 64).to(DEV))
+    monkeypatch.setenv("FUMA_LEAN", "0")
+    ref = pred(data, stress=True)
+    monkeypatch.setenv("FUMA_LEAN", "1")
+    got = pred(data, stress=True)
+    assert pred.backbone.ce.layers[0].lean
+    for k in ("energy", "forces", "stress"):
+        assert torch.equal(got[k], ref[k]), k

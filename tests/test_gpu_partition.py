@@ -1,5 +1,5 @@
 """Spatially partitioned CUDA path over NCCL (needs >= 2 GPUs; skipped otherwise): slab
-decomposition with per-layer halo exchange reproduces the single-GPU energy and forces."""
+decomposition with per-layer halo exchange reproduces the single-GPU energy, forces and stress."""
 import os
 import socket
 
@@ -44,11 +44,13 @@ def _worker(rank, world, port, out_path):
         csd = z.csd_embedding(d.charge, d.spin).float().detach()
         plan = make_plan(s.positions, s.cell, data.edge_index.numpy(), world, rank)
         pm = PartitionedModel(z.ce, plan, dev)
-        e, f = pm.energy_forces(head, d.pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd)
-        e2, f2 = pm.energy_forces(head, d.pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd)
-        assert torch.equal(f, f2)       # reproducible across calls
+        e, f, st = pm.energy_forces(head, d.pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd,
+                                    stress=True)
+        e2, f2, st2 = pm.energy_forces(head, d.pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd,
+                                       stress=True)
+        assert torch.equal(f, f2) and torch.equal(st, st2)      # reproducible across calls
         if rank == 0:
-            torch.save({"energy": e.cpu(), "forces": f.cpu()}, out_path)
+            torch.save({"energy": e.cpu(), "forces": f.cpu(), "stress": st.cpu()}, out_path)
     finally:
         dist.destroy_process_group()
 
@@ -62,6 +64,7 @@ def test_partitioned_cuda_matches_single_gpu(tmp_path):
     got = torch.load(out)
     s, data, bb, head = _setup()
     dev = torch.device("cuda", 0)
-    ref = Predictor(ZeroAllocBackbone(bb.to(dev)), head.to(dev))(data.to(dev))
+    ref = Predictor(ZeroAllocBackbone(bb.to(dev)), head.to(dev))(data.to(dev), stress=True)
     assert torch.allclose(got["energy"], ref["energy"].cpu(), rtol=2e-6)
     assert (got["forces"] - ref["forces"].cpu()).abs().max() < 2e-5
+    assert (got["stress"] - ref["stress"].cpu()).abs().max() < 2e-5 * max(1.0, ref["stress"].abs().max().item())

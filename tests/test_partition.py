@@ -1,5 +1,5 @@
 """Spatial decomposition (CPU): plan invariants, and the partitioned driver over gloo ranks
-(world sizes 2 and 4) reproducing the single-process energy and forces. The CPU oracle runs
+(world sizes 2 and 4) reproducing the single-process energy, forces and stress. The CPU oracle runs
 the model stages; the same driver runs the CUDA model over NCCL on GPUs."""
 import os
 import socket
@@ -68,10 +68,10 @@ def _worker(rank, world, port, out_path):
         csd = model.csd_embedding(data.charge, data.spin).double()
         plan = P.make_plan(s.positions, s.cell, data.edge_index.numpy(), world, rank)
         pm = P.PartitionedModel(model, plan, torch.device("cpu"))
-        e, f = pm.energy_forces(head, data.pos.double(), data.atomic_numbers, data.batch, data.cell_offsets.double(),
-                                data.cell[0].double(), csd)
+        e, f, st = pm.energy_forces(head, data.pos.double(), data.atomic_numbers, data.batch,
+                                    data.cell_offsets.double(), data.cell[0].double(), csd, stress=True)
         if rank == 0:
-            torch.save({"energy": e, "forces": f}, out_path)
+            torch.save({"energy": e, "forces": f, "stress": st}, out_path)
     finally:
         dist.destroy_process_group()
 
@@ -91,6 +91,7 @@ def test_partitioned_oracle_matches_single_process(world, tmp_path):
     bb = SyntheticESCNMDBackbone(num_layers=2, sphere_channels=16, hidden_channels=16, num_distance_basis=8, seed=3)
     ref = Predictor(OracleBackbone(copy.deepcopy(bb).double(), torch.float64), make_energy_head(16, 16).double())(
         type(data)(**{**data.__dict__, "pos": data.pos.double(), "cell": data.cell.double(),
-                      "cell_offsets": data.cell_offsets.double()}))
+                      "cell_offsets": data.cell_offsets.double()}), stress=True)
     assert torch.allclose(got["energy"], ref["energy"], rtol=1e-12, atol=1e-10)
     assert (got["forces"] - ref["forces"]).abs().max() < 1e-10
+    assert (got["stress"] - ref["stress"]).abs().max() < 1e-10
