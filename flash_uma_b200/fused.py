@@ -240,62 +240,20 @@ def message_block(layer, x_norm, x_in, xe, wigner, env, csd, idx_i, idx_j, batch
                                  csd.contiguous(), layer, idx_i, idx_j, batch, graph, bool(lean))
 
 
-def lean_needed(E: int, C: int, H: int, L: int, device) -> bool:
-    """Whether the saved activations of an L-layer step over E edges would crowd the device:
-    ~4 (L (32C + 2H) + 45C) bytes per edge in the default mode (92 KB at C = H = 128, L = 4;
-    measured: 139 GB for 1.51M edges), against 90% of the device memory. FUMA_LEAN=0/1 forces it."""
+def lean_bytes_per_edge(C: int, H: int, L: int) -> int:
+    """Estimated device bytes per edge of a default-mode step (saved activations of L layers plus
+    the largest transient of a layer's backward): 4 (L (32C + 2H) + 45C); 92,672 at C = H = 128,
+    L = 4 (measured: 139 GB for 1.51M edges)."""
+    return 4 * (L * (32 * C + 2 * H) + 45 * C)
+
+
+def lean_needed(E: int, C: int, H: int, L: int, device=None, total_bytes: int | None = None) -> bool:
+    """Whether the default-mode activations of an L-layer step over E edges would exceed 90% of
+    the device memory (``total_bytes``, default: the device's). FUMA_LEAN=0/1 forces it."""
     import os
     force = os.environ.get("FUMA_LEAN")
     if force is not None:
         return force == "1"
-    per_edge = 4 * (L * (32 * C + 2 * H) + 45 * C)
-    return E * per_edge > 0.9 * torch.cuda.get_device_properties(device).total_memory
-
-
-# ---- initial edge-degree embedding -----------------------------------------------------------
-
-class _InitBlockFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, xe_p, x_gauss, wigner, env, Z, batch, model, csd, graph, N):
-        E = xe_p.shape[0]
-        C = model.C
-        err = error_flag(xe_p.device)
-        rad, rsaved = radial_fwd(model.rad_init, xe_p, err)
-        x = _empty((N, 9, C), xe_p)
-        nat.call("fuma_init_scatter_fwd", ptr(rad), ptr(wigner), ptr(env), ptr(Z), ptr(batch), ptr(model.W_sphere),
-                 ptr(csd), ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(x), stream_of(xe_p))
-        ctx.save_for_backward(rad, wigner, env, *rsaved)
-        ctx.model, ctx.graph, ctx.N = model, graph, N
-        return x
-
-    @staticmethod
-    def backward(ctx, g_out):
-        rad, wigner, env, *rsaved = ctx.saved_tensors
-        model, graph, N = ctx.model, ctx.graph, ctx.N
-        g_out = g_out.contiguous()
-        E, C = rad.shape[0], model.C
-        err = error_flag(rad.device)
-        g_rad = torch.empty_like(rad)
-        g_w, g_env = _empty((E, 34), rad), _empty((E,), rad)
-        nat.call("fuma_init_scatter_bwd_f16x3", ptr(g_out), ptr(rad), ptr(wigner), ptr(env), ptr(graph.dst_row_ptr),
-                 ptr(graph.dst_col), N, E, C, ptr(g_rad), ptr(g_w), ptr(g_env), ptr(err), stream_of(rad))
-        g_xe = radial_bwd(model.rad_init, rsaved, g_rad, err)
-        return None, g_xe, g_w, g_env, None, None, None, None, None, None
-
-
-def init_block(model, xe, wigner, env, Z, batch, csd, graph, N):
-    """Initial node embedding from the split edge features (fp32 out)."""
-    xe_p, x_gauss = xe
-    return _InitBlockFn.apply(xe_p, x_gauss, wigner, env, Z.long().contiguous(), batch.long().contiguous(), model,
-                              csd.contiguous(), graph, int(N))
-
-
-def fusable(model) -> bool:
-    """True if every dense contraction of ``model`` (an ESCNInferenceModel in f16x3 mode) has
-    widths that are multiples of 16, so the fused blocks apply."""
-    lins = [model.rad_init.l1, model.rad_init.l2, model.rad_init.l3]
-    for lay in model.layers:
-        lins += [lay.rad.l1, lay.rad.l2, lay.rad.l3, lay.conv1_m0, lay.conv1_m1, lay.conv1_m2, lay.conv2_m0,
-                 lay.conv2_m1, lay.conv2_m2]
-    return (all(l.mode == "f16x3" and l.N % 16 == 0 and l.K % 16 == 0 for l in lins) and model.C % 16 == 0
-            and model.B % 16 == 0)
+    if total_bytes is None:
+        total_bytes = torch.cuda.get_device_properties(device).total_memory
+    return E * lean_bytes_per_edge(C, H, L) > 0.9 * total_bytes

@@ -1,0 +1,48 @@
+"""Host-side logic of the bench and of the lean-mode choice (no GPU)."""
+import csv
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def test_lean_mode_threshold(monkeypatch):
+    from flash_uma_b200.fused import lean_bytes_per_edge, lean_needed
+    monkeypatch.delenv("FUMA_LEAN", raising=False)
+    assert lean_bytes_per_edge(128, 128, 4) == 92672
+    total = 178 * 2 ** 30   # a B200
+    assert not lean_needed(1_512_000, 128, 128, 4, total_bytes=total)   # config 5 over 2 GPUs
+    assert lean_needed(3_024_000, 128, 128, 4, total_bytes=total)       # config 5 on one GPU
+    monkeypatch.setenv("FUMA_LEAN", "1")
+    assert lean_needed(10, 128, 128, 4, total_bytes=total)
+    monkeypatch.setenv("FUMA_LEAN", "0")
+    assert not lean_needed(10 ** 9, 128, 128, 4, total_bytes=total)
+
+
+@pytest.mark.parametrize("workload,world,atoms,stress,scaling", [
+    ("default", 1, 4000, False, "weak"), ("default", 2, 8000, False, "weak"),
+    ("config4", 1, 9999, True, "strong"), ("config5", 4, 100800, False, "strong")])
+def test_workloads(workload, world, atoms, stress, scaling):
+    import bench
+    system, with_stress, sc, label = bench.workload_system(workload, world)
+    assert system.natoms == atoms and with_stress == stress and sc == scaling and label
+
+
+def test_summarize_launches(tmp_path, capsys):
+    import bench
+    p = tmp_path / "launches.csv"
+    rows = [["ID", "Kernel Name", "Metric Name", "Metric Unit", "Metric Value"]]
+    seq = [("void at::native::FillFunctor<float>(x)", "usecond", "40"), ("fuma::gemm_f16x3_kernel<128>(a)", "usecond", "100"),
+           ("fuma::gather_fwd_kernel(b)", "nsecond", "50000"), ("fuma::gemm_f16x3_kernel<128>(c)", "msecond", "0.1"),
+           ("void at::native::FillFunctor<float>(x)", "usecond", "40"), ("fuma::gather_fwd_kernel(b)", "usecond", "7")]
+    for i, (n, u, v) in enumerate(seq):
+        rows.append([str(i), n, "gpu__time_duration.sum", u, v])
+    with open(p, "w", newline="") as f:
+        csv.writer(f).writerows(rows)
+    bench.summarize_launches(str(p))
+    out = capsys.readouterr().out
+    assert "one timed step: 3 launches, 0.25 ms" in out
+    assert "fuma::gemm_f16x3_kernel<128>" in out and "80.0%" in out
