@@ -491,6 +491,62 @@ def run_micro(args, device):
                       "kernels": dict(sorted(kernels.items(), key=lambda kv: -kv[1]["ms_per_step"]))}), flush=True)
 
 
+# the reference's published FlashUMA step times for its atom-count sweep (random graphs, ~50
+# edges per atom, pretrained uma-s-1p2, E+F+S, torch.compile, GPU model not stated):
+# examples/make_plots.py:14
+REFERENCE_SWEEP_MS = {100: 15.27, 200: 16.88, 500: 16.92, 1000: 23.00, 2000: 43.51}
+
+
+def run_sweep(args, device):
+    """Step time (energy + forces + stress) over the reference's atom-count sweep: random
+    clusters of 100-2,000 atoms with 50 edges per atom, C = 128, 4 layers, random-init weights.
+    Each size: CUDA-graph replays (the whole step captured once) and eager launches, CUDA-event
+    medians over ``--steps`` steps after ``--warmup``."""
+    import dataclasses
+    import statistics as st
+
+    from flash_uma_b200 import _native
+    from flash_uma_b200.predict import GraphedStep, Predictor
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
+    from flash_uma_b200.systems import random_cluster_graph
+    from flash_uma_b200.wrapper import ZeroAllocBackbone
+    _native.load()
+    off = SyntheticESCNMDBackbone(seed=0).to(device)
+    pred = Predictor(ZeroAllocBackbone(off, gemm=args.gemm), make_energy_head(128, 128, seed=1).to(device))
+    rows = []
+    for n in sorted(REFERENCE_SWEEP_MS):
+        data = random_cluster_graph(n, 50, seed=n).to(device)
+        g = torch.Generator().manual_seed(n)
+        pos = [data.pos + 0.01 * torch.randn(data.pos.shape, generator=g).to(device) for _ in range(args.steps)]
+
+        def timed(fn):
+            for k in range(args.warmup):
+                fn(pos[k % len(pos)])
+            torch.cuda.synchronize()
+            ts = []
+            for k in range(args.steps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn(pos[k])
+                b.record()
+                ts.append((a, b))
+            torch.cuda.synchronize()
+            return st.median(x.elapsed_time(y) for x, y in ts)
+
+        eager = timed(lambda p: pred(dataclasses.replace(data, pos=p), stress=True))
+        step = GraphedStep(pred, data, stress=True)
+        graph = timed(step)
+        rows.append({"atoms": n, "edges": int(data.edge_index.shape[1]), "ms_per_step_graph": graph,
+                     "ms_per_step_eager": eager, "reference_published_ms": REFERENCE_SWEEP_MS[n]})
+        del step
+    print(json.dumps({"metric": "ms per energy+forces+stress step, reference atom-count sweep (50 edges/atom)",
+                      "unit": "ms", "higher_is_better": False, "gemm": args.gemm, "steps": args.steps,
+                      "warmup": args.warmup, "data": "synthetic random clusters, random-init weights",
+                      "reference_note": "published FlashUMA times (examples/make_plots.py:14) are for the "
+                                        "pretrained uma-s-1p2 on an unstated GPU with torch.compile",
+                      "sizes": rows}), flush=True)
+
+
 def cpu_oracle_rate(atoms_sample: int = 256, min_seconds: float = 8.0, max_steps: int = 4):
     """Time the CPU oracle (PyTorch restatement of the reference) on a bulk-Cu sample."""
     from flash_uma_b200.predict import Predictor
@@ -601,6 +657,8 @@ def main():
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every kernel from the host each step instead of replaying a CUDA graph")
     ap.add_argument("--micro", action="store_true", help="one-layer kernel microbench (BASELINE config 2)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="step time over the reference's atom-count sweep (100-2,000 atoms, 50 edges/atom, E+F+S)")
     ap.add_argument("--nodes", type=int, default=20000)
     ap.add_argument("--edges", type=int, default=600000)
     args = ap.parse_args()
@@ -626,6 +684,10 @@ def main():
     if args.micro:
         if rank == 0:
             run_micro(args, device)
+        return
+    if args.sweep:
+        if rank == 0:
+            run_sweep(args, device)
         return
     if world > 1:
         import datetime

@@ -257,3 +257,14 @@ def lean_needed(E: int, C: int, H: int, L: int, device=None, total_bytes: int | 
     if total_bytes is None:
         total_bytes = torch.cuda.get_device_properties(device).total_memory
     return E * lean_bytes_per_edge(C, H, L) > 0.9 * total_bytes
+
+
+def fusable(model) -> bool:
+    """True if every dense contraction of ``model`` (an ESCNInferenceModel in f16x3 mode) has
+    widths that are multiples of 16, so the fused blocks apply."""
+    lins = [model.rad_init.l1, model.rad_init.l2, model.rad_init.l3]
+    for lay in model.layers:
+        lins += [lay.rad.l1, lay.rad.l2, lay.rad.l3, lay.conv1_m0, lay.conv1_m1, lay.conv1_m2, lay.conv2_m0,
+                 lay.conv2_m1, lay.conv2_m2]
+    return (all(l.mode == "f16x3" and l.N % 16 == 0 and l.K % 16 == 0 for l in lins) and model.C % 16 == 0
+            and model.B % 16 == 0)

@@ -248,6 +248,40 @@ def to_graph(systems, cutoff: float = 6.0, max_neighbors: int = 30, dtype=torch.
     )
 
 
+def random_cluster_graph(num_atoms: int, degree: int = 50, cutoff: float = 6.0, seed: int = 0,
+                         dtype=torch.float32) -> AtomicGraph:
+    """Random non-periodic cluster with exactly ``num_atoms * degree`` directed edges: uniform
+    positions in a cube, scaled so that the (N * degree)-th smallest distance between distinct
+    atoms sits just inside the cutoff; every ordered pair closer than the cutoff is an edge (no
+    per-atom cap), emitted by destination. Random atomic numbers 1..99. The same workload shape
+    as the reference's atom-count sweep (random graphs of fixed mean degree); the cell is a
+    cube enclosing the cluster (used only for the stress normalisation)."""
+    rng = np.random.default_rng(seed)
+    pos = rng.random((num_atoms, 3))
+    d = np.sqrt(((pos[:, None, :] - pos[None, :, :]) ** 2).sum(-1))
+    np.fill_diagonal(d, np.inf)
+    k = min(num_atoms * degree, num_atoms * (num_atoms - 1))
+    kth = np.partition(d.ravel(), k - 1)[k - 1]
+    scale = (cutoff - 1e-4) / kth
+    pos = pos * scale
+    d = d * scale
+    dst, src = np.nonzero(d.T < cutoff)          # rows of d.T are destinations: emitted by destination
+    E = src.shape[0]
+    side = float(pos.max() + cutoff)
+    return AtomicGraph(
+        pos=torch.tensor(pos, dtype=dtype),
+        atomic_numbers=torch.tensor(rng.integers(1, 100, num_atoms), dtype=torch.long),
+        cell=torch.tensor(np.eye(3)[None] * side, dtype=dtype),
+        cell_offsets=torch.zeros(E, 3, dtype=dtype),
+        edge_index=torch.tensor(np.stack([src, dst]), dtype=torch.long),
+        natoms=torch.tensor([num_atoms], dtype=torch.long),
+        nedges=torch.tensor([E], dtype=torch.long),
+        charge=torch.zeros(1, dtype=torch.long),
+        spin=torch.zeros(1, dtype=torch.long),
+        batch=torch.zeros(num_atoms, dtype=torch.long),
+    )
+
+
 # ---- benchmark configurations (BASELINE.json "configs") --------------------------------------
 
 def config1_system() -> AtomicSystem:

@@ -46,3 +46,18 @@ def test_summarize_launches(tmp_path, capsys):
     out = capsys.readouterr().out
     assert "one timed step: 3 launches, 0.25 ms" in out
     assert "fuma::gemm_f16x3_kernel<128>" in out and "80.0%" in out
+
+
+@pytest.mark.parametrize("C,B,gemm,fused", [(128, 64, "f16x3", True), (32, 16, "f16x3", True),
+                                            (16, 8, "f16x3", False), (128, 64, "tf32x3", False)])
+def test_model_construction_and_path_choice(C, B, gemm, fused, monkeypatch):
+    """Building the model needs no GPU; the fused blocks are chosen exactly when every GEMM
+    width is a multiple of 16 in the f16x3 mode."""
+    monkeypatch.delenv("FUMA_FUSED", raising=False)
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone
+    from flash_uma_b200.wrapper import ZeroAllocBackbone
+    off = SyntheticESCNMDBackbone(num_layers=2, sphere_channels=C, hidden_channels=C, num_distance_basis=B)
+    bb = ZeroAllocBackbone(off, gemm=gemm)
+    assert bb.ce.fused is fused
+    assert all(lay.fused is fused for lay in bb.ce.layers)
+    assert bb.ce.set_fused(False) is False and not bb.ce.layers[0].fused
