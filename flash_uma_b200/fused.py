@@ -259,6 +259,44 @@ def lean_needed(E: int, C: int, H: int, L: int, device=None, total_bytes: int | 
     return E * lean_bytes_per_edge(C, H, L) > 0.9 * total_bytes
 
 
+# ---- initial edge-degree embedding -----------------------------------------------------------
+
+class _InitBlockFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xe_p, x_gauss, wigner, env, Z, batch, model, csd, graph, N):
+        E = xe_p.shape[0]
+        C = model.C
+        err = error_flag(xe_p.device)
+        rad, rsaved = radial_fwd(model.rad_init, xe_p, err)
+        x = _empty((N, 9, C), xe_p)
+        nat.call("fuma_init_scatter_fwd", ptr(rad), ptr(wigner), ptr(env), ptr(Z), ptr(batch), ptr(model.W_sphere),
+                 ptr(csd), ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(x), stream_of(xe_p))
+        ctx.save_for_backward(rad, wigner, env, *rsaved)
+        ctx.model, ctx.graph, ctx.N = model, graph, N
+        return x
+
+    @staticmethod
+    def backward(ctx, g_out):
+        rad, wigner, env, *rsaved = ctx.saved_tensors
+        model, graph, N = ctx.model, ctx.graph, ctx.N
+        g_out = g_out.contiguous()
+        E, C = rad.shape[0], model.C
+        err = error_flag(rad.device)
+        g_rad = torch.empty_like(rad)
+        g_w, g_env = _empty((E, 34), rad), _empty((E,), rad)
+        nat.call("fuma_init_scatter_bwd_f16x3", ptr(g_out), ptr(rad), ptr(wigner), ptr(env), ptr(graph.dst_row_ptr),
+                 ptr(graph.dst_col), N, E, C, ptr(g_rad), ptr(g_w), ptr(g_env), ptr(err), stream_of(rad))
+        g_xe = radial_bwd(model.rad_init, rsaved, g_rad, err)
+        return None, g_xe, g_w, g_env, None, None, None, None, None, None
+
+
+def init_block(model, xe, wigner, env, Z, batch, csd, graph, N):
+    """Initial node embedding from the split edge features (fp32 out)."""
+    xe_p, x_gauss = xe
+    return _InitBlockFn.apply(xe_p, x_gauss, wigner, env, Z.long().contiguous(), batch.long().contiguous(), model,
+                              csd.contiguous(), graph, int(N))
+
+
 def fusable(model) -> bool:
     """True if every dense contraction of ``model`` (an ESCNInferenceModel in f16x3 mode) has
     widths that are multiples of 16, so the fused blocks apply."""

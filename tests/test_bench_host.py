@@ -61,3 +61,10 @@ def test_model_construction_and_path_choice(C, B, gemm, fused, monkeypatch):
     assert bb.ce.fused is fused
     assert all(lay.fused is fused for lay in bb.ce.layers)
     assert bb.ce.set_fused(False) is False and not bb.ce.layers[0].fused
+
+
+def test_fused_module_surface():
+    """Every entry point the model and the bench use exists (a missing one only fails on a GPU)."""
+    from flash_uma_b200 import fused
+    for name in ("geometry", "message_block", "init_block", "fusable", "lean_needed", "radial_fwd", "radial_bwd"):
+        assert callable(getattr(fused, name)), name
