@@ -87,6 +87,11 @@ def gemm_flops_per_step(E, C, B, L, H=None, gauss_only=True):
 
 GEMM_OPS = ("fuma_linear_f16x3", "fuma_linear")
 
+# DRAM bytes per call (dram__bytes_read.sum + dram__bytes_write.sum) measured by ncu on the
+# config-3 step with the f16x3 fused path: profiles/ncu_dram_traffic_bench_config3_step.md
+# (GEMM: average over the step's launches; gather backward: its four launches per call).
+NCU_TRAFFIC_BYTES = {"fuma_linear_f16x3": 374.7e6, "fuma_gather_bwd_f16x3": 2716.0e6}
+
 
 def gemm_mode(mode, bf16):
     """Tensor-pipe products per fp32 product, the pipe's peak (TF/s) and labels of a GEMM mode."""
@@ -348,7 +353,8 @@ def run_flash(args, rank, world, device):
         roof = {"kernel": gm["kernel"], "bound": "tensor", "achieved": achieved,
                 "peak": gm["peak"], "unit": "TFLOP/s", "frac": achieved / gm["peak"],
                 "peak_kind": f"{peak_kind}: {gm['peak_note']}",
-                "traffic": None, "alg_flops_per_launch": flops_launch}
+                "traffic": NCU_TRAFFIC_BYTES.get(dominant) if args.workload == "default" and world == 1 else None,
+                "alg_flops_per_launch": flops_launch}
     else:
         nbytes = alg_bytes(dominant, Nk, Ek, C, B, M_rows=Ek, D=128)
         achieved = nbytes / (avg_ms * 1e-3) / 1e9 if nbytes and avg_ms > 0 else None
@@ -367,7 +373,8 @@ def run_flash(args, rank, world, device):
         nb = alg_bytes(top_mem, Nk, Ek, C, B, M_rows=Ek, D=128)
         gbs = nb / (ms_launch * 1e-3) / 1e9
         roof_mem = {"kernel": top_mem, "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                    "frac": gbs / hbm, "alg_bytes_per_launch": nb, "avg_launch_ms": ms_launch}
+                    "frac": gbs / hbm, "alg_bytes_per_launch": nb, "avg_launch_ms": ms_launch,
+                    "traffic": NCU_TRAFFIC_BYTES.get(top_mem) if args.workload == "default" and world == 1 else None}
     atoms_total = N if world > 1 else world * N
     out = {
         "metric": METRIC, "value": atoms_total * K / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
