@@ -494,7 +494,7 @@ __global__ void split_rows_f16_kernel(const float* __restrict__ x, int64_t lda, 
 
 void launch_split_rows_f16(const float* x, int64_t lda, int64_t M, int K, void* out, int64_t ldp, int* err,
                            cudaStream_t s) {
-  split_rows_f16_kernel<<<grid_for(M * (K / 4), 256, 8), 256, 0, s>>>(x, lda, M, K, static_cast<uint8_t*>(out), ldp,
+  split_rows_f16_kernel<<<grid_resident(split_rows_f16_kernel, 256, M * (K / 4), 256), 256, 0, s>>>(x, lda, M, K, static_cast<uint8_t*>(out), ldp,
                                                                      err);
 }
 

@@ -278,13 +278,13 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_short_kernel(const float* __r
 
 void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,
                        int C, bool split, int* err, cudaStream_t s) {
-  gating_fwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(Y0, Y1, Y2, Z0, Z1, Z2, E, C, split, err);
+  gating_fwd_kernel<<<grid_resident(gating_fwd_kernel, 256, E * (C / 4), 256), 256, 0, s>>>(Y0, Y1, Y2, Z0, Z1, Z2, E, C, split, err);
 }
 
 void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, const float* Y0, const float* Y1,
                        const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, bool split, int* err,
                        cudaStream_t s) {
-  gating_bwd_kernel<<<grid_for(E * (C / 4), 256, 8), 256, 0, s>>>(gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C,
+  gating_bwd_kernel<<<grid_resident(gating_bwd_kernel, 256, E * (C / 4), 256), 256, 0, s>>>(gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C,
                                                                    split, err);
 }
 
@@ -294,10 +294,10 @@ void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, f
   // rows of <= 128 values: 8 lanes per row; longer rows: one row per warp (several rows per
   // warp at 32 lanes each raised the register count and measured slower on B200)
 #define FWD(V, R) \
-  ln_silu_fwd_kernel<V, R><<<grid_for((M + R - 1) / R, 8, 8), 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps, \
+  ln_silu_fwd_kernel<V, R><<<grid_resident(ln_silu_fwd_kernel<V, R>, 256, (M + R - 1) / R, 8), 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps, \
                                                                            split, err)
   if (d4 <= 32) {
-    ln_silu_fwd_short_kernel<<<grid_for((M + 3) / 4, 8, 8), 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps,
+    ln_silu_fwd_short_kernel<<<grid_resident(ln_silu_fwd_short_kernel, 256, (M + 3) / 4, 8), 256, 0, s>>>(x, gamma, beta, out, mean, rstd, M, D, eps,
                                                                          split, err);
   } else if (d4 <= 64) FWD(2, 1);
   else if (d4 <= 128) FWD(4, 1);
@@ -310,7 +310,7 @@ void launch_ln_silu_bwd(const float* x, const float* gamma, const float* beta, c
                         const float* g_out, float* g_x, int64_t M, int D, bool split, int* err, cudaStream_t s) {
   const int d4 = D / 4;
 #define BWD(V, R)                                                                                                      \
-  ln_silu_bwd_kernel<V, R><<<grid_for((M + R - 1) / R, 8, 8), 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, \
+  ln_silu_bwd_kernel<V, R><<<grid_resident(ln_silu_bwd_kernel<V, R>, 256, (M + R - 1) / R, 8), 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, \
                                                                            D, split, err)
   if (d4 <= 32) BWD(1, 1);   // the 8-lanes-per-row variant measured slower here (0.68 vs 0.53 ms / step)
   else if (d4 <= 64) BWD(2, 1);

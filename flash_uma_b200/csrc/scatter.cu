@@ -432,14 +432,14 @@ void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, c
 void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,
                              const float* env, const int64_t* Z, const int64_t* batch, const float* W_sphere,
                              const float* csd, float* x_out, int64_t N, int C, cudaStream_t s) {
-  init_scatter_fwd_kernel<8><<<grid_for(N, 8, 8), 256, 0, s>>>(row_ptr, col_idx, rad, wig, env, Z, batch, W_sphere,
+  init_scatter_fwd_kernel<8><<<grid_resident(init_scatter_fwd_kernel<8>, 256, N, 8), 256, 0, s>>>(row_ptr, col_idx, rad, wig, env, Z, batch, W_sphere,
                                                                csd, x_out, N, C);
 }
 
 void launch_init_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* rad,
                              const float* wig, const float* env, float* g_rad, float* g_wig, float* g_env, int64_t N,
                              int C, bool split, int* err, cudaStream_t s) {
-  init_scatter_bwd_kernel<4><<<grid_for(N, 4, 16), 128, 0, s>>>(row_ptr, col_idx, g_out, rad, wig, env, g_rad, g_wig,
+  init_scatter_bwd_kernel<4><<<grid_resident(init_scatter_bwd_kernel<4>, 128, N, 4), 128, 0, s>>>(row_ptr, col_idx, g_out, rad, wig, env, g_rad, g_wig,
                                                                  g_env, N, C, split, err);
 }
 
