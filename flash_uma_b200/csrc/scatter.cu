@@ -28,13 +28,18 @@ __device__ __forceinline__ void stage_edge(float* sw, const float* __restrict__ 
   if (lane == 2) sw[34] = __ldg(env + e);
 }
 
+constexpr int kFwdWarps = 4;   // rotate-scatter forward: warps per block (static ring below 48 KB)
+constexpr int kRing = 4;       // rotate-scatter forward: edges staged per warp
+
 }  // namespace
 
-// One launch per coefficient block: PART 0 accumulates rows 0-3 (l = 0, 1; D1), PART 1 rows 4-8
-// (l = 2; D2); the two write disjoint rows of x_out. The CSR chunk (edge ids and envelopes) is
-// loaded once into the lanes and broadcast with shuffles.
+// Forward, warp per destination atom, one launch per coefficient block (PART 0: rows 0-3, l <= 1,
+// Wigner 0-8; PART 1: rows 4-8, l = 2, Wigner 9-33; disjoint rows of x_out). The atom's edges are summed one at a time in CSR
+// order into fp64 accumulators; their Z slots, Wigner block and envelope are copied into a
+// per-warp ring of kRing shared-memory buffers with cp.async, kRing - 1 edges ahead of the sum,
+// so a warp waits for memory about once per kRing - 1 edges instead of once per edge.
 template <int PART>
-__global__ void __launch_bounds__(256, 2) rotate_scatter_fwd_kernel(
+__global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ Z0,
     const float* __restrict__ Z1, const float* __restrict__ Z2, const float* __restrict__ wig,
     const float* __restrict__ env, const float* __restrict__ x_res, float* __restrict__ x_out, int64_t N, int C) {
@@ -42,97 +47,103 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_fwd_kernel(
   constexpr int kW = PART ? 25 : 9;
   constexpr int kWoff = PART ? 9 : 0;
   constexpr int kRow0 = PART ? 4 : 0;
-  __shared__ float s_w[8][56];   // two edges' Wigner blocks
+  constexpr int kS = PART ? 5 : 4;   // Z slots per edge and lane (16-byte copies)
+  __shared__ float4 s_stage[kFwdWarps][kRing][kS][32];
+  __shared__ float s_w[kFwdWarps][kRing][28];   // Wigner block (0..kW-1) and envelope (27)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
-  float* sw = s_w[warp];
-  for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
+  for (int64_t jn = (int64_t)blockIdx.x * kFwdWarps + warp; jn < N; jn += (int64_t)gridDim.x * kFwdWarps) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
-    for (int c0 = 0; c0 < C4; c0 += 32) {
-      const int c4 = c0 + lane;
-      const bool act = c4 < C4;
+    for (int cb = 0; cb < C4; cb += 32) {
+      const int c4 = cb + lane;
+      const bool on = c4 < C4;
       const int co = c4 * 4;
+      // copies of edge e's Z slots (in the order the sum reads them), Wigner block and envelope
+      // into ring buffer b, one commit group per edge
+      auto issue = [&](int64_t e, int b) {
+        if (on) {
+          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
+          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
+          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+          float4* d = &s_stage[warp][b][0][lane];
+          if constexpr (PART == 0) {
+            cp_async16(d + 0 * 32, z0);
+            cp_async16(d + 1 * 32, z1 + 2 * C);
+            cp_async16(d + 2 * 32, z0 + C);
+            cp_async16(d + 3 * 32, z1);
+          } else {
+            cp_async16(d + 0 * 32, z2 + C);
+            cp_async16(d + 1 * 32, z1 + 3 * C);
+            cp_async16(d + 2 * 32, z0 + 2 * C);
+            cp_async16(d + 3 * 32, z1 + C);
+            cp_async16(d + 4 * 32, z2);
+          }
+        }
+        if (lane < kW) cp_async4(&s_w[warp][b][lane], wig + e * kWig + kWoff + lane);
+        if (lane == 31) cp_async4(&s_w[warp][b][27], env + e);
+        cp_async_commit();
+      };
+      // the edge list, 32 entries at a time in a lane register; `ib` is the window's first edge
+      int ib = kb;
+      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
+      int ki = kb;   // next CSR position to copy
+      auto issue_next = [&]() {
+        if (ki < ke) {
+          if (ki - ib >= 32) {
+            ib += 32;
+            e_l = (ib + lane < ke) ? col_idx[ib + lane] : 0;
+          }
+          issue(__shfl_sync(kFull, e_l, ki - ib), (ki - kb) % kRing);
+        } else {
+          cp_async_commit();   // empty group keeps "groups in flight" counting edges
+        }
+        ++ki;
+      };
+#pragma unroll 1
+      for (int p = 0; p < kRing - 1; ++p) issue_next();
       d4 acc[kRows];
-      if (act) {
+      if (on) {
         const float* xr = x_res + jn * 9 * (int64_t)C + kRow0 * C + co;
 #pragma unroll
         for (int l = 0; l < kRows; ++l) acc[l] = d4_of(ld4(xr + l * C));
       }
-      for (int k0 = kb; k0 < ke; k0 += 32) {
-        int64_t e_l = 0;
-        float env_l = 0.f;
-        if (k0 + lane < ke) {
-          e_l = col_idx[k0 + lane];
-          env_l = __ldg(env + e_l);
-        }
-        const int cnt = (ke - k0) < 32 ? (ke - k0) : 32;
-        // two edges per iteration (their loads in flight together), accumulated in CSR order
-        for (int q = 0; q < cnt; q += 2) {
-          const bool two = q + 1 < cnt;
-          const int q1 = two ? q + 1 : q;
-          const int64_t e0 = __shfl_sync(kFull, e_l, q), e1 = __shfl_sync(kFull, e_l, q1);
-          const float ev0 = __shfl_sync(kFull, env_l, q), ev1 = __shfl_sync(kFull, env_l, q1);
-          if (lane < kW) {
-            sw[lane] = __ldg(wig + e0 * kWig + kWoff + lane);
-            sw[28 + lane] = __ldg(wig + e1 * kWig + kWoff + lane);
-          }
-          __syncwarp();
-          if (act) {
-            if constexpr (PART == 0) {
-              float4 m[2][3], z[2];
+#pragma unroll 1
+      for (int k = kb; k < ke; ++k) {
+        issue_next();   // refills the buffer summed in the previous iteration
+        cp_async_wait<kRing - 1>();
+        __syncwarp();
+        const int b = (k - kb) % kRing;
+        const float* D = s_w[warp][b];
+        const float ev = D[27];
+        const float4* src = &s_stage[warp][b][0][lane];
+        if (on) {
+          if constexpr (PART == 0) {
+            acc[0] += src[0] * ev;
+            const float4 m0 = src[32], m1 = src[64], m2 = src[96];
 #pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int64_t e = u ? e1 : e0;
-                const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-                const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-                m[u][0] = ld4_stream(z1 + 2 * C); m[u][1] = ld4_stream(z0 + C); m[u][2] = ld4_stream(z1);
-                z[u] = ld4_stream(z0);
-              }
+            for (int kk = 0; kk < 3; ++kk) {
+              float4 a = D[kk] * m0;
+              fma4(a, D[3 + kk], m1);
+              fma4(a, D[6 + kk], m2);
+              acc[1 + kk] += a * ev;
+            }
+          } else {
+            float4 m[5];
 #pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                if (u == 1 && !two) break;
-                const float* D = sw + 28 * u;
-                const float ev = u ? ev1 : ev0;
-                acc[0] += z[u] * ev;
+            for (int r = 0; r < 5; ++r) m[r] = src[32 * r];
 #pragma unroll
-                for (int kk = 0; kk < 3; ++kk) {
-                  float4 a = D[kk] * m[u][0];
-                  fma4(a, D[3 + kk], m[u][1]);
-                  fma4(a, D[6 + kk], m[u][2]);
-                  acc[1 + kk] += a * ev;
-                }
-              }
-            } else {
-              float4 m[2][5];
+            for (int kk = 0; kk < 5; ++kk) {
+              float4 a = D[kk] * m[0];
 #pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int64_t e = u ? e1 : e0;
-                const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-                const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-                const float* z2 = Z2 + e * 2 * (int64_t)C + co;
-                m[u][0] = ld4_stream(z2 + C); m[u][1] = ld4_stream(z1 + 3 * C); m[u][2] = ld4_stream(z0 + 2 * C);
-                m[u][3] = ld4_stream(z1 + C); m[u][4] = ld4_stream(z2);
-              }
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                if (u == 1 && !two) break;
-                const float* D = sw + 28 * u;
-                const float ev = u ? ev1 : ev0;
-#pragma unroll
-                for (int kk = 0; kk < 5; ++kk) {
-                  float4 a = D[kk] * m[u][0];
-#pragma unroll
-                  for (int r = 1; r < 5; ++r) fma4(a, D[r * 5 + kk], m[u][r]);
-                  acc[kk] += a * ev;
-                }
-              }
+              for (int r = 1; r < 5; ++r) fma4(a, D[r * 5 + kk], m[r]);
+              acc[kk] += a * ev;
             }
           }
-          __syncwarp();
         }
+        __syncwarp();   // buffer b is refilled by the next iteration's copies
       }
-      if (act) {
+      cp_async_wait<0>();   // the trailing (empty) groups
+      if (on) {
         float* xo = x_out + jn * 9 * (int64_t)C + kRow0 * C + co;
 #pragma unroll
         for (int l = 0; l < kRows; ++l) st4(xo + l * C, f4_of(acc[l]));
@@ -413,9 +424,11 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
 void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* Z0, const float* Z1,
                                const float* Z2, const float* wig, const float* env, const float* x_res, float* x_out,
                                int64_t N, int C, cudaStream_t s) {
-  const unsigned g = grid_for(N, 8, 2);
-  rotate_scatter_fwd_kernel<0><<<g, 256, 0, s>>>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
-  rotate_scatter_fwd_kernel<1><<<g, 256, 0, s>>>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
+  const int t = kFwdWarps * 32;
+  rotate_scatter_fwd_kernel<0><<<grid_resident(rotate_scatter_fwd_kernel<0>, t, N, kFwdWarps), t, 0, s>>>(
+      row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
+  rotate_scatter_fwd_kernel<1><<<grid_resident(rotate_scatter_fwd_kernel<1>, t, N, kFwdWarps), t, 0, s>>>(
+      row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
 }
 
 void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* Z0,
