@@ -225,11 +225,26 @@ def build_partitioned(device, gemm: str, world: int, rank: int, system=None, str
     d = data.to(device)
     csd = bb.csd_embedding(d.charge, d.spin).float().detach()
 
+    fixed = (d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd)
+
     def step(pos):
-        out = pm.energy_forces(head, pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd, stress=stress)
+        out = pm.energy_forces(head, pos, *fixed, stress=stress)
         return dict(zip(("energy", "forces", "stress"), out))
 
-    return system, data, step, plan
+    def make_graph(pos0, capture_hook=None):
+        """The step captured as one CUDA graph with its NCCL collectives (every rank calls this)."""
+        from flash_uma_b200.partition import GraphedPartitionedStep
+        g = GraphedPartitionedStep(pm, head, pos0, *fixed, stress=stress, capture_hook=capture_hook)
+
+        class Step:
+            def __call__(self, pos):
+                return dict(zip(("energy", "forces", "stress"), g(pos)))
+
+            def release(self):
+                g.release()
+        return Step()
+
+    return system, data, step, plan, make_graph
 
 
 def run_flash(args, rank, world, device):
@@ -240,7 +255,8 @@ def run_flash(args, rank, world, device):
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     system, with_stress, scaling, label = workload_system(args.workload, world)
     if world > 1:
-        system, data_cpu, step, plan = build_partitioned(device, args.gemm, world, rank, system, with_stress)
+        system, data_cpu, step, plan, make_graph = build_partitioned(device, args.gemm, world, rank, system,
+                                                                      with_stress)
         N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
         pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, K + W, seed=0)]
     else:
@@ -269,15 +285,21 @@ def run_flash(args, rank, world, device):
     dominant = max(per_op, key=per_op.get)
     launches_per_step = probe.launches
 
-    graphed = world == 1 and args.graph
+    graphed = args.graph
+    gstep = None
     if graphed:
-        # the whole step (graph build, forward, backward) as one CUDA graph. The probe is active
-        # during the capture: it counts the launches of one step and records event nodes around
-        # the dominant kernel's launches, whose elapsed times then read the last replay.
-        from flash_uma_b200.predict import GraphedStep
+        # the whole step (graph build, forward, backward; with N > 1 also the NCCL halo exchanges
+        # and all-reduces) as one CUDA graph. The probe is active during the capture: it counts
+        # the launches of one step and records event nodes around the dominant kernel's
+        # launches, whose elapsed times then read the last replay.
         gprobe = _native.LaunchProbe(timed=[dominant], external=True)
-        gstep = GraphedStep(pred, dataclasses.replace(data, pos=pos_seq[0]), stress=with_stress,
-                            capture_hook=lambda on: _native.set_probe(gprobe if on else None))
+        hook = lambda on: _native.set_probe(gprobe if on else None)   # noqa: E731
+        if world > 1:
+            gstep = make_graph(pos_seq[0], capture_hook=hook)
+        else:
+            from flash_uma_b200.predict import GraphedStep
+            gstep = GraphedStep(pred, dataclasses.replace(data, pos=pos_seq[0]), stress=with_stress,
+                                capture_hook=hook)
         graph_launches = gprobe.launches
         step = gstep
     # ---- timed region 1: inputs resident in HBM. Launch counting covers every timed step; the
@@ -334,6 +356,8 @@ def run_flash(args, rank, world, device):
     torch.cuda.synchronize()
     e2e_ms = sum(a.elapsed_time(b) for a, b in evs2)
 
+    if gstep is not None and world > 1:
+        gstep.release()   # the graph holds NCCL work: free it before the process group goes
     t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -385,7 +409,8 @@ def run_flash(args, rank, world, device):
                    "atoms": N, "edges": E, "sphere_channels": C, "layers": L, "num_distance_basis": B,
                    "cutoff": 6.0, "max_neighbors": 30, "gemm": gm["label"],
                    "l2": "flushed (256 MB write) before every step, outside the timed events",
-                   "launch": "one CUDA graph replay per step (graph build, forward, backward captured once)"
+                   "launch": ("one CUDA graph replay per step (graph build, forward, backward"
+                              + (", NCCL halo exchanges and all-reduces" if world > 1 else "") + " captured once)")
                    if graphed else "eager (every kernel launched from the host)",
                    "parallelism": f"spatial slabs x{world} (halo atoms per rank: {len(plan.halo)} on rank 0)"
                    if world > 1 else "single GPU"},

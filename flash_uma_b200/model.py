@@ -124,11 +124,15 @@ class PackedLayer(nn.Module):
     fused = False   # set by ESCNInferenceModel: x_edge is then the row-packed split of the edge features
     lean = False    # set per step by ESCNInferenceModel for graphs too large to keep every activation
 
-    def forward(self, x_in, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch):
+    def forward(self, x_in, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, n_out=None):
+        """``n_out``: return only the first ``n_out`` atoms' outputs (the partitioned model's owned
+        atoms; the node-wise tail then skips the halo rows, whose messages are not computed here)."""
         x_norm = self.norm_1(x_in)
         if self.fused:
             x_mid = fused.message_block(self, x_norm, x_in, x_edge, wigner, env, csd_emb, idx_i, idx_j, batch, graph,
                                         self.lean)
+            if n_out is not None:
+                x_mid = x_mid[:n_out]
             return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
         rad_out = self.rad(x_edge)
         X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch, graph=graph)
@@ -136,6 +140,8 @@ class PackedLayer(nn.Module):
         O0, O1, O2 = self.conv2_m0(Z0), self.conv2_m1(Z1), self.conv2_m2(Z2)
         x_mid = ops.rotate_scatter_split(O0, O1, O2, wigner, env, x_in, idx_j, graph.dst_row_ptr, graph.dst_col,
                                          x_in.shape[0])
+        if n_out is not None:
+            x_mid = x_mid[:n_out]
         return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
 
 
@@ -204,8 +210,10 @@ class ESCNInferenceModel(nn.Module):
                                      graph.dst_col, N)
 
     def layer_forward(self, k, x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, charge=None, spin=None,
-                      natoms=None):
-        x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch)
+                      natoms=None, n_out=None):
+        x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, n_out)
+        if n_out is not None:
+            batch = batch[:n_out]
         if self.charge_end > self.charge_start:
             x = balance_channels_batched(x, charge, natoms, batch, self.charge_start, self.charge_end, 0.0)
         if self.spin_end > self.spin_start:

@@ -166,7 +166,9 @@ class PartitionedModel:
         for k in range(len(m.layers)):
             x_owned = x[: self.n_owned]
             x = torch.cat([x_owned, halo_exchange(x_owned, self.ex)], 0)
-            x = m.layer_forward(k, x, xe, wig, env, self.idx_i, self.idx_j, self.graph, csd_emb, b_l)
+            # owned rows out: the halo rows' layer outputs would be replaced by the next exchange
+            x = m.layer_forward(k, x, xe, wig, env, self.idx_i, self.idx_j, self.graph, csd_emb, b_l,
+                                n_out=self.n_owned)
         return m.final(x[: self.n_owned])
 
     def energy_forces(self, head, pos, Z, batch, cell_offsets, cell, csd_emb, num_systems: int = 1,
@@ -202,3 +204,53 @@ class PartitionedModel:
         dist.all_reduce(g_disp, group=self.group)
         vol = torch.linalg.det(cell.detach()).abs()
         return energy, -g, (g_disp / vol)[None]
+
+
+class GraphedPartitionedStep:
+    """:meth:`PartitionedModel.energy_forces` on a fixed partition (new positions every call),
+    captured once as a CUDA graph together with its NCCL collectives (the per-layer halo
+    exchanges in both directions and the energy / gradient all-reduces): a call copies the
+    global positions into the captured input and replays the whole step with one launch.
+    Every rank must construct it, call it and :meth:`release` it in the same order (the
+    collectives inside are matched across ranks). Warm-up runs eagerly on a side stream first,
+    so the NCCL communicators and every cached tensor exist before the capture. Returns the
+    captured output tuple (overwritten by the next call). :meth:`release` frees the graph; do
+    it before ``destroy_process_group``, which otherwise waits for the graph's NCCL work."""
+
+    def __init__(self, pm: PartitionedModel, head, pos, Z, batch, cell_offsets, cell, csd_emb, num_systems: int = 1,
+                 stress: bool = False, warmup: int = 3, capture_hook=None):
+        self._pos = pos.detach().clone()
+        args = (head, self._pos, Z, batch, cell_offsets, cell, csd_emb, num_systems, stress)
+        dev = self._pos.device
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                pm.energy_forces(*args)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=pm.group)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            if capture_hook is not None:
+                capture_hook(True)
+            try:
+                self.out = pm.energy_forces(*args)
+            finally:
+                if capture_hook is not None:
+                    capture_hook(False)
+        torch.cuda.synchronize(dev)
+
+    def __call__(self, pos: torch.Tensor):
+        from . import linear
+        linear.poll_errors()
+        self._pos.copy_(pos, non_blocking=True)
+        self.graph.replay()
+        return self.out
+
+    def release(self) -> None:
+        if self.graph is not None:
+            torch.cuda.synchronize(self._pos.device)
+            self.graph.reset()
+            self.graph = None
+            self.out = None

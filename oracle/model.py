@@ -90,7 +90,7 @@ class OracleLayer:
         w = d(c2.so2_m_conv[1].fc.weight); self.W2_m2 = pack_complex(w[:C], w[C:])
         self.norm_1, self.norm_2, self.atom_wise = blk.norm_1, blk.norm_2, blk.atom_wise
 
-    def __call__(self, x_in, x_edge, wigner, env, idx_i, idx_j, row_ptr, col_idx, csd_emb, batch):
+    def __call__(self, x_in, x_edge, wigner, env, idx_i, idx_j, row_ptr, col_idx, csd_emb, batch, n_out=None):
         x_norm = self.norm_1(x_in)
         rad_out = self.rad(x_edge)
         X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch)
@@ -98,6 +98,8 @@ class OracleLayer:
         Z0, Z1, Z2 = ops.fused_gating_split(Y0, Y1, Y2, self.C)
         O0, O1, O2 = F.linear(Z0, self.W2_m0, self.b2_m0), F.linear(Z1, self.W2_m1), F.linear(Z2, self.W2_m2)
         x_mid = ops.rotate_scatter_split(O0, O1, O2, wigner, env, x_in, idx_j, row_ptr, col_idx, x_in.shape[0])
+        if n_out is not None:   # only the first n_out atoms' outputs are wanted (partitioned model)
+            x_mid = x_mid[:n_out]
         return self.atom_wise(self.norm_2(x_mid)) + x_mid
 
 
@@ -146,9 +148,11 @@ class OracleBackbone:
         return ops.init_node_scatter(rad0, wigner, env, Z, batch, self.W_sphere, csd_emb, idx_j, graph[0], graph[1], N)
 
     def layer_forward(self, k, x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, charge=None, spin=None,
-                      natoms=None):
+                      natoms=None, n_out=None):
         from flash_uma_b200.nodewise import balance_channels_batched
-        x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph[0], graph[1], csd_emb, batch)
+        x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph[0], graph[1], csd_emb, batch, n_out)
+        if n_out is not None:
+            batch = batch[:n_out]
         if self.charge_range[1] > self.charge_range[0]:
             x = balance_channels_batched(x, charge, natoms, batch, *self.charge_range, target_offset=0.0)
         if self.spin_range[1] > self.spin_range[0]:

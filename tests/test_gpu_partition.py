@@ -68,3 +68,48 @@ def test_partitioned_cuda_matches_single_gpu(tmp_path):
     assert torch.allclose(got["energy"], ref["energy"].cpu(), rtol=2e-6)
     assert (got["forces"] - ref["forces"].cpu()).abs().max() < 2e-5
     assert (got["stress"] - ref["stress"].cpu()).abs().max() < 2e-5 * max(1.0, ref["stress"].abs().max().item())
+
+
+def _graph_worker(rank, world, port, out_path):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    gs = None
+    try:
+        from flash_uma_b200.partition import GraphedPartitionedStep, PartitionedModel, make_plan
+        from flash_uma_b200.wrapper import ZeroAllocBackbone
+        s, data, bb, head = _setup()
+        bb, head = bb.to(dev), head.to(dev)
+        z = ZeroAllocBackbone(bb)
+        d = data.to(dev)
+        csd = z.csd_embedding(d.charge, d.spin).float().detach()
+        plan = make_plan(s.positions, s.cell, data.edge_index.numpy(), world, rank)
+        pm = PartitionedModel(z.ce, plan, dev)
+        fixed = (d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd)
+        gs = GraphedPartitionedStep(pm, head, d.pos, *fixed, stress=True)
+        g = torch.Generator().manual_seed(3)
+        res = []
+        for k in range(3):   # replays with new positions against eager calls on the same positions
+            pos = d.pos + (0.02 * torch.randn(d.pos.shape, generator=g)).to(dev)
+            e_g, f_g, s_g = (t.clone() for t in gs(pos))
+            e, f, st = pm.energy_forces(head, pos, *fixed, stress=True)
+            res.append((e_g.cpu(), f_g.cpu(), s_g.cpu(), e.cpu(), f.cpu(), st.cpu()))
+        if rank == 0:
+            torch.save(res, out_path)
+    finally:
+        if gs is not None:
+            gs.release()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_graphed_partitioned_step_matches_eager(tmp_path):
+    out = str(tmp_path / "g.pt")
+    mp.spawn(_graph_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    for e_g, f_g, s_g, e, f, st in torch.load(out):
+        assert torch.allclose(e_g, e, rtol=1e-6, atol=0)
+        assert (f_g - f).abs().max() <= 1e-6 * max(1.0, f.abs().max().item())
+        assert (s_g - st).abs().max() <= 1e-6 * max(1.0, st.abs().max().item())
