@@ -31,20 +31,24 @@ __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict
     const float* y0 = Y0 + e * 5 * (int64_t)C + co;
     const float* y1 = Y1 + e * 4 * (int64_t)C + co;
     const float* y2 = Y2 + e * 2 * (int64_t)C + co;
-    const float4 g0 = sig4(ld4_stream(y0)), g1 = sig4(ld4_stream(y0 + C));
-    const float4 a = ld4_stream(y0 + 2 * C);
+    // every load of the row first (11 x 16 bytes in flight per thread), then the arithmetic
+    const float4 p0 = ld4_stream(y0), p1 = ld4_stream(y0 + C), a = ld4_stream(y0 + 2 * C);
+    const float4 y3 = ld4_stream(y0 + 3 * C), y4 = ld4_stream(y0 + 4 * C);
+    const float4 u0 = ld4_stream(y1), u1 = ld4_stream(y1 + C), u2 = ld4_stream(y1 + 2 * C), u3 = ld4_stream(y1 + 3 * C);
+    const float4 w0 = ld4_stream(y2), w1 = ld4_stream(y2 + C);
+    const float4 g0 = sig4(p0), g1 = sig4(p1);
     float* z0 = Z0 + e * 3 * (int64_t)C;
     float* z1 = Z1 + e * 4 * (int64_t)C;
     float* z2 = Z2 + e * 2 * (int64_t)C;
     st_out4(z0, 3 * C, co, a * sig4(a), split, bad);
-    st_out4(z0, 3 * C, C + co, ld4_stream(y0 + 3 * C) * g0, split, bad);
-    st_out4(z0, 3 * C, 2 * C + co, ld4_stream(y0 + 4 * C) * g1, split, bad);
-    st_out4(z1, 4 * C, co, ld4_stream(y1) * g0, split, bad);
-    st_out4(z1, 4 * C, C + co, ld4_stream(y1 + C) * g1, split, bad);
-    st_out4(z1, 4 * C, 2 * C + co, ld4_stream(y1 + 2 * C) * g0, split, bad);
-    st_out4(z1, 4 * C, 3 * C + co, ld4_stream(y1 + 3 * C) * g1, split, bad);
-    st_out4(z2, 2 * C, co, ld4_stream(y2) * g1, split, bad);
-    st_out4(z2, 2 * C, C + co, ld4_stream(y2 + C) * g1, split, bad);
+    st_out4(z0, 3 * C, C + co, y3 * g0, split, bad);
+    st_out4(z0, 3 * C, 2 * C + co, y4 * g1, split, bad);
+    st_out4(z1, 4 * C, co, u0 * g0, split, bad);
+    st_out4(z1, 4 * C, C + co, u1 * g1, split, bad);
+    st_out4(z1, 4 * C, 2 * C + co, u2 * g0, split, bad);
+    st_out4(z1, 4 * C, 3 * C + co, u3 * g1, split, bad);
+    st_out4(z2, 2 * C, co, w0 * g1, split, bad);
+    st_out4(z2, 2 * C, C + co, w1 * g1, split, bad);
   }
   report_split_range(bad, err);
 }
