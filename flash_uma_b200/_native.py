@@ -96,6 +96,8 @@ for _name in ("fuma_ln_silu_fwd", "fuma_ln_silu_bwd", "fuma_gather_fwd", "fuma_g
 
 KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3
+KERNELS_PER_CALL["fuma_gather_fwd"] = 2
+KERNELS_PER_CALL["fuma_gather_fwd_f16x3"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2
 KERNELS_PER_CALL["fuma_gather_bwd_noalloc"] = 3
