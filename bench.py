@@ -295,13 +295,27 @@ def run_flash(args, rank, world, device):
         gprobe = _native.LaunchProbe(timed=[dominant], external=True)
         hook = lambda on: _native.set_probe(gprobe if on else None)   # noqa: E731
         if world > 1:
-            gstep = make_graph(pos_seq[0], capture_hook=hook)
+            # captured collectives do not communicate, so a capture that fails on one rank leaves
+            # the others consistent: all ranks agree on graph or eager with one all-reduce
+            try:
+                gstep = make_graph(pos_seq[0], capture_hook=hook)
+            except Exception as exc:   # noqa: BLE001 - reported, then the eager step is used
+                print(f"rank {rank}: CUDA-graph capture of the partitioned step failed ({exc}); "
+                      "falling back to eager launches", file=sys.stderr, flush=True)
+                gstep = None
+            ok = torch.tensor([0 if gstep is None else 1], device=device)
+            torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+            if int(ok.item()) == 0:
+                if gstep is not None:
+                    gstep.release()
+                gstep, graphed = None, False
         else:
             from flash_uma_b200.predict import GraphedStep
             gstep = GraphedStep(pred, dataclasses.replace(data, pos=pos_seq[0]), stress=with_stress,
                                 capture_hook=hook)
-        graph_launches = gprobe.launches
-        step = gstep
+        if graphed:
+            graph_launches = gprobe.launches
+            step = gstep
     # ---- timed region 1: inputs resident in HBM. Launch counting covers every timed step; the
     # dominant kernel's launches are bracketed with CUDA events in the last timed step only
     # (pre-created events), so the instrumentation does not slow the other steps.
