@@ -34,12 +34,6 @@ namespace fuma {
 
 namespace {
 
-// Load the 34 Wigner values of edge e into smem.
-__device__ __forceinline__ void stage_wigner(float* sw, const float* __restrict__ wig, int64_t e, int lane) {
-  sw[lane] = __ldg(wig + e * kWig + lane);
-  if (lane < 2) sw[32 + lane] = __ldg(wig + e * kWig + 32 + lane);
-}
-
 // out[r] = sum_k D[r*n + k] v[k]
 template <int n>
 __device__ __forceinline__ void rot(const float* D, const float4* v, float4* out) {

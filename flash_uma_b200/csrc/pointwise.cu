@@ -220,6 +220,99 @@ __global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restric
   report_split_range(bad, err);
 }
 
+// Backward of rows of at most 128 values, one row per warp per iteration with the next row's
+// loads (x, dL/dh, mean, 1/std) issued before the current row is reduced, so two rows' loads
+// are in flight per warp; 64 registers, 4 blocks per SM. Same arithmetic as
+// ln_silu_bwd_kernel<1, 1>; 47 -> 37 us at E = 120,000 (B200).
+__global__ void __launch_bounds__(256, 4) ln_silu_bwd_row_kernel(const float* __restrict__ x,
+                                                              const float* __restrict__ gamma,
+                                                              const float* __restrict__ beta,
+                                                              const float* __restrict__ mean,
+                                                              const float* __restrict__ rstd,
+                                                              const float* __restrict__ g_out,
+                                                              float* __restrict__ g_x, int64_t M, int D, bool split,
+                                                              int* err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int D4 = D >> 2;
+  const bool act = lane < D4;
+  const float invD = 1.0f / (float)D;
+  const float4 gm = act ? ld4_keep(gamma + lane * 4) : f4(0.f), bt = act ? ld4_keep(beta + lane * 4) : f4(0.f);
+  bool bad = false;
+  int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  float4 nx = f4(0.f), ng = f4(0.f);
+  float nmu = 0.f, nrs = 0.f;
+  if (r < M) {
+    if (act) {
+      nx = ld4_stream(x + r * D + lane * 4);
+      ng = ld4_stream(g_out + r * D + lane * 4);
+    }
+    nmu = mean[r];
+    nrs = rstd[r];
+  }
+  for (; r < M; r += stride) {
+    const float4 xv = nx, gv = ng;
+    const float mu = nmu, rs = nrs;
+    const int64_t rn = r + stride;
+    if (rn < M) {
+      if (act) {
+        nx = ld4_stream(x + rn * D + lane * 4);
+        ng = ld4_stream(g_out + rn * D + lane * 4);
+      }
+      nmu = mean[rn];
+      nrs = rstd[rn];
+    }
+    float4 xh = f4(0.f), gxh = f4(0.f);
+    if (act) {
+      xh = (xv - f4(mu)) * rs;
+      const float4 y = xh * gm + bt;
+      const float4 sg = sig4(y);
+      const float4 ds = sg + y * (sg * (f4(1.f) - sg));
+      gxh = gv * ds * gm;
+    }
+    const float s1 = warp_sum((gxh.x + gxh.y) + (gxh.z + gxh.w));
+    const float s2 = warp_sum(dot4(gxh, xh));
+    if (act) st_out4(g_x + r * D, D, lane * 4, (gxh - (f4(s1) + xh * s2) * invD) * rs, split, bad);
+  }
+  report_split_range(bad, err);
+}
+
+// Forward of rows of at most 128 values, one row per warp per iteration with the next row's
+// load issued before the current row is reduced (the scheme of ln_silu_bwd_row_kernel).
+__global__ void __launch_bounds__(256, 4) ln_silu_fwd_row_kernel(const float* __restrict__ x,
+                                                                 const float* __restrict__ gamma,
+                                                                 const float* __restrict__ beta, float* __restrict__ out,
+                                                                 float* __restrict__ mean_out,
+                                                                 float* __restrict__ rstd_out, int64_t M, int D,
+                                                                 float eps, bool split, int* err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int D4 = D >> 2;
+  const bool act = lane < D4;
+  const float4 gm = act ? ld4_keep(gamma + lane * 4) : f4(0.f), bt = act ? ld4_keep(beta + lane * 4) : f4(0.f);
+  bool bad = false;
+  int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  float4 nx = f4(0.f);
+  if (r < M && act) nx = ld4_stream(x + r * D + lane * 4);
+  for (; r < M; r += stride) {
+    const float4 v = nx;
+    const int64_t rn = r + stride;
+    if (rn < M && act) nx = ld4_stream(x + rn * D + lane * 4);
+    const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) / (float)D;
+    const float4 c = v - f4(mean);
+    const float rstd = 1.0f / sqrtf(warp_sum(act ? dot4(c, c) : 0.f) / (float)D + eps);
+    if (lane == 0) {
+      mean_out[r] = mean;
+      rstd_out[r] = rstd;
+    }
+    if (act) {
+      const float4 y = c * rstd * gm + bt;
+      st_out4(out + r * D, D, lane * 4, y * sig4(y), split, bad);
+    }
+  }
+  report_split_range(bad, err);
+}
+
 // Forward LayerNorm + SiLU of rows of at most 128 values: 8 lanes per row, 4 rows per warp
 // (lane = 4 float4 of its row; reductions over the 8 lanes of a row), so four rows' loads are in
 // flight per warp, for the radial MLP's E x 128 LayerNorms (0.46 -> 0.40 ms per step measured).
@@ -316,7 +409,10 @@ void launch_ln_silu_bwd(const float* x, const float* gamma, const float* beta, c
 #define BWD(V, R)                                                                                                      \
   ln_silu_bwd_kernel<V, R><<<grid_resident(ln_silu_bwd_kernel<V, R>, 256, (M + R - 1) / R, 8), 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, \
                                                                            D, split, err)
-  if (d4 <= 32) BWD(1, 1);   // the 8-lanes-per-row variant measured slower here (0.68 vs 0.53 ms / step)
+  if (d4 <= 32) {   // (an 8-lanes-per-row variant measured slower: 0.68 vs 0.53 ms / step)
+    ln_silu_bwd_row_kernel<<<grid_resident(ln_silu_bwd_row_kernel, 256, M, 8), 256, 0, s>>>(
+        x, gamma, beta, mean, rstd, g_out, g_x, M, D, split, err);
+  }
   else if (d4 <= 64) BWD(2, 1);
   else if (d4 <= 128) BWD(4, 1);
   else if (d4 <= 256) BWD(8, 1);
