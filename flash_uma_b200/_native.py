@@ -39,6 +39,7 @@ _SIGS = {
     "fuma_linear_f16x3": [_P, _I64, _I32, _P, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _P, _P],
     "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
     "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
+    "fuma_csr_permute": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P],
     "fuma_gather_bwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P,
                                 _P],
 }
@@ -97,6 +98,7 @@ for _name in ("fuma_ln_silu_fwd", "fuma_ln_silu_bwd", "fuma_gather_fwd", "fuma_g
 KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3
 KERNELS_PER_CALL["fuma_gather_fwd"] = 2
+KERNELS_PER_CALL["fuma_csr_permute"] = 2
 KERNELS_PER_CALL["fuma_gather_fwd_f16x3"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2

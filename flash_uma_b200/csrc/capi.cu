@@ -454,6 +454,26 @@ int fuma_split_rows_f16(const float* x, int64_t lda, int64_t M, int32_t K, void*
   return launched("split_rows_f16");
 }
 
+int fuma_csr_permute(const int32_t* dst_row_ptr, const int32_t* dst_col, const int32_t* src_row_ptr,
+                     const int32_t* src_col, const int64_t* perm, int64_t N, int64_t E, int32_t* new_dst_row_ptr,
+                     int32_t* new_dst_col, int32_t* new_src_row_ptr, int32_t* new_src_col, void* stream) {
+  REQUIRE(N >= 0 && E >= 0 && E < (int64_t(1) << 31), "csr_permute: bad sizes N=%lld E=%lld", (long long)N,
+          (long long)E);
+  REQUIRE(dst_row_ptr && new_dst_row_ptr, "csr_permute: null row pointer");
+  REQUIRE(E == 0 || (dst_col && new_dst_col), "csr_permute: null column pointer");
+  const bool two = src_row_ptr != nullptr;
+  REQUIRE(!two || (new_src_row_ptr && (E == 0 || (src_col && new_src_col))),
+          "csr_permute: the source CSR needs all four of its pointers");
+  REQUIRE(N == 0 || perm, "csr_permute: null permutation");
+  BIND(dst_row_ptr);
+  const int32_t* rp[2] = {dst_row_ptr, src_row_ptr};
+  const int32_t* cl[2] = {dst_col, src_col};
+  int32_t* nrp[2] = {new_dst_row_ptr, new_src_row_ptr};
+  int32_t* ncl[2] = {new_dst_col, new_src_col};
+  launch_csr_permute(two ? 2 : 1, rp, cl, perm, N, nrp, ncl, (cudaStream_t)stream);
+  return launched("csr_permute");
+}
+
 int fuma_split_f16(const float* x, int64_t n, float scale, void* hi, void* lo, void* stream) {
   REQUIRE(n >= 0, "split_f16: bad n");
   REQUIRE(scale > 0.0f, "split_f16: scale must be positive");

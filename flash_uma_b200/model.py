@@ -187,6 +187,13 @@ class ESCNInferenceModel(nn.Module):
     def build_graph(self, idx_i, idx_j, N):
         return build_graph_cached(idx_i, idx_j, N)
 
+    def build_graph_renumbered(self, edge_index, perm, N):
+        """CSRs of the Morton-renumbered edges (``model.py:189-191``): the CSRs of the caller's
+        numbering are cached on the caller's edge list, which stays the same across MD steps,
+        and renumbered on every call without a sort (:func:`ops.permute_graph`); the result is
+        bitwise the stable-argsort CSR of the renumbered edges."""
+        return ops.permute_graph(build_graph_cached(edge_index[0], edge_index[1], N), perm)
+
     def geometry(self, pos, Z, idx_i, idx_j, shifts, graph):
         """(x_edge, wigner, env); in the fused mode x_edge comes back as (its row-packed split,
         its Gaussian-basis columns), see :func:`flash_uma_b200.fused.geometry`."""
@@ -226,7 +233,7 @@ class ESCNInferenceModel(nn.Module):
     def forward(self, pos, Z, batch, edge_index, shifts, csd_emb, charge=None, spin=None, natoms=None):
         pos_s, Z_s, batch_s, ii, jj, perm, inv_perm = reorder_graph_morton(pos, Z, batch, edge_index[0], edge_index[1])
         N = pos_s.shape[0]
-        graph = self.build_graph(ii, jj, N)
+        graph = self.build_graph_renumbered(edge_index, perm, N)
         x_edge, wigner, env = self.geometry(pos_s, Z_s, ii, jj, shifts, graph)
         x = self.init_embedding(x_edge, wigner, env, Z_s, batch_s, csd_emb, jj, graph, N)
         for k in range(len(self.layers)):

@@ -55,6 +55,22 @@ def build_graph_csr(idx_i: torch.Tensor, idx_j: torch.Tensor, N: int) -> GraphCS
     return GraphCSR(N=N, E=int(idx_i.shape[0]), dst_row_ptr=d_ptr, dst_col=d_col, src_row_ptr=s_ptr, src_col=s_col)
 
 
+def permute_graph(g: GraphCSR, perm: torch.Tensor) -> GraphCSR:
+    """The CSRs of the same edges after renumbering the nodes (new node a = old node perm[a]),
+    from ``g`` without a sort (``fuma_csr_permute``): bitwise ``build_graph_csr(inv[idx_i],
+    inv[idx_j], N)`` for ``inv`` the inverse of ``perm``."""
+    nat.require_cuda(g.dst_row_ptr, perm)
+    perm = _i64(perm)
+    N, E = g.N, g.E
+    dev = g.dst_row_ptr.device
+    i32 = dict(device=dev, dtype=torch.int32)
+    d_ptr, s_ptr = torch.empty(N + 1, **i32), torch.empty(N + 1, **i32)
+    d_col, s_col = torch.empty(E, **i32), torch.empty(E, **i32)
+    nat.call("fuma_csr_permute", ptr(g.dst_row_ptr), ptr(g.dst_col), ptr(g.src_row_ptr), ptr(g.src_col), ptr(perm),
+             N, E, ptr(d_ptr), ptr(d_col), ptr(s_ptr), ptr(s_col), stream_of(perm))
+    return GraphCSR(N=N, E=E, dst_row_ptr=d_ptr, dst_col=d_col, src_row_ptr=s_ptr, src_col=s_col)
+
+
 def _f32(t: torch.Tensor, name: str) -> torch.Tensor:
     if t.dtype != torch.float32:
         raise TypeError(f"{name} must be float32 (got {t.dtype})")

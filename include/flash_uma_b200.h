@@ -150,6 +150,15 @@ int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* 
  * err_flag receives 16 on an out-of-range value. */
 int fuma_split_rows_f16(const float* x, int64_t lda, int64_t M, int32_t K, void* out, int64_t ldp, int* err_flag,
                         void* stream);
+/* Destination (and optionally source) CSR of a renumbered edge list, from the CSR of the
+ * original numbering: new node a is original node perm[a] (perm: int64 [N]), edge ids are
+ * unchanged. Replaces the per-step stable-argsort CSR build of the reference on its renumbered
+ * (Morton-ordered) edges (model.py:17-46, called at model.py:189-191): the result is bitwise
+ * that CSR, since row a holds the edges of node perm[a] in increasing edge id. Inputs and
+ * outputs are int32 [N + 1] row pointers and [E] columns (edge ids); src_* may all be NULL. */
+int fuma_csr_permute(const int32_t* dst_row_ptr, const int32_t* dst_col, const int32_t* src_row_ptr,
+                     const int32_t* src_col, const int64_t* perm, int64_t N, int64_t E, int32_t* new_dst_row_ptr,
+                     int32_t* new_dst_col, int32_t* new_src_row_ptr, int32_t* new_src_col, void* stream);
 /* hi = fp16_rn(x * scale), lo = fp16_rn((x * scale - hi) * 2^11), n elements (f16x3 weight split). */
 int fuma_split_f16(const float* x, int64_t n, float scale, void* hi, void* lo, void* stream);
 

@@ -134,3 +134,23 @@ def test_lean_mode_is_bitwise_identical(monkeypatch):
     assert pred.backbone.ce.layers[0].lean
     for k in ("energy", "forces", "stress"):
         assert torch.equal(got[k], ref[k]), k
+
+
+@pytest.mark.parametrize("N,E", [(1, 0), (7, 40), (500, 9000), (4000, 120000)])
+def test_csr_permute_matches_sorted_build(N, E):
+    """fuma_csr_permute: the renumbered CSRs equal the stable-argsort CSRs of the renumbered edges,
+    bitwise, including empty rows (random graphs, random permutations)."""
+    from flash_uma_b200 import ops
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(N + E)
+    idx_i = torch.randint(0, N, (E,), generator=g).to(dev)
+    idx_j = torch.randint(0, max(1, N // 2), (E,), generator=g).to(dev)   # half the nodes without in-edges
+    perm = torch.randperm(N, generator=g).to(dev)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(N, device=dev)
+    base = ops.build_graph_csr(idx_i, idx_j, N)
+    got = ops.permute_graph(base, perm)
+    ref = ops.build_graph_csr(inv[idx_i], inv[idx_j], N)
+    torch.cuda.synchronize()
+    for f in ("dst_row_ptr", "dst_col", "src_row_ptr", "src_col"):
+        assert torch.equal(getattr(got, f), getattr(ref, f)), f
