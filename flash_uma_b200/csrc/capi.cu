@@ -454,6 +454,32 @@ int fuma_split_rows_f16(const float* x, int64_t lda, int64_t M, int32_t K, void*
   return launched("split_rows_f16");
 }
 
+int fuma_rmsnorm_sh_fwd(const float* x, const float* affine_weight, const float* affine_bias,
+                        const float* degree_weight, float eps, int64_t N, int32_t C, float* out, float* rstd,
+                        void* stream) {
+  REQUIRE(N >= 0 && C > 0 && C % 4 == 0 && C <= 256, "rmsnorm_sh_fwd: C=%d must be a multiple of 4 up to 256", C);
+  REQUIRE(eps > 0.0f, "rmsnorm_sh_fwd: eps must be positive");
+  if (N == 0) return FUMA_OK;
+  REQUIRE(x && affine_weight && affine_bias && degree_weight && out && rstd, "rmsnorm_sh_fwd: null pointer");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(out, "out"); REQUIRE_ALIGNED(affine_weight, "affine_weight");
+  REQUIRE_ALIGNED(affine_bias, "affine_bias");
+  BIND(x);
+  launch_rmsnorm_sh_fwd(x, affine_weight, affine_bias, degree_weight, eps, N, C, out, rstd, (cudaStream_t)stream);
+  return launched("rmsnorm_sh_fwd");
+}
+
+int fuma_rmsnorm_sh_bwd(const float* x, const float* affine_weight, const float* degree_weight, const float* rstd,
+                        const float* g_out, int64_t N, int32_t C, float* g_x, void* stream) {
+  REQUIRE(N >= 0 && C > 0 && C % 4 == 0 && C <= 256, "rmsnorm_sh_bwd: C=%d must be a multiple of 4 up to 256", C);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(x && affine_weight && degree_weight && rstd && g_out && g_x, "rmsnorm_sh_bwd: null pointer");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(g_out, "g_out"); REQUIRE_ALIGNED(g_x, "g_x");
+  REQUIRE_ALIGNED(affine_weight, "affine_weight");
+  BIND(x);
+  launch_rmsnorm_sh_bwd(x, affine_weight, degree_weight, rstd, g_out, N, C, g_x, (cudaStream_t)stream);
+  return launched("rmsnorm_sh_bwd");
+}
+
 int fuma_csr_permute(const int32_t* dst_row_ptr, const int32_t* dst_col, const int32_t* src_row_ptr,
                      const int32_t* src_col, const int64_t* perm, int64_t N, int64_t E, int32_t* new_dst_row_ptr,
                      int32_t* new_dst_col, int32_t* new_src_row_ptr, int32_t* new_src_col, void* stream) {

@@ -54,6 +54,10 @@ int launch_gemm_tf32(const float* A, int64_t lda, const float* W_hi, const float
                      int64_t ldc, int64_t M, int N, int K, bool split, int* err, cudaStream_t s);
 void launch_split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s);
 const char* gemm_map_error();
+void launch_rmsnorm_sh_fwd(const float* x, const float* aw, const float* ab, const float* bal, float eps, int64_t N,
+                           int C, float* out, float* rstd, cudaStream_t s);
+void launch_rmsnorm_sh_bwd(const float* x, const float* aw, const float* bal, const float* rstd, const float* g_out,
+                           int64_t N, int C, float* g_x, cudaStream_t s);
 void launch_csr_permute(int ngraphs, const int32_t* const* row_ptr, const int32_t* const* col, const int64_t* perm,
                         int64_t N, int32_t* const* new_row_ptr, int32_t* const* new_col, cudaStream_t s);
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,

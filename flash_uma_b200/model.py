@@ -19,7 +19,7 @@ import os
 
 from . import fused, ops
 from .linear import FrozenLinear
-from .nodewise import balance_channels_batched
+from .nodewise import EquivariantRMSNormSH, balance_channels_batched
 
 # ---- graph preparation ---------------------------------------------------------------------
 
@@ -101,6 +101,14 @@ class RadialMLP(nn.Module):
         return self.l3(h2)
 
 
+def apply_norm(norm, x):
+    """``norm(x)``: the fused CUDA kernels for the :class:`EquivariantRMSNormSH` modules (the
+    stand-in norms), the module itself for any other normalisation module."""
+    if type(norm) is EquivariantRMSNormSH and x.is_cuda and norm.lmax == 2:
+        return ops.rms_norm_sh(x, norm)
+    return norm(x)
+
+
 class PackedLayer(nn.Module):
     """One eSCN message-passing block (``Packed_eSCN_Layer``, ``model.py:81-157``)."""
 
@@ -127,13 +135,13 @@ class PackedLayer(nn.Module):
     def forward(self, x_in, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, n_out=None):
         """``n_out``: return only the first ``n_out`` atoms' outputs (the partitioned model's owned
         atoms; the node-wise tail then skips the halo rows, whose messages are not computed here)."""
-        x_norm = self.norm_1(x_in)
+        x_norm = apply_norm(self.norm_1, x_in)
         if self.fused:
             x_mid = fused.message_block(self, x_norm, x_in, x_edge, wigner, env, csd_emb, idx_i, idx_j, batch, graph,
                                         self.lean)
             if n_out is not None:
                 x_mid = x_mid[:n_out]
-            return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
+            return (self.atom_wise(apply_norm(self.norm_2, x_mid)) + x_mid).contiguous()
         rad_out = self.rad(x_edge)
         X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch, graph=graph)
         Z0, Z1, Z2 = ops.fused_gating_split(self.conv1_m0(X0), self.conv1_m1(X1), self.conv1_m2(X2), self.C)
@@ -142,7 +150,7 @@ class PackedLayer(nn.Module):
                                          x_in.shape[0])
         if n_out is not None:
             x_mid = x_mid[:n_out]
-        return (self.atom_wise(self.norm_2(x_mid)) + x_mid).contiguous()
+        return (self.atom_wise(apply_norm(self.norm_2, x_mid)) + x_mid).contiguous()
 
 
 class ESCNInferenceModel(nn.Module):
@@ -228,7 +236,7 @@ class ESCNInferenceModel(nn.Module):
         return x
 
     def final(self, x):
-        return self.final_norm(x)
+        return apply_norm(self.final_norm, x)
 
     def forward(self, pos, Z, batch, edge_index, shifts, csd_emb, charge=None, spin=None, natoms=None):
         pos_s, Z_s, batch_s, ii, jj, perm, inv_perm = reorder_graph_morton(pos, Z, batch, edge_index[0], edge_index[1])

@@ -86,6 +86,43 @@ def _i32(t: torch.Tensor) -> torch.Tensor:
 
 
 # ---------------------------------------------------------------------------------------------
+class _RMSNormSH(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, aw, ab, bal, eps):
+        nat.require_cuda(x)
+        x = _f32(x, "x")
+        N, K, C = x.shape
+        if K != 9:
+            raise ValueError(f"rms_norm_sh: x must be [N, 9, C], got {tuple(x.shape)}")
+        out = torch.empty_like(x)
+        rstd = torch.empty(N, device=x.device, dtype=torch.float32)
+        nat.call("fuma_rmsnorm_sh_fwd", ptr(x), ptr(aw), ptr(ab), ptr(bal), eps, N, C, ptr(out), ptr(rstd),
+                 stream_of(x))
+        ctx.save_for_backward(x, aw, bal, rstd)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, aw, bal, rstd = ctx.saved_tensors
+        N, _, C = x.shape
+        g = _f32(g, "g")
+        gx = torch.empty_like(x)
+        nat.call("fuma_rmsnorm_sh_bwd", ptr(x), ptr(aw), ptr(bal), ptr(rstd), ptr(g), N, C, ptr(gx), stream_of(x))
+        return gx, None, None, None, None
+
+
+def rms_norm_sh(x: torch.Tensor, norm) -> torch.Tensor:
+    """``norm(x)`` for an :class:`~flash_uma_b200.nodewise.EquivariantRMSNormSH` (lmax 2) in one
+    CUDA kernel per direction (``fuma_rmsnorm_sh_fwd`` / ``_bwd``); its affine parameters are
+    treated as constants (frozen, as in the inference model)."""
+    if norm.lmax != 2:
+        raise ValueError("rms_norm_sh: lmax must be 2")
+    f = lambda t: t.detach().float().contiguous()   # noqa: E731
+    return _RMSNormSH.apply(x, f(norm.affine_weight), f(norm.affine_bias), f(norm.balance_degree_weight),
+                            float(norm.eps))
+
+
+# ---------------------------------------------------------------------------------------------
 class _PrecomputeGeometry(torch.autograd.Function):
     @staticmethod
     def forward(ctx, pos, Z, idx_i, idx_j, shifts, W_src, W_tgt, offset_g, coeff_g, cutoff, graph):

@@ -150,6 +150,17 @@ int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* 
  * err_flag receives 16 on an out-of-range value. */
 int fuma_split_rows_f16(const float* x, int64_t lda, int64_t M, int32_t K, void* out, int64_t ldp, int* err_flag,
                         void* stream);
+/* Equivariant RMS norm of node embeddings x [N, 9, C] (the norm_1 / norm_2 / final_norm
+ * modules the reference's layers call, model.py:145,157,218; here the stand-in
+ * EquivariantRMSNormSH): l = 0 row centred over channels, all rows scaled by
+ * 1 / sqrt(mean_c sum_k w_k f_k^2 + eps) with degree_weight w [9], then by affine_weight
+ * [3, C] (per degree) and affine_bias [C] (l = 0). rstd [N] receives the per-atom scale for the
+ * backward, which returns g_x (frozen affine parameters). C a multiple of 4, at most 256. */
+int fuma_rmsnorm_sh_fwd(const float* x, const float* affine_weight, const float* affine_bias,
+                        const float* degree_weight, float eps, int64_t N, int32_t C, float* out, float* rstd,
+                        void* stream);
+int fuma_rmsnorm_sh_bwd(const float* x, const float* affine_weight, const float* degree_weight, const float* rstd,
+                        const float* g_out, int64_t N, int32_t C, float* g_x, void* stream);
 /* Destination (and optionally source) CSR of a renumbered edge list, from the CSR of the
  * original numbering: new node a is original node perm[a] (perm: int64 [N]), edge ids are
  * unchanged. Replaces the per-step stable-argsort CSR build of the reference on its renumbered

@@ -1,0 +1,30 @@
+"""Fused node-wise kernels against the stand-in modules' own PyTorch definitions on the GPU
+(fp32): forward values and input gradients."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+@pytest.mark.parametrize("N,C", [(1, 64), (333, 128), (4000, 128), (50, 256), (17, 32)])
+def test_rms_norm_sh_matches_module(N, C):
+    from flash_uma_b200 import ops
+    from flash_uma_b200.linear import check_errors
+    from flash_uma_b200.nodewise import EquivariantRMSNormSH
+    g = torch.Generator().manual_seed(N * C)
+    norm = EquivariantRMSNormSH(C)
+    with torch.no_grad():
+        norm.affine_weight.copy_(torch.rand(3, C, generator=g) + 0.5)
+        norm.affine_bias.copy_(torch.randn(C, generator=g))
+    norm = norm.to(DEV)
+    x = (torch.randn(N, 9, C, generator=g) * torch.rand(N, 1, 1, generator=g) * 3 + 0.5).to(DEV)
+    r = torch.randn(N, 9, C, generator=g).to(DEV)
+    xa, xb = x.clone().requires_grad_(True), x.clone().requires_grad_(True)
+    ya, yb = norm(xa), ops.rms_norm_sh(xb, norm)
+    (ga,) = torch.autograd.grad((ya * r).sum(), xa)
+    (gb,) = torch.autograd.grad((yb * r).sum(), xb)
+    torch.cuda.synchronize()
+    check_errors()
+    assert (ya - yb).abs().max() <= 2e-6 * (1 + ya.abs().max())
+    assert (ga - gb).abs().max() <= 1e-5 * (1 + ga.abs().max())
