@@ -40,6 +40,9 @@ _SIGS = {
     "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
     "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
     "fuma_csr_permute": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P],
+    "fuma_atomwise_gate_fwd": [_P, _P, _P, _I64, _I32, _P, _P],
+    "fuma_atomwise_gate_bwd": [_P, _P, _P, _P, _I64, _I32, _P, _P, _P],
+    "fuma_coef_to_node": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
     "fuma_rmsnorm_sh_fwd": [_P, _P, _P, _P, _F32, _I64, _I32, _P, _P, _P],
     "fuma_rmsnorm_sh_bwd": [_P, _P, _P, _P, _P, _I64, _I32, _P, _P],
     "fuma_gather_bwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P,

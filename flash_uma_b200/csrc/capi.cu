@@ -480,6 +480,42 @@ int fuma_rmsnorm_sh_bwd(const float* x, const float* affine_weight, const float*
   return launched("rmsnorm_sh_bwd");
 }
 
+int fuma_atomwise_gate_fwd(const float* h, const float* u, const float* b1, int64_t N, int32_t H, float* z,
+                           void* stream) {
+  REQUIRE(N >= 0 && H > 0 && H % 4 == 0, "atomwise_gate_fwd: H=%d must be a positive multiple of 4", H);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(h && u && b1 && z, "atomwise_gate_fwd: null pointer");
+  REQUIRE_ALIGNED(h, "h"); REQUIRE_ALIGNED(u, "u"); REQUIRE_ALIGNED(b1, "b1"); REQUIRE_ALIGNED(z, "z");
+  BIND(h);
+  launch_atomwise_gate_fwd(h, u, b1, N, H, z, (cudaStream_t)stream);
+  return launched("atomwise_gate_fwd");
+}
+
+int fuma_atomwise_gate_bwd(const float* gz, const float* h, const float* u, const float* b1, int64_t N, int32_t H,
+                           float* gh, float* gu, void* stream) {
+  REQUIRE(N >= 0 && H > 0 && H % 4 == 0, "atomwise_gate_bwd: H=%d must be a positive multiple of 4", H);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(gz && h && u && b1 && gh && gu, "atomwise_gate_bwd: null pointer");
+  REQUIRE_ALIGNED(gz, "gz"); REQUIRE_ALIGNED(h, "h"); REQUIRE_ALIGNED(u, "u"); REQUIRE_ALIGNED(b1, "b1");
+  REQUIRE_ALIGNED(gh, "gh"); REQUIRE_ALIGNED(gu, "gu");
+  BIND(h);
+  launch_atomwise_gate_bwd(gz, h, u, b1, N, H, gh, gu, (cudaStream_t)stream);
+  return launched("atomwise_gate_bwd");
+}
+
+int fuma_coef_to_node(const float* src, const float* add, const float* row0, int32_t row0_per_node, int64_t N,
+                      int32_t W, float* out, void* stream) {
+  REQUIRE(N >= 0 && W > 0 && W % 4 == 0, "coef_to_node: W=%d must be a positive multiple of 4", W);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(src && out, "coef_to_node: null pointer");
+  REQUIRE_ALIGNED(src, "src"); REQUIRE_ALIGNED(out, "out");
+  if (add) REQUIRE_ALIGNED(add, "add");
+  if (row0) REQUIRE_ALIGNED(row0, "row0");
+  BIND(src);
+  launch_coef_to_node(src, add, row0, row0_per_node != 0, N, W, out, (cudaStream_t)stream);
+  return launched("coef_to_node");
+}
+
 int fuma_csr_permute(const int32_t* dst_row_ptr, const int32_t* dst_col, const int32_t* src_row_ptr,
                      const int32_t* src_col, const int64_t* perm, int64_t N, int64_t E, int32_t* new_dst_row_ptr,
                      int32_t* new_dst_col, int32_t* new_src_row_ptr, int32_t* new_src_col, void* stream) {

@@ -58,6 +58,12 @@ void launch_rmsnorm_sh_fwd(const float* x, const float* aw, const float* ab, con
                            int C, float* out, float* rstd, cudaStream_t s);
 void launch_rmsnorm_sh_bwd(const float* x, const float* aw, const float* bal, const float* rstd, const float* g_out,
                            int64_t N, int C, float* g_x, cudaStream_t s);
+void launch_atomwise_gate_fwd(const float* h, const float* u, const float* b1, int64_t N, int H, float* z,
+                              cudaStream_t s);
+void launch_atomwise_gate_bwd(const float* gz, const float* h, const float* u, const float* b1, int64_t N, int H,
+                              float* gh, float* gu, cudaStream_t s);
+void launch_coef_to_node(const float* src, const float* add, const float* row0, int row0_per_node, int64_t N, int W,
+                         float* out, cudaStream_t s);
 void launch_csr_permute(int ngraphs, const int32_t* const* row_ptr, const int32_t* const* col, const int64_t* perm,
                         int64_t N, int32_t* const* new_row_ptr, int32_t* const* new_col, cudaStream_t s);
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,

@@ -157,4 +157,116 @@ void launch_rmsnorm_sh_bwd(const float* x, const float* aw, const float* bal, co
         x, aw, bal, rstd, g_out, N, C, g_x);
 }
 
+// ---- gated atom-wise block (the stand-in SpectralAtomwise, flash_uma_b200/nodewise.py; the
+// atom_wise module of the reference's layers, model.py:157) --------------------------------------
+// With h [9, N, H] the per-coefficient output of the first per-degree linear map (no bias) and
+// u [N, 2H] the scalar MLP pre-activation (bias included):
+//   z_0 = SiLU(h_0 + b1),  z_k = h_k * sigmoid(SiLU(u))[l(k) - 1 block]  (k >= 1)
+// Thread per (atom, 4 channels); the 9 coefficient rows of h and z are coefficient-major
+// [9, N, H] (the layout of a batched GEMM over the coefficients).
+namespace {
+
+__device__ __forceinline__ float4 silu4(float4 a) {
+  return make_float4(a.x * sigmoidf_(a.x), a.y * sigmoidf_(a.y), a.z * sigmoidf_(a.z), a.w * sigmoidf_(a.w));
+}
+__device__ __forceinline__ float dsilu(float a) {   // d/da a sigmoid(a)
+  const float s = sigmoidf_(a);
+  return s * (1.0f + a * (1.0f - s));
+}
+__device__ __forceinline__ float4 dsilu4(float4 a) { return make_float4(dsilu(a.x), dsilu(a.y), dsilu(a.z), dsilu(a.w)); }
+__device__ __forceinline__ float4 sig4n(float4 a) {
+  return make_float4(sigmoidf_(a.x), sigmoidf_(a.y), sigmoidf_(a.z), sigmoidf_(a.w));
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(256) atomwise_gate_fwd_kernel(const float* __restrict__ h,
+                                                                 const float* __restrict__ u,
+                                                                 const float* __restrict__ b1, int64_t N, int H,
+                                                                 float* __restrict__ z) {
+  const int H4 = H >> 2;
+  const int64_t plane = N * (int64_t)H;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * H4; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = t / H4;
+    const int c = (int)(t - n * H4) * 4;
+    const int64_t o = n * H + c;
+    const float4 g1 = sig4n(silu4(ld4(u + n * 2 * H + c))), g2 = sig4n(silu4(ld4(u + n * 2 * H + H + c)));
+    st4(z + o, silu4(ld4(h + o) + ld4_keep(b1 + c)));
+#pragma unroll
+    for (int k = 1; k < 9; ++k) st4(z + k * plane + o, ld4(h + k * plane + o) * (k < 4 ? g1 : g2));
+  }
+}
+
+// Backward of the gating, given gz = dL/dz [9, N, H]: gh = dL/dh [9, N, H], gu = dL/du [N, 2H].
+__global__ void __launch_bounds__(256) atomwise_gate_bwd_kernel(const float* __restrict__ gz,
+                                                                 const float* __restrict__ h,
+                                                                 const float* __restrict__ u,
+                                                                 const float* __restrict__ b1, int64_t N, int H,
+                                                                 float* __restrict__ gh, float* __restrict__ gu) {
+  const int H4 = H >> 2;
+  const int64_t plane = N * (int64_t)H;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * H4; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = t / H4;
+    const int c = (int)(t - n * H4) * 4;
+    const int64_t o = n * H + c;
+    const float4 u1 = ld4(u + n * 2 * H + c), u2 = ld4(u + n * 2 * H + H + c);
+    const float4 a1 = silu4(u1), a2 = silu4(u2);
+    const float4 g1 = sig4n(a1), g2 = sig4n(a2);
+    st4(gh + o, ld4(gz + o) * dsilu4(ld4(h + o) + ld4_keep(b1 + c)));
+    float4 s1 = f4(0.f), s2 = f4(0.f);
+#pragma unroll
+    for (int k = 1; k < 9; ++k) {
+      const float4 g = ld4(gz + k * plane + o);
+      st4(gh + k * plane + o, g * (k < 4 ? g1 : g2));
+      if (k < 4)
+        s1 += g * ld4(h + k * plane + o);
+      else
+        s2 += g * ld4(h + k * plane + o);
+    }
+    const float4 one = f4(1.f);
+    st4(gu + n * 2 * H + c, s1 * (g1 * (one - g1)) * dsilu4(u1));
+    st4(gu + n * 2 * H + H + c, s2 * (g2 * (one - g2)) * dsilu4(u2));
+  }
+}
+
+// out[n, k, :] = src[k, n, :] (+ add[n, k, :]) (+ row0[n or 0, :] on k = 0): coefficient-major
+// rows back to the node-major [N, 9, W] layout, with the residual and the l = 0 bias (forward) or
+// the scalar-MLP input gradient (backward) folded in.
+__global__ void __launch_bounds__(256) coef_to_node_kernel(const float* __restrict__ src,
+                                                           const float* __restrict__ add,
+                                                           const float* __restrict__ row0, int row0_per_node,
+                                                           int64_t N, int W, float* __restrict__ out) {
+  const int W4 = W >> 2;
+  const int64_t plane = N * (int64_t)W;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * 9 * W4;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t nk = t / W4;
+    const int c = (int)(t - nk * W4) * 4;
+    const int64_t n = nk / 9;
+    const int k = (int)(nk - n * 9);
+    float4 v = ld4(src + k * plane + n * W + c);
+    if (add) v = v + ld4(add + nk * W + c);
+    if (k == 0 && row0) v = v + ld4(row0 + (row0_per_node ? n * W : 0) + c);
+    st4(out + nk * W + c, v);
+  }
+}
+
+void launch_atomwise_gate_fwd(const float* h, const float* u, const float* b1, int64_t N, int H, float* z,
+                              cudaStream_t s) {
+  atomwise_gate_fwd_kernel<<<grid_resident(atomwise_gate_fwd_kernel, 256, N * (H / 4), 256), 256, 0, s>>>(h, u, b1, N,
+                                                                                                         H, z);
+}
+
+void launch_atomwise_gate_bwd(const float* gz, const float* h, const float* u, const float* b1, int64_t N, int H,
+                              float* gh, float* gu, cudaStream_t s) {
+  atomwise_gate_bwd_kernel<<<grid_resident(atomwise_gate_bwd_kernel, 256, N * (H / 4), 256), 256, 0, s>>>(
+      gz, h, u, b1, N, H, gh, gu);
+}
+
+void launch_coef_to_node(const float* src, const float* add, const float* row0, int row0_per_node, int64_t N, int W,
+                         float* out, cudaStream_t s) {
+  coef_to_node_kernel<<<grid_resident(coef_to_node_kernel, 256, N * 9 * (W / 4), 256), 256, 0, s>>>(
+      src, add, row0, row0_per_node, N, W, out);
+}
+
 }  // namespace fuma

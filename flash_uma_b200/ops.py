@@ -122,6 +122,75 @@ def rms_norm_sh(x: torch.Tensor, norm) -> torch.Tensor:
                             float(norm.eps))
 
 
+class _AtomwiseResidual(torch.autograd.Function):
+    """y = x_mid + atom_wise(xn) for a SpectralAtomwise block (constants from atomwise_constants)."""
+
+    @staticmethod
+    def forward(ctx, xn, x_mid, prm):
+        nat.require_cuda(xn, x_mid)
+        Ws, bs, W1e, b1, W2e, b2 = prm
+        xn, x_mid = _f32(xn, "xn"), _f32(x_mid, "x_mid")
+        N, _, C = xn.shape
+        H = b1.shape[0]
+        s = stream_of(xn)
+        u = torch.addmm(bs, xn[:, 0], Ws.t())                       # [N, 2H]
+        h = torch.bmm(xn.transpose(0, 1), W1e.transpose(1, 2))      # [9, N, H], coefficient-major
+        z = torch.empty_like(h)
+        nat.call("fuma_atomwise_gate_fwd", ptr(h), ptr(u), ptr(b1), N, H, ptr(z), s)
+        o = torch.bmm(z, W2e.transpose(1, 2))                       # [9, N, C]
+        y = torch.empty_like(x_mid)
+        nat.call("fuma_coef_to_node", ptr(o), ptr(x_mid), ptr(b2), 0, N, C, ptr(y), s)
+        ctx.save_for_backward(h, u)
+        ctx.prm = prm
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        h, u = ctx.saved_tensors
+        Ws, bs, W1e, b1, W2e, b2 = ctx.prm
+        gy = _f32(gy, "gy")
+        _, N, H = h.shape
+        C = gy.shape[2]
+        s = stream_of(gy)
+        gz = torch.bmm(gy.transpose(0, 1), W2e)                     # [9, N, H]
+        gh, gu = torch.empty_like(h), torch.empty_like(u)
+        nat.call("fuma_atomwise_gate_bwd", ptr(gz), ptr(h), ptr(u), ptr(b1), N, H, ptr(gh), ptr(gu), s)
+        gx9 = torch.bmm(gh, W1e)                                    # [9, N, C]
+        gu_x = torch.mm(gu, Ws)                                     # [N, C], into the l = 0 row
+        gxn = torch.empty_like(gy)
+        nat.call("fuma_coef_to_node", ptr(gx9), None, ptr(gu_x), 1, N, C, ptr(gxn), s)
+        return gxn, gy, None
+
+
+_DEG9 = [0, 1, 1, 1, 2, 2, 2, 2, 2]
+
+
+def atomwise_constants(aw) -> tuple:
+    """The frozen parameters of a SpectralAtomwise block as the fused path uses them, cached on
+    the module: scalar MLP (W [2H, C], b [2H]), the two per-degree maps expanded to the 9
+    coefficients (W1e [9, H, C], W2e [9, C, H]) and their l = 0 biases."""
+    dev = aw.so3_linear_1.weight.device
+    cached = getattr(aw, "_fuma_constants", None)
+    if cached is not None and cached[0].device == dev:
+        return cached
+    f = lambda t: t.detach().float().contiguous()   # noqa: E731
+    idx = torch.tensor(_DEG9, device=dev)
+    lin = aw.scalar_mlp[0]
+    prm = (f(lin.weight), f(lin.bias), f(aw.so3_linear_1.weight.index_select(0, idx)), f(aw.so3_linear_1.bias),
+           f(aw.so3_linear_2.weight.index_select(0, idx)), f(aw.so3_linear_2.bias))
+    aw._fuma_constants = prm
+    return prm
+
+
+def atomwise_residual(aw, xn: torch.Tensor, x_mid: torch.Tensor) -> torch.Tensor:
+    """``x_mid + aw(xn)`` for a :class:`~flash_uma_b200.nodewise.SpectralAtomwise` (lmax 2): the
+    per-coefficient linear maps as batched fp32 GEMMs on the coefficient-major view, the gating
+    and the layout change (with residual and biases) as CUDA kernels. Frozen parameters."""
+    if aw.lmax != 2 or (aw.hidden % 4) or (xn.shape[2] % 4):
+        raise ValueError("atomwise_residual: lmax 2 and channel counts that are multiples of 4")
+    return _AtomwiseResidual.apply(xn, x_mid, atomwise_constants(aw))
+
+
 # ---------------------------------------------------------------------------------------------
 class _PrecomputeGeometry(torch.autograd.Function):
     @staticmethod

@@ -161,6 +161,21 @@ int fuma_rmsnorm_sh_fwd(const float* x, const float* affine_weight, const float*
                         void* stream);
 int fuma_rmsnorm_sh_bwd(const float* x, const float* affine_weight, const float* degree_weight, const float* rstd,
                         const float* g_out, int64_t N, int32_t C, float* g_x, void* stream);
+/* Gated atom-wise block (the atom_wise module the reference's layers call, model.py:157; here
+ * the stand-in SpectralAtomwise). h [9, N, H]: the per-coefficient output of its first
+ * per-degree linear map without bias, coefficient-major; u [N, 2H]: its scalar MLP
+ * pre-activation (bias included). z_0 = SiLU(h_0 + b1), z_k = h_k sigmoid(SiLU(u))[degree - 1]
+ * for k >= 1, written [9, N, H]. The backward returns gh [9, N, H] and gu [N, 2H] from gz.
+ * H a multiple of 4. */
+int fuma_atomwise_gate_fwd(const float* h, const float* u, const float* b1, int64_t N, int32_t H, float* z,
+                           void* stream);
+int fuma_atomwise_gate_bwd(const float* gz, const float* h, const float* u, const float* b1, int64_t N, int32_t H,
+                           float* gh, float* gu, void* stream);
+/* out[n, k, :] = src[k, n, :] + add[n, k, :] (add may be NULL) + row0 on k = 0 (row0 [N, W] when
+ * row0_per_node, else [W]; may be NULL): coefficient-major [9, N, W] rows back to the node-major
+ * [N, 9, W] embedding layout. W a multiple of 4. */
+int fuma_coef_to_node(const float* src, const float* add, const float* row0, int32_t row0_per_node, int64_t N,
+                      int32_t W, float* out, void* stream);
 /* Destination (and optionally source) CSR of a renumbered edge list, from the CSR of the
  * original numbering: new node a is original node perm[a] (perm: int64 [N]), edge ids are
  * unchanged. Replaces the per-step stable-argsort CSR build of the reference on its renumbered

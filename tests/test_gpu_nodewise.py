@@ -28,3 +28,30 @@ def test_rms_norm_sh_matches_module(N, C):
     check_errors()
     assert (ya - yb).abs().max() <= 2e-6 * (1 + ya.abs().max())
     assert (ga - gb).abs().max() <= 1e-5 * (1 + ga.abs().max())
+
+
+@pytest.mark.parametrize("N,C,H", [(1, 64, 64), (333, 128, 128), (4000, 128, 128), (70, 64, 96)])
+def test_atomwise_residual_matches_module(N, C, H):
+    from flash_uma_b200 import ops
+    from flash_uma_b200.linear import check_errors
+    from flash_uma_b200.nodewise import SpectralAtomwise
+    g = torch.Generator().manual_seed(N + C + H)
+    aw = SpectralAtomwise(C, H)
+    with torch.no_grad():
+        for p in aw.parameters():
+            p.copy_(torch.randn(p.shape, generator=g) / (p.shape[-1] ** 0.5))
+    aw = aw.to(DEV)
+    xn = torch.randn(N, 9, C, generator=g).to(DEV)
+    xm = torch.randn(N, 9, C, generator=g).to(DEV)
+    r = torch.randn(N, 9, C, generator=g).to(DEV)
+    a = [xn.clone().requires_grad_(True), xm.clone().requires_grad_(True)]
+    b = [xn.clone().requires_grad_(True), xm.clone().requires_grad_(True)]
+    ya = aw(a[0]) + a[1]
+    yb = ops.atomwise_residual(aw, b[0], b[1])
+    ga = torch.autograd.grad((ya * r).sum(), a)
+    gb = torch.autograd.grad((yb * r).sum(), b)
+    torch.cuda.synchronize()
+    check_errors()
+    assert (ya - yb).abs().max() <= 2e-5 * (1 + ya.abs().max())
+    for u, v in zip(ga, gb):
+        assert (u - v).abs().max() <= 2e-5 * (1 + u.abs().max())
