@@ -40,6 +40,7 @@ _SIGS = {
     "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
     "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
     "fuma_csr_permute": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P],
+    "fuma_morton_reorder": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
     "fuma_atomwise_gate_fwd": [_P, _P, _P, _I64, _I32, _P, _P],
     "fuma_atomwise_gate_bwd": [_P, _P, _P, _P, _I64, _I32, _P, _P, _P],
     "fuma_coef_to_node": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
@@ -104,6 +105,7 @@ KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3
 KERNELS_PER_CALL["fuma_gather_fwd"] = 2
 KERNELS_PER_CALL["fuma_csr_permute"] = 2
+KERNELS_PER_CALL["fuma_morton_reorder"] = 2
 KERNELS_PER_CALL["fuma_gather_fwd_f16x3"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2

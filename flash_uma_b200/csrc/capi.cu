@@ -516,6 +516,22 @@ int fuma_coef_to_node(const float* src, const float* add, const float* row0, int
   return launched("coef_to_node");
 }
 
+int fuma_morton_reorder(const float* pos, const int64_t* Z, const int64_t* batch, const int64_t* idx_i,
+                        const int64_t* idx_j, int64_t N, int64_t E, int64_t* perm, int64_t* inv_perm, float* pos_s,
+                        int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, void* stream) {
+  REQUIRE(N >= 0 && N <= kMortonMaxAtoms, "morton_reorder: N=%lld beyond the %d atoms one block sorts",
+          (long long)N, kMortonMaxAtoms);
+  REQUIRE(E >= 0, "morton_reorder: bad E");
+  if (N == 0 && E == 0) return FUMA_OK;
+  REQUIRE(pos && Z && batch && perm && inv_perm && Z_s && batch_s, "morton_reorder: null atom pointer");
+  REQUIRE(E == 0 || (idx_i && idx_j && ii && jj), "morton_reorder: null edge pointer");
+  BIND(pos);
+  const cudaError_t st = launch_morton_reorder(pos, Z, batch, idx_i, idx_j, N, E, perm, inv_perm, pos_s, Z_s,
+                                               batch_s, ii, jj, (cudaStream_t)stream);
+  if (st != cudaSuccess) return fail((int)st, "morton_reorder: launch failed: %s", cudaGetErrorString(st));
+  return launched("morton_reorder");
+}
+
 int fuma_csr_permute(const int32_t* dst_row_ptr, const int32_t* dst_col, const int32_t* src_row_ptr,
                      const int32_t* src_col, const int64_t* perm, int64_t N, int64_t E, int32_t* new_dst_row_ptr,
                      int32_t* new_dst_col, int32_t* new_src_row_ptr, int32_t* new_src_col, void* stream) {

@@ -61,9 +61,20 @@ def _expand_bits(v: torch.Tensor) -> torch.Tensor:
     return v
 
 
+MORTON_MAX_ATOMS = 16384   # the native reorder sorts up to this many atoms in one block
+
+
 def reorder_graph_morton(pos, Z, batch, idx_i, idx_j):
     """Sort atoms by (system, 30-bit Morton code of the position quantised to 10 bits per
-    axis over the bounding box) and remap the edges (``model.py:47-74``); stable sort."""
+    axis over the bounding box) and remap the edges (``model.py:47-74``); stable sort. On the
+    GPU up to ``MORTON_MAX_ATOMS`` atoms, ``fuma_morton_reorder`` does all but the position
+    gather (kept in torch, so forces flow back through it) in two launches."""
+    if pos.is_cuda and 0 < pos.shape[0] <= MORTON_MAX_ATOMS:
+        return _reorder_native(pos, Z, batch, idx_i, idx_j)
+    return _reorder_torch(pos, Z, batch, idx_i, idx_j)
+
+
+def _reorder_torch(pos, Z, batch, idx_i, idx_j):
     pos_min = pos.min(dim=0, keepdim=True)[0]
     pos_max = pos.max(dim=0, keepdim=True)[0]
     scale = 1023.0 / torch.clamp(pos_max - pos_min, min=1e-5)
@@ -74,6 +85,21 @@ def reorder_graph_morton(pos, Z, batch, idx_i, idx_j):
     inv_perm = torch.empty_like(perm)
     inv_perm[perm] = torch.arange(len(perm), device=pos.device)
     return pos[perm], Z[perm], batch[perm], inv_perm[idx_i], inv_perm[idx_j], perm, inv_perm
+
+
+def _reorder_native(pos, Z, batch, idx_i, idx_j):
+    from ._native import call, ptr, stream_of
+    N, E = pos.shape[0], idx_i.shape[0]
+    p = pos.detach().float().contiguous()
+    Z, batch = Z.long().contiguous(), batch.long().contiguous()
+    idx_i, idx_j = idx_i.long().contiguous(), idx_j.long().contiguous()
+    i64 = dict(device=pos.device, dtype=torch.int64)
+    perm, inv_perm = torch.empty(N, **i64), torch.empty(N, **i64)
+    Z_s, batch_s = torch.empty(N, **i64), torch.empty(N, **i64)
+    ii, jj = torch.empty(E, **i64), torch.empty(E, **i64)
+    call("fuma_morton_reorder", ptr(p), ptr(Z), ptr(batch), ptr(idx_i), ptr(idx_j), N, E, ptr(perm), ptr(inv_perm),
+         None, ptr(Z_s), ptr(batch_s), ptr(ii), ptr(jj), stream_of(p))
+    return pos[perm], Z_s, batch_s, ii, jj, perm, inv_perm
 
 
 # ---- layers ------------------------------------------------------------------------------------

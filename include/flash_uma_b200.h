@@ -176,6 +176,14 @@ int fuma_atomwise_gate_bwd(const float* gz, const float* h, const float* u, cons
  * [N, 9, W] embedding layout. W a multiple of 4. */
 int fuma_coef_to_node(const float* src, const float* add, const float* row0, int32_t row0_per_node, int64_t N,
                       int32_t W, float* out, void* stream);
+/* Morton order of up to 16,384 atoms and the renumbered graph (replaces reorder_graph_morton,
+ * model.py:47-74): 30-bit codes of the positions quantised to 10 bits per axis over their
+ * bounding box, a stable sort by (system << 32 | code), perm [N] (new -> old) and inv_perm [N],
+ * the permuted pos_s [N, 3] (may be NULL), Z_s and batch_s [N], and the renumbered edge rows
+ * ii = inv_perm[idx_i], jj = inv_perm[idx_j] [E]. Same arithmetic and order as the reference. */
+int fuma_morton_reorder(const float* pos, const int64_t* Z, const int64_t* batch, const int64_t* idx_i,
+                        const int64_t* idx_j, int64_t N, int64_t E, int64_t* perm, int64_t* inv_perm, float* pos_s,
+                        int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, void* stream);
 /* Destination (and optionally source) CSR of a renumbered edge list, from the CSR of the
  * original numbering: new node a is original node perm[a] (perm: int64 [N]), edge ids are
  * unchanged. Replaces the per-step stable-argsort CSR build of the reference on its renumbered

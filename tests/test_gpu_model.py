@@ -154,3 +154,25 @@ def test_csr_permute_matches_sorted_build(N, E):
     torch.cuda.synchronize()
     for f in ("dst_row_ptr", "dst_col", "src_row_ptr", "src_col"):
         assert torch.equal(getattr(got, f), getattr(ref, f)), f
+
+
+@pytest.mark.parametrize("N,E,nsys", [(1, 0, 1), (29, 500, 1), (4000, 120000, 1), (3000, 50000, 3), (16384, 1000, 2)])
+def test_native_morton_reorder_matches_torch(N, E, nsys):
+    """fuma_morton_reorder against the torch statement of reorder_graph_morton (model.py:47-74)
+    on the GPU: identical permutation (ties, e.g. duplicated positions, ordered by index), atom
+    data and renumbered edges."""
+    from flash_uma_b200.model import _reorder_native, _reorder_torch
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(N + E)
+    pos = torch.rand(N, 3, generator=g) * 30.0
+    if N > 10:
+        pos[N // 2:N // 2 + 5] = pos[3]             # duplicated positions: equal keys
+    batch = torch.sort(torch.randint(0, nsys, (N,), generator=g))[0]
+    Z = torch.randint(1, 90, (N,), generator=g)
+    idx = torch.randint(0, N, (2, E), generator=g)
+    args = [t.to(dev) for t in (pos, Z, batch, idx[0], idx[1])]
+    got = _reorder_native(*args)
+    ref = _reorder_torch(*args)
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
