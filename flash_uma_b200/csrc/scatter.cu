@@ -21,15 +21,8 @@ namespace fuma {
 
 namespace {
 
-__device__ __forceinline__ void stage_edge(float* sw, const float* __restrict__ wig, const float* __restrict__ env,
-                                           int64_t e, int lane) {
-  sw[lane] = __ldg(wig + e * kWig + lane);
-  if (lane < 2) sw[32 + lane] = __ldg(wig + e * kWig + 32 + lane);
-  if (lane == 2) sw[34] = __ldg(env + e);
-}
-
 constexpr int kFwdWarps = 4;   // rotate-scatter forward: warps per block (static ring below 48 KB)
-constexpr int kRing = 4;       // rotate-scatter forward: edges staged per warp
+constexpr int kRing = 4;       // edges staged per warp (rotate-scatter forward, init scatter)
 
 }  // namespace
 
@@ -306,16 +299,21 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
   report_split_range(bad, err);
 }
 
+// Initial embedding scatter (the reference's init_node_scatter forward, ops/scatter.py:382-423),
+// warp per destination atom: x[n] = W_sphere[Z_n] + csd[batch_n] on l = 0, plus over the atom's
+// edges in CSR order env * [r0; D1 row 1 r1; D2 row 2 r2] / 5 in fp64 accumulators. Each edge's
+// radial row, Wigner entries and envelope are copied into a per-warp cp.async ring kRing - 1
+// edges ahead of the sum (the per-edge arithmetic and its order are unchanged).
 template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) init_scatter_fwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ rad,
     const float* __restrict__ wig, const float* __restrict__ env, const int64_t* __restrict__ Z,
     const int64_t* __restrict__ batch, const float* __restrict__ W_sphere, const float* __restrict__ csd,
     float* __restrict__ x_out, int64_t N, int C) {
-  __shared__ float s_w[WARPS][36];
+  __shared__ float4 s_stage[WARPS][kRing][3][32];   // radial slots 0-2 of the staged edges
+  __shared__ float s_w[WARPS][kRing][12];          // D1 row 1 (0-2), D2 row 2 (3-7), envelope (8)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
-  float* sw = s_w[warp];
   for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     const int64_t z = Z[jn], b = batch[jn];
@@ -323,28 +321,62 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_fwd_kernel(
       const int c4 = c0 + lane;
       const bool act = c4 < C4;
       const int co = c4 * 4;
+      auto issue = [&](int64_t e, int bf) {
+        if (act) {
+          const float* rr = rad + e * 3 * (int64_t)C + co;
+          float4* d = &s_stage[warp][bf][0][lane];
+          cp_async16(d, rr);
+          cp_async16(d + 32, rr + C);
+          cp_async16(d + 64, rr + 2 * C);
+        }
+        if (lane < 3) cp_async4(&s_w[warp][bf][lane], wig + e * kWig + 3 + lane);
+        else if (lane < 8) cp_async4(&s_w[warp][bf][lane], wig + e * kWig + 19 + (lane - 3));
+        else if (lane == 8) cp_async4(&s_w[warp][bf][8], env + e);
+        cp_async_commit();
+      };
+      int ib = kb;
+      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
+      int ki = kb;
+      auto issue_next = [&]() {
+        if (ki < ke) {
+          if (ki - ib >= 32) {
+            ib += 32;
+            e_l = (ib + lane < ke) ? col_idx[ib + lane] : 0;
+          }
+          issue(__shfl_sync(kFull, e_l, ki - ib), (ki - kb) % kRing);
+        } else {
+          cp_async_commit();
+        }
+        ++ki;
+      };
+#pragma unroll 1
+      for (int p = 0; p < kRing - 1; ++p) issue_next();
       d4 acc[9];
       if (act) {
         acc[0] = d4_of(ld4_keep(W_sphere + z * C + co) + ld4_keep(csd + b * C + co));
 #pragma unroll
         for (int l = 1; l < 9; ++l) acc[l] = d4{0.0, 0.0, 0.0, 0.0};
       }
+#pragma unroll 1
       for (int k = kb; k < ke; ++k) {
-        const int64_t e = col_idx[k];
-        stage_edge(sw, wig, env, e, lane);
+        issue_next();
+        cp_async_wait<kRing - 1>();
         __syncwarp();
+        const int bf = (k - kb) % kRing;
+        const float* sw = s_w[warp][bf];
         if (act) {
-          const float ev = sw[34];
-          const float* rr = rad + e * 3 * (int64_t)C + co;
-          const float4 r0 = ld4_stream(rr), r1 = ld4_stream(rr + C), r2 = ld4_stream(rr + 2 * C);
+          const float ev = sw[8];
+          const float4* src = &s_stage[warp][bf][0][lane];
+          const float4 r0 = src[0], r1 = src[32], r2 = src[64];
           acc[0] += div4(r0 * ev, 5.f);
 #pragma unroll
-          for (int kk = 0; kk < 3; ++kk) acc[1 + kk] += div4((r1 * sw[3 + kk]) * ev, 5.f);
+          for (int kk = 0; kk < 3; ++kk) acc[1 + kk] += div4((r1 * sw[kk]) * ev, 5.f);
 #pragma unroll
-          for (int kk = 0; kk < 5; ++kk) acc[4 + kk] += div4((r2 * sw[9 + 10 + kk]) * ev, 5.f);
+          for (int kk = 0; kk < 5; ++kk) acc[4 + kk] += div4((r2 * sw[3 + kk]) * ev, 5.f);
         }
-        __syncwarp();
+        __syncwarp();   // buffer bf is refilled by the next iteration's copies
       }
+      cp_async_wait<0>();
       if (act) {
         float* xo = x_out + jn * 9 * (int64_t)C + co;
 #pragma unroll
@@ -354,68 +386,113 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_fwd_kernel(
   }
 }
 
-// Init-scatter backward (destination-grouped): g_rad = [g0, D1[1,:].g_l1, D2[2,:].g_l2] * env / 5,
-// g_wigner (m=0 rows only, other entries zero) = env * sum_c g (x) r / 5, g_env = sum_c g . contrib / env.
+// Backward of the initial embedding scatter, warp per destination atom over its CSR edges:
+//   g_rad = env * [g0, D1 row 1 . g1, D2 row 2 . g2] / 5, and per edge the Wigner entries of
+//   D1 row 1 / D2 row 2 and the envelope gradient (channel sums).
+// The atom's gradient rows (divided by 5) stay in registers across its edges; each edge's
+// radial row, Wigner entries and envelope are copied into a per-warp cp.async ring kRing - 1
+// edges ahead; the nine channel sums of an edge use the transpose reduction.
 template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ rad, const float* __restrict__ wig, const float* __restrict__ env,
     float* __restrict__ g_rad, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, bool split,
     int* err) {
-  __shared__ float s_w[WARPS][36];
-  __shared__ float s_red[WARPS][12];
+  __shared__ float4 s_stage[WARPS][kRing][3][32];   // radial slots 0-2 of the staged edges
+  __shared__ float s_w[WARPS][kRing][12];          // D1 row 1 (0-2), D2 row 2 (3-7), envelope (8)
   bool bad = false;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
-  float* sw = s_w[warp];
   for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
-    for (int k = kb; k < ke; ++k) {
-      const int64_t e = col_idx[k];
-      stage_edge(sw, wig, env, e, lane);
-      __syncwarp();
-      const float ev = sw[34];
-      float part[9];
+    for (int cb = 0; cb < C4; cb += 32) {
+      const int c4 = cb + lane;
+      const bool on = c4 < C4;
+      const int co = c4 * 4;
+      auto issue = [&](int64_t e, int b) {
+        if (on) {
+          const float* rr = rad + e * 3 * (int64_t)C + co;
+          float4* d = &s_stage[warp][b][0][lane];
+          cp_async16(d, rr);
+          cp_async16(d + 32, rr + C);
+          cp_async16(d + 64, rr + 2 * C);
+        }
+        if (lane < 3) cp_async4(&s_w[warp][b][lane], wig + e * kWig + 3 + lane);
+        else if (lane < 8) cp_async4(&s_w[warp][b][lane], wig + e * kWig + 19 + (lane - 3));
+        else if (lane == 8) cp_async4(&s_w[warp][b][8], env + e);
+        cp_async_commit();
+      };
+      int ib = kb;
+      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
+      int ki = kb;
+      auto issue_next = [&]() {
+        if (ki < ke) {
+          if (ki - ib >= 32) {
+            ib += 32;
+            e_l = (ib + lane < ke) ? col_idx[ib + lane] : 0;
+          }
+          issue(__shfl_sync(kFull, e_l, ki - ib), (ki - kb) % kRing);
+        } else {
+          cp_async_commit();
+        }
+        ++ki;
+      };
+#pragma unroll 1
+      for (int p = 0; p < kRing - 1; ++p) issue_next();
+      // this atom's gradient rows / 5, kept for all its edges
+      float4 g[9];
 #pragma unroll
-      for (int m = 0; m < 9; ++m) part[m] = 0.f;
-      for (int c4 = lane; c4 < C4; c4 += 32) {
-        const int co = c4 * 4;
-        const float* go = g_out + jn * 9 * (int64_t)C + co;
-        float4 g[9];
+      for (int l = 0; l < 9; ++l) g[l] = on ? div4(ld4_keep(g_out + (jn * 9 + l) * (int64_t)C + co), 5.f) : f4(0.f);
+      int base_c = kb, e_lc = e_l;   // edge ids for the sum side (its own 32-wide window)
+#pragma unroll 1
+      for (int k = kb; k < ke; ++k) {
+        issue_next();
+        cp_async_wait<kRing - 1>();
+        __syncwarp();
+        if (k - base_c >= 32) {
+          base_c += 32;
+          e_lc = (base_c + lane < ke) ? col_idx[base_c + lane] : 0;
+        }
+        const int64_t e = __shfl_sync(kFull, e_lc, k - base_c);
+        const int b = (k - kb) % kRing;
+        const float* sw = s_w[warp][b];
+        const float ev = sw[8];
+        const float4* src = &s_stage[warp][b][0][lane];
+        const float4 r0 = on ? src[0] : f4(0.f), r1 = on ? src[32] : f4(0.f), r2 = on ? src[64] : f4(0.f);
+        float4 s1 = g[1] * sw[0];
+        fma4(s1, sw[1], g[2]);
+        fma4(s1, sw[2], g[3]);
+        float4 s2 = g[4] * sw[3];
 #pragma unroll
-        for (int l = 0; l < 9; ++l) g[l] = div4(ld4_keep(go + l * C), 5.f);
-        const float* rr = rad + e * 3 * (int64_t)C + co;
-        const float4 r0 = ld4_stream(rr), r1 = ld4_stream(rr + C), r2 = ld4_stream(rr + 2 * C);
-        float4 s1 = g[1] * sw[3];
-        fma4(s1, sw[4], g[2]);
-        fma4(s1, sw[5], g[3]);
-        float4 s2 = g[4] * sw[19];
+        for (int kk = 1; kk < 5; ++kk) fma4(s2, sw[3 + kk], g[4 + kk]);
+        if (on) {
+          float* gr = g_rad + e * 3 * (int64_t)C;
+          st_out4(gr, 3 * C, co, g[0] * ev, split, bad);
+          st_out4(gr, 3 * C, C + co, s1 * ev, split, bad);
+          st_out4(gr, 3 * C, 2 * C + co, s2 * ev, split, bad);
+        }
+        float part[16];
 #pragma unroll
-        for (int kk = 1; kk < 5; ++kk) fma4(s2, sw[19 + kk], g[4 + kk]);
-        float* gr = g_rad + e * 3 * (int64_t)C;
-        st_out4(gr, 3 * C, co, g[0] * ev, split, bad);
-        st_out4(gr, 3 * C, C + co, s1 * ev, split, bad);
-        st_out4(gr, 3 * C, 2 * C + co, s2 * ev, split, bad);
+        for (int kk = 0; kk < 3; ++kk) part[kk] = dot4(g[1 + kk], r1);
 #pragma unroll
-        for (int kk = 0; kk < 3; ++kk) part[kk] += dot4(g[1 + kk], r1);
+        for (int kk = 0; kk < 5; ++kk) part[3 + kk] = dot4(g[4 + kk], r2);
+        part[8] = dot4(g[0], r0) + dot4(s1, r1) + dot4(s2, r2);
 #pragma unroll
-        for (int kk = 0; kk < 5; ++kk) part[3 + kk] += dot4(g[4 + kk], r2);
-        part[8] += dot4(g[0], r0) + dot4(s1, r1) + dot4(s2, r2);
+        for (int m = 9; m < 16; ++m) part[m] = 0.f;
+        const float tot = warp_transpose_sum<16>(part, lane);   // lane m < 9: channel sum of partial m
+        // full 34-wide row: D1 row 1 -> entries 3..5, D2 row 2 -> entries 19..23, zeros elsewhere
+        const float t3 = __shfl_sync(kFull, tot, (lane - 3) & 31), t19 = __shfl_sync(kFull, tot, (lane - 16) & 31);
+        float v = 0.f;
+        if (lane >= 3 && lane < 6) v = t3 * ev;
+        if (lane >= 19 && lane < 24) v = t19 * ev;
+        float* gw = g_wig + e * kWig;
+        gw[lane] = cb == 0 ? v : gw[lane] + v;
+        if (lane < 2) gw[32 + lane] = 0.f;
+        const float t8 = __shfl_sync(kFull, tot, 8);
+        if (lane == 0) g_env[e] = cb == 0 ? t8 : g_env[e] + t8;
+        __syncwarp();   // buffer b is refilled by the next iteration's copies
       }
-#pragma unroll
-      for (int m = 0; m < 9; ++m) {
-        const float t = warp_sum(part[m]);
-        if (lane == 0) s_red[warp][m] = t;
-      }
-      __syncwarp();
-      // full 34-wide row: D1 row 1 -> entries 3..5, D2 row 2 -> entries 19..23, zeros elsewhere
-      float v = 0.f;
-      if (lane >= 3 && lane < 6) v = s_red[warp][lane - 3] * ev;
-      if (lane >= 19 && lane < 24) v = s_red[warp][3 + lane - 19] * ev;
-      g_wig[e * kWig + lane] = v;
-      if (lane < 2) g_wig[e * kWig + 32 + lane] = 0.f;
-      if (lane == 0) g_env[e] = s_red[warp][8];
-      __syncwarp();
+      cp_async_wait<0>();
     }
   }
   report_split_range(bad, err);
@@ -445,7 +522,7 @@ void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, c
 void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,
                              const float* env, const int64_t* Z, const int64_t* batch, const float* W_sphere,
                              const float* csd, float* x_out, int64_t N, int C, cudaStream_t s) {
-  init_scatter_fwd_kernel<8><<<grid_resident(init_scatter_fwd_kernel<8>, 256, N, 8), 256, 0, s>>>(row_ptr, col_idx, rad, wig, env, Z, batch, W_sphere,
+  init_scatter_fwd_kernel<4><<<grid_resident(init_scatter_fwd_kernel<4>, 128, N, 4), 128, 0, s>>>(row_ptr, col_idx, rad, wig, env, Z, batch, W_sphere,
                                                                csd, x_out, N, C);
 }
 
