@@ -87,11 +87,6 @@ def gemm_flops_per_step(E, C, B, L, H=None, gauss_only=True):
 
 GEMM_OPS = ("fuma_linear_f16x3", "fuma_linear")
 
-# DRAM bytes per call (dram__bytes_read.sum + dram__bytes_write.sum) measured by ncu on the
-# config-3 step with the f16x3 fused path: profiles/ncu_dram_traffic_bench_config3_step.md
-# (GEMM: average over the step's launches; gather backward: its four launches per call).
-NCU_TRAFFIC_BYTES = {"fuma_linear_f16x3": 374.7e6, "fuma_gather_bwd_f16x3": 2716.0e6}
-
 
 def gemm_mode(mode, bf16):
     """Tensor-pipe products per fp32 product, the pipe's peak (TF/s) and labels of a GEMM mode."""
@@ -277,9 +272,12 @@ def run_flash(args, rank, world, device):
         step(pos_seq[w])
     torch.cuda.synchronize()
     _native.set_probe(probe)
-    step(pos_seq[0])
+    res0 = step(pos_seq[0])
     torch.cuda.synchronize()
     _native.set_probe(None)
+    # results at the first position, for the parity check against the reference's Triton path
+    check0 = (res0["energy"].detach().clone(), res0["forces"].detach().clone())
+    del res0
     per_op = {n: sum(probe.times_ms(n)) for n in probe.events}
     probe_counts = dict(probe.counts)
     dominant = max(per_op, key=per_op.get)
@@ -350,6 +348,7 @@ def run_flash(args, rank, world, device):
     f_host = torch.empty(N, 3).pin_memory()
     e_host = torch.empty(1).pin_memory()
     s_host = torch.empty(1, 3, 3).pin_memory()
+    st_host = torch.zeros(K, dtype=torch.int32).pin_memory()   # each step's GEMM error status
     pos_dev = torch.empty(N, 3, device=device)
     if world > 1:
         torch.distributed.barrier()
@@ -365,10 +364,15 @@ def run_flash(args, rank, world, device):
         e_host.copy_(res["energy"], non_blocking=True)
         if with_stress:
             s_host.copy_(res["stress"], non_blocking=True)
+        if "status" in res:
+            st_host[k:k + 1].copy_(res["status"], non_blocking=True)
         e1.record()
         evs2.append((e0, e1))
     torch.cuda.synchronize()
     e2e_ms = sum(a.elapsed_time(b) for a, b in evs2)
+    from flash_uma_b200.linear import raise_status
+    for k in range(K):   # a failed GEMM in any timed step invalidates the run
+        raise_status(st_host[k:k + 1], device)
 
     if gstep is not None and world > 1:
         gstep.release()   # the graph holds NCCL work: free it before the process group goes
@@ -383,16 +387,22 @@ def run_flash(args, rank, world, device):
     Ek, Nk = (len(plan.edges), len(plan.local_ids)) if world > 1 else (E, N)
     gm = gemm_mode(args.gemm, bf16)
     if dominant in GEMM_OPS:
-        # tensor-bound: tensor-pipe FLOPs per launch (3 products per fp32 product in the split modes)
+        # tensor-bound. achieved / frac: ALGORITHMIC fp32 FLOPs per launch (the model's dense
+        # FLOPs, 2 x M x N x K per product) over the measured dense bf16 peak; the split modes run
+        # ``passes`` tensor-pipe products per fp32 product, reported apart as the pipe utilisation
         launches = gprobe.counts.get(dominant, 1) if graphed else probe.counts.get(dominant, 1) // K
         flops = gemm_flops_per_step(Ek, C, B, L, gauss_only=args.gemm == "f16x3")
-        flops_launch = gm["passes"] * flops / max(1, launches)
+        flops_launch = flops / max(1, launches)
         achieved = flops_launch / (avg_ms * 1e-3) / 1e12
         roof = {"kernel": gm["kernel"], "bound": "tensor", "achieved": achieved,
-                "peak": gm["peak"], "unit": "TFLOP/s", "frac": achieved / gm["peak"],
-                "peak_kind": f"{peak_kind}: {gm['peak_note']}",
-                "traffic": NCU_TRAFFIC_BYTES.get(dominant) if args.workload == "default" and world == 1 else None,
-                "alg_flops_per_launch": flops_launch}
+                "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
+                "peak_kind": f"{peak_kind} dense bf16 (burst)",
+                "traffic": None,
+                "alg_flops_per_launch": flops_launch,
+                "tensor_pipe_util": {"pipe": gm["pipe"], "products_per_fp32_product": gm["passes"],
+                                     "pipe_tflops": gm["passes"] * achieved,
+                                     "frac_of_pipe_peak": gm["passes"] * achieved / gm["peak"],
+                                     "pipe_peak": gm["peak"], "pipe_peak_note": gm["peak_note"]}}
     else:
         nbytes = alg_bytes(dominant, Nk, Ek, C, B, M_rows=Ek, D=128)
         achieved = nbytes / (avg_ms * 1e-3) / 1e9 if nbytes and avg_ms > 0 else None
@@ -411,8 +421,7 @@ def run_flash(args, rank, world, device):
         nb = alg_bytes(top_mem, Nk, Ek, C, B, M_rows=Ek, D=128)
         gbs = nb / (ms_launch * 1e-3) / 1e9
         roof_mem = {"kernel": top_mem, "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                    "frac": gbs / hbm, "alg_bytes_per_launch": nb, "avg_launch_ms": ms_launch,
-                    "traffic": NCU_TRAFFIC_BYTES.get(top_mem) if args.workload == "default" and world == 1 else None}
+                    "frac": gbs / hbm, "alg_bytes_per_launch": nb, "avg_launch_ms": ms_launch, "traffic": None}
     atoms_total = N if world > 1 else world * N
     out = {
         "metric": METRIC, "value": atoms_total * K / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
@@ -429,7 +438,7 @@ def run_flash(args, rank, world, device):
                    "parallelism": f"spatial slabs x{world} (halo atoms per rank: {len(plan.halo)} on rank 0)"
                    if world > 1 else "single GPU"},
         "e2e": {"value": atoms_total * K / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4,
-                "d2h_bytes_per_step": N * 3 * 4 + 4 + (36 if with_stress else 0)},
+                "d2h_bytes_per_step": N * 3 * 4 + 4 + (36 if with_stress else 0) + 4},
         "max_device_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
         "roofline": roof,
         "roofline_top_hbm_kernel": roof_mem,
@@ -438,6 +447,28 @@ def run_flash(args, rank, world, device):
         "per_kernel_ms_one_step": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
         "clocks": clocks,
     }
+    out["_check"] = check0
+    out["_pos0"] = pos_seq[0].detach().cpu()
+    return out
+
+
+def partition_parity(args, device, check0, pos0):
+    """N > 1: the same system and positions on this one GPU (single-GPU path, no partition)
+    against the partitioned result of every rank (energy, forces; stress with it)."""
+    import dataclasses
+    system, with_stress, _, _ = workload_system(args.workload, int(os.environ.get("WORLD_SIZE", "1")))
+    torch.cuda.empty_cache()
+    _, data_cpu, pred = build_problem(device, args.gemm, system)
+    data = data_cpu.to(device)
+    res = pred(dataclasses.replace(data, pos=pos0.to(device)), stress=with_stress, check=True)
+    e, f = check0[0].double(), check0[1].double()
+    er, fr = res["energy"].double(), res["forces"].double()
+    out = {"energy_rel": float(((e - er).abs() / er.abs().clamp_min(1.0)).max()),
+           "forces_max_abs": float((f - fr).abs().max()),
+           "against": "single-GPU path on the same system and positions (rank 0, after the timed run)",
+           "bar": {"energy_rel": 1e-5, "forces_max_abs": 1e-4}}
+    del pred, res, data
+    torch.cuda.empty_cache()
     return out
 
 
@@ -528,13 +559,33 @@ def run_micro(args, device):
         rad = 2 * ((B + 2 * C) * H + H * H + H * 12 * C)
         flops = 2 * E * (so2 + rad) - (E * 2 * 2 * C * H if use_fused else 0)
         ms = kernels[gm["op"]]["ms_per_step"]
-        tf = gm["passes"] * flops / (ms * 1e-3) / 1e12
-        kernels[gm["op"]].update(flops_per_step=flops, passes=gm["passes"], pipe=gm["pipe"], tflops_pipe=tf,
-                                 frac_pipe_peak=tf / gm["peak"])
-    print(json.dumps({"metric": "one message-passing layer fwd+bwd (BASELINE config 2)", "nodes": N, "edges": E,
-                      "ms_per_layer": total, "gemm": gm["label"],
-                      "peaks": {"hbm_gbs": hbm, "pipe_tflops": gm["peak"], "kind": kind, "note": gm["peak_note"]},
-                      "kernels": dict(sorted(kernels.items(), key=lambda kv: -kv[1]["ms_per_step"]))}), flush=True)
+        tf = flops / (ms * 1e-3) / 1e12
+        kernels[gm["op"]].update(alg_flops_per_step=flops, alg_tflops=tf, frac_tensor_peak=tf / bf16,
+                                 passes=gm["passes"], pipe=gm["pipe"], tflops_pipe=gm["passes"] * tf,
+                                 frac_pipe_peak=gm["passes"] * tf / gm["peak"])
+    del step, layer, inp, gout, x0, xe, wig, env, graph
+    torch.cuda.empty_cache()
+    return {"metric": "one message-passing layer fwd+bwd (BASELINE config 2)", "nodes": N, "edges": E,
+            "ms_per_layer": total, "gemm": gm["label"],
+            "peaks": {"hbm_gbs": hbm, "tensor_tflops": bf16, "pipe_tflops": gm["peak"], "kind": kind,
+                      "note": gm["peak_note"]},
+            "kernels": dict(sorted(kernels.items(), key=lambda kv: -kv[1]["ms_per_step"]))}
+
+
+def kernel_fractions(micro):
+    """Compact per-kernel HBM fractions of the config-2 microbench for the bench line."""
+    out = {}
+    for name, k in micro["kernels"].items():
+        if "frac_hbm" in k:
+            out[name] = {"frac_hbm": round(k["frac_hbm"], 4), "achieved_gbs": round(k["achieved_gbs"], 1),
+                         "ms_per_call": round(k["ms_per_step"] / max(1, k["launches_per_step"]), 4)}
+        elif "frac_tensor_peak" in k:
+            out[name] = {"frac_tensor_peak": round(k["frac_tensor_peak"], 4),
+                         "frac_pipe_peak": round(k["frac_pipe_peak"], 4), "ms_per_step": round(k["ms_per_step"], 4)}
+    return {"workload": f"BASELINE config 2: one layer fwd+bwd, N={micro['nodes']}, E={micro['edges']}",
+            "ms_per_layer": round(micro["ms_per_layer"], 4), "hbm_peak_gbs": micro["peaks"]["hbm_gbs"],
+            "timing": "CUDA events around every C-ABI call (fwd+bwd of the layer, inputs resident)",
+            "kernels": out}
 
 
 # the reference's published FlashUMA step times for its atom-count sweep (random graphs, ~50
@@ -593,58 +644,160 @@ def run_sweep(args, device):
                       "sizes": rows}), flush=True)
 
 
-def cpu_oracle_rate(atoms_sample: int = 256, min_seconds: float = 8.0, max_steps: int = 4):
-    """Time the CPU oracle (PyTorch restatement of the reference) on a bulk-Cu sample."""
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def load_reference_gpu():
+    """The unmodified reference implementation from ``baseline/_ref`` (installed by
+    ``baseline/install_reference.py``): its wrapper module, whose ``ZeroAllocBackbone`` runs the
+    reference's Triton kernels natively on the GPU. ``model.py`` imports
+    ``balance_channels_batched`` from fairchem at load time (``model.py:11``), which is not
+    installed; the same stand-in this build uses is registered under that module name (it is
+    only called for models with charge / spin channel ranges). None if not installed."""
+    import types
+    if not os.path.isfile(os.path.join(REF_DIR, "wrapper.py")):
+        return None
+    from flash_uma_b200.nodewise import balance_channels_batched
+    for name in ["fairchem", "fairchem.core", "fairchem.core.models", "fairchem.core.models.uma",
+                 "fairchem.core.models.uma.escn_md"]:
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.modules["fairchem.core.models.uma.escn_md"].balance_channels_batched = balance_channels_batched
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import wrapper as ref_wrapper   # noqa: E402  (baseline/_ref/wrapper.py)
+    return ref_wrapper
+
+
+def run_reference_gpu(device, steps: int, warmup: int, system, tf32: bool, check=None):
+    """The reference's own Triton path on this GPU (``ZeroAllocBackbone`` of ``baseline/_ref``,
+    ``wrapper.py:171-211`` -> ``model.py:187-221`` -> ``ops/*.py``) on the bench workload: the
+    same seed-0 weights, node-wise stand-ins, energy head and MD-like positions as the flash arm,
+    energy + forces per step, eager launches (its stock path), CUDA events per step with the L2
+    flushed in between, as ``examples/benchmark.py:33-56`` times it. ``tf32``: cuBLAS TF32 for
+    its F.linear calls (the reference's published setting) or full fp32. ``check``: (energy,
+    forces) of the flash arm at the first position, compared with the reference's result."""
+    import dataclasses
+
     from flash_uma_b200.predict import Predictor
     from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
-    from flash_uma_b200.systems import bulk_fcc, to_graph
+    from flash_uma_b200.systems import to_graph
+    ref_wrapper = load_reference_gpu()
+    if ref_wrapper is None:
+        return {"unavailable": "baseline/_ref not installed (python baseline/install_reference.py <reference>)"}
+    prev = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = tf32
+    torch.backends.cudnn.allow_tf32 = tf32
+    try:
+        off = SyntheticESCNMDBackbone(seed=0).to(device)
+        head = make_energy_head(128, 128, seed=1).to(device)
+        pred = Predictor(ref_wrapper.ZeroAllocBackbone(off, dtype=torch.float32), head)
+        data_cpu = to_graph([system])
+        data = data_cpu.to(device)
+        N = data_cpu.pos.shape[0]
+        pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, steps + warmup, seed=0)]
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+        t0 = time.perf_counter()
+        for w in range(warmup):   # the first call autotunes and compiles the Triton kernels
+            res = pred(dataclasses.replace(data, pos=pos_seq[w]))
+        torch.cuda.synchronize()
+        warm_s = time.perf_counter() - t0
+        parity = None
+        if check is not None:
+            res = pred(dataclasses.replace(data, pos=pos_seq[0]))
+            e_ref, f_ref = res["energy"].double(), res["forces"].double()
+            e, f = check[0].double(), check[1].double()
+            parity = {"energy_rel": float(((e - e_ref).abs() / e_ref.abs().clamp_min(1.0)).max()),
+                      "forces_max_abs": float((f - f_ref).abs().max()),
+                      "note": "flash arm vs this reference run at the same positions"}
+        sampler = ClockSampler(device.index if device.index is not None else 0)
+        torch.cuda.synchronize()
+        sampler.start()
+        evs = []
+        for k in range(steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            pred(dataclasses.replace(data, pos=pos_seq[warmup + k]))
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+        out = {"value": N / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "steps": steps, "warmup": warmup,
+               "tf32": tf32, "launch": "eager (the reference's stock path)", "warmup_s": round(warm_s, 1),
+               "max_device_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9, "clocks": clocks}
+        if parity is not None:
+            out["parity"] = parity
+        return out
+    except Exception as exc:   # noqa: BLE001 - reported in the line, the flash arm's number stands
+        return {"unavailable": f"reference Triton path failed: {type(exc).__name__}: {exc}"[:400]}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = prev
+        torch.cuda.empty_cache()
+
+
+def _oracle_predictor():
+    from flash_uma_b200.predict import Predictor
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
     from oracle.model import OracleBackbone
-    n = {256: 4, 500: 5, 864: 6}[atoms_sample]
+    return Predictor(OracleBackbone(SyntheticESCNMDBackbone(seed=0)), make_energy_head(128, 128, seed=1))
+
+
+def cpu_oracle_rate(max_seconds: float = 30.0):
+    """``cpu_baseline`` of the N = 1 line: the CPU oracle (PyTorch restatement of the reference,
+    fp32, all host threads) on the full config-3 system, one E+F step timed after a warm-up step
+    on a 256-atom bulk-Cu cell (thread pool and allocator); more steps while under max_seconds."""
+    from flash_uma_b200.systems import bulk_fcc, config3_system, to_graph
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    data = to_graph([bulk_fcc(n, n, n, jitter=0.05, seed=0)])
-    off = SyntheticESCNMDBackbone(seed=0)
-    pred = Predictor(OracleBackbone(off), make_energy_head(128, 128, seed=1))
-    pred(data)  # warm-up
+    pred = _oracle_predictor()
+    pred(to_graph([bulk_fcc(4, 4, 4, jitter=0.05, seed=0)]))
+    data = to_graph([config3_system()])
+    atoms = data.pos.shape[0]
     t0 = time.perf_counter()
     steps = 0
-    while steps < max_steps and (time.perf_counter() - t0 < min_seconds or steps == 0):
+    while steps == 0 or time.perf_counter() - t0 < max_seconds / 2:
         pred(data)
         steps += 1
     dt = time.perf_counter() - t0
-    return {"value": atoms_sample * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"bulk fcc Cu {n}x{n}x{n} ({atoms_sample} atoms, same per-atom work as config 3), "
-                      f"{steps} E+F step(s), {dt:.1f} s"}
+    return {"value": atoms * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"the full config-3 system (bulk Cu 10x10x10, {atoms} atoms, {data.edge_index.shape[1]} edges), "
+                      f"{steps} E+F step(s) in {dt:.1f} s after a 256-atom warm-up step"}
 
 
-def run_reference(args):
-    """The reference's CPU implementation of the path (its restatement, ``oracle/``) on the host."""
-    from flash_uma_b200.predict import Predictor
-    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
-    from flash_uma_b200.systems import bulk_fcc, to_graph
-    from oracle.model import OracleBackbone
+def run_reference(args, budget_s: float = 180.0):
+    """``--impl reference``: the reference's CPU implementation of the path (its PyTorch
+    restatement, ``oracle/``; the reference itself is Triton-only) on all host threads, on the
+    same workload as the flash arm (config 3, 4,000 atoms, E+F per step). A CPU step takes tens
+    of seconds, so the run is bounded: one warm-up step, then timed steps until ``--steps`` are
+    done or ``budget_s`` has passed (at least two); ``steps`` reports the steps actually timed."""
+    from flash_uma_b200.systems import config3_system, to_graph
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    n = 4
-    data = to_graph([bulk_fcc(n, n, n, jitter=0.05, seed=0)])
-    atoms = data.pos.shape[0]
-    pred = Predictor(OracleBackbone(SyntheticESCNMDBackbone(seed=0)), make_energy_head(128, 128, seed=1))
-    for _ in range(args.warmup):
+    data = to_graph([config3_system()])
+    atoms, edges = data.pos.shape[0], data.edge_index.shape[1]
+    pred = _oracle_predictor()
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
         pred(data)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    steps = 0
+    while steps < args.steps and (steps < 2 or time.perf_counter() - t0 < budget_s):
         pred(data)
+        steps += 1
     dt = time.perf_counter() - t0
-    v = atoms * args.steps / dt
+    v = atoms * steps / dt
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+            "steps": steps, "steps_requested": args.steps, "warmup": warm, "ms_per_step": dt * 1e3 / steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded bulk Cu positions, random-init weights)",
-            "config": {"workload": "bulk_cu_4000 (BASELINE config 3), each step a bounded sample: bulk Cu 4x4x4 "
-                                   f"({atoms} atoms, same per-atom work), E+F, CPU",
-                       "atoms_per_step": atoms, "sphere_channels": 128, "layers": 4, "num_distance_basis": 64},
+            "config": {"workload": f"bulk_cu_4000 (BASELINE config 3), E+F per step: {atoms} atoms, {edges} edges, "
+                                   "CPU (PyTorch restatement of the reference)",
+                       "atoms": atoms, "edges": edges, "sphere_channels": 128, "layers": 4,
+                       "num_distance_basis": 64, "same_config": True},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"bulk fcc Cu 4x4x4 ({atoms} atoms) per step, {args.steps} steps"},
+                             "sample": f"the full config-3 system per step ({atoms} atoms), {steps} timed steps "
+                                       f"(bounded to ~{budget_s:.0f} s), {warm} warm-up"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -705,6 +858,10 @@ def main():
     ap.add_argument("--micro", action="store_true", help="one-layer kernel microbench (BASELINE config 2)")
     ap.add_argument("--sweep", action="store_true",
                     help="step time over the reference's atom-count sweep (100-2,000 atoms, 50 edges/atom, E+F+S)")
+    ap.add_argument("--no-reference-gpu", dest="reference_gpu", action="store_false",
+                    help="skip timing the reference's Triton path on this GPU (N = 1 default workload)")
+    ap.add_argument("--no-kernels", dest="kernels", action="store_false",
+                    help="skip the per-kernel config-2 fractions of the N = 1 line")
     ap.add_argument("--nodes", type=int, default=20000)
     ap.add_argument("--edges", type=int, default=600000)
     args = ap.parse_args()
@@ -729,7 +886,7 @@ def main():
     torch.cuda.set_device(device)
     if args.micro:
         if rank == 0:
-            run_micro(args, device)
+            print(json.dumps(run_micro(args, device)), flush=True)
         return
     if args.sweep:
         if rank == 0:
@@ -740,13 +897,37 @@ def main():
         torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     try:
         out = run_flash(args, rank, world, device)
-        if rank == 0:
-            if world == 1 and not args.no_cpu_baseline:
-                out["cpu_baseline"] = cpu_oracle_rate()
-            print(json.dumps(out), flush=True)
+        check0 = out.pop("_check")
+        pos0 = out.pop("_pos0")
+        if rank == 0 and world == 1 and args.workload == "default":
+            if args.reference_gpu:
+                # the reference's own Triton path on the same GPU and workload: full fp32 (the
+                # accuracy class of this build's f16x3 path and of the parity bar) and TF32 (its
+                # published setting); ratio = this build's value / the reference's
+                system, _, _, _ = workload_system(args.workload, world)
+                rg = {}
+                for key, tf32 in (("fp32", False), ("tf32", True)):
+                    r = run_reference_gpu(device, min(args.steps, 10), 3, system, tf32,
+                                          check=check0 if not tf32 else None)
+                    if "value" in r:
+                        r["ratio"] = out["value"] / r["value"]
+                        r["e2e_ratio"] = out["e2e"]["value"] / r["value"]
+                    rg[key] = r
+                out["reference_triton_gpu"] = rg
+            if args.kernels:
+                margs = argparse.Namespace(**vars(args))
+                margs.nodes, margs.edges, margs.steps, margs.warmup = 20000, 600000, 5, 3
+                out["kernels"] = kernel_fractions(run_micro(margs, device))
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()
+    if rank == 0:
+        if world > 1:
+            # after the process group is gone, so no rank waits on a collective meanwhile
+            out["parity"] = partition_parity(args, device, check0, pos0)
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_oracle_rate()
+        print(json.dumps(out), flush=True)
 
 
 if __name__ == "__main__":

@@ -85,6 +85,30 @@ def snapshot_errors() -> None:
         h.copy_(t, non_blocking=True)
 
 
+def step_status(device: torch.device) -> torch.Tensor:
+    """A device-side copy of ``device``'s GEMM error flag, taken on the current stream after
+    everything queued so far (no synchronisation): the status of the step that was just queued,
+    0 when every GEMM of it (and of earlier unreported steps) succeeded. Callers that copy a
+    step's results to the host copy this 4-byte tensor with them and pass it to
+    :func:`raise_status`."""
+    return error_flag(device).clone()
+
+
+def raise_status(status: torch.Tensor, device: torch.device | None = None) -> None:
+    """Raise (and clear the device flag) if a :func:`step_status` value holds an error code.
+    Reads the value: a device tensor synchronises, a host copy does not (``device``: the GPU
+    the host copy came from, default the current one)."""
+    code = int(status.reshape(-1)[0])
+    if code:
+        if device is not None and device.index is not None:
+            idx = device.index
+        else:
+            idx = status.device.index if status.is_cuda else torch.cuda.current_device()
+        if idx in _err_flags:
+            _reset(idx)
+        _raise(idx, code)
+
+
 def poll_errors() -> None:
     """Raise if an earlier :func:`snapshot_errors` copy has landed with an error code (no sync:
     an error is seen at the first poll after its snapshot completed)."""

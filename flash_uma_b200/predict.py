@@ -20,7 +20,12 @@ class Predictor:
         self.backbone = backbone
         self.head = head
 
-    def __call__(self, data, forces: bool = True, stress: bool = False):
+    def __call__(self, data, forces: bool = True, stress: bool = False, check: bool = False):
+        """Energy [nsys] (+ forces [N, 3], stress [nsys, 3, 3]) of ``data``. On a GPU the result
+        also holds ``status``: a 1-element device int32 tensor, 0 unless a GEMM of this step (or
+        of an earlier step not yet reported) failed (f16x3 range error 16, pipeline timeout
+        1-5). Copy it to the host with the results and pass it to ``linear.raise_status``, or
+        call with ``check=True`` to synchronise and raise here, before the results are used."""
         nsys = len(data.natoms)
         pos = data.pos.detach().clone().requires_grad_(forces or stress)
         cell = data.cell.detach().clone()
@@ -48,6 +53,10 @@ class Predictor:
             if stress:
                 vol = torch.linalg.det(cell).abs()
                 res["stress"] = grads[1] / vol[:, None, None]
+        if pos.is_cuda:
+            res["status"] = linear.step_status(pos.device)
+            if check:
+                linear.raise_status(res["status"])
         return res
 
 
@@ -57,8 +66,9 @@ class GraphedStep:
     replays every kernel of the forward and backward pass with one launch, so the host does
     no per-kernel work. The graph build, Morton order and CSRs are part of the capture and are
     recomputed from the positions on every replay, exactly as in an eager call. Returns the
-    captured output tensors (overwritten by the next call). Errors recorded by the GEMMs
-    (pipeline timeouts, f16x3 range) are polled before each replay, one call late."""
+    captured output tensors (overwritten by the next call), including ``status``, the GEMM
+    error status of this replay (see :class:`Predictor`): ``check=True`` synchronises and raises
+    on an error before returning; otherwise errors also surface at the next call's poll."""
 
     def __init__(self, predictor, data, forces: bool = True, stress: bool = False, warmup: int = 3,
                  capture_hook=None):
@@ -82,8 +92,10 @@ class GraphedStep:
                 if capture_hook is not None:
                     capture_hook(False)
 
-    def __call__(self, pos: torch.Tensor):
+    def __call__(self, pos: torch.Tensor, check: bool = False):
         linear.poll_errors()
         self._pos.copy_(pos, non_blocking=True)
         self.graph.replay()
+        if check:
+            linear.raise_status(self.out["status"])
         return self.out

@@ -106,8 +106,12 @@ class OracleLayer:
 class OracleBackbone:
     """CPU oracle of ``ZeroAllocBackbone`` (``wrapper.py:88-211``) + ``eSCN_Inference_Model``."""
 
-    def __init__(self, off_bb, dtype=torch.float32):
+    def __init__(self, off_bb, dtype=torch.float32, checkpoint_layers: bool = False):
+        """``checkpoint_layers``: keep only each layer's input for the backward and recompute the
+        layer there (torch.utils.checkpoint), which bounds host memory by one layer's activations
+        (the full-size configurations); the arithmetic is unchanged."""
         self.dtype = dtype
+        self.checkpoint_layers = checkpoint_layers
         self.C = off_bb.sphere_channels
         self.B = off_bb.num_distance_basis
         self.cutoff = float(off_bb.cutoff)
@@ -170,7 +174,12 @@ class OracleBackbone:
         x_edge, wigner, env = self.geometry(pos_s, Z_s, ii, jj, shifts, graph)
         x = self.init_embedding(x_edge, wigner, env, Z_s, batch_s, csd_emb, jj, graph, N)
         for k in range(len(self.layers)):
-            x = self.layer_forward(k, x, x_edge, wigner, env, ii, jj, graph, csd_emb, batch_s, charge, spin, natoms)
+            args = (k, x, x_edge, wigner, env, ii, jj, graph, csd_emb, batch_s, charge, spin, natoms)
+            if self.checkpoint_layers and torch.is_grad_enabled():
+                from torch.utils.checkpoint import checkpoint
+                x = checkpoint(self.layer_forward, *args, use_reentrant=False)
+            else:
+                x = self.layer_forward(*args)
         return self.final(x)[inv_perm]
 
     def forward(self, data):
