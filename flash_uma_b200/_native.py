@@ -40,7 +40,7 @@ _SIGS = {
     "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
     "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
     "fuma_csr_permute": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P],
-    "fuma_morton_reorder": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
+    "fuma_morton_reorder": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _P],
     "fuma_atomwise_gate_fwd": [_P, _P, _P, _I64, _I32, _P, _P],
     "fuma_atomwise_gate_bwd": [_P, _P, _P, _P, _I64, _I32, _P, _P, _P],
     "fuma_coef_to_node": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
@@ -77,13 +77,15 @@ def load(allow_build: bool = False) -> ctypes.CDLL:
             fn.argtypes = args
             fn.restype = ctypes.c_int
         lib.fuma_version.restype = ctypes.c_int
+        lib.fuma_morton_scratch_bytes.argtypes = [_I64]
+        lib.fuma_morton_scratch_bytes.restype = ctypes.c_int64
         lib.fuma_last_error.restype = ctypes.c_char_p
         _lib = lib
         return lib
 
 
 def exported_symbols():
-    return ["fuma_version", "fuma_last_error", *_SIGS.keys()]
+    return ["fuma_version", "fuma_last_error", "fuma_morton_scratch_bytes", *_SIGS.keys()]
 
 
 def ptr(t: torch.Tensor | None) -> int | None:
@@ -105,13 +107,20 @@ KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3
 KERNELS_PER_CALL["fuma_gather_fwd"] = 2
 KERNELS_PER_CALL["fuma_csr_permute"] = 2
-KERNELS_PER_CALL["fuma_morton_reorder"] = 2
+KERNELS_PER_CALL["fuma_morton_reorder"] = 2   # up to 16,384 atoms (launches_of)
 KERNELS_PER_CALL["fuma_gather_fwd_f16x3"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2
 KERNELS_PER_CALL["fuma_gather_bwd_noalloc"] = 3
 KERNELS_PER_CALL["fuma_gather_bwd_f16x3"] = 3
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd_f16x3"] = 2
+
+
+def launches_of(name: str, args) -> int:
+    """Kernel launches of one call of entry point ``name`` with arguments ``args``."""
+    if name == "fuma_morton_reorder" and args[5] > 16384:
+        return 28   # bounds, keys, 8 radix passes of 3 kernels, permutation, renumbering
+    return KERNELS_PER_CALL.get(name, 1)
 
 
 class LaunchProbe:
@@ -142,7 +151,7 @@ class LaunchProbe:
 
     def before(self, name, args):
         self.counts[name] = self.counts.get(name, 0) + 1
-        self.launches += KERNELS_PER_CALL.get(name, 1)
+        self.launches += launches_of(name, args)
         if self.timing and name in self.timed:
             ev0 = self._event()
             ev0.record()

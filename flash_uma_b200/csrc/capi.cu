@@ -516,18 +516,26 @@ int fuma_coef_to_node(const float* src, const float* add, const float* row0, int
   return launched("coef_to_node");
 }
 
+int64_t fuma_morton_scratch_bytes(int64_t N) { return N < 0 ? 0 : morton_scratch_bytes(N); }
+
 int fuma_morton_reorder(const float* pos, const int64_t* Z, const int64_t* batch, const int64_t* idx_i,
                         const int64_t* idx_j, int64_t N, int64_t E, int64_t* perm, int64_t* inv_perm, float* pos_s,
-                        int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, void* stream) {
-  REQUIRE(N >= 0 && N <= kMortonMaxAtoms, "morton_reorder: N=%lld beyond the %d atoms one block sorts",
-          (long long)N, kMortonMaxAtoms);
+                        int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, void* scratch,
+                        int64_t scratch_bytes, int* err_flag, void* stream) {
+  REQUIRE(N >= 0 && N < (int64_t(1) << 31), "morton_reorder: bad N=%lld", (long long)N);
   REQUIRE(E >= 0, "morton_reorder: bad E");
   if (N == 0 && E == 0) return FUMA_OK;
   REQUIRE(pos && Z && batch && perm && inv_perm && Z_s && batch_s, "morton_reorder: null atom pointer");
   REQUIRE(E == 0 || (idx_i && idx_j && ii && jj), "morton_reorder: null edge pointer");
+  const int64_t need = morton_scratch_bytes(N);
+  REQUIRE(scratch_bytes >= need && (need == 0 || scratch),
+          "morton_reorder: N=%lld needs %lld bytes of scratch (fuma_morton_scratch_bytes), got %lld",
+          (long long)N, (long long)need, (long long)scratch_bytes);
+  REQUIRE(need == 0 || (reinterpret_cast<uintptr_t>(scratch) & 255u) == 0,
+          "morton_reorder: scratch must be 256-byte aligned");
   BIND(pos);
   const cudaError_t st = launch_morton_reorder(pos, Z, batch, idx_i, idx_j, N, E, perm, inv_perm, pos_s, Z_s,
-                                               batch_s, ii, jj, (cudaStream_t)stream);
+                                               batch_s, ii, jj, scratch, err_flag, (cudaStream_t)stream);
   if (st != cudaSuccess) return fail((int)st, "morton_reorder: launch failed: %s", cudaGetErrorString(st));
   return launched("morton_reorder");
 }

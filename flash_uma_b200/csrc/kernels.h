@@ -64,11 +64,13 @@ void launch_atomwise_gate_bwd(const float* gz, const float* h, const float* u, c
                               float* gh, float* gu, cudaStream_t s);
 void launch_coef_to_node(const float* src, const float* add, const float* row0, int row0_per_node, int64_t N, int W,
                          float* out, cudaStream_t s);
-constexpr int kMortonMaxAtoms = 16384;   // one block sorts the atoms in shared memory
+constexpr int kMortonMaxAtoms = 16384;   // up to this many atoms one block sorts them in shared memory
+// scratch bytes of the radix-sort path (0 up to kMortonMaxAtoms atoms)
+int64_t morton_scratch_bytes(int64_t N);
 cudaError_t launch_morton_reorder(const float* pos, const int64_t* Z, const int64_t* batch, const int64_t* idx_i,
                                   const int64_t* idx_j, int64_t N, int64_t E, int64_t* perm, int64_t* inv_perm,
                                   float* pos_s, int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj,
-                                  cudaStream_t s);
+                                  void* scratch, int* err, cudaStream_t s);
 void launch_csr_permute(int ngraphs, const int32_t* const* row_ptr, const int32_t* const* col, const int64_t* perm,
                         int64_t N, int32_t* const* new_row_ptr, int32_t* const* new_col, cudaStream_t s);
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,

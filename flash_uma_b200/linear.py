@@ -31,6 +31,7 @@ _err_flags: dict[int, torch.Tensor] = {}
 _err_host: dict[int, torch.Tensor] = {}     # pinned mirrors, filled asynchronously by snapshot_errors()
 
 _ERR_RANGE = 16
+_ERR_INDEX = 32   # fuma_morton_reorder: an edge index outside [0, N)
 
 
 def default_mode() -> str:
@@ -41,8 +42,9 @@ def default_mode() -> str:
 
 
 def error_flag(device: torch.device) -> torch.Tensor:
-    """Per-device int32 flag that the GEMM kernels set if one of their pipeline waits times out
-    (codes 1-5) or an f16x3 input is out of the fp16 range (code 16)."""
+    """Per-device int32 flag (the first error recorded is kept): a GEMM pipeline wait timed out
+    (codes 1-5), an f16x3 input is out of the fp16 range (code 16), or the Morton reorder met an
+    edge index outside [0, N) (code 32)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _err_flags.get(idx)
     if t is None:
@@ -52,6 +54,9 @@ def error_flag(device: torch.device) -> torch.Tensor:
 
 
 def _raise(idx: int, code: int):
+    if code == _ERR_INDEX:
+        raise RuntimeError(f"fuma_morton_reorder: an edge index on cuda:{idx} is outside [0, num_atoms); the edge "
+                           "was renumbered to atom 0 and the results are invalid")
     if code == _ERR_RANGE:
         raise RuntimeError(f"fuma_linear_f16x3: an input value on cuda:{idx} is beyond the fp16 range of the f16x3 "
                            "split (|x| >= 65520); construct the model with gemm='tf32x3' for such data")

@@ -61,15 +61,13 @@ def _expand_bits(v: torch.Tensor) -> torch.Tensor:
     return v
 
 
-MORTON_MAX_ATOMS = 16384   # the native reorder sorts up to this many atoms in one block
-
-
 def reorder_graph_morton(pos, Z, batch, idx_i, idx_j):
     """Sort atoms by (system, 30-bit Morton code of the position quantised to 10 bits per
     axis over the bounding box) and remap the edges (``model.py:47-74``); stable sort. On the
-    GPU up to ``MORTON_MAX_ATOMS`` atoms, ``fuma_morton_reorder`` does all but the position
-    gather (kept in torch, so forces flow back through it) in two launches."""
-    if pos.is_cuda and 0 < pos.shape[0] <= MORTON_MAX_ATOMS:
+    GPU ``fuma_morton_reorder`` does all but the position gather (kept in torch, so forces flow
+    back through it): one shared-memory sort for up to 16,384 atoms, a multi-block radix sort
+    on a scratch buffer above that."""
+    if pos.is_cuda and pos.shape[0] > 0:
         return _reorder_native(pos, Z, batch, idx_i, idx_j)
     return _reorder_torch(pos, Z, batch, idx_i, idx_j)
 
@@ -88,7 +86,8 @@ def _reorder_torch(pos, Z, batch, idx_i, idx_j):
 
 
 def _reorder_native(pos, Z, batch, idx_i, idx_j):
-    from ._native import call, ptr, stream_of
+    from ._native import call, load, ptr, stream_of
+    from .linear import error_flag
     N, E = pos.shape[0], idx_i.shape[0]
     p = pos.detach().float().contiguous()
     Z, batch = Z.long().contiguous(), batch.long().contiguous()
@@ -97,8 +96,10 @@ def _reorder_native(pos, Z, batch, idx_i, idx_j):
     perm, inv_perm = torch.empty(N, **i64), torch.empty(N, **i64)
     Z_s, batch_s = torch.empty(N, **i64), torch.empty(N, **i64)
     ii, jj = torch.empty(E, **i64), torch.empty(E, **i64)
+    nbytes = int(load().fuma_morton_scratch_bytes(N))
+    scratch = torch.empty(max(nbytes, 1), device=pos.device, dtype=torch.uint8) if nbytes else None
     call("fuma_morton_reorder", ptr(p), ptr(Z), ptr(batch), ptr(idx_i), ptr(idx_j), N, E, ptr(perm), ptr(inv_perm),
-         None, ptr(Z_s), ptr(batch_s), ptr(ii), ptr(jj), stream_of(p))
+         None, ptr(Z_s), ptr(batch_s), ptr(ii), ptr(jj), ptr(scratch), nbytes, ptr(error_flag(pos.device)), stream_of(p))
     return pos[perm], Z_s, batch_s, ii, jj, perm, inv_perm
 
 

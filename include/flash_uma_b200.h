@@ -176,14 +176,21 @@ int fuma_atomwise_gate_bwd(const float* gz, const float* h, const float* u, cons
  * [N, 9, W] embedding layout. W a multiple of 4. */
 int fuma_coef_to_node(const float* src, const float* add, const float* row0, int32_t row0_per_node, int64_t N,
                       int32_t W, float* out, void* stream);
-/* Morton order of up to 16,384 atoms and the renumbered graph (replaces reorder_graph_morton,
+/* Morton order of the atoms and the renumbered graph (replaces reorder_graph_morton,
  * model.py:47-74): 30-bit codes of the positions quantised to 10 bits per axis over their
  * bounding box, a stable sort by (system << 32 | code), perm [N] (new -> old) and inv_perm [N],
  * the permuted pos_s [N, 3] (may be NULL), Z_s and batch_s [N], and the renumbered edge rows
- * ii = inv_perm[idx_i], jj = inv_perm[idx_j] [E]. Same arithmetic and order as the reference. */
+ * ii = inv_perm[idx_i], jj = inv_perm[idx_j] [E]. Same arithmetic and order as the reference.
+ * System ids must be non-negative. Up to 16,384 atoms one block sorts in shared memory and no
+ * scratch is needed; above that a multi-block radix sort uses scratch_bytes >=
+ * fuma_morton_scratch_bytes(N) bytes of device scratch (256-byte aligned, contents irrelevant;
+ * about 24 bytes per atom). An edge index outside [0, N) sets code 32 in err_flag (device int,
+ * may be NULL) and renumbers that edge to atom 0. */
+int64_t fuma_morton_scratch_bytes(int64_t N);
 int fuma_morton_reorder(const float* pos, const int64_t* Z, const int64_t* batch, const int64_t* idx_i,
                         const int64_t* idx_j, int64_t N, int64_t E, int64_t* perm, int64_t* inv_perm, float* pos_s,
-                        int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, void* stream);
+                        int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, void* scratch,
+                        int64_t scratch_bytes, int* err_flag, void* stream);
 /* Destination (and optionally source) CSR of a renumbered edge list, from the CSR of the
  * original numbering: new node a is original node perm[a] (perm: int64 [N]), edge ids are
  * unchanged. Replaces the per-step stable-argsort CSR build of the reference on its renumbered

@@ -156,18 +156,25 @@ def test_csr_permute_matches_sorted_build(N, E):
         assert torch.equal(getattr(got, f), getattr(ref, f)), f
 
 
-@pytest.mark.parametrize("N,E,nsys", [(1, 0, 1), (29, 500, 1), (4000, 120000, 1), (3000, 50000, 3), (16384, 1000, 2)])
+@pytest.mark.parametrize("N,E,nsys", [(1, 0, 1), (29, 500, 1), (4000, 120000, 1), (3000, 50000, 3), (16384, 1000, 2),
+                                      (16385, 5000, 1), (100800, 3024000, 1), (70000, 1000, 300),
+                                      (40000, 100, 1 << 20), (50000, 10, -7)])
 def test_native_morton_reorder_matches_torch(N, E, nsys):
     """fuma_morton_reorder against the torch statement of reorder_graph_morton (model.py:47-74)
     on the GPU: identical permutation (ties, e.g. duplicated positions, ordered by index), atom
-    data and renumbered edges."""
+    data and renumbered edges. Up to 16,384 atoms the one-block sort runs; above, the radix sort
+    (config 5 has 100,800 atoms), with one or more system-id passes (300 and 2^20 systems), and
+    with unsorted system ids (nsys < 0: |nsys| systems in random order)."""
     from flash_uma_b200.model import _reorder_native, _reorder_torch
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(N + E)
     pos = torch.rand(N, 3, generator=g) * 30.0
     if N > 10:
         pos[N // 2:N // 2 + 5] = pos[3]             # duplicated positions: equal keys
-    batch = torch.sort(torch.randint(0, nsys, (N,), generator=g))[0]
+    if nsys < 0:
+        batch = torch.randint(0, -nsys, (N,), generator=g)
+    else:
+        batch = torch.sort(torch.randint(0, nsys, (N,), generator=g))[0]
     Z = torch.randint(1, 90, (N,), generator=g)
     idx = torch.randint(0, N, (2, E), generator=g)
     args = [t.to(dev) for t in (pos, Z, batch, idx[0], idx[1])]
@@ -176,3 +183,30 @@ def test_native_morton_reorder_matches_torch(N, E, nsys):
     torch.cuda.synchronize()
     for a, b in zip(got, ref):
         assert torch.equal(a, b)
+
+
+def test_morton_reorder_flags_out_of_range_edges():
+    """An edge index outside [0, N) is recorded (error code 32, raised by check_errors) and the
+    edge is renumbered to atom 0 instead of being read out of bounds; valid edges are unaffected."""
+    from flash_uma_b200.linear import check_errors
+    from flash_uma_b200.model import _reorder_native, _reorder_torch
+    dev = torch.device("cuda")
+    for N in (100, 20000):   # both sort paths
+        g = torch.Generator().manual_seed(N)
+        pos = (torch.rand(N, 3, generator=g) * 20).to(dev)
+        Z = torch.full((N,), 29, dtype=torch.long, device=dev)
+        batch = torch.zeros(N, dtype=torch.long, device=dev)
+        idx = torch.randint(0, N, (2, 50), generator=g).to(dev)
+        bad = idx.clone()
+        bad[0, 3] = N
+        bad[1, 7] = -1
+        got = _reorder_native(pos, Z, batch, bad[0], bad[1])
+        ref = _reorder_torch(pos, Z, batch, idx[0], idx[1])
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="outside"):
+            check_errors()
+        ok = torch.ones(50, dtype=torch.bool, device=dev)
+        ok[3] = ok[7] = False
+        assert torch.equal(got[3][ok], ref[3][ok]) and torch.equal(got[4][ok], ref[4][ok])
+        assert got[3][3].item() == 0 and got[4][7].item() == 0
+        check_errors()   # the flag was cleared by the raise
