@@ -472,6 +472,66 @@ def partition_parity(args, device, check0, pos0):
     return out
 
 
+def run_strong5(args, rank, world, device, steps: int = 3, warmup: int = 2):
+    """BASELINE config 5 (bulk fcc Cu 30x30x28, 100,800 atoms, 3,024,000 edges, energy + forces) at
+    this run's N (strong scaling: the same system at every N): atom-steps/s, ms per step (CUDA
+    events, max over ranks), halo atoms per rank, device memory, and the device time of every
+    collective kind per step (halo all-to-all forward / backward, the energy / force all-reduce).
+    Eager launches; one GPU runs the memory-lean mode when the activations would not fit."""
+    import dataclasses
+
+    from flash_uma_b200 import partition as part
+    from flash_uma_b200.systems import config5_system
+    torch.cuda.empty_cache()
+    torch.cuda.reset_peak_memory_stats(device)
+    system = config5_system()
+    halo = 0
+    if world > 1:
+        system, data_cpu, step, plan, _ = build_partitioned(device, args.gemm, world, rank, system, False)
+        halo = len(plan.halo)
+    else:
+        _, data_cpu, pred = build_problem(device, args.gemm, system)
+        data = data_cpu.to(device)
+
+        def step(pos):
+            return pred(dataclasses.replace(data, pos=pos))
+    N, E = data_cpu.pos.shape[0], data_cpu.edge_index.shape[1]
+    pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, steps + warmup, seed=0)]
+    for w in range(warmup):
+        step(pos_seq[w])
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    part.collective_events = [] if world > 1 else None
+    evs = []
+    for k in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step(pos_seq[warmup + k])
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    coll = {k: v / steps for k, v in part.collective_times_ms().items()}
+    part.collective_events = None
+    ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    halos = torch.zeros(world, dtype=torch.float64, device=device)
+    halos[rank] = halo
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(halos)
+    ms = float(t.item())
+    from flash_uma_b200 import fused
+    lean = fused.lean_needed(E // world if world > 1 else E, 128, 128, 4, device)
+    return {"workload": "bulk_cu_100800 (BASELINE config 5), E+F per step, strong scaling", "atoms": N, "edges": E,
+            "n_gpus": world, "value": N / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "warmup": warmup, "launch": "eager", "memory_lean_mode": lean,
+            "halo_atoms_per_rank": [int(h) for h in halos.tolist()] if world > 1 else [0],
+            "max_device_memory_gb_rank0": torch.cuda.max_memory_allocated(device) / 1e9,
+            "collectives_ms_per_step_rank0": {k: round(v, 4) for k, v in coll.items()},
+            "timing": "CUDA events per step, max over ranks; collectives: events around each NCCL call on rank 0"}
+
+
 def run_micro(args, device):
     """one message-passing layer (radial MLP with LN-SiLU -> gather-rotate ->
     SO(2) conv1 -> gating -> conv2 -> FP64 rotate-scatter), forward + backward, inputs resident.
@@ -860,6 +920,8 @@ def main():
                     help="step time over the reference's atom-count sweep (100-2,000 atoms, 50 edges/atom, E+F+S)")
     ap.add_argument("--no-reference-gpu", dest="reference_gpu", action="store_false",
                     help="skip timing the reference's Triton path on this GPU (N = 1 default workload)")
+    ap.add_argument("--no-strong5", dest="strong5", action="store_false",
+                    help="skip the config-5 strong-scaling object (100,800 atoms at this run's N)")
     ap.add_argument("--no-kernels", dest="kernels", action="store_false",
                     help="skip the per-kernel config-2 fractions of the N = 1 line")
     ap.add_argument("--nodes", type=int, default=20000)
@@ -899,6 +961,9 @@ def main():
         out = run_flash(args, rank, world, device)
         check0 = out.pop("_check")
         pos0 = out.pop("_pos0")
+        if args.strong5 and args.workload == "default":
+            # every rank takes part (the partitioned step has collectives)
+            out["strong_config5"] = run_strong5(args, rank, world, device)
         if rank == 0 and world == 1 and args.workload == "default":
             if args.reference_gpu:
                 # the reference's own Triton path on the same GPU and workload: full fp32 (the

@@ -39,6 +39,7 @@ _SIGS = {
     "fuma_linear_f16x3": [_P, _I64, _I32, _P, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _P, _P],
     "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
     "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
+    "fuma_neighbor_list": [_P, _I64, _P, _P, ctypes.c_double, _I32, _P, _I64, _P, _P, _P, _P, _P, _P],
     "fuma_csr_permute": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P],
     "fuma_morton_reorder": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _P],
     "fuma_atomwise_gate_fwd": [_P, _P, _P, _I64, _I32, _P, _P],
@@ -79,13 +80,16 @@ def load(allow_build: bool = False) -> ctypes.CDLL:
         lib.fuma_version.restype = ctypes.c_int
         lib.fuma_morton_scratch_bytes.argtypes = [_I64]
         lib.fuma_morton_scratch_bytes.restype = ctypes.c_int64
+        lib.fuma_neighbor_scratch_bytes.argtypes = [_I64, _P]
+        lib.fuma_neighbor_scratch_bytes.restype = ctypes.c_int64
         lib.fuma_last_error.restype = ctypes.c_char_p
         _lib = lib
         return lib
 
 
 def exported_symbols():
-    return ["fuma_version", "fuma_last_error", "fuma_morton_scratch_bytes", *_SIGS.keys()]
+    return ["fuma_version", "fuma_last_error", "fuma_morton_scratch_bytes", "fuma_neighbor_scratch_bytes",
+            *_SIGS.keys()]
 
 
 def ptr(t: torch.Tensor | None) -> int | None:
@@ -107,6 +111,7 @@ KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3
 KERNELS_PER_CALL["fuma_gather_fwd"] = 2
 KERNELS_PER_CALL["fuma_csr_permute"] = 2
+KERNELS_PER_CALL["fuma_neighbor_list"] = 4
 KERNELS_PER_CALL["fuma_morton_reorder"] = 2   # up to 16,384 atoms (launches_of)
 KERNELS_PER_CALL["fuma_gather_fwd_f16x3"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2

@@ -540,6 +540,33 @@ int fuma_morton_reorder(const float* pos, const int64_t* Z, const int64_t* batch
   return launched("morton_reorder");
 }
 
+int64_t fuma_neighbor_scratch_bytes(int64_t N, const int32_t* grid) {
+  if (N < 0 || !grid || grid[0] < 1 || grid[1] < 1 || grid[2] < 1) return 0;
+  return neighbor_scratch_bytes(N, (int64_t)grid[0] * grid[1] * grid[2]);
+}
+
+int fuma_neighbor_list(const double* pos, int64_t N, const double* geom, const int32_t* grid, double cutoff,
+                       int32_t max_neighbors, void* scratch, int64_t scratch_bytes, int32_t* counts, int64_t* src,
+                       int64_t* offsets, double* dist, int* err_flag, void* stream) {
+  REQUIRE(N >= 0 && N < (int64_t(1) << 31), "neighbor_list: bad N=%lld", (long long)N);
+  REQUIRE(geom && grid, "neighbor_list: null geometry / grid (host arrays)");
+  REQUIRE(cutoff > 0 && max_neighbors > 0, "neighbor_list: cutoff and max_neighbors must be positive");
+  for (int k = 0; k < 3; ++k)
+    REQUIRE(grid[k] >= 1 && grid[3 + k] <= grid[6 + k], "neighbor_list: bad bin grid / image range on axis %d", k);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(pos && counts && src && offsets && dist && scratch, "neighbor_list: null pointer");
+  const int64_t need = neighbor_scratch_bytes(N, (int64_t)grid[0] * grid[1] * grid[2]);
+  REQUIRE(scratch_bytes >= need, "neighbor_list: needs %lld bytes of scratch, got %lld", (long long)need,
+          (long long)scratch_bytes);
+  REQUIRE((reinterpret_cast<uintptr_t>(scratch) & 255u) == 0, "neighbor_list: scratch must be 256-byte aligned");
+  BIND(pos);
+  const cudaError_t st = launch_neighbor_list(pos, N, geom, geom + 9, grid, grid + 3, grid + 6, grid + 9, cutoff,
+                                              max_neighbors, scratch, counts, src, offsets, dist, err_flag,
+                                              (cudaStream_t)stream);
+  if (st != cudaSuccess) return fail((int)st, "neighbor_list: launch failed: %s", cudaGetErrorString(st));
+  return launched("neighbor_list");
+}
+
 int fuma_csr_permute(const int32_t* dst_row_ptr, const int32_t* dst_col, const int32_t* src_row_ptr,
                      const int32_t* src_col, const int64_t* perm, int64_t N, int64_t E, int32_t* new_dst_row_ptr,
                      int32_t* new_dst_col, int32_t* new_src_row_ptr, int32_t* new_src_col, void* stream) {

@@ -80,6 +80,12 @@ void launch_split_rows_f16(const float* x, int64_t lda, int64_t M, int K, void* 
                            cudaStream_t s);
 void launch_split_f16(const float* x, void* hi, void* lo, float scale, int64_t n, cudaStream_t s);
 
+int64_t neighbor_scratch_bytes(int64_t N, int64_t nbins);
+cudaError_t launch_neighbor_list(const double* pos, int64_t N, const double* cell, const double* inv,
+                                 const int32_t* nb, const int32_t* lo, const int32_t* hi, const int32_t* pbc,
+                                 double cutoff, int max_nb, void* scratch, int32_t* counts, int64_t* out_src,
+                                 int64_t* out_off, double* out_dist, int* err, cudaStream_t s);
+
 // Record `fmt` as the calling thread's fuma_last_error() message and return `code`.
 int report_error(int code, const char* fmt, ...);
 

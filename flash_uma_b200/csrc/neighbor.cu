@@ -1,0 +1,312 @@
+// Deterministic capped periodic neighbour list on the device.
+//
+// The reference takes its graph from outside the backbone (FAIRChem / pymatgen radius graph,
+// readme.md:35-72, external_graph_gen). This build defines the graph as a deterministic capped
+// list (flash_uma_b200/systems.py::neighbor_list, the host statement): every ordered pair
+// (source i, destination j, integer cell offset s) with |pos_i - pos_j + s @ cell| < cutoff (a
+// self pair only with s != 0) is a candidate; per destination the candidates are ordered by
+// (distance, source, s_0, s_1, s_2) in fp64 and the first max_neighbors are kept. This file
+// computes the same list:
+//
+//   1. nl_bin_kernel      fractional coordinates (pos @ inv_cell), wrapped into [0, 1), the
+//                         integer wrap shift, the wrapped Cartesian position and the bin of
+//                         every atom (bins of side >= cutoff in fractional space); atomic bin
+//                         counts.
+//   2. nl_scan_kernel     exclusive scan of the bin counts (one block).
+//   3. nl_fill_kernel     atoms into their bins (order inside a bin is irrelevant: step 4 sorts
+//                         its candidates completely).
+//   4. nl_search_kernel   warp per destination atom: the host statement's bin and periodic
+//                         image loops, candidate test in wrapped coordinates, then the distance
+//                         of the pair recomputed from the unwrapped positions and the integer
+//                         offset exactly as the host statement computes it (fp64, no fused
+//                         multiply-adds), the candidates collected in shared memory and the
+//                         first max_neighbors selected in (distance, source, offset) order.
+//
+// Outputs are per-destination slots: counts [N], src [N, max_nb], off [N, max_nb, 3] and dist
+// [N, max_nb]; the caller compacts them into the destination-sorted edge list. A destination
+// with more than kMaxCand candidates records code 64 in the error flag (its list is then
+// incomplete).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fuma {
+
+namespace {
+
+constexpr int kNlWarps = 4;
+constexpr int kMaxCand = 512;          // candidates per destination kept in shared memory
+constexpr int kErrNeighborOverflow = 64;
+
+__device__ __forceinline__ double dmul(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ double dadd(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ double dsub(double a, double b) { return __dsub_rn(a, b); }
+
+// x @ M for a row vector x [3] and M [3, 3] row-major: out_k = (x0 M0k + x1 M1k) + x2 M2k
+__device__ __forceinline__ double rowmat(const double* x, const double* M, int k) {
+  return dadd(dadd(dmul(x[0], M[k]), dmul(x[1], M[3 + k])), dmul(x[2], M[6 + k]));
+}
+
+}  // namespace
+
+struct NlParams {
+  double cell[9], inv[9];
+  int nb[3];
+  int lo[3], hi[3];        // image / bin offset range per axis (inclusive)
+  int pbc[3];
+  double cutoff, cut2;
+  int max_nb;
+};
+
+__global__ void __launch_bounds__(256) nl_bin_kernel(const double* __restrict__ pos, int N, NlParams p,
+                                                     double* __restrict__ wpos, int32_t* __restrict__ wshift,
+                                                     int32_t* __restrict__ bin, int32_t* __restrict__ bin_count) {
+  for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < N; a += gridDim.x * blockDim.x) {
+    const double x[3] = {pos[a * 3], pos[a * 3 + 1], pos[a * 3 + 2]};
+    double w[3];
+    int b[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const double f = rowmat(x, p.inv, k);
+      const double fl = floor(f);
+      w[k] = dsub(f, fl);
+      wshift[a * 3 + k] = (int32_t)fl;
+      int bk = (int)(w[k] * p.nb[k]);
+      b[k] = bk < p.nb[k] - 1 ? bk : p.nb[k] - 1;
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k) wpos[a * 3 + k] = rowmat(w, p.cell, k);
+    const int id = (b[0] * p.nb[1] + b[1]) * p.nb[2] + b[2];
+    bin[a] = id;
+    atomicAdd(&bin_count[id], 1);
+  }
+}
+
+// exclusive scan of bin_count[nbins] into bin_start[nbins + 1], one block of 1024 threads;
+// bin_cursor receives a copy of the starts (filled by nl_fill_kernel)
+__global__ void __launch_bounds__(1024) nl_scan_kernel(const int32_t* __restrict__ count, int nbins,
+                                                       int32_t* __restrict__ start, int32_t* __restrict__ cursor) {
+  __shared__ int32_t s_warp[32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int chunk = (nbins + 1023) / 1024;
+  const int b0 = min(nbins, t * chunk), b1 = min(nbins, b0 + chunk);
+  int sum = 0;
+  for (int i = b0; i < b1; ++i) sum += count[i];
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = s_warp[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFull, w, o);
+      if (lane >= o) w += v;
+    }
+    s_warp[lane] = w;
+  }
+  __syncthreads();
+  int run = incl - sum + (warp > 0 ? s_warp[warp - 1] : 0);
+  for (int i = b0; i < b1; ++i) {
+    start[i] = run;
+    cursor[i] = run;
+    run += count[i];
+  }
+  if (t == 1023) start[nbins] = run;
+}
+
+__global__ void __launch_bounds__(256) nl_fill_kernel(const int32_t* __restrict__ bin, int N,
+                                                      int32_t* __restrict__ cursor, int32_t* __restrict__ members) {
+  for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < N; a += gridDim.x * blockDim.x)
+    members[atomicAdd(&cursor[bin[a]], 1)] = a;
+}
+
+// candidate key: (distance bits, source << 32 | packed offset), both compared as unsigned
+struct Cand {
+  unsigned long long k1, k2;
+};
+
+__device__ __forceinline__ bool cand_less(unsigned long long a1, unsigned long long a2, unsigned long long b1,
+                                          unsigned long long b2) {
+  return a1 < b1 || (a1 == b1 && a2 < b2);
+}
+
+__global__ void __launch_bounds__(kNlWarps * 32) nl_search_kernel(
+    const double* __restrict__ pos, const double* __restrict__ wpos, const int32_t* __restrict__ wshift,
+    const int32_t* __restrict__ bin, const int32_t* __restrict__ bin_start, const int32_t* __restrict__ members,
+    int N, NlParams p, int32_t* __restrict__ counts, int64_t* __restrict__ out_src, int64_t* __restrict__ out_off,
+    double* __restrict__ out_dist, int* __restrict__ err) {
+  __shared__ unsigned long long s_k1[kNlWarps][kMaxCand];
+  __shared__ unsigned long long s_k2[kNlWarps][kMaxCand];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long* k1s = s_k1[warp];
+  unsigned long long* k2s = s_k2[warp];
+  for (int d = blockIdx.x * kNlWarps + warp; d < N; d += gridDim.x * kNlWarps) {
+    const int bd = bin[d];
+    const int b[3] = {bd / (p.nb[1] * p.nb[2]), (bd / p.nb[2]) % p.nb[1], bd % p.nb[2]};
+    const double wd[3] = {wpos[d * 3], wpos[d * 3 + 1], wpos[d * 3 + 2]};
+    const double pd[3] = {pos[d * 3], pos[d * 3 + 1], pos[d * 3 + 2]};
+    const int wsd[3] = {wshift[d * 3], wshift[d * 3 + 1], wshift[d * 3 + 2]};
+    int n = 0;   // candidates collected (uniform across the warp)
+    bool overflow = false;
+    for (int dx = p.lo[0]; dx <= p.hi[0]; ++dx)
+      for (int dy = p.lo[1]; dy <= p.hi[1]; ++dy)
+        for (int dz = p.lo[2]; dz <= p.hi[2]; ++dz) {
+          const int c[3] = {b[0] + dx, b[1] + dy, b[2] + dz};
+          int ix[3], img[3];
+          bool skip = false;
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            ix[k] = ((c[k] % p.nb[k]) + p.nb[k]) % p.nb[k];
+            img[k] = (c[k] - ix[k]) / p.nb[k];
+            if (!p.pbc[k] && img[k] != 0) skip = true;
+          }
+          if (skip) continue;
+          const int sb = (ix[0] * p.nb[1] + ix[1]) * p.nb[2] + ix[2];
+          const double imgd[3] = {(double)img[0], (double)img[1], (double)img[2]};
+          double shift[3];
+#pragma unroll
+          for (int k = 0; k < 3; ++k) shift[k] = rowmat(imgd, p.cell, k);
+          const int s0 = bin_start[sb], s1 = bin_start[sb + 1];
+          for (int base = s0; base < s1; base += 32) {
+            const int idx = base + lane;
+            bool take = false;
+            unsigned long long key1 = 0, key2 = 0;
+            if (idx < s1) {
+              const int s = members[idx];
+              double v[3];
+#pragma unroll
+              for (int k = 0; k < 3; ++k) v[k] = dsub(dadd(wpos[s * 3 + k], shift[k]), wd[k]);
+              const double d2 = dadd(dadd(dmul(v[0], v[0]), dmul(v[1], v[1])), dmul(v[2], v[2]));
+              const bool self = (s == d) && img[0] == 0 && img[1] == 0 && img[2] == 0;
+              if (d2 < p.cut2 && !self) {
+                // the offset in terms of the unwrapped positions, and the distance the model sees
+                int off[3];
+                double offd[3];
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                  off[k] = img[k] + wsd[k] - wshift[s * 3 + k];
+                  offd[k] = (double)off[k];
+                }
+                double u[3];
+#pragma unroll
+                for (int k = 0; k < 3; ++k) u[k] = dadd(dsub(pos[s * 3 + k], pd[k]), rowmat(offd, p.cell, k));
+                const double dist = __dsqrt_rn(dadd(dadd(dmul(u[0], u[0]), dmul(u[1], u[1])), dmul(u[2], u[2])));
+                if (dist < p.cutoff) {
+                  take = true;
+                  key1 = (unsigned long long)__double_as_longlong(dist);
+                  key2 = ((unsigned long long)(uint32_t)s << 32) | ((unsigned long long)(off[0] + 512) << 20) |
+                         ((unsigned long long)(off[1] + 512) << 10) | (unsigned long long)(off[2] + 512);
+                }
+              }
+            }
+            const unsigned m = __ballot_sync(kFull, take);
+            const int slot = n + __popc(m & ((1u << lane) - 1u));
+            if (take) {
+              if (slot < kMaxCand) {
+                k1s[slot] = key1;
+                k2s[slot] = key2;
+              } else {
+                overflow = true;
+              }
+            }
+            n += __popc(m);
+          }
+        }
+    __syncwarp();
+    if (__any_sync(kFull, overflow) && lane == 0 && err) atomicCAS(err, 0, kErrNeighborOverflow);
+    const int total = min(n, kMaxCand);
+    const int keep = min(total, p.max_nb);
+    // selection: the smallest remaining key, max_nb times (taken slots get the largest key)
+    for (int r = 0; r < keep; ++r) {
+      unsigned long long b1 = ~0ull, b2 = ~0ull;
+      int bi = -1;
+      for (int i = lane; i < total; i += 32) {
+        const unsigned long long a1 = k1s[i], a2 = k2s[i];
+        if (cand_less(a1, a2, b1, b2)) {
+          b1 = a1;
+          b2 = a2;
+          bi = i;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long o1 = __shfl_xor_sync(kFull, b1, o), o2 = __shfl_xor_sync(kFull, b2, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (cand_less(o1, o2, b1, b2)) {
+          b1 = o1;
+          b2 = o2;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        const int64_t slot = (int64_t)d * p.max_nb + r;
+        out_src[slot] = (int64_t)(b2 >> 32);
+        out_off[slot * 3] = (int64_t)((b2 >> 20) & 1023) - 512;
+        out_off[slot * 3 + 1] = (int64_t)((b2 >> 10) & 1023) - 512;
+        out_off[slot * 3 + 2] = (int64_t)(b2 & 1023) - 512;
+        out_dist[slot] = __longlong_as_double((long long)b1);
+        k1s[bi] = ~0ull;
+        k2s[bi] = ~0ull;
+      }
+      __syncwarp();
+    }
+    if (lane == 0) counts[d] = keep;
+    __syncwarp();
+  }
+}
+
+int64_t neighbor_scratch_bytes(int64_t N, int64_t nbins) {
+  auto al = [](int64_t b) { return (b + 255) & ~int64_t(255); };
+  return al(N * 3 * 8) + al(N * 3 * 4) + al(N * 4) + al(N * 4) + 3 * al((nbins + 1) * 4);
+}
+
+cudaError_t launch_neighbor_list(const double* pos, int64_t N, const double* cell, const double* inv,
+                                 const int32_t* nb, const int32_t* lo, const int32_t* hi, const int32_t* pbc,
+                                 double cutoff, int max_nb, void* scratch, int32_t* counts, int64_t* out_src,
+                                 int64_t* out_off, double* out_dist, int* err, cudaStream_t s) {
+  NlParams p;
+  for (int k = 0; k < 9; ++k) {
+    p.cell[k] = cell[k];
+    p.inv[k] = inv[k];
+  }
+  for (int k = 0; k < 3; ++k) {
+    p.nb[k] = nb[k];
+    p.lo[k] = lo[k];
+    p.hi[k] = hi[k];
+    p.pbc[k] = pbc[k];
+  }
+  p.cutoff = cutoff;
+  p.cut2 = cutoff * cutoff;
+  p.max_nb = max_nb;
+  const int64_t nbins = (int64_t)nb[0] * nb[1] * nb[2];
+  auto al = [](int64_t b) { return (b + 255) & ~int64_t(255); };
+  char* c = static_cast<char*>(scratch);
+  double* wpos = reinterpret_cast<double*>(c);
+  c += al(N * 3 * 8);
+  int32_t* wshift = reinterpret_cast<int32_t*>(c);
+  c += al(N * 3 * 4);
+  int32_t* bin = reinterpret_cast<int32_t*>(c);
+  c += al(N * 4);
+  int32_t* members = reinterpret_cast<int32_t*>(c);
+  c += al(N * 4);
+  int32_t* bcount = reinterpret_cast<int32_t*>(c);
+  c += al((nbins + 1) * 4);
+  int32_t* bstart = reinterpret_cast<int32_t*>(c);
+  c += al((nbins + 1) * 4);
+  int32_t* bcursor = reinterpret_cast<int32_t*>(c);
+  cudaError_t st = cudaMemsetAsync(bcount, 0, sizeof(int32_t) * nbins, s);
+  if (st != cudaSuccess) return st;
+  const int n = (int)N;
+  nl_bin_kernel<<<grid_resident(nl_bin_kernel, 256, N, 256), 256, 0, s>>>(pos, n, p, wpos, wshift, bin, bcount);
+  nl_scan_kernel<<<1, 1024, 0, s>>>(bcount, (int)nbins, bstart, bcursor);
+  nl_fill_kernel<<<grid_resident(nl_fill_kernel, 256, N, 256), 256, 0, s>>>(bin, n, bcursor, members);
+  nl_search_kernel<<<grid_resident(nl_search_kernel, kNlWarps * 32, N, kNlWarps), kNlWarps * 32, 0, s>>>(
+      pos, wpos, wshift, bin, bstart, members, n, p, counts, out_src, out_off, out_dist, err);
+  return cudaGetLastError();
+}
+
+}  // namespace fuma

@@ -104,12 +104,43 @@ class HaloExchanger:
         self.n_halo = sum(self.recv_splits)
 
 
+# Optional timing of the collectives (bench breakdown): when a list, every collective of a step
+# appends (name, start event, end event) recorded on the current stream around it.
+collective_events: list | None = None
+
+
+class _Timed:
+    def __init__(self, name):
+        self.name = name
+
+    def __enter__(self):
+        if collective_events is not None:
+            self.e0 = torch.cuda.Event(enable_timing=True)
+            self.e0.record()
+
+    def __exit__(self, *exc):
+        if collective_events is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            collective_events.append((self.name, self.e0, e1))
+
+
+def collective_times_ms() -> dict:
+    """Total milliseconds per collective kind over the recorded events (synchronises)."""
+    out: dict = {}
+    for name, a, b in collective_events or []:
+        b.synchronize()
+        out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+    return out
+
+
 class _HaloExchange(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_owned, ex: HaloExchanger):
         send = x_owned.index_select(0, ex.send_cat).contiguous()
         recv = x_owned.new_empty((ex.n_halo,) + tuple(x_owned.shape[1:]))
-        dist.all_to_all_single(recv, send, ex.recv_splits, ex.send_splits, group=ex.group)
+        with _Timed("halo_all_to_all_fwd"):
+            dist.all_to_all_single(recv, send, ex.recv_splits, ex.send_splits, group=ex.group)
         ctx.ex, ctx.n_owned = ex, x_owned.shape[0]
         return recv
 
@@ -117,7 +148,8 @@ class _HaloExchange(torch.autograd.Function):
     def backward(ctx, g_recv):
         ex = ctx.ex
         g_send = g_recv.new_empty((ex.n_send,) + tuple(g_recv.shape[1:]))
-        dist.all_to_all_single(g_send, g_recv.contiguous(), ex.send_splits, ex.recv_splits, group=ex.group)
+        with _Timed("halo_all_to_all_bwd"):
+            dist.all_to_all_single(g_send, g_recv.contiguous(), ex.send_splits, ex.recv_splits, group=ex.group)
         g_owned = g_recv.new_zeros((ctx.n_owned,) + tuple(g_recv.shape[1:]))
         off = 0
         for idx, n in zip(ex.send_idx, ex.send_splits):   # fixed peer order; indices unique per peer
@@ -195,13 +227,15 @@ class PartitionedModel:
         e_local = head(x, b_owned, num_systems)
         grads = torch.autograd.grad(e_local.sum(), wrt)
         energy = e_local.detach().clone()
-        dist.all_reduce(energy, group=self.group)
-        g = grads[0]
-        dist.all_reduce(g, group=self.group)
+        with _Timed("all_reduce_energy_forces"):
+            dist.all_reduce(energy, group=self.group)
+            g = grads[0]
+            dist.all_reduce(g, group=self.group)
         if not stress:
             return energy, -g
         g_disp = grads[1].contiguous()
-        dist.all_reduce(g_disp, group=self.group)
+        with _Timed("all_reduce_stress"):
+            dist.all_reduce(g_disp, group=self.group)
         vol = torch.linalg.det(cell.detach()).abs()
         return energy, -g, (g_disp / vol)[None]
 

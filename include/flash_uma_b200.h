@@ -191,6 +191,25 @@ int fuma_morton_reorder(const float* pos, const int64_t* Z, const int64_t* batch
                         const int64_t* idx_j, int64_t N, int64_t E, int64_t* perm, int64_t* inv_perm, float* pos_s,
                         int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, void* scratch,
                         int64_t scratch_bytes, int* err_flag, void* stream);
+/* Deterministic capped periodic neighbour list. Replaces the graph generation the reference
+ * leaves to FAIRChem / pymatgen outside its backbone (readme.md:35-72, external_graph_gen; its
+ * output is the edge_index / cell_offsets the backbone reads at wrapper.py:171-197), with this
+ * build's deterministic rule: every (source i, destination j, integer offset s) with
+ * |pos_i - pos_j + s @ cell| < cutoff (self pairs only with s != 0), per destination ordered by
+ * (distance, i, s_0, s_1, s_2) in fp64, the first max_neighbors kept.
+ * pos [N, 3] fp64 (device). geom (HOST memory): cell [3, 3] row-major (rows = lattice vectors)
+ * then its inverse [3, 3]. grid (HOST memory, int32 [12]): bins per axis nb[3] (fractional bins
+ * of side >= cutoff), the bin-offset range lo[3], hi[3] searched around an atom's bin (periodic
+ * images included), pbc[3] (0/1). Outputs per destination d (device): counts[d], and for its
+ * r < counts[d] neighbours src[d * max + r], offsets[(d * max + r) * 3 + k] (int64), dist[d *
+ * max + r] (fp64). Scratch: fuma_neighbor_scratch_bytes(N, grid) bytes, 256-byte aligned.
+ * More than 512 candidates for one destination sets code 64 in err_flag (device int, may be
+ * NULL). Integer offsets must stay within +-511. */
+int64_t fuma_neighbor_scratch_bytes(int64_t N, const int32_t* grid);
+int fuma_neighbor_list(const double* pos, int64_t N, const double* geom, const int32_t* grid, double cutoff,
+                       int32_t max_neighbors, void* scratch, int64_t scratch_bytes, int32_t* counts, int64_t* src,
+                       int64_t* offsets, double* dist, int* err_flag, void* stream);
+
 /* Destination (and optionally source) CSR of a renumbered edge list, from the CSR of the
  * original numbering: new node a is original node perm[a] (perm: int64 [N]), edge ids are
  * unchanged. Replaces the per-step stable-argsort CSR build of the reference on its renumbered

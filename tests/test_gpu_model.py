@@ -210,3 +210,28 @@ def test_morton_reorder_flags_out_of_range_edges():
         assert torch.equal(got[3][ok], ref[3][ok]) and torch.equal(got[4][ok], ref[4][ok])
         assert got[3][3].item() == 0 and got[4][7].item() == 0
         check_errors()   # the flag was cleared by the raise
+
+
+@pytest.mark.parametrize("which", ["config1", "config3", "config4", "config5", "small_cell", "slab_open"])
+def test_device_neighbor_list_matches_host(which):
+    """fuma_neighbor_list gives exactly the host statement's edges (systems.neighbor_list): the
+    same (source, destination, offset) triples in the same order, and the same fp64 distances,
+    on the benchmark systems (configs 1, 3, 4, 5), on a cell smaller than the cutoff (many
+    periodic images) and on a slab that is not periodic along z."""
+    from flash_uma_b200.linear import check_errors
+    from flash_uma_b200.neighbors import neighbor_list_device
+    from flash_uma_b200 import systems as S
+    sysm = {"config1": S.config1_system, "config3": S.config3_system, "config4": S.config4_system,
+            "config5": S.config5_system, "small_cell": lambda: S.bulk_fcc(1, 1, 2, jitter=0.05, seed=3),
+            "slab_open": lambda: S.AtomicSystem(S.bulk_fcc(4, 4, 3, jitter=0.05, seed=5).positions,
+                                                np.full(192, 29), np.diag([14.44, 14.44, 30.0]),
+                                                pbc=(True, True, False))}[which]()
+    ei, off, dist = S.neighbor_list(sysm)
+    pos = torch.tensor(sysm.positions, dtype=torch.float64, device="cuda")
+    ei_d, off_d, dist_d = neighbor_list_device(pos, sysm.cell, sysm.pbc)
+    torch.cuda.synchronize()
+    check_errors()
+    assert ei_d.shape == ei.shape
+    assert np.array_equal(ei_d.cpu().numpy(), ei)
+    assert np.array_equal(off_d.cpu().numpy(), off)
+    np.testing.assert_array_equal(dist_d.cpu().numpy(), dist)
