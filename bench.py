@@ -85,7 +85,7 @@ def gemm_flops_per_step(E, C, B, L, H=None, gauss_only=True):
     return fwd + bwd
 
 
-GEMM_OPS = ("fuma_linear_f16x3", "fuma_linear")
+GEMM_OPS = ("fuma_linear_f16x3", "fuma_linear", "fuma_linear_f16")
 
 
 def gemm_mode(mode, bf16):
@@ -93,6 +93,11 @@ def gemm_mode(mode, bf16):
     if mode == "f16x3":
         return {"passes": 3, "peak": bf16, "pipe": "fp16", "op": "fuma_linear_f16x3",
                 "kernel": "fuma_linear_f16x3 (gemm_f16x3_kernel)", "label": "tcgen05 f16x3 (fp16 split, fp32-level)",
+                "peak_note": "dense fp16 = measured dense bf16 rate"}
+    if mode == "f16":
+        return {"passes": 1, "peak": bf16, "pipe": "fp16", "op": "fuma_linear_f16",
+                "kernel": "fuma_linear_f16 (gemm_f16x3_kernel, single product)",
+                "label": "tcgen05 f16 (single fp16 product, TF32 accuracy class)",
                 "peak_note": "dense fp16 = measured dense bf16 rate"}
     return {"passes": 3 if mode == "tf32x3" else 1, "peak": bf16 / 2, "pipe": "tf32", "op": "fuma_linear",
             "kernel": "fuma_linear (gemm_tf32_kernel)",
@@ -107,7 +112,7 @@ def gemm_summary(per_op, E, C, B, L, mode):
     ms = per_op.get(g["op"])
     if not ms:
         return None
-    flops = gemm_flops_per_step(E, C, B, L, gauss_only=mode == "f16x3")
+    flops = gemm_flops_per_step(E, C, B, L, gauss_only=mode in ("f16x3", "f16"))
     return {"flops_per_step": flops, "ms_per_step": ms, "tflops_fp32_equiv": flops / (ms * 1e-3) / 1e12,
             "tflops_pipe": g["passes"] * flops / (ms * 1e-3) / 1e12, "pipe": g["pipe"], "passes": g["passes"]}
 
@@ -391,7 +396,7 @@ def run_flash(args, rank, world, device):
         # FLOPs, 2 x M x N x K per product) over the measured dense bf16 peak; the split modes run
         # ``passes`` tensor-pipe products per fp32 product, reported apart as the pipe utilisation
         launches = gprobe.counts.get(dominant, 1) if graphed else probe.counts.get(dominant, 1) // K
-        flops = gemm_flops_per_step(Ek, C, B, L, gauss_only=args.gemm == "f16x3")
+        flops = gemm_flops_per_step(Ek, C, B, L, gauss_only=args.gemm in ("f16x3", "f16"))
         flops_launch = flops / max(1, launches)
         achieved = flops_launch / (avg_ms * 1e-3) / 1e12
         roof = {"kernel": gm["kernel"], "bound": "tensor", "achieved": achieved,
@@ -468,6 +473,49 @@ def partition_parity(args, device, check0, pos0):
            "against": "single-GPU path on the same system and positions (rank 0, after the timed run)",
            "bar": {"energy_rel": 1e-5, "forces_max_abs": 1e-4}}
     del pred, res, data
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_mode(device, gemm: str, steps: int, warmup: int, system, check=None):
+    """This build's step in another GEMM mode on the same workload (CUDA-graph replay, CUDA events
+    per step, L2 flushed in between): atom-steps/s and, with ``check`` (energy, forces of the
+    default f16x3 mode at the first position), the deviation from that fp32-level result."""
+    import dataclasses
+
+    from flash_uma_b200.predict import GraphedStep
+    system, data_cpu, pred = build_problem(device, gemm, system)
+    data = data_cpu.to(device)
+    N = data_cpu.pos.shape[0]
+    pos_seq = [p.to(device) for p in md_positions(data_cpu.pos, steps + warmup, seed=0)]
+    out = {}
+    if check is not None:
+        res = pred(dataclasses.replace(data, pos=pos_seq[0]), check=True)
+        e, f = res["energy"].double(), res["forces"].double()
+        out["deviation_from_f16x3"] = {
+            "energy_rel": float(((e - check[0].double()).abs() / check[0].double().abs().clamp_min(1.0)).max()),
+            "forces_max_abs": float((f - check[1].double()).abs().max())}
+        del res
+    step = GraphedStep(pred, dataclasses.replace(data, pos=pos_seq[0]))
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    for w in range(warmup):
+        step(pos_seq[w])
+    torch.cuda.synchronize()
+    evs = []
+    for k in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step(pos_seq[warmup + k])
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    from flash_uma_b200.linear import raise_status
+    raise_status(step.out["status"])
+    ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    out.update(value=N / (ms * 1e-3), unit=UNIT, ms_per_step=ms, gemm=gemm_mode(gemm, 0.0)["label"],
+               launch="one CUDA graph replay per step", steps=steps, warmup=warmup)
+    del step, pred, flush
     torch.cuda.empty_cache()
     return out
 
@@ -557,7 +605,7 @@ def run_micro(args, device):
     offset = torch.linspace(0, 6.0, B, device=device)
     coeff = float(-0.5 / (2.0 * (6.0 / (B - 1))) ** 2)
     # f16x3: the production path, one fused message block (split operands, pre-split GEMMs)
-    use_fused = args.gemm == "f16x3"
+    use_fused = args.gemm in ("f16x3", "f16")
     geom = fused.geometry if use_fused else functools.partial(ops.precompute_geometry, graph=graph)
     geom_args = (inp["pos"].to(device), Z, ii, jj, inp["shifts"].to(device), off.source_embedding.weight.detach(),
                  off.target_embedding.weight.detach(), offset, coeff, 6.0) + ((graph,) if use_fused else ())
@@ -717,6 +765,12 @@ def load_reference_gpu():
     import types
     if not os.path.isfile(os.path.join(REF_DIR, "wrapper.py")):
         return None
+    # The reference autotunes its Triton kernels on first use (minutes of compiling and timing
+    # candidate configurations on a fresh machine). Triton's own on-disk cache, with autotuning
+    # results included, is kept next to the installed reference so that a fresh box starts from
+    # the results of an earlier run on the same GPU model; an explicit TRITON_CACHE_DIR wins.
+    os.environ.setdefault("TRITON_CACHE_DIR", os.path.join(REF_DIR, "triton_cache"))
+    os.environ.setdefault("TRITON_CACHE_AUTOTUNING", "1")
     from flash_uma_b200.nodewise import balance_channels_batched
     for name in ["fairchem", "fairchem.core", "fairchem.core.models", "fairchem.core.models.uma",
                  "fairchem.core.models.uma.escn_md"]:
@@ -906,7 +960,7 @@ def main():
     ap.add_argument("--workload", default="default", choices=["default", "config4", "config5"],
                     help="default: config 3 (weak scaling of it for N > 1); config4: water box E+F+S; "
                          "config5: 100,800-atom bulk Cu (strong scaling)")
-    ap.add_argument("--gemm", default="f16x3", choices=["f16x3", "tf32x3", "tf32"],
+    ap.add_argument("--gemm", default="f16x3", choices=["f16x3", "tf32x3", "tf32", "f16"],
                     help="dense-contraction mode: f16x3 / tf32x3 (fp32-level) or tf32 (single pass, the "
                          "reference's published setup)")
     ap.add_argument("--summarize-launches", metavar="CSV",
@@ -972,13 +1026,21 @@ def main():
                 system, _, _, _ = workload_system(args.workload, world)
                 rg = {}
                 for key, tf32 in (("fp32", False), ("tf32", True)):
-                    r = run_reference_gpu(device, min(args.steps, 10), 3, system, tf32,
-                                          check=check0 if not tf32 else None)
+                    r = run_reference_gpu(device, min(args.steps, 10), 3, system, tf32, check=check0)
                     if "value" in r:
                         r["ratio"] = out["value"] / r["value"]
                         r["e2e_ratio"] = out["e2e"]["value"] / r["value"]
                     rg[key] = r
                 out["reference_triton_gpu"] = rg
+            if args.gemm == "f16x3":
+                # the TF32 accuracy class on both sides: this build's single-product fp16 mode
+                # against the reference with TF32 on
+                fast = run_mode(device, "f16", min(args.steps, 10), 3, workload_system(args.workload, world)[0],
+                                check=check0)
+                ref_tf32 = out.get("reference_triton_gpu", {}).get("tf32", {})
+                if "value" in ref_tf32:
+                    fast["ratio_vs_reference_tf32"] = fast["value"] / ref_tf32["value"]
+                out["tf32_class_mode"] = fast
             if args.kernels:
                 margs = argparse.Namespace(**vars(args))
                 margs.nodes, margs.edges, margs.steps, margs.warmup = 20000, 600000, 5, 3

@@ -37,6 +37,7 @@ _SIGS = {
     "fuma_linear": [_P, _I64, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _P],
     "fuma_split_tf32": [_P, _I64, _P, _P, _P],
     "fuma_linear_f16x3": [_P, _I64, _I32, _P, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _P, _P],
+    "fuma_linear_f16": [_P, _I64, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _P, _P],
     "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
     "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
     "fuma_neighbor_list": [_P, _I64, _P, _P, ctypes.c_double, _I32, _P, _I64, _P, _P, _P, _P, _P, _P],

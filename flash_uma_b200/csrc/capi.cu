@@ -442,6 +442,26 @@ int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* 
   return launched("linear_f16x3");
 }
 
+int fuma_linear_f16(const float* A, int64_t lda, const void* W_hi, int64_t ldw, float w_scale_inv, const float* bias,
+                    int64_t M, int32_t N, int32_t K, float* C, int64_t ldc, int* err_flag, void* stream) {
+  REQUIRE(M >= 0 && M < (int64_t(1) << 31), "linear_f16: M=%lld out of range", (long long)M);
+  REQUIRE(N > 0 && N % 16 == 0 && N <= 65536 * 16, "linear_f16: N=%d must be a positive multiple of 16", N);
+  REQUIRE(K > 0 && K % 8 == 0, "linear_f16: K=%d must be a positive multiple of 8", K);
+  REQUIRE(lda >= K && lda % 8 == 0 && ldc >= N && ldc % 4 == 0, "linear_f16: bad leading dimensions of A or C");
+  REQUIRE(ldw >= K && ldw % 8 == 0, "linear_f16: ldw=%lld must be >= K and a multiple of 8", (long long)ldw);
+  REQUIRE(w_scale_inv > 0.0f, "linear_f16: w_scale_inv must be positive");
+  if (M == 0) return FUMA_OK;
+  REQUIRE(A && W_hi && C, "linear_f16: null pointer");
+  REQUIRE_ALIGNED(A, "A"); REQUIRE_ALIGNED(W_hi, "W_hi"); REQUIRE_ALIGNED(C, "C");
+  if (bias) REQUIRE_ALIGNED(bias, "bias");
+  BIND(A);
+  const int r = launch_gemm_f16x3(A, lda, true, W_hi, W_hi, ldw, w_scale_inv, bias, C, ldc, M, N, K, err_flag,
+                                  (cudaStream_t)stream, true);
+  if (r == -1) return fail(FUMA_E_INVALID, "linear_f16: could not encode the TMA tensor maps: %s", gemm_map_error());
+  if (r != 0) return fail(r, "linear_f16: launch failed: %s", cudaGetErrorString((cudaError_t)r));
+  return launched("linear_f16");
+}
+
 int fuma_split_rows_f16(const float* x, int64_t lda, int64_t M, int32_t K, void* out, int64_t ldp, int* err_flag,
                         void* stream) {
   REQUIRE(M >= 0 && K > 0 && K % 4 == 0, "split_rows_f16: bad shape M=%lld K=%d", (long long)M, K);

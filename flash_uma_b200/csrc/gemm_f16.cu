@@ -55,12 +55,15 @@ constexpr float kLoScaleInv = 1.0f / kSplitLoScale;
 
 // kPre: A arrives pre-split (row-packed hi | lo fp16, see split_rows_f16_kernel), so a stage
 // holds no raw fp32 tile and no split work is done in the kernel.
-template <int BN, int STAGES, bool kPre>
+// kX3 = false (pre-split A only): the single-product mode, main += A_hi . W_hi; the lo halves
+// are neither loaded nor multiplied (fp16 operand precision, the accuracy class of TF32).
+template <int BN, int STAGES, bool kPre, bool kX3 = true>
 struct F16Smem {
   static constexpr int kRaw = kPre ? 0 : kBM * kBK * 4;   // 16 KB fp32 A, 128-byte swizzle
   static constexpr int kA16 = kBM * kBK * 2;   // 8 KB fp16 A half, 64-byte swizzle
   static constexpr int kW16 = BN * kBK * 2;    // fp16 W half, 64-byte swizzle
-  static constexpr int kStage = kRaw + 2 * kA16 + 2 * kW16;
+  static constexpr int kHalves = kX3 ? 2 : 1;  // hi (+ lo) tiles of each operand per stage
+  static constexpr int kStage = kRaw + kHalves * kA16 + kHalves * kW16;
   // epilogue staging for the TMA store: per epilogue warp two [32 rows x 32 fp32] boxes
   static constexpr bool kTmaStore = BN >= 32;
   static constexpr int kStaging = kTmaStore ? 4 * 2 * 4096 : 0;
@@ -124,7 +127,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 }  // namespace
 
-template <int BN, int STAGES, bool kPre>
+template <int BN, int STAGES, bool kPre, bool kX3>
 __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                  const __grid_constant__ CUtensorMap tmAl,
                                                                  const __grid_constant__ CUtensorMap tmWh,
@@ -133,7 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
                                                                  float* __restrict__ C, const float* __restrict__ bias,
                                                                  float w_scale_inv, int M, int N, int K, int64_t ldc,
                                                                  int* err) {
-  using L = F16Smem<BN, STAGES, kPre>;
+  static_assert(kX3 || kPre, "the single-product mode takes pre-split operands");
+  using L = F16Smem<BN, STAGES, kPre, kX3>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_c = smem + STAGES * L::kStage;   // epilogue staging (TMA store path)
@@ -150,14 +154,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
   const int num_n = N / BN;
   const int num_tiles = ((M + kBM - 1) / kBM) * num_n;
   const int num_k = (K + kBK - 1) / kBK;
-  // stage layout: [raw A | A_hi | A_lo | W_hi | W_lo]
+  // stage layout: [raw A | A_hi | A_lo | W_hi | W_lo] (no lo tiles in the single-product mode)
+  constexpr int kH = L::kHalves;
   auto stage_raw = [&](int s) { return smem + s * L::kStage; };
   auto stage_Ah = [&](int s) { return smem + s * L::kStage + L::kRaw; };
   auto stage_Al = [&](int s) { return smem + s * L::kStage + L::kRaw + L::kA16; };
-  auto stage_Wh = [&](int s) { return smem + s * L::kStage + L::kRaw + 2 * L::kA16; };
-  auto stage_Wl = [&](int s) { return smem + s * L::kStage + L::kRaw + 2 * L::kA16 + L::kW16; };
-  constexpr uint32_t kBufCols = 2 * BN;            // main + cross of one buffer
-  constexpr int kAcc = BN <= 128 ? 2 : 1;          // accumulator buffers (BN = 256 fills TMEM with one)
+  auto stage_Wh = [&](int s) { return smem + s * L::kStage + L::kRaw + kH * L::kA16; };
+  auto stage_Wl = [&](int s) { return smem + s * L::kStage + L::kRaw + kH * L::kA16 + L::kW16; };
+  constexpr uint32_t kBufCols = kX3 ? 2 * BN : BN;       // main (+ cross) of one buffer
+  constexpr int kAcc = kBufCols <= 256 ? 2 : 1;          // accumulator buffers (TMEM holds 512 columns)
   constexpr uint32_t kTmemCols = kAcc * kBufCols;  // 64..512, a power of 2
 
   if (threadIdx.x == 0) {
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
 
   if (warp == kWarpProducer) {
     if (lane == 0) {
-      constexpr uint32_t bytes = (kPre ? 2 * L::kA16 : L::kRaw) + 2 * L::kW16;
+      constexpr uint32_t bytes = (kPre ? kH * L::kA16 : L::kRaw) + kH * L::kW16;
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         const int m0 = (tile / num_n) * kBM, n0 = (tile % num_n) * BN;
@@ -198,12 +203,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
           mbar_expect_tx(&bar_full[s], bytes);
           if (kPre) {
             tma_load_2d(stage_Ah(s), &tmA, kt * kBK, m0, &bar_full[s]);
-            tma_load_2d(stage_Al(s), &tmAl, kt * kBK, m0, &bar_full[s]);
+            if (kX3) tma_load_2d(stage_Al(s), &tmAl, kt * kBK, m0, &bar_full[s]);
           } else {
             tma_load_2d(stage_raw(s), &tmA, kt * kBK, m0, &bar_full[s]);
           }
           tma_load_2d(stage_Wh(s), &tmWh, kt * kBK, n0, &bar_full[s]);
-          tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, n0, &bar_full[s]);
+          if (kX3) tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, n0, &bar_full[s]);
         }
       }
       if (*abort_flag) {
@@ -240,8 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
             const uint32_t off = kk * 32;  // 16 fp16 = 32 bytes along K inside the 64-byte swizzle row
             const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
             mma_f16(acc_main, smem_desc_sw64(a_hi + off), smem_desc_sw64(w_hi + off), idesc, acc);
-            mma_f16(acc_cross, smem_desc_sw64(a_hi + off), smem_desc_sw64(w_lo + off), idesc, acc);
-            mma_f16(acc_cross, smem_desc_sw64(a_lo + off), smem_desc_sw64(w_hi + off), idesc, 1u);
+            if constexpr (kX3) {
+              mma_f16(acc_cross, smem_desc_sw64(a_hi + off), smem_desc_sw64(w_lo + off), idesc, acc);
+              mma_f16(acc_cross, smem_desc_sw64(a_lo + off), smem_desc_sw64(w_hi + off), idesc, 1u);
+            }
           }
           mma_commit(&bar_empty[s]);
         }
@@ -310,8 +317,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t rm[32], rc[32];
           tmem_ld32(taddr + (uint32_t)c0, rm);
-          tmem_ld32(taddr + (uint32_t)(BN + c0), rc);
+          if constexpr (kX3) tmem_ld32(taddr + (uint32_t)(BN + c0), rc);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if constexpr (!kX3) {
+#pragma unroll
+            for (int u = 0; u < 32; ++u) rc[u] = 0u;
+          }
           uint8_t* box = smem_c + (q * 2 + (nbox & 1)) * 4096;
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           __syncwarp();
@@ -339,8 +350,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
         for (int c0 = 0; c0 < BN; c0 += 16) {
           uint32_t rm[16], rc[16];
           tmem_ld16(taddr + (uint32_t)c0, rm);
-          tmem_ld16(taddr + (uint32_t)(BN + c0), rc);
+          if constexpr (kX3) tmem_ld16(taddr + (uint32_t)(BN + c0), rc);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if constexpr (!kX3) {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) rc[u] = 0u;
+          }
           if (row < M) {
             float* out = C + (int64_t)row * ldc + n0 + c0;
   #pragma unroll
@@ -375,12 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
 
 namespace {
 
-template <int BN, int STAGES, bool kPre>
+template <int BN, int STAGES, bool kPre, bool kX3>
 cudaError_t launch_f16(const CUtensorMap& a, const CUtensorMap& al, const CUtensorMap& wh, const CUtensorMap& wl,
                        const CUtensorMap& mc, float* C, const float* bias, float w_scale_inv, int M, int N, int K, int64_t ldc, int* err,
                        cudaStream_t s) {
-  using L = F16Smem<BN, STAGES, kPre>;
-  auto kern = gemm_f16x3_kernel<BN, STAGES, kPre>;
+  using L = F16Smem<BN, STAGES, kPre, kX3>;
+  auto kern = gemm_f16x3_kernel<BN, STAGES, kPre, kX3>;
   static thread_local uint64_t configured = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -400,11 +415,23 @@ cudaError_t launch_bn(int BN, const CUtensorMap& a, const CUtensorMap& al, const
                       const CUtensorMap& wl, const CUtensorMap& mc, float* C, const float* bias, float inv, int M, int N, int K,
                       int64_t ldc, int* err, cudaStream_t s) {
   switch (BN) {
-    case 256: return launch_f16<256, kPre ? 4 : 3, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
-    case 128: return launch_f16<128, kPre ? 5 : 4, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
-    case 64: return launch_f16<64, kPre ? 6 : 4, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
-    case 32: return launch_f16<32, kPre ? 8 : 5, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
-    default: return launch_f16<16, kPre ? 8 : 6, kPre>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 256: return launch_f16<256, kPre ? 4 : 3, kPre, true>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 128: return launch_f16<128, kPre ? 5 : 4, kPre, true>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 64: return launch_f16<64, kPre ? 6 : 4, kPre, true>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 32: return launch_f16<32, kPre ? 8 : 5, kPre, true>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+    default: return launch_f16<16, kPre ? 8 : 6, kPre, true>(a, al, wh, wl, mc, C, bias, inv, M, N, K, ldc, err, s);
+  }
+}
+
+// single-product mode (pre-split A): half the operand bytes per stage, so deeper rings
+cudaError_t launch_bn_x1(int BN, const CUtensorMap& a, const CUtensorMap& wh, const CUtensorMap& mc, float* C,
+                         const float* bias, float inv, int M, int N, int K, int64_t ldc, int* err, cudaStream_t s) {
+  switch (BN) {
+    case 256: return launch_f16<256, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 128: return launch_f16<128, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 64: return launch_f16<64, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 32: return launch_f16<32, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    default: return launch_f16<16, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
   }
 }
 
@@ -422,8 +449,9 @@ const int g_bn256_min_k = [] {
 
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,
                       float w_scale_inv, const float* bias, float* C, int64_t ldc, int64_t M, int N, int K, int* err,
-                      cudaStream_t s) {
-  const int BN = (N % 256 == 0 && K >= g_bn256_min_k) ? 256
+                      cudaStream_t s, bool x1) {
+  // single-product mode: one accumulator, so 256-wide tiles stay double-buffered at any K
+  const int BN = (N % 256 == 0 && (x1 || K >= g_bn256_min_k)) ? 256
                  : (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : (N % 32 == 0) ? 32 : 16;
   CUtensorMap ma, mal, mh, ml;
   if (a_split) {
@@ -451,8 +479,9 @@ int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_h
     return -1;
   const int m = (int)M;
   const cudaError_t st =
-      a_split ? launch_bn<true>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s)
-              : launch_bn<false>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s);
+      x1 ? launch_bn_x1(BN, ma, mh, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s)
+      : a_split ? launch_bn<true>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s)
+                : launch_bn<false>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s);
   return st == cudaSuccess ? 0 : (int)st;
 }
 

@@ -75,7 +75,7 @@ void launch_csr_permute(int ngraphs, const int32_t* const* row_ptr, const int32_
                         int64_t N, int32_t* const* new_row_ptr, int32_t* const* new_col, cudaStream_t s);
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,
                       float w_scale_inv, const float* bias, float* C, int64_t ldc, int64_t M, int N, int K, int* err,
-                      cudaStream_t s);
+                      cudaStream_t s, bool x1 = false);
 void launch_split_rows_f16(const float* x, int64_t lda, int64_t M, int K, void* out, int64_t ldp, int* err,
                            cudaStream_t s);
 void launch_split_f16(const float* x, void* hi, void* lo, float scale, int64_t n, cudaStream_t s);

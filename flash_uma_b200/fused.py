@@ -127,8 +127,8 @@ def radial_bwd(rad, saved, g_out_p, err):
     del g_h1
     # only the Gaussian-basis columns of the edge features depend on positions: rows :B of W1^T
     B = rad.n_gauss
-    hi, lo, inv = rad.l1.wt16
-    return _gemm16(g_y1, (hi[:B], lo[:B], inv), None, g_y1.shape[1])
+    hi, lo, inv, x1 = rad.l1.wt16
+    return _gemm16(g_y1, (hi[:B], lo[:B], inv, x1), None, g_y1.shape[1])
 
 
 def _conv2(layer, Y0, Y1, Y2, C, err, s):
@@ -304,5 +304,6 @@ def fusable(model) -> bool:
     for lay in model.layers:
         lins += [lay.rad.l1, lay.rad.l2, lay.rad.l3, lay.conv1_m0, lay.conv1_m1, lay.conv1_m2, lay.conv2_m0,
                  lay.conv2_m1, lay.conv2_m2]
-    return (all(l.mode == "f16x3" and l.N % 16 == 0 and l.K % 16 == 0 for l in lins) and model.C % 16 == 0
-            and model.B % 16 == 0)
+    modes = {l.mode for l in lins}
+    return (len(modes) == 1 and modes <= {"f16x3", "f16"} and all(l.N % 16 == 0 and l.K % 16 == 0 for l in lins)
+            and model.C % 16 == 0 and model.B % 16 == 0)

@@ -11,6 +11,9 @@ are frozen, so no weight gradients). Precision modes:
 * ``"tf32x3"``: three TF32 products on hi/lo TF32 splits - fp32-level accuracy, full fp32
   range.
 * ``"tf32"``: a single TF32 product (what the reference runs with ``allow_tf32``).
+* ``"f16"``: a single fp16 product A_hi . W_hi on the same split operands (``fuma_linear_f16``):
+  the accuracy class of TF32 (about 11 significant bits per operand) at a third of the f16x3
+  tensor work; the fast mode to set beside the reference's published TF32 setting.
 
 The weight splits (and the transposed weights for the backward) are built once, on the
 device, when the module is first used on a device.
@@ -26,7 +29,8 @@ import torch.nn as nn
 from . import _native as nat
 from ._native import ptr, stream_of
 
-_MODES = ("f16x3", "tf32x3", "tf32")
+_MODES = ("f16x3", "tf32x3", "tf32", "f16")
+_F16_MODES = ("f16x3", "f16")   # fp16 tensor cores on the row-packed split operands
 _err_flags: dict[int, torch.Tensor] = {}
 _err_host: dict[int, torch.Tensor] = {}     # pinned mirrors, filled asynchronously by snapshot_errors()
 
@@ -131,8 +135,9 @@ def _split(w: torch.Tensor):
     return hi, lo
 
 
-def _split16(w: torch.Tensor):
-    """fp16 hi/lo split of ``w * scale`` (scale a power of two keeping |w * scale| < 2^14)."""
+def _split16(w: torch.Tensor, x1: bool = False):
+    """fp16 hi/lo split of ``w * scale`` (scale a power of two keeping |w * scale| < 2^14):
+    (hi, lo, 1 / scale, x1); ``x1``: products use the hi halves only (the "f16" mode)."""
     w = w.contiguous()
     amax = float(w.abs().max()) if w.numel() else 0.0
     e = max(0, math.ceil(math.log2(amax)) - 14) if amax > 0 else 0
@@ -140,7 +145,7 @@ def _split16(w: torch.Tensor):
     hi = torch.empty(w.shape, device=w.device, dtype=torch.float16)
     lo = torch.empty_like(hi)
     nat.call("fuma_split_f16", ptr(w), w.numel(), scale, ptr(hi), ptr(lo), stream_of(w))
-    return hi, lo, 1.0 / scale
+    return hi, lo, 1.0 / scale, x1
 
 
 def _as_operand(a: torch.Tensor) -> torch.Tensor:
@@ -173,20 +178,29 @@ def split_rows(x: torch.Tensor, ldp: int | None = None) -> torch.Tensor:
 
 
 def _gemm16(a: torch.Tensor, w16, bias: torch.Tensor | None, K: int | None = None):
-    """f16x3 product with a weight split ``w16 = (hi, lo, scale_inv)`` of W [N, ldw]. ``K`` given:
-    ``a`` is a row-packed split (:func:`split_rows`) of a [M, K] activation."""
-    hi, lo, inv = w16
+    """fp16 tensor-core product with a weight split ``w16 = (hi, lo, scale_inv, x1)`` of W [N, ldw]:
+    three products (f16x3) or, with ``x1``, the single hi . hi product. ``K`` given: ``a`` is a
+    row-packed split (:func:`split_rows`) of a [M, K] activation."""
+    hi, lo, inv, x1 = w16
     N, ldw = hi.shape
     if K is None:
         M, K = a.shape
-        a = _as_operand(a)
-        pre = 0
+        if x1:
+            a = split_rows(a)
+            pre = 1
+        else:
+            a = _as_operand(a)
+            pre = 0
     else:
         M = a.shape[0]
         pre = 1
     out = torch.empty(M, N, device=a.device, dtype=torch.float32)
-    nat.call("fuma_linear_f16x3", ptr(a), a.stride(0), pre, ptr(hi), ptr(lo), ldw, inv, ptr(bias), M, N, K, ptr(out),
-             N, ptr(error_flag(a.device)), stream_of(a))
+    if x1:
+        nat.call("fuma_linear_f16", ptr(a), a.stride(0), ptr(hi), ldw, inv, ptr(bias), M, N, K, ptr(out), N,
+                 ptr(error_flag(a.device)), stream_of(a))
+    else:
+        nat.call("fuma_linear_f16x3", ptr(a), a.stride(0), pre, ptr(hi), ptr(lo), ldw, inv, ptr(bias), M, N, K,
+                 ptr(out), N, ptr(error_flag(a.device)), stream_of(a))
     return out
 
 
@@ -198,7 +212,7 @@ class _LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, mod):
         ctx.mod = mod
-        if mod.mode == "f16x3":
+        if mod.mode in _F16_MODES:
             y = _gemm16(x, mod.w16, mod.bias_p)
         else:
             y = _gemm(x, mod.w_hi, mod.w_lo, mod.bias_p, mod.mode == "tf32x3")
@@ -210,7 +224,7 @@ class _LinearFn(torch.autograd.Function):
         g = g.contiguous()
         if mod.Np != mod.N:
             g = torch.nn.functional.pad(g, (0, mod.Np - mod.N))
-        if mod.mode == "f16x3":
+        if mod.mode in _F16_MODES:
             gx = _gemm16(g, mod.wt16, None)
         else:
             gx = _gemm(g, mod.wt_hi, mod.wt_lo, None, mod.mode == "tf32x3")
@@ -247,12 +261,13 @@ class FrozenLinear(nn.Module):
         if not self.weight.is_cuda:
             raise RuntimeError("FrozenLinear runs on CUDA only; move the module to a GPU first")
         dev = self.weight.device
-        if self.mode == "f16x3":
+        if self.mode in _F16_MODES:
             wf = torch.zeros(self.Np, (self.K + 7) // 8 * 8, device=dev)   # rows 16-byte aligned in fp16
             wf[: self.N, : self.K] = self.weight
             wt = torch.zeros(self.Kp, self.Np, device=dev)
             wt[: self.K, : self.N] = self.weight.t()
-            self.w16, self.wt16 = _split16(wf), _split16(wt)
+            x1 = self.mode == "f16"
+            self.w16, self.wt16 = _split16(wf, x1), _split16(wt, x1)
         else:
             wf = torch.zeros(self.Np, self.K, device=dev)
             wf[: self.N] = self.weight

@@ -32,9 +32,10 @@ def validate_atoms_data(self, atoms, task_name):
 class ZeroAllocBackbone(nn.Module):
     def __init__(self, off_bb, dtype=torch.float32, gemm: str | None = None):
         """``gemm``: "f16x3" (default; fp16 tensor cores with fp32-level accuracy, inputs of the
-        dense layers inside the fp16 range), "tf32x3" (fp32-level accuracy, full fp32 range) or
-        "tf32" (single pass, as the reference runs with TF32 enabled); default from the
-        FUMA_GEMM environment variable."""
+        dense layers inside the fp16 range), "tf32x3" (fp32-level accuracy, full fp32 range),
+        "tf32" (single pass, as the reference runs with TF32 enabled) or "f16" (single fp16
+        product, the same accuracy class as TF32, the fastest mode); default from the FUMA_GEMM
+        environment variable."""
         super().__init__()
         lmax = getattr(off_bb, "lmax", None)
         if lmax is not None and lmax != 2:

@@ -144,6 +144,14 @@ int fuma_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* strea
 int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* W_hi, const void* W_lo, int64_t ldw,
                       float w_scale_inv, const float* bias, int64_t M, int32_t N, int32_t K, float* C, int64_t ldc,
                       int* err_flag, void* stream);
+/* Same contraction (same reference call sites) in the single-product mode: C = A_hi . W_hi^T
+ * * w_scale_inv (+ bias), fp16 operands with fp32 accumulation - the accuracy class of TF32
+ * (about 11 significant bits per operand, what the reference runs with allow_tf32, its published
+ * setting) at a third of the f16x3 tensor work. A is a row-packed split (the layout of
+ * fuma_split_rows_f16 and of the *_f16x3 producers; only its hi half is read), W_hi the hi half
+ * of fuma_split_f16. K a multiple of 8; lda, ldw multiples of 8. */
+int fuma_linear_f16(const float* A, int64_t lda, const void* W_hi, int64_t ldw, float w_scale_inv, const float* bias,
+                    int64_t M, int32_t N, int32_t K, float* C, int64_t ldc, int* err_flag, void* stream);
 /* Row-packed f16x3 split of an activation matrix x [M, K] (rows lda floats apart) into out,
  * whose row r spans 4 * ldp bytes: fp16 hi values of x[r, :K] at byte 0, the scaled fp16 lo
  * values at byte 2 * ldp (the same footprint as fp32 [M, ldp]). ldp >= K, a multiple of 8.

@@ -118,3 +118,30 @@ def test_f16x3_out_of_range_input_is_reported():
     check_errors()                       # the flag was cleared by the raise
     lin(torch.randn(300, 64, device=DEV))
     check_errors()
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES[:11])
+def test_linear_f16_single_product(M, N, K):
+    """``fuma_linear_f16`` (the "f16" mode): C = fp16(A) . fp16(W s)^T / s, fp32 accumulation.
+    Against fp64 arithmetic on the same fp16-rounded operands the only error is the tensor core's
+    accumulation (bound as above); against the exact fp32 product it is within fp16 rounding
+    (the TF32 accuracy class, 2e-3)."""
+    from flash_uma_b200.linear import check_errors
+    W, b, lin = _lin(N, K, True, "f16", M + 3 * N + K)
+    g = torch.Generator().manual_seed(K + 1)
+    x = torch.randn(M, K, generator=g)
+    gy = torch.randn(M, N, generator=g)
+    xd = x.to(DEV).requires_grad_(True)
+    y = lin(xd)
+    (gx,) = torch.autograd.grad(y, [xd], gy.to(DEV))
+    torch.cuda.synchronize()
+    check_errors()
+    hi, _, inv, x1 = lin.w16
+    assert x1
+    w_r = hi[:N, :K].double().cpu() * inv
+    y_rnd = x.half().double() @ w_r.t() + b.double()
+    assert (y.cpu().double() - y_rnd).abs().max() <= tol(K) * y_rnd.abs().max()
+    y_ref = x.double() @ W.double().t() + b.double()
+    assert (y.cpu().double() - y_ref).abs().max() <= 2e-3 * y_ref.abs().max()
+    gx_ref = gy.double() @ W.double()
+    assert (gx.cpu().double() - gx_ref).abs().max() <= 2e-3 * gx_ref.abs().max()

@@ -235,3 +235,18 @@ def test_device_neighbor_list_matches_host(which):
     assert np.array_equal(ei_d.cpu().numpy(), ei)
     assert np.array_equal(off_d.cpu().numpy(), off)
     np.testing.assert_array_equal(dist_d.cpu().numpy(), dist)
+
+
+def test_config1_f16_mode_tf32_accuracy_class():
+    """The single-product "f16" GEMM mode end to end on config 1 (fused blocks): within the TF32
+    accuracy class of the reference's published setting, i.e. errors of fp16 operand rounding
+    (about 5e-4 relative per operand), far below what separates physics (1e-3 relative energy,
+    1e-2 eV/A forces), and deterministic run to run."""
+    from flash_uma_b200.systems import config1_system
+    g = dict(np.load(os.path.join(GOLD, "e2e_config1.npz")))
+    data, res = _run([config1_system()], int(g["C"]), int(g["layers"]), int(g["B"]), stress=True, gemm="f16")
+    from flash_uma_b200.linear import check_errors
+    check_errors()
+    e = res["energy"].cpu().numpy()
+    assert np.abs(e - g["energy"]).max() <= 1e-3 * np.abs(g["energy"]).max()
+    assert np.abs(res["forces"].cpu().numpy() - g["forces"]).max() < 1e-2
