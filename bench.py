@@ -680,6 +680,53 @@ def run_micro(args, device):
             "kernels": dict(sorted(kernels.items(), key=lambda kv: -kv[1]["ms_per_step"]))}
 
 
+# (K, N, launches per config-3 step) of the step's dense contractions (M = edges): forward radial
+# MLPs (4 layers + the initial one), SO(2) convolutions, and the input-gradient GEMMs
+STEP_GEMMS = [(320, 128, 5), (128, 128, 5), (128, 1536, 4), (128, 384, 1), (768, 640, 4), (1024, 512, 4),
+              (512, 256, 4), (384, 384, 4), (512, 512, 4), (256, 256, 4),
+              (384, 384, 4), (512, 512, 4), (256, 256, 4), (640, 768, 4), (512, 1024, 4), (256, 512, 4),
+              (1536, 128, 4), (384, 128, 1), (128, 128, 5), (128, 64, 5)]
+
+
+def run_gemm_shapes(args, device, M=120000, reps=10):
+    """Device time of every dense-contraction shape of the config-3 step on pre-split operands,
+    row-major tiles against the transposed 128 x 256 tiles (FUMA_GEMM_T), CUDA events over
+    ``reps`` launches with the L2 flushed first; fp16-pipe TF/s (3 products per fp32 product)."""
+    from flash_uma_b200 import _native
+    from flash_uma_b200.linear import _gemm16, _split16, check_errors, split_rows
+    _native.load()
+    _, bf16, _ = load_peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=device)
+    rows, tot = [], {"0": 0.0, "1": 0.0}
+    g = torch.Generator(device=device).manual_seed(0)
+    for K, N, count in STEP_GEMMS:
+        W = torch.randn(N, K, device=device, generator=g) / K ** 0.5
+        w16 = _split16(W)
+        xp = split_rows(torch.randn(M, K, device=device, generator=g))
+        row = {"K": K, "N": N, "launches_per_step": count}
+        for t in ("0", "1"):
+            os.environ["FUMA_GEMM_T"] = t
+            for _ in range(3):
+                _gemm16(xp, w16, None, K)
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                _gemm16(xp, w16, None, K)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            row[f"ms_T{t}"] = round(ms, 4)
+            row[f"pipe_frac_T{t}"] = round(3 * 2 * M * N * K / (ms * 1e-3) / 1e12 / bf16, 4)
+            tot[t] += ms * count
+        rows.append(row)
+    os.environ.pop("FUMA_GEMM_T", None)
+    check_errors()
+    print(json.dumps({"metric": "dense-contraction shapes of the config-3 step (M = 120,000, pre-split f16x3)",
+                      "ms_per_step_T0": round(tot["0"], 3), "ms_per_step_T1": round(tot["1"], 3),
+                      "shapes": rows}), flush=True)
+
+
 def kernel_fractions(micro):
     """Compact per-kernel HBM fractions of the config-2 microbench for the bench line."""
     out = {}
@@ -978,6 +1025,8 @@ def main():
                     help="skip the config-5 strong-scaling object (100,800 atoms at this run's N)")
     ap.add_argument("--no-kernels", dest="kernels", action="store_false",
                     help="skip the per-kernel config-2 fractions of the N = 1 line")
+    ap.add_argument("--gemm-shapes", action="store_true",
+                    help="time the step's dense-contraction shapes, row-major vs transposed tiles")
     ap.add_argument("--nodes", type=int, default=20000)
     ap.add_argument("--edges", type=int, default=600000)
     args = ap.parse_args()
@@ -1007,6 +1056,10 @@ def main():
     if args.sweep:
         if rank == 0:
             run_sweep(args, device)
+        return
+    if args.gemm_shapes:
+        if rank == 0:
+            run_gemm_shapes(args, device)
         return
     if world > 1:
         import datetime

@@ -388,6 +388,192 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
   }
 }
 
+// Transposed tiles: D[f, e] = sum_k W[f, k] A[e, k] with the 128 output features f of a tile on
+// the MMA's M side and 256 edges e on its N side (tcgen05 M=128, N=256), for output widths that
+// are a multiple of 128 but not of 256 (or short K): those shapes otherwise run 128-wide tiles,
+// whose per-instruction operand traffic (A and W tiles of equal size for half the products)
+// keeps the tensor pipe near two thirds of its rate. Same f16x3 arithmetic as
+// gemm_f16x3_kernel (main += W_hi A_hi, cross += W_lo A_hi + W_hi A_lo, one pre-split operand
+// format); the epilogue transposes through the staging boxes: the TMEM lane of a thread is an
+// output feature, its registers run over edges, and each [32 edges x 32 features] box goes out
+// with one TMA store. One accumulator pair fills TMEM, so the epilogue is not overlapped.
+constexpr int kTF = 128;   // output features per tile (MMA M)
+constexpr int kTE = 256;   // edges per tile (MMA N)
+
+template <int STAGES>
+struct F16TSmem {
+  static constexpr int kW16 = kTF * kBK * 2;   // 8 KB
+  static constexpr int kA16 = kTE * kBK * 2;   // 16 KB
+  static constexpr int kStage = 2 * kW16 + 2 * kA16;
+  static constexpr int kStaging = 4 * 2 * 4096;
+  static constexpr int kBytes = STAGES * kStage + kStaging + 1024 + 1024;
+  static_assert(kBytes <= 227 * 1024, "shared memory plan exceeds 227 KB");
+};
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                   const __grid_constant__ CUtensorMap tmAl,
+                                                                   const __grid_constant__ CUtensorMap tmWh,
+                                                                   const __grid_constant__ CUtensorMap tmWl,
+                                                                   const __grid_constant__ CUtensorMap tmC,
+                                                                   const float* __restrict__ bias, float w_scale_inv,
+                                                                   int M, int N, int K, int* err) {
+  using L = F16TSmem<STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_c = smem + STAGES * L::kStage;
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem_c + L::kStaging);
+  uint64_t* bar_empty = bar_full + STAGES;
+  uint64_t* bar_acc_full = bar_empty + STAGES;
+  uint64_t* bar_acc_empty = bar_acc_full + 1;
+  uint64_t* bar_done = bar_acc_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_f = N / kTF;
+  const int num_tiles = ((M + kTE - 1) / kTE) * num_f;
+  const int num_k = (K + kBK - 1) / kBK;
+  // stage layout: [W_hi | W_lo | A_hi | A_lo]
+  auto stage_Wh = [&](int s) { return smem + s * L::kStage; };
+  auto stage_Wl = [&](int s) { return smem + s * L::kStage + L::kW16; };
+  auto stage_Ah = [&](int s) { return smem + s * L::kStage + 2 * L::kW16; };
+  auto stage_Al = [&](int s) { return smem + s * L::kStage + 2 * L::kW16 + L::kA16; };
+  constexpr uint32_t kTmemCols = 2 * kTE;   // main + cross
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    mbar_init(bar_acc_full, 1);
+    mbar_init(bar_acc_empty, 128);
+    mbar_init(bar_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kWarpMma) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kWarpProducer) {
+    if (lane == 0) {
+      constexpr uint32_t bytes = 2 * L::kW16 + 2 * L::kA16;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int e0 = (tile / num_f) * kTE, f0 = (tile % num_f) * kTF;
+        for (int kt = 0; kt < num_k; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&bar_empty[s], ((it / STAGES) - 1) & 1, abort_flag, err, kErrWaitEmpty))
+            break;
+          mbar_expect_tx(&bar_full[s], bytes);
+          tma_load_2d(stage_Wh(s), &tmWh, kt * kBK, f0, &bar_full[s]);
+          tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, f0, &bar_full[s]);
+          tma_load_2d(stage_Ah(s), &tmA, kt * kBK, e0, &bar_full[s]);
+          tma_load_2d(stage_Al(s), &tmAl, kt * kBK, e0, &bar_full[s]);
+        }
+      }
+      if (*abort_flag) {
+        for (int j = it - 1; j >= 0 && j >= it - STAGES; --j) {
+          for (uint32_t i = 0; i < kWaitLimit && !mbar_try(&bar_full[j % STAGES], (j / STAGES) & 1); ++i) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc_f16<kTE>();   // M = 128, N = 256
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++lt) {
+        if (lt >= 1 && !mbar_wait(bar_acc_empty, (lt - 1) & 1, abort_flag, err, kErrWaitAccEmpty)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc_main = tmem, acc_cross = tmem + (uint32_t)kTE;
+        for (int kt = 0; kt < num_k; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&bar_full[s], (it / STAGES) & 1, abort_flag, err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t w_hi = smem_u32(stage_Wh(s)), w_lo = smem_u32(stage_Wl(s));
+          const uint32_t a_hi = smem_u32(stage_Ah(s)), a_lo = smem_u32(stage_Al(s));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint32_t off = kk * 32;
+            const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+            mma_f16(acc_main, smem_desc_sw64(w_hi + off), smem_desc_sw64(a_hi + off), idesc, acc);
+            mma_f16(acc_cross, smem_desc_sw64(w_lo + off), smem_desc_sw64(a_hi + off), idesc, acc);
+            mma_f16(acc_cross, smem_desc_sw64(w_hi + off), smem_desc_sw64(a_lo + off), idesc, 1u);
+          }
+          mma_commit(&bar_empty[s]);
+        }
+        if (ok) mma_commit(bar_acc_full);
+      }
+      mma_commit(bar_done);
+      for (uint32_t i = 0; i < kWaitLimit && !mbar_try(bar_done, 0); ++i) {
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kWarpEpi0) {
+    // epilogue (warps 6-9): TMEM lane quadrant q = output features f0 + 32q .. f0 + 32q + 31
+    const int q = warp & 3;
+    int lt = 0, nbox = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+      bool ok = mbar_wait(bar_acc_full, lt & 1, abort_flag, err, kErrWaitAcc);
+      ok = __all_sync(kFull, ok && !*abort_flag);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int e0 = (tile / num_f) * kTE, f0 = (tile % num_f) * kTF;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      const float bv = bias ? bias[f0 + q * 32 + lane] : 0.0f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kTE; c0 += 32) {
+        if (e0 + c0 >= M) break;   // whole box beyond the last edge
+        uint32_t rm[32], rc[32];
+        tmem_ld32(taddr + (uint32_t)c0, rm);
+        tmem_ld32(taddr + (uint32_t)(kTE + c0), rc);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        uint8_t* box = smem_c + (q * 2 + (nbox & 1)) * 4096;
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
+        // box row j = edge e0 + c0 + j (128 bytes = 32 features), 128-byte swizzle: 16-byte chunk
+        // (lane / 4) of row j at chunk (lane / 4) ^ (j & 7); one row per store instruction
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float v = fmaf(__uint_as_float(rc[j]), kLoScaleInv, __uint_as_float(rm[j])) * w_scale_inv + bv;
+          *reinterpret_cast<float*>(box + j * 128 + ((((lane >> 2) ^ (j & 7))) << 4) + ((lane & 3) << 2)) = v;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, box, f0 + q * 32, e0 + c0);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        ++nbox;
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(bar_acc_empty);
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == kWarpMma) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 namespace {
 
 template <int BN, int STAGES, bool kPre, bool kX3>
@@ -423,6 +609,26 @@ cudaError_t launch_bn(int BN, const CUtensorMap& a, const CUtensorMap& al, const
   }
 }
 
+template <int STAGES>
+cudaError_t launch_f16_t(const CUtensorMap& a, const CUtensorMap& al, const CUtensorMap& wh, const CUtensorMap& wl,
+                         const CUtensorMap& mc, const float* bias, float w_scale_inv, int M, int N, int K, int* err,
+                         cudaStream_t s) {
+  using L = F16TSmem<STAGES>;
+  auto kern = gemm_f16x3_t_kernel<STAGES>;
+  static thread_local uint64_t configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> (dev & 63) & 1)) {
+    cudaError_t st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (st != cudaSuccess) return st;
+    configured |= uint64_t(1) << (dev & 63);
+  }
+  const int tiles = ((M + kTE - 1) / kTE) * (N / kTF);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, kThreads, L::kBytes, s>>>(a, al, wh, wl, mc, bias, w_scale_inv, M, N, K, err);
+  return cudaGetLastError();
+}
+
 // single-product mode (pre-split A): half the operand bytes per stage, so deeper rings
 cudaError_t launch_bn_x1(int BN, const CUtensorMap& a, const CUtensorMap& wh, const CUtensorMap& mc, float* C,
                          const float* bias, float inv, int M, int N, int K, int64_t ldc, int* err, cudaStream_t s) {
@@ -447,6 +653,14 @@ const int g_bn256_min_k = [] {
   return e ? atoi(e) : 512;
 }();
 
+// Transposed 128 x 256 tiles (gemm_f16x3_t_kernel) for pre-split f16x3 products whose N is a
+// multiple of 128 that would otherwise run 128-wide tiles. FUMA_GEMM_T=1 enables them (read
+// at every call, so a process can compare both).
+bool use_t() {
+  const char* e = getenv("FUMA_GEMM_T");
+  return e && atoi(e) != 0;
+}
+
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,
                       float w_scale_inv, const float* bias, float* C, int64_t ldc, int64_t M, int N, int K, int* err,
                       cudaStream_t s, bool x1) {
@@ -454,6 +668,20 @@ int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_h
   const int BN = (N % 256 == 0 && (x1 || K >= g_bn256_min_k)) ? 256
                  : (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : (N % 32 == 0) ? 32 : 16;
   CUtensorMap ma, mal, mh, ml;
+  if (a_split && !x1 && BN == 128 && N % 128 == 0 && use_t()) {
+    const uint8_t* base = reinterpret_cast<const uint8_t*>(A);
+    if (!make_map_t(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, M, K, lda * 4, kBK, kTE, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map_t(&mal, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base + lda * 2, M, K, lda * 4, kBK, kTE,
+                    CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map_t(&mh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, W_hi, N, K, ldw * 2, kBK, kTF, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map_t(&ml, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, W_lo, N, K, ldw * 2, kBK, kTF, CU_TENSOR_MAP_SWIZZLE_64B))
+      return -1;
+    CUtensorMap mc;
+    if (!make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, ldc * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+      return -1;
+    const cudaError_t st = launch_f16_t<4>(ma, mal, mh, ml, mc, bias, w_scale_inv, (int)M, N, K, err, s);
+    return st == cudaSuccess ? 0 : (int)st;
+  }
   if (a_split) {
     // row-packed split operand: row r holds K fp16 hi values at byte 4*lda*r and the K lo values
     // 2*lda bytes further

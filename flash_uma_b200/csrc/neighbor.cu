@@ -6,7 +6,9 @@
 // (source i, destination j, integer cell offset s) with |pos_i - pos_j + s @ cell| < cutoff (a
 // self pair only with s != 0) is a candidate; per destination the candidates are ordered by
 // (distance, source, s_0, s_1, s_2) in fp64 and the first max_neighbors are kept. This file
-// computes the same list:
+// computes the same list, bit for bit for orthorhombic cells (with a general cell, the wrapped
+// coordinates' 3-term sums may round differently from numpy's, which can only matter for a pair
+// within one rounding of the cutoff):
 //
 //   1. nl_bin_kernel      fractional coordinates (pos @ inv_cell), wrapped into [0, 1), the
 //                         integer wrap shift, the wrapped Cartesian position and the bin of
@@ -40,6 +42,11 @@ constexpr int kErrNeighborOverflow = 64;
 __device__ __forceinline__ double dmul(double a, double b) { return __dmul_rn(a, b); }
 __device__ __forceinline__ double dadd(double a, double b) { return __dadd_rn(a, b); }
 __device__ __forceinline__ double dsub(double a, double b) { return __dsub_rn(a, b); }
+
+// squared length in the host statement's fixed order: (x^2 + z^2) + y^2, no fused multiply-add
+__device__ __forceinline__ double sq3(const double* v) {
+  return dadd(dadd(dmul(v[0], v[0]), dmul(v[2], v[2])), dmul(v[1], v[1]));
+}
 
 // x @ M for a row vector x [3] and M [3, 3] row-major: out_k = (x0 M0k + x1 M1k) + x2 M2k
 __device__ __forceinline__ double rowmat(const double* x, const double* M, int k) {
@@ -125,10 +132,6 @@ __global__ void __launch_bounds__(256) nl_fill_kernel(const int32_t* __restrict_
 }
 
 // candidate key: (distance bits, source << 32 | packed offset), both compared as unsigned
-struct Cand {
-  unsigned long long k1, k2;
-};
-
 __device__ __forceinline__ bool cand_less(unsigned long long a1, unsigned long long a2, unsigned long long b1,
                                           unsigned long long b2) {
   return a1 < b1 || (a1 == b1 && a2 < b2);
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(kNlWarps * 32) nl_search_kernel(
               double v[3];
 #pragma unroll
               for (int k = 0; k < 3; ++k) v[k] = dsub(dadd(wpos[s * 3 + k], shift[k]), wd[k]);
-              const double d2 = dadd(dadd(dmul(v[0], v[0]), dmul(v[1], v[1])), dmul(v[2], v[2]));
+              const double d2 = sq3(v);
               const bool self = (s == d) && img[0] == 0 && img[1] == 0 && img[2] == 0;
               if (d2 < p.cut2 && !self) {
                 // the offset in terms of the unwrapped positions, and the distance the model sees
@@ -194,7 +197,7 @@ __global__ void __launch_bounds__(kNlWarps * 32) nl_search_kernel(
                 double u[3];
 #pragma unroll
                 for (int k = 0; k < 3; ++k) u[k] = dadd(dsub(pos[s * 3 + k], pd[k]), rowmat(offd, p.cell, k));
-                const double dist = __dsqrt_rn(dadd(dadd(dmul(u[0], u[0]), dmul(u[1], u[1])), dmul(u[2], u[2])));
+                const double dist = __dsqrt_rn(sq3(u));
                 if (dist < p.cutoff) {
                   take = true;
                   key1 = (unsigned long long)__double_as_longlong(dist);

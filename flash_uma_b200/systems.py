@@ -117,6 +117,14 @@ def water_box(n_mol: int = 3333, density: float = 1.0, oh: float = 0.96, angle_d
     return AtomicSystem(pos, numbers, np.diag([L, L, L]), name=f"water_{n_mol}")
 
 
+def _sq3(v: np.ndarray) -> np.ndarray:
+    """Squared length over the last axis (3) in a fixed order, (x^2 + z^2) + y^2, each operation
+    rounded once (no fused multiply-add), so that the device list (fuma_neighbor_list) computes
+    the same bits. (This is the order numpy's einsum("...k,...k") uses here, with which the
+    committed fixtures' graphs were built.)"""
+    return (v[..., 0] * v[..., 0] + v[..., 2] * v[..., 2]) + v[..., 1] * v[..., 1]
+
+
 def neighbor_list(system: AtomicSystem, cutoff: float = 6.0, max_neighbors: int = 30):
     """Deterministic capped periodic neighbour list (see module docstring).
 
@@ -167,7 +175,7 @@ def neighbor_list(system: AtomicSystem, cutoff: float = 6.0, max_neighbors: int 
                                 continue
                             shift = img @ cell
                             vec = wpos[s_ids][None, :, :] + shift[None, None, :] - wpos[d_ids][:, None, :]
-                            d2 = np.einsum("dsk,dsk->ds", vec, vec)
+                            d2 = _sq3(vec)
                             dd, ss = np.nonzero(d2 < cutoff * cutoff)
                             si, di = s_ids[ss], d_ids[dd]
                             keep = ~((si == di) & np.all(img == 0))
@@ -185,7 +193,7 @@ def neighbor_list(system: AtomicSystem, cutoff: float = 6.0, max_neighbors: int 
     off = np.concatenate(off_l).astype(np.int64); dist = np.concatenate(dist_l)
     # recompute the distance from the unwrapped positions and offsets (what the model sees)
     vec = pos[src] - pos[dst] + off @ cell
-    dist = np.sqrt(np.einsum("ek,ek->e", vec, vec))
+    dist = np.sqrt(_sq3(vec))
     order = np.lexsort((off[:, 2], off[:, 1], off[:, 0], src, dist, dst))
     src, dst, off, dist = src[order], dst[order], off[order], dist[order]
     # rank within each destination and cap

@@ -80,7 +80,7 @@ class ZeroAllocBackbone(nn.Module):
     def forward(self, data):
         # errors recorded by earlier GEMMs (pipeline timeouts, f16x3 range) surface here, one
         # call late, without a synchronisation
-        linear.poll_errors()
+        _poll()
         data.atomic_numbers = data.atomic_numbers.long()
         data.atomic_numbers_full = data.atomic_numbers
         data.batch_full = data.batch
@@ -97,7 +97,23 @@ class ZeroAllocBackbone(nn.Module):
         else:
             cell_per_edge = data.cell.repeat_interleave(data.nedges, dim=0)
             shifts = torch.einsum("ij,ijk->ik", data.cell_offsets.to(cell_per_edge.dtype), cell_per_edge)
-        x_node = self.ce(pos=data.pos, Z=data.atomic_numbers, batch=data.batch, edge_index=data.edge_index,
-                         shifts=shifts, csd_emb=csd.float(), charge=data.charge, spin=data.spin, natoms=data.natoms)
-        linear.snapshot_errors()
+        x_node = _run_model(self.ce, data.pos, data.atomic_numbers, data.batch, data.edge_index, shifts, csd.float(),
+                            data.charge, data.spin, data.natoms)
         return {"node_embedding": x_node, "batch": data.batch}
+
+
+@torch.compiler.disable
+def _poll():
+    linear.poll_errors()
+
+
+@torch.compiler.disable
+def _run_model(ce, pos, Z, batch, edge_index, shifts, csd, charge, spin, natoms):
+    """The CUDA model (and the host-side error snapshot after it). Under ``torch.compile`` this is
+    one opaque region: the compiler traces the embeddings and shifts around it (the reference's
+    own ops compile through torch.library custom operators, see ``flash_uma_b200.library``);
+    the model itself is captured whole with CUDA graphs (``predict.GraphedStep``) instead."""
+    x_node = ce(pos=pos, Z=Z, batch=batch, edge_index=edge_index, shifts=shifts, csd_emb=csd, charge=charge,
+                spin=spin, natoms=natoms)
+    linear.snapshot_errors()
+    return x_node

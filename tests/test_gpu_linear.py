@@ -145,3 +145,27 @@ def test_linear_f16_single_product(M, N, K):
     assert (y.cpu().double() - y_ref).abs().max() <= 2e-3 * y_ref.abs().max()
     gx_ref = gy.double() @ W.double()
     assert (gx.cpu().double() - gx_ref).abs().max() <= 2e-3 * gx_ref.abs().max()
+
+
+@pytest.mark.parametrize("M,N,K", [(120000, 640, 768), (777, 640, 768), (300, 384, 384), (513, 128, 320),
+                                   (4097, 1536, 128), (1, 128, 128), (2000, 128, 1536), (257, 384, 96)])
+def test_linear_f16x3_transposed_tiles(M, N, K, monkeypatch):
+    """The transposed 128 x 256 tiles (FUMA_GEMM_T=1, output features on the MMA's M side) on the
+    pre-split operands give the same products as the row-major tiles: within the f16x3 bound of
+    fp64, ragged edge counts included."""
+    from flash_uma_b200.linear import _gemm16, _split16, check_errors, split_rows
+    g = torch.Generator().manual_seed(M + N + K)
+    W = (torch.randn(N, K, generator=g) / K ** 0.5).to(DEV)
+    b = torch.randn(N, generator=g).to(DEV)
+    x = torch.randn(M, K, generator=g).to(DEV)
+    w16 = _split16(torch.nn.functional.pad(W, (0, (K + 7) // 8 * 8 - K)))
+    xp = split_rows(x)
+    monkeypatch.setenv("FUMA_GEMM_T", "0")
+    y0 = _gemm16(xp, w16, b, K)
+    monkeypatch.setenv("FUMA_GEMM_T", "1")
+    y1 = _gemm16(xp, w16, b, K)
+    torch.cuda.synchronize()
+    check_errors()
+    ref = x.double() @ W.double().t() + b.double()
+    for y in (y0, y1):
+        assert (y.double() - ref).abs().max() <= tol(K) * ref.abs().max()

@@ -17,7 +17,7 @@ def brute_force(system, cutoff, max_nb):
                 if i == j and s == (0, 0, 0):
                     continue
                 v = pos[i] - pos[j] + np.array(s) @ cell
-                d = float(np.sqrt(v @ v))
+                d = float(np.sqrt((v[0] * v[0] + v[2] * v[2]) + v[1] * v[1]))   # the rule's fixed order
                 if d < cutoff:
                     cand.append((d, i, s))
         cand.sort()
