@@ -390,7 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
 
 // Transposed tiles: D[f, e] = sum_k W[f, k] A[e, k] with the 128 output features f of a tile on
 // the MMA's M side and 256 edges e on its N side (tcgen05 M=128, N=256), for output widths that
-// are a multiple of 128 but not of 256 (or short K): those shapes otherwise run 128-wide tiles,
+// are a multiple of 128 but not of 256 (or K below the 256-wide threshold): those shapes
+// otherwise run 128-wide tiles,
 // whose per-instruction operand traffic (A and W tiles of equal size for half the products)
 // keeps the tensor pipe near two thirds of its rate. Same f16x3 arithmetic as
 // gemm_f16x3_kernel (main += W_hi A_hi, cross += W_lo A_hi + W_hi A_lo, one pre-split operand
@@ -654,11 +655,15 @@ const int g_bn256_min_k = [] {
 }();
 
 // Transposed 128 x 256 tiles (gemm_f16x3_t_kernel) for pre-split f16x3 products whose N is a
-// multiple of 128 that would otherwise run 128-wide tiles. FUMA_GEMM_T=1 enables them (read
-// at every call, so a process can compare both).
-bool use_t() {
+// multiple of 128 that would otherwise run 128-wide tiles, when K >= 384: measured on B200 at
+// M = 120,000, K = 768, N = 640 0.346 -> 0.290 ms, K = 384, N = 384 0.116 -> 0.109 ms,
+// K = 1536, N = 128 0.179 -> 0.169 ms; shorter K is faster with the double-buffered 128-wide
+// tiles (K = 128: 0.027 -> 0.031 ms). FUMA_GEMM_T=0 / 1 forces them off / on for every
+// eligible shape (read at every call).
+bool use_t(int K) {
   const char* e = getenv("FUMA_GEMM_T");
-  return e && atoi(e) != 0;
+  if (e) return atoi(e) != 0;
+  return K >= 384;
 }
 
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,
@@ -668,7 +673,7 @@ int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_h
   const int BN = (N % 256 == 0 && (x1 || K >= g_bn256_min_k)) ? 256
                  : (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : (N % 32 == 0) ? 32 : 16;
   CUtensorMap ma, mal, mh, ml;
-  if (a_split && !x1 && BN == 128 && N % 128 == 0 && use_t()) {
+  if (a_split && !x1 && BN == 128 && N % 128 == 0 && use_t(K)) {
     const uint8_t* base = reinterpret_cast<const uint8_t*>(A);
     if (!make_map_t(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, M, K, lda * 4, kBK, kTE, CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map_t(&mal, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base + lda * 2, M, K, lda * 4, kBK, kTE,
