@@ -68,8 +68,7 @@ __device__ __forceinline__ void rotT(const float* D, const float4* g, float4* ou
 }
 
 constexpr int kFwdWarps = 8;
-constexpr int kBwdWarps = 4;
-constexpr int kBwdRing = 3;   // gather backward: edges staged per warp
+constexpr int kBwdWarps = 8;
 
 }  // namespace
 
@@ -149,15 +148,15 @@ struct BwdSlots {
 };
 
 // One side (SIDE 1: target pass over the destination CSR, SIDE 0: source pass over the source
-// CSR) and one coefficient block (PART 0: rows 0-3, radial slots 0-3 and 6-7, D1; PART 1: rows
-// 4-8, radial slots 4-5 and 8-11, D2) of the gather backward. Warp per node n, lane = 4
-// channels (channel chunks of 128 in an outer loop); the node's rows stay in registers and are
-// rotated into every edge's frame. Each edge's gradient and radial slots and Wigner block come
-// through a per-warp ring of kBwdRing shared-memory buffers filled with cp.async kBwdRing - 1
-// edges ahead of the edge being computed.
-// Dynamic shared memory: kBwdWarps * kBwdRing * BwdSlots<PART>::n * 512 bytes.
+// CSR) and one coefficient block (PART 0: rows 0-3, radial slots 0-3 and 6-7, D1; PART 1:
+// rows 4-8, radial slots 4-5 and 8-11, D2) of the gather backward. Warp per node n, lane =
+// 4 channels (channel chunks of 128 in an outer loop); the node's rows stay in registers
+// and are rotated into every edge's frame. The next edge's gradient and radial slots and
+// Wigner block are copied into shared memory (cp.async, double-buffered per warp) while the
+// current edge is computed, so two edges' loads are in flight per warp.
+// Dynamic shared memory: kBwdWarps * 2 * BwdSlots<PART>::n * 512 bytes.
 template <int SIDE, int PART>
-__global__ void __launch_bounds__(kBwdWarps * 32, 4) gather_bwd_side_kernel(
+__global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
     const float* __restrict__ gX0, const float* __restrict__ gX1, const float* __restrict__ gX2,
     const float* __restrict__ x, const float* __restrict__ wig, const float* __restrict__ rad,
     const float* __restrict__ csd, const int64_t* __restrict__ batch, const int32_t* __restrict__ row_ptr,
@@ -171,11 +170,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4) gather_bwd_side_kernel(
   constexpr int NV = PART ? 32 : 16;
   constexpr int kS = BwdSlots<PART>::n;
   extern __shared__ float4 s_stage[];
-  __shared__ float s_w[kBwdWarps][kBwdRing][28];
+  __shared__ float s_w[kBwdWarps][2][28];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   const int W = 12 * C;   // g_rad / rad row width
-  float4* stage = s_stage + (size_t)warp * kBwdRing * kS * 32;   // [buffer][slot][lane]
+  float4* stage = s_stage + (size_t)warp * 2 * kS * 32;   // [buffer][slot][lane]
   bool bad = false;
   for (int64_t n = (int64_t)blockIdx.x * kBwdWarps + warp; n < N; n += (int64_t)gridDim.x * kBwdWarps) {
     const int kb = row_ptr[n], ke = row_ptr[n + 1];
@@ -214,25 +213,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4) gather_bwd_side_kernel(
         if (lane < nw) cp_async4(&s_w[warp][b][lane], wig + e * kWig + woff + lane);
         cp_async_commit();
       };
-      int ib = kb;
-      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
-      int ki = kb;   // next CSR position to copy
-      auto issue_next = [&]() {
-        if (ki < ke) {
-          if (ki - ib >= 32) {
-            ib += 32;
-            e_l = (ib + lane < ke) ? col_idx[ib + lane] : 0;
-          }
-          issue(__shfl_sync(kFull, e_l, ki - ib), (ki - kb) % kBwdRing);
-        } else {
-          cp_async_commit();   // empty group keeps "groups in flight" counting edges
-        }
-        ++ki;
-      };
-      int ob = kb;       // window of edge ids for the edge being computed
-      int eo_l = e_l;
-#pragma unroll 1
-      for (int p = 0; p < kBwdRing - 1; ++p) issue_next();
       // the node's rows of this block (l = 0 with the system embedding added)
       float4 v[nrows], acc[nrows];
 #pragma unroll
@@ -241,17 +221,26 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4) gather_bwd_side_kernel(
         acc[r] = f4(0.f);
       }
       if (PART == 0 && on) v[0] = v[0] + ld4_keep(csd + bn * C + co);
-#pragma unroll 1
+      int base = kb;
+      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
+      int64_t e_cur = __shfl_sync(kFull, e_l, 0);
+      if (kb < ke) issue(e_cur, 0);
       for (int k = kb; k < ke; ++k) {
-        issue_next();   // refills the buffer computed in the previous iteration
-        cp_async_wait<kBwdRing - 1>();
-        __syncwarp();   // edge k's Wigner block, copied by lanes < nw, is visible to the warp
-        if (k - ob >= 32) {
-          ob += 32;
-          eo_l = (ob + lane < ke) ? col_idx[ob + lane] : 0;
+        const int b = (k - kb) & 1;
+        int64_t e_next = 0;
+        if (k + 1 < ke) {
+          if (k + 1 - base >= 32) {
+            base += 32;
+            e_l = (base + lane < ke) ? col_idx[base + lane] : 0;
+          }
+          e_next = __shfl_sync(kFull, e_l, k + 1 - base);
+          issue(e_next, b ^ 1);
+        } else {
+          cp_async_commit();   // empty group: keeps "all but the newest group" = edge k
         }
-        const int64_t e = __shfl_sync(kFull, eo_l, k - ob);
-        const int b = (k - kb) % kBwdRing;
+        cp_async_wait1();
+        __syncwarp();   // edge k's Wigner block, copied by lanes < nw, is visible to the warp
+        const int64_t e = e_cur;
         const float4* src = stage + b * kS * 32 + lane;
         const float* sw = s_w[warp][b];
         float* grow = g_rad + e * (int64_t)W;
@@ -309,8 +298,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4) gather_bwd_side_kernel(
           *dst = (SIDE == 1 && cb == 0) ? tot : *dst + tot;
         }
         __syncwarp();   // buffer b is refilled by the next iteration's copies
+        e_cur = e_next;
       }
-      cp_async_wait<0>();   // the trailing (empty) groups
       if (on) {
         float* gx = g_x + (n * 9 + row0) * (int64_t)C + co;
 #pragma unroll
@@ -338,10 +327,10 @@ void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, con
                        cudaStream_t s) {
   (void)idx_i;
   (void)scratch;   // the two-pass backward needs no scratch rows
-  const unsigned g = grid_for(N, kBwdWarps, 4);
+  const unsigned g = grid_for(N, kBwdWarps, 2);
   const int b = kBwdWarps * 32;
-  const size_t sm0 = (size_t)kBwdWarps * kBwdRing * BwdSlots<0>::n * 32 * sizeof(float4);
-  const size_t sm1 = (size_t)kBwdWarps * kBwdRing * BwdSlots<1>::n * 32 * sizeof(float4);
+  const size_t sm0 = (size_t)kBwdWarps * 2 * BwdSlots<0>::n * 32 * sizeof(float4);
+  const size_t sm1 = (size_t)kBwdWarps * 2 * BwdSlots<1>::n * 32 * sizeof(float4);
   static thread_local uint64_t configured = 0;   // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);

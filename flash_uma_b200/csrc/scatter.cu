@@ -145,16 +145,15 @@ __global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
   }
 }
 
-// Backward, grouped by destination so g_out[j] stays in registers across the node's edges, one launch
+// Backward, grouped by destination so g_out[j] stays in L1 across the node's edges, one launch
 // per coefficient block (PART 0: rows 0-3 / Z slots of l <= 1 / Wigner 0-8; PART 1: rows 4-8 /
 // l = 2 slots / Wigner 9-33):
 //   g_Z = env * (rows of D applied to g_out[j]); g_wigner[e] = env * sum_c g_out[j] (x) m;
 //   g_env[e] = sum_c g_out[j] . (unscaled message): PART 0 writes its share, PART 1 (launched
 //   after it on the same stream) adds the rest, so the sum has a fixed order.
-// (g_x_res = g_out is returned by the host.) Each edge's Z slots, Wigner block and envelope come
-// through the same per-warp cp.async ring as the forward, kRing - 1 edges ahead.
+// (g_x_res = g_out is returned by the host.)
 template <int PART>
-__global__ void __launch_bounds__(kFwdWarps * 32, 4) rotate_scatter_bwd_kernel(
+__global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ Z0, const float* __restrict__ Z1, const float* __restrict__ Z2,
     const float* __restrict__ wig, const float* __restrict__ env, float* __restrict__ gZ0, float* __restrict__ gZ1,
@@ -166,19 +165,20 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 4) rotate_scatter_bwd_kernel(
   constexpr int kRow0 = PART ? 4 : 0;
   constexpr int kS = PART ? 5 : 4;     // Z slots per edge and lane (16-byte copies)
   constexpr int NV = PART ? 32 : 16;   // kW Wigner partials (+ g0 . Z0_0 at index 9 in PART 0), padded
-  __shared__ float4 s_stage[kFwdWarps][kRing][kS][32];
-  __shared__ float s_w[kFwdWarps][kRing][28];   // Wigner block (0..kW-1) and envelope (27) of a staged edge
+  __shared__ float4 s_stage[8][2][kS][32];
+  __shared__ float s_w[8][2][28];      // Wigner block (0..kW-1) and envelope (27) of the staged edge
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
   bool bad = false;
-  for (int64_t jn = (int64_t)blockIdx.x * kFwdWarps + warp; jn < N; jn += (int64_t)gridDim.x * kFwdWarps) {
+  for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     for (int cb = 0; cb < C4; cb += 32) {
       const int c4 = cb + lane;
       const bool on = c4 < C4;
       const int co = c4 * 4;
-      // copies of edge e's Z slots, Wigner block and envelope into ring buffer b (one commit
-      // group per edge), kRing - 1 edges ahead of the edge being computed
+      // copies of edge e's Z slots, Wigner block and envelope into buffer b (one commit group);
+      // the next edge's copies are in flight while the current edge is computed
       auto issue = [&](int64_t e, int b) {
         if (on) {
           const float* z0 = Z0 + e * 3 * (int64_t)C + co;
@@ -202,41 +202,30 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 4) rotate_scatter_bwd_kernel(
         if (lane == 31) cp_async4(&s_w[warp][b][27], env + e);
         cp_async_commit();
       };
-      int ib = kb;
-      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
-      int ki = kb;   // next CSR position to copy
-      auto issue_next = [&]() {
-        if (ki < ke) {
-          if (ki - ib >= 32) {
-            ib += 32;
-            e_l = (ib + lane < ke) ? col_idx[ib + lane] : 0;
-          }
-          issue(__shfl_sync(kFull, e_l, ki - ib), (ki - kb) % kRing);
-        } else {
-          cp_async_commit();   // empty group keeps "groups in flight" counting edges
-        }
-        ++ki;
-      };
-      // the edge ids in CSR order for the output rows, in a second lane register window
-      int ob = kb;
-      int eo_l = e_l;
-#pragma unroll 1
-      for (int p = 0; p < kRing - 1; ++p) issue_next();
       // this block's rows of g_out[j], loaded once per node
       float4 g[kRows];
 #pragma unroll
       for (int l = 0; l < kRows; ++l) g[l] = on ? ld4_keep(g_out + (jn * 9 + kRow0 + l) * (int64_t)C + co) : f4(0.f);
-#pragma unroll 1
+      int base = kb;
+      int e_l = (kb + lane < ke) ? col_idx[kb + lane] : 0;
+      int64_t e_cur = __shfl_sync(kFull, e_l, 0);
+      if (kb < ke) issue(e_cur, 0);
       for (int k = kb; k < ke; ++k) {
-        issue_next();   // refills the buffer computed in the previous iteration
-        cp_async_wait<kRing - 1>();
-        __syncwarp();
-        if (k - ob >= 32) {
-          ob += 32;
-          eo_l = (ob + lane < ke) ? col_idx[ob + lane] : 0;
+        const int b = (k - kb) & 1;
+        int64_t e_next = 0;
+        if (k + 1 < ke) {
+          if (k + 1 - base >= 32) {
+            base += 32;
+            e_l = (base + lane < ke) ? col_idx[base + lane] : 0;
+          }
+          e_next = __shfl_sync(kFull, e_l, k + 1 - base);
+          issue(e_next, b ^ 1);
+        } else {
+          cp_async_commit();   // empty group: "all but the newest group" is then edge k
         }
-        const int64_t e = __shfl_sync(kFull, eo_l, k - ob);
-        const int b = (k - kb) % kRing;
+        cp_async_wait1();
+        __syncwarp();
+        const int64_t e = e_cur;
         const float* sw = s_w[warp][b];
         const float ev = sw[27];
         const float4* src = &s_stage[warp][b][0][lane];
@@ -303,8 +292,8 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 4) rotate_scatter_bwd_kernel(
         }
         if (lane == 0) g_env[e] = (PART == 0 && cb == 0) ? genv : g_env[e] + genv;
         __syncwarp();   // buffer b is refilled by the next iteration's copies
+        e_cur = e_next;
       }
-      cp_async_wait<0>();   // the trailing (empty) groups
     }
   }
   report_split_range(bad, err);
@@ -523,11 +512,11 @@ void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, c
                                const float* Z1, const float* Z2, const float* wig, const float* env, float* gZ0,
                                float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, bool split,
                                int* err, cudaStream_t s) {
-  const int t = kFwdWarps * 32;
-  rotate_scatter_bwd_kernel<0><<<grid_resident(rotate_scatter_bwd_kernel<0>, t, N, kFwdWarps), t, 0, s>>>(
-      row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig, g_env, N, C, split, err);
-  rotate_scatter_bwd_kernel<1><<<grid_resident(rotate_scatter_bwd_kernel<1>, t, N, kFwdWarps), t, 0, s>>>(
-      row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig, g_env, N, C, split, err);
+  const unsigned g = grid_for(N, 8, 2);
+  rotate_scatter_bwd_kernel<0><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
+                                                 g_env, N, C, split, err);
+  rotate_scatter_bwd_kernel<1><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
+                                                 g_env, N, C, split, err);
 }
 
 void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,
