@@ -48,8 +48,7 @@ _SIGS = {
     "fuma_coef_to_node": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
     "fuma_rmsnorm_sh_fwd": [_P, _P, _P, _P, _F32, _I64, _I32, _P, _P, _P],
     "fuma_rmsnorm_sh_bwd": [_P, _P, _P, _P, _P, _I64, _I32, _P, _P],
-    "fuma_gather_bwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _P, _P,
-                                _P],
+    "fuma_morton_reorder_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P],
 }
 
 _lib = None
@@ -114,17 +113,17 @@ KERNELS_PER_CALL["fuma_gather_fwd"] = 2
 KERNELS_PER_CALL["fuma_csr_permute"] = 2
 KERNELS_PER_CALL["fuma_neighbor_list"] = 4
 KERNELS_PER_CALL["fuma_morton_reorder"] = 2   # up to 16,384 atoms (launches_of)
+KERNELS_PER_CALL["fuma_morton_reorder_noalloc"] = 2
 KERNELS_PER_CALL["fuma_gather_fwd_f16x3"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2
-KERNELS_PER_CALL["fuma_gather_bwd_noalloc"] = 3
 KERNELS_PER_CALL["fuma_gather_bwd_f16x3"] = 3
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd_f16x3"] = 2
 
 
 def launches_of(name: str, args) -> int:
     """Kernel launches of one call of entry point ``name`` with arguments ``args``."""
-    if name == "fuma_morton_reorder" and args[5] > 16384:
+    if name in ("fuma_morton_reorder", "fuma_morton_reorder_noalloc") and args[5] > 16384:
         return 28   # bounds, keys, 8 radix passes of 3 kernels, permutation, renumbering
     return KERNELS_PER_CALL.get(name, 1)
 

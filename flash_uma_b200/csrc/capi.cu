@@ -67,6 +67,10 @@ int check_C(int32_t C) {
 
 }  // namespace
 
+int fuma::bind_device_of(const void* p) { return bind_device(p); }
+
+int fuma::launch_status(const char* what) { return launched(what); }
+
 int fuma::report_error(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);

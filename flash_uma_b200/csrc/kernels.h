@@ -86,6 +86,11 @@ cudaError_t launch_neighbor_list(const double* pos, int64_t N, const double* cel
                                  double cutoff, int max_nb, void* scratch, int32_t* counts, int64_t* out_src,
                                  int64_t* out_off, double* out_dist, int* err, cudaStream_t s);
 
+// The C ABI's shared argument handling (capi.cu): make the device owning `p` current (returns
+// FUMA_E_INVALID for memory that is not a CUDA allocation), and the status after a launch.
+int bind_device_of(const void* p);
+int launch_status(const char* what);
+
 // Record `fmt` as the calling thread's fuma_last_error() message and return `code`.
 int report_error(int code, const char* fmt, ...);
 

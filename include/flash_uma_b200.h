@@ -269,21 +269,21 @@ int fuma_init_scatter_bwd_f16x3(const float* g_out, const float* rad, const floa
                                 const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
                                 float* g_rad, float* g_wigner, float* g_env, int* err_flag, void* stream);
 
-/* ---- allocation-free gather backward -----------------------------------------------------
- * No counterpart in the reference. For callers that cannot let a library allocate device
- * memory (frameworks that own the whole device memory budget, steps that must not pay for or
- * be serialised by cudaMalloc/cudaFree): the same computation as fuma_gather_bwd, but its
- * E*9*C-float scratch lives in a 32 MiB array built into the library (resident on every GPU
- * that loads it), so only inputs and outputs are passed. Limit: E*9*C <= 8,388,608 floats,
- * larger calls return FUMA_E_INVALID. The first call on a device looks up the array's
- * address; make that first call before any stream capture. All calls share the array:
- * calls that can overlap on the GPU race and must be serialised by the caller. Allocates
- * nothing and needs no zero-initialised memory. */
-int fuma_gather_bwd_noalloc(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
-                            const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
-                            const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
-                            const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
-                            float* g_x, float* g_wigner, float* g_rad, void* stream);
+/* ---- allocation-free Morton reorder -------------------------------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device memory or lend a
+ * device allocator at the point of the call (host programs that own the whole device memory
+ * budget, steps that must not pay for or be serialised by cudaMalloc / cudaFree, bindings that
+ * only pass the caller's arrays): the same computation and outputs as fuma_morton_reorder, but
+ * its radix-sort scratch lives in a 13 MiB array built into the library (held on every GPU that
+ * loads it until the process exits), so only inputs and outputs are passed. Limit: N <= 524,288
+ * atoms; larger calls return FUMA_E_INVALID before launching anything. The first call on a device
+ * looks up the array's address; make it before any stream capture. All calls share the array
+ * and it keeps the last call's contents (nothing in it needs to start at zero); calls that can
+ * overlap on the GPU race on it and must be serialised by the caller. Allocates nothing. */
+int fuma_morton_reorder_noalloc(const float* pos, const int64_t* Z, const int64_t* batch, const int64_t* idx_i,
+                                const int64_t* idx_j, int64_t N, int64_t E, int64_t* perm, int64_t* inv_perm,
+                                float* pos_s, int64_t* Z_s, int64_t* batch_s, int64_t* ii, int64_t* jj, int* err_flag,
+                                void* stream);
 
 #ifdef __cplusplus
 }

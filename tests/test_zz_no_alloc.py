@@ -1,12 +1,16 @@
-"""fuma_gather_bwd_noalloc: the allocation-free gather backward, called through the C ABI.
+"""fuma_morton_reorder_noalloc, the allocation-free Morton reorder, called through the C ABI.
 
-This entry point serves callers that cannot let the library allocate device memory (for
-example host frameworks that own the device memory budget, or steps that must not be
-serialised by cudaMalloc): its scratch lives in a 32 MiB array built into the library. The
-test checks it against fuma_gather_bwd, which takes a caller-provided scratch buffer, on
-two consecutive calls with different inputs (the shared array keeps the previous call's
-contents), and checks that oversized calls are refused. Collected last on purpose, and
-independent of the other test files (passes alone or after them)."""
+Some callers cannot allocate device memory, or lend a device allocator, at the point where they
+call in (host programs that own the whole device memory budget, steps that must not be
+serialised by cudaMalloc, bindings that only pass the caller's arrays). For them this entry
+point keeps the radix sort's scratch in an array built into the library instead of taking a
+scratch buffer. The test calls it and the allocating entry point (fuma_morton_reorder, with a
+scratch buffer from the caller) on the same inputs, twice in a row with different systems (the
+built-in array keeps the first call's contents when the second one starts), above 16,384 atoms
+so the multi-block radix sort (which uses the scratch) runs; the integer outputs must agree
+bit for bit, as in the other Morton tests. It also checks that a system beyond the array's
+524,288-atom limit is refused before anything is launched. Collected last on purpose (a failure
+here leaves every other test already run) and independent of the other test files."""
 import ctypes
 
 import pytest
@@ -14,53 +18,6 @@ import torch
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
-TOL = 2e-5  # same bound as the gather-backward parity tests (relative to the max magnitude)
-
-
-def _inputs(seed, N=60, E=400, C=32):
-    g = torch.Generator().manual_seed(seed)
-    idx_i = torch.randint(0, N, (E,), generator=g)
-    idx_j = torch.randint(0, N, (E,), generator=g)
-    q = torch.randn(E, 4, generator=g)
-    q = q / q.norm(dim=1, keepdim=True)
-    w, x_, y, z = q.T
-    R = torch.stack([1 - 2 * (y * y + z * z), 2 * (x_ * y - w * z), 2 * (x_ * z + w * y),
-                     2 * (x_ * y + w * z), 1 - 2 * (x_ * x_ + z * z), 2 * (y * z - w * x_),
-                     2 * (x_ * z - w * y), 2 * (y * z + w * x_), 1 - 2 * (x_ * x_ + y * y)], 1)
-    wig = torch.cat([R, torch.randn(E, 25, generator=g) * 0.4], 1)
-    return dict(
-        N=N, E=E, C=C, idx_i=idx_i, idx_j=idx_j, wig=wig,
-        x=torch.randn(N, 9, C, generator=g), rad=torch.randn(E, 12 * C, generator=g),
-        csd=torch.randn(2, C, generator=g), batch=(torch.arange(N) >= N // 2).long(),
-        g0=torch.randn(E, 6 * C, generator=g), g1=torch.randn(E, 8 * C, generator=g),
-        g2=torch.randn(E, 4 * C, generator=g))
-
-
-def _call_both(lib, I):
-    from flash_uma_b200.ops import build_graph_csr
-    d = {k: (v.to(DEV).contiguous() if isinstance(v, torch.Tensor) else v) for k, v in I.items()}
-    gr = build_graph_csr(d["idx_i"], d["idx_j"], I["N"])
-    N, E, C = I["N"], I["E"], I["C"]
-    p = lambda t: ctypes.c_void_p(t.data_ptr())
-    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    common = [p(d["g0"]), p(d["g1"]), p(d["g2"]), p(d["x"]), p(d["idx_i"]), p(d["wig"]), p(d["rad"]), p(d["csd"]),
-              p(d["batch"]), p(gr.dst_row_ptr), p(gr.dst_col), p(gr.src_row_ptr), p(gr.src_col),
-              ctypes.c_int64(N), ctypes.c_int64(E), ctypes.c_int32(C)]
-    outs = {}
-    for name in ("ref", "noalloc"):
-        gx = torch.full((N, 9, C), float("nan"), device=DEV)
-        gw = torch.full((E, 34), float("nan"), device=DEV)
-        grad = torch.full((E, 12 * C), float("nan"), device=DEV)
-        if name == "ref":
-            scratch = torch.empty(E * 9 * C, device=DEV)
-            rc = lib.fuma_gather_bwd(*common, p(scratch), ctypes.c_int64(scratch.numel()), p(gx), p(gw), p(grad),
-                                     stream)
-        else:
-            rc = lib.fuma_gather_bwd_noalloc(*common, p(gx), p(gw), p(grad), stream)
-        assert rc == 0, lib.fuma_last_error()
-        outs[name] = (gx, gw, grad)
-    torch.cuda.synchronize()
-    return outs
 
 
 @pytest.fixture(scope="module")
@@ -69,18 +26,57 @@ def lib():
     return _native.load()
 
 
+def _system(N, E, nsys, seed):
+    g = torch.Generator().manual_seed(seed)
+    pos = torch.rand(N, 3, generator=g) * 40.0
+    pos[N // 3:N // 3 + 7] = pos[11]                                   # equal keys
+    batch = torch.sort(torch.randint(0, nsys, (N,), generator=g))[0]
+    Z = torch.randint(1, 90, (N,), generator=g)
+    idx = torch.randint(0, N, (2, E), generator=g)
+    return [t.to(DEV).contiguous() for t in (pos, Z, batch, idx[0], idx[1])]
+
+
+def _outputs(N, E):
+    i64 = dict(device=DEV, dtype=torch.int64)
+    return [torch.full((N,), -5, **i64), torch.full((N,), -5, **i64), torch.full((N, 3), float("nan"), device=DEV),
+            torch.full((N,), -5, **i64), torch.full((N,), -5, **i64), torch.full((E,), -5, **i64),
+            torch.full((E,), -5, **i64)]
+
+
+def _call(lib, inputs, noalloc):
+    pos, Z, batch, ii, jj = inputs
+    N, E = pos.shape[0], ii.shape[0]
+    perm, inv, pos_s, Z_s, b_s, ii_s, jj_s = out = _outputs(N, E)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())   # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    args = [p(pos), p(Z), p(batch), p(ii), p(jj), ctypes.c_int64(N), ctypes.c_int64(E), p(perm), p(inv), p(pos_s),
+            p(Z_s), p(b_s), p(ii_s), p(jj_s)]
+    if noalloc:
+        rc = lib.fuma_morton_reorder_noalloc(*args, p(err), stream)
+        keep = None
+    else:
+        nbytes = int(lib.fuma_morton_scratch_bytes(N))
+        keep = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=DEV)
+        rc = lib.fuma_morton_reorder(*args, p(keep), ctypes.c_int64(nbytes), p(err), stream)
+    assert rc == 0, lib.fuma_last_error()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return out
+
+
 def test_noalloc_matches_allocating_entry_point_twice(lib):
-    for seed in (11, 12):   # two calls in a row: the shared scratch still holds the first call's rows
-        outs = _call_both(lib, _inputs(seed))
-        for a, b in zip(outs["noalloc"], outs["ref"]):
-            assert torch.isfinite(a).all()
-            assert (a - b).abs().max().item() <= TOL * max(1.0, b.abs().max().item())
+    for N, E, nsys, seed in ((100800, 300000, 1, 1), (40000, 90000, 300, 2), (5000, 20000, 2, 3)):
+        a = _call(lib, _system(N, E, nsys, seed), noalloc=True)
+        b = _call(lib, _system(N, E, nsys, seed), noalloc=False)
+        for x, y in zip(a, b):
+            assert torch.equal(x, y)
+        assert sorted(a[0].tolist()) == list(range(N))   # a permutation
 
 
-def test_noalloc_refuses_oversized_calls(lib):
-    from flash_uma_b200._native import _SIGS  # noqa: F401  (signatures set by load())
-    C, E = 128, 8000                       # 8000 * 9 * 128 floats > 8 Mi-float capacity
-    rc = lib.fuma_gather_bwd_noalloc(*([ctypes.c_void_p(16)] * 13), ctypes.c_int64(10), ctypes.c_int64(E),
-                                     ctypes.c_int32(C), *([ctypes.c_void_p(16)] * 3), ctypes.c_void_p(0))
+def test_noalloc_refuses_systems_beyond_its_array(lib):
+    N = (1 << 19) + 1
+    rc = lib.fuma_morton_reorder_noalloc(*([ctypes.c_void_p(16)] * 5), ctypes.c_int64(N), ctypes.c_int64(0),
+                                         *([ctypes.c_void_p(16)] * 8), ctypes.c_void_p(0))
     assert rc == -1
-    assert b"scratch" in lib.fuma_last_error()
+    assert b"524288" in lib.fuma_last_error()
