@@ -226,15 +226,16 @@ def build_partitioned(device, gemm: str, world: int, rank: int, system=None, str
     csd = bb.csd_embedding(d.charge, d.spin).float().detach()
 
     fixed = (d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd)
+    csd_sys = dict(charge=d.charge, spin=d.spin, natoms=d.natoms)
 
     def step(pos):
-        out = pm.energy_forces(head, pos, *fixed, stress=stress)
+        out = pm.energy_forces(head, pos, *fixed, stress=stress, **csd_sys)
         return dict(zip(("energy", "forces", "stress"), out))
 
     def make_graph(pos0, capture_hook=None):
         """The step captured as one CUDA graph with its NCCL collectives (every rank calls this)."""
         from flash_uma_b200.partition import GraphedPartitionedStep
-        g = GraphedPartitionedStep(pm, head, pos0, *fixed, stress=stress, capture_hook=capture_hook)
+        g = GraphedPartitionedStep(pm, head, pos0, *fixed, stress=stress, capture_hook=capture_hook, **csd_sys)
 
         class Step:
             def __call__(self, pos):

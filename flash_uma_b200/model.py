@@ -260,14 +260,18 @@ class ESCNInferenceModel(nn.Module):
                                      graph.dst_col, N)
 
     def layer_forward(self, k, x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, charge=None, spin=None,
-                      natoms=None, n_out=None):
+                      natoms=None, n_out=None, partitioned: bool = False, group=None):
+        """``partitioned``: x holds one rank's atoms of systems spread over ``group`` (the channel
+        balancing then sums over all ranks)."""
         x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, n_out)
         if n_out is not None:
             batch = batch[:n_out]
         if self.charge_end > self.charge_start:
-            x = balance_channels_batched(x, charge, natoms, batch, self.charge_start, self.charge_end, 0.0)
+            x = balance_channels_batched(x, charge, natoms, batch, self.charge_start, self.charge_end, 0.0,
+                                         partitioned, group)
         if self.spin_end > self.spin_start:
-            x = balance_channels_batched(x, spin, natoms, batch, self.spin_start, self.spin_end, 1.0)
+            x = balance_channels_batched(x, spin, natoms, batch, self.spin_start, self.spin_end, 1.0, partitioned,
+                                         group)
         return x
 
     def final(self, x):

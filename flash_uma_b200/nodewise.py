@@ -120,13 +120,20 @@ class EnergyHead(nn.Module):
         return onehot.t() @ e_atom
 
 
-def balance_channels_batched(emb, target, natoms, batch, start_idx, end_idx, target_offset=0.0):
+def balance_channels_batched(emb, target, natoms, batch, start_idx, end_idx, target_offset=0.0,
+                             partitioned: bool = False, group=None):
     """Shift channels [start_idx, end_idx) of l=0 so that their per-system sum
     equals ``target + target_offset`` (stand-in for FAIRChem's charge/spin
-    channel balancing called at ``model.py:213-216``)."""
+    channel balancing called at ``model.py:213-216``). ``partitioned``: ``emb`` holds this
+    rank's atoms of systems spread over the ranks of ``group``; the per-system sums are
+    all-reduced across them (differentiably) before the correction."""
     chans = emb[:, 0, start_idx:end_idx]
     nsys = natoms.shape[0]
     sums = torch.zeros(nsys, chans.shape[1], dtype=emb.dtype, device=emb.device).index_add(0, batch, chans)
+    if partitioned:
+        import torch.distributed as dist
+        import torch.distributed.nn.functional as dfn
+        sums = dfn.all_reduce(sums, op=dist.ReduceOp.SUM, group=group if group is not None else dist.group.WORLD)
     tgt = (target.to(emb.dtype) + target_offset)[:, None]
     corr = ((tgt - sums) / natoms.to(emb.dtype)[:, None]).index_select(0, batch)
     out = emb.clone()

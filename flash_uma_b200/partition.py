@@ -168,13 +168,6 @@ class PartitionedModel:
     """Runs a stage-protocol model on this rank's part of one periodic system."""
 
     def __init__(self, model, plan: PartitionPlan, device, group=None):
-        charge = getattr(model, "charge_end", 0) > getattr(model, "charge_start", 0) or \
-            getattr(model, "charge_range", (0, 0))[1] > getattr(model, "charge_range", (0, 0))[0]
-        spin = getattr(model, "spin_end", 0) > getattr(model, "spin_start", 0) or \
-            getattr(model, "spin_range", (0, 0))[1] > getattr(model, "spin_range", (0, 0))[0]
-        if charge or spin:
-            raise NotImplementedError("charge/spin channel balancing needs per-system sums across ranks; "
-                                      "not supported by the partitioned model")
         self.model, self.plan, self.device, self.group = model, plan, device, group
         self.n_owned = int(plan.owned.shape[0])
         self.local_ids = torch.as_tensor(plan.local_ids, dtype=torch.long, device=device)
@@ -185,9 +178,11 @@ class PartitionedModel:
         self.ex = HaloExchanger(plan, device, group)
         self.graph = model.build_graph(self.idx_i, self.idx_j, self.n_local)
 
-    def node_embedding(self, pos, Z, batch, cell_offsets, cell, csd_emb):
+    def node_embedding(self, pos, Z, batch, cell_offsets, cell, csd_emb, charge=None, spin=None, natoms=None):
         """Final node embedding of the owned atoms. ``pos``, ``Z``, ``batch`` are global [N];
-        ``cell_offsets`` is the global [E, 3]; ``cell`` is [3, 3]."""
+        ``cell_offsets`` is the global [E, 3]; ``cell`` is [3, 3]; ``charge``, ``spin``, ``natoms``
+        are per system (needed by models with charge / spin channel ranges, whose per-system
+        channel sums are all-reduced across the ranks after every layer, ``model.py:213-216``)."""
         m = self.model
         pos_l = pos.index_select(0, self.local_ids)
         Z_l = Z.index_select(0, self.local_ids)
@@ -199,12 +194,12 @@ class PartitionedModel:
             x_owned = x[: self.n_owned]
             x = torch.cat([x_owned, halo_exchange(x_owned, self.ex)], 0)
             # owned rows out: the halo rows' layer outputs would be replaced by the next exchange
-            x = m.layer_forward(k, x, xe, wig, env, self.idx_i, self.idx_j, self.graph, csd_emb, b_l,
-                                n_out=self.n_owned)
+            x = m.layer_forward(k, x, xe, wig, env, self.idx_i, self.idx_j, self.graph, csd_emb, b_l, charge, spin,
+                                natoms, n_out=self.n_owned, partitioned=True, group=self.group)
         return m.final(x[: self.n_owned])
 
     def energy_forces(self, head, pos, Z, batch, cell_offsets, cell, csd_emb, num_systems: int = 1,
-                      stress: bool = False):
+                      stress: bool = False, charge=None, spin=None, natoms=None):
         """Global energy [num_systems] and forces [N, 3] (and, with ``stress``, the virial stress
         [1, 3, 3] of the one periodic system), identical on every rank.
 
@@ -222,7 +217,7 @@ class PartitionedModel:
             p = pos + pos @ sym
             c = cell + cell @ sym
             wrt.append(disp)
-        x = self.node_embedding(p, Z, batch, cell_offsets, c, csd_emb)
+        x = self.node_embedding(p, Z, batch, cell_offsets, c, csd_emb, charge, spin, natoms)
         b_owned = batch.index_select(0, self.local_ids[: self.n_owned])
         e_local = head(x, b_owned, num_systems)
         grads = torch.autograd.grad(e_local.sum(), wrt)
@@ -252,9 +247,9 @@ class GraphedPartitionedStep:
     it before ``destroy_process_group``, which otherwise waits for the graph's NCCL work."""
 
     def __init__(self, pm: PartitionedModel, head, pos, Z, batch, cell_offsets, cell, csd_emb, num_systems: int = 1,
-                 stress: bool = False, warmup: int = 3, capture_hook=None):
+                 stress: bool = False, warmup: int = 3, capture_hook=None, charge=None, spin=None, natoms=None):
         self._pos = pos.detach().clone()
-        args = (head, self._pos, Z, batch, cell_offsets, cell, csd_emb, num_systems, stress)
+        args = (head, self._pos, Z, batch, cell_offsets, cell, csd_emb, num_systems, stress, charge, spin, natoms)
         dev = self._pos.device
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))

@@ -152,15 +152,17 @@ class OracleBackbone:
         return ops.init_node_scatter(rad0, wigner, env, Z, batch, self.W_sphere, csd_emb, idx_j, graph[0], graph[1], N)
 
     def layer_forward(self, k, x, x_edge, wigner, env, idx_i, idx_j, graph, csd_emb, batch, charge=None, spin=None,
-                      natoms=None, n_out=None):
+                      natoms=None, n_out=None, partitioned: bool = False, group=None):
         from flash_uma_b200.nodewise import balance_channels_batched
         x = self.layers[k](x, x_edge, wigner, env, idx_i, idx_j, graph[0], graph[1], csd_emb, batch, n_out)
         if n_out is not None:
             batch = batch[:n_out]
         if self.charge_range[1] > self.charge_range[0]:
-            x = balance_channels_batched(x, charge, natoms, batch, *self.charge_range, target_offset=0.0)
+            x = balance_channels_batched(x, charge, natoms, batch, *self.charge_range, target_offset=0.0,
+                                         partitioned=partitioned, group=group)
         if self.spin_range[1] > self.spin_range[0]:
-            x = balance_channels_batched(x, spin, natoms, batch, *self.spin_range, target_offset=1.0)
+            x = balance_channels_batched(x, spin, natoms, batch, *self.spin_range, target_offset=1.0,
+                                         partitioned=partitioned, group=group)
         return x
 
     def final(self, x):

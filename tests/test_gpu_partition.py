@@ -17,17 +17,21 @@ def _free_port():
         return sk.getsockname()[1]
 
 
-def _setup():
+def _setup(balance=False):
     from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
     from flash_uma_b200.systems import bulk_fcc, to_graph
     s = bulk_fcc(6, 6, 8, jitter=0.05, seed=11)
     data = to_graph([s])
     bb = SyntheticESCNMDBackbone(num_layers=2, sphere_channels=64, hidden_channels=64, seed=5)
+    if balance:   # charge / spin channel balancing after every layer, sums across the ranks
+        bb.charge_channel_start, bb.charge_channel_end = 0, 8
+        bb.spin_channel_start, bb.spin_channel_end = 8, 16
+        data.charge, data.spin = torch.tensor([1]), torch.tensor([2])
     head = make_energy_head(64, 64, seed=2)
     return s, data, bb, head
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, balance=False):
     import datetime
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dev = torch.device("cuda", rank)
@@ -37,17 +41,18 @@ def _worker(rank, world, port, out_path):
     try:
         from flash_uma_b200.partition import PartitionedModel, make_plan
         from flash_uma_b200.wrapper import ZeroAllocBackbone
-        s, data, bb, head = _setup()
+        s, data, bb, head = _setup(balance)
         bb, head = bb.to(dev), head.to(dev)
         z = ZeroAllocBackbone(bb)
         d = data.to(dev)
         csd = z.csd_embedding(d.charge, d.spin).float().detach()
         plan = make_plan(s.positions, s.cell, data.edge_index.numpy(), world, rank)
         pm = PartitionedModel(z.ce, plan, dev)
+        sysargs = dict(charge=d.charge, spin=d.spin, natoms=d.natoms)
         e, f, st = pm.energy_forces(head, d.pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd,
-                                    stress=True)
+                                    stress=True, **sysargs)
         e2, f2, st2 = pm.energy_forces(head, d.pos, d.atomic_numbers, d.batch, d.cell_offsets, d.cell[0], csd,
-                                       stress=True)
+                                       stress=True, **sysargs)
         assert torch.equal(f, f2) and torch.equal(st, st2)      # reproducible across calls
         if rank == 0:
             torch.save({"energy": e.cpu(), "forces": f.cpu(), "stress": st.cpu()}, out_path)
@@ -56,13 +61,14 @@ def _worker(rank, world, port, out_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_partitioned_cuda_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("balance", [False, True])
+def test_partitioned_cuda_matches_single_gpu(tmp_path, balance):
     from flash_uma_b200.predict import Predictor
     from flash_uma_b200.wrapper import ZeroAllocBackbone
     out = str(tmp_path / "res.pt")
-    mp.spawn(_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), out, balance), nprocs=2, join=True)
     got = torch.load(out)
-    s, data, bb, head = _setup()
+    s, data, bb, head = _setup(balance)
     dev = torch.device("cuda", 0)
     ref = Predictor(ZeroAllocBackbone(bb.to(dev)), head.to(dev))(data.to(dev), stress=True)
     assert torch.allclose(got["energy"], ref["energy"].cpu(), rtol=2e-6)

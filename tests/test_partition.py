@@ -49,7 +49,25 @@ def _free_port():
         return sk.getsockname()[1]
 
 
-def _worker(rank, world, port, out_path):
+def _backbone(balance: bool):
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone
+    bb = SyntheticESCNMDBackbone(num_layers=2, sphere_channels=16, hidden_channels=16, num_distance_basis=8, seed=3)
+    if balance:   # charge / spin channel balancing after every layer (model.py:213-216)
+        bb.charge_channel_start, bb.charge_channel_end = 0, 4
+        bb.spin_channel_start, bb.spin_channel_end = 4, 8
+    return bb
+
+
+def _data(balance: bool):
+    from flash_uma_b200.systems import to_graph
+    s, _, _ = _system()
+    data = to_graph([s])
+    if balance:
+        data.charge, data.spin = torch.tensor([1]), torch.tensor([2])
+    return s, data
+
+
+def _worker(rank, world, port, out_path, balance=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -58,10 +76,8 @@ def _worker(rank, world, port, out_path):
         from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
         from flash_uma_b200.systems import to_graph
         from oracle.model import OracleBackbone
-        s, ei, off = _system()
-        data = to_graph([s])
-        bb = SyntheticESCNMDBackbone(num_layers=2, sphere_channels=16, hidden_channels=16, num_distance_basis=8,
-                                     seed=3)
+        s, data = _data(balance)
+        bb = _backbone(balance)
         bb64 = copy.deepcopy(bb).double()
         head = make_energy_head(16, 16).double()
         model = OracleBackbone(bb64, torch.float64)
@@ -69,26 +85,26 @@ def _worker(rank, world, port, out_path):
         plan = P.make_plan(s.positions, s.cell, data.edge_index.numpy(), world, rank)
         pm = P.PartitionedModel(model, plan, torch.device("cpu"))
         e, f, st = pm.energy_forces(head, data.pos.double(), data.atomic_numbers, data.batch,
-                                    data.cell_offsets.double(), data.cell[0].double(), csd, stress=True)
+                                    data.cell_offsets.double(), data.cell[0].double(), csd, stress=True,
+                                    charge=data.charge, spin=data.spin, natoms=data.natoms)
         if rank == 0:
             torch.save({"energy": e, "forces": f, "stress": st}, out_path)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_partitioned_oracle_matches_single_process(world, tmp_path):
+@pytest.mark.parametrize("world,balance", [(2, False), (4, False), (3, True)])
+def test_partitioned_oracle_matches_single_process(world, balance, tmp_path):
+    """``balance``: charge / spin channel balancing on, whose per-system sums span the ranks."""
     import copy
     from flash_uma_b200.predict import Predictor
-    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
-    from flash_uma_b200.systems import to_graph
+    from flash_uma_b200.synthetic import make_energy_head
     from oracle.model import OracleBackbone
     out = str(tmp_path / "res.pt")
-    mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), out, balance), nprocs=world, join=True)
     got = torch.load(out)
-    s, _, _ = _system()
-    data = to_graph([s])
-    bb = SyntheticESCNMDBackbone(num_layers=2, sphere_channels=16, hidden_channels=16, num_distance_basis=8, seed=3)
+    s, data = _data(balance)
+    bb = _backbone(balance)
     ref = Predictor(OracleBackbone(copy.deepcopy(bb).double(), torch.float64), make_energy_head(16, 16).double())(
         type(data)(**{**data.__dict__, "pos": data.pos.double(), "cell": data.cell.double(),
                       "cell_offsets": data.cell_offsets.double()}), stress=True)
