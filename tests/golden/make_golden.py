@@ -2,7 +2,7 @@
 
 Usage (only where the reference source tree is present; not on the GPU box):
 
-    python tests/golden/make_golden.py [ops] [e2e]   # default: both
+    FLASHUMA_REFERENCE=<reference source tree> python tests/golden/make_golden.py [ops] [e2e]   # default: both
 
 The reference's Triton kernels run on CPU tensors under the Triton interpreter
 (see ``refharness.py``); autotune keeps each kernel's first config. Outputs:

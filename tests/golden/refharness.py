@@ -1,8 +1,9 @@
 """Load the reference implementation's own ops on CPU (fixture generation only).
 
-Runs only where the reference source tree exists (``FLASHUMA_REFERENCE`` or the
-default path); never on the GPU box and never from the tests themselves - the
-tests read the committed ``.npz`` fixtures this produces.
+Runs only where the reference source tree exists; its location comes from the
+``FLASHUMA_REFERENCE`` environment variable (there is no default path). Never on
+the GPU box and never from the tests themselves - the tests read the committed
+``.npz`` fixtures this produces.
 
 The reference ops are Triton kernels; with ``TRITON_INTERPRET=1`` they execute
 on CPU tensors. Two patches make that possible:
@@ -18,17 +19,18 @@ import os
 import sys
 import types
 
-REFERENCE_DIR = os.environ.get("FLASHUMA_REFERENCE", "/" + "/".join(["root", "reference"]))
+REFERENCE_DIR = os.environ.get("FLASHUMA_REFERENCE", "")
 
 
 def available() -> bool:
-    return os.path.isfile(os.path.join(REFERENCE_DIR, "ops", "gather.py"))
+    return bool(REFERENCE_DIR) and os.path.isfile(os.path.join(REFERENCE_DIR, "ops", "gather.py"))
 
 
 def load():
     """Import and return the reference modules: (ops namespace, model module, wrapper module)."""
     if not available():
-        raise RuntimeError(f"reference source tree not found at {REFERENCE_DIR}")
+        raise RuntimeError("the reference source tree was not found: set FLASHUMA_REFERENCE to its path "
+                           f"(got {REFERENCE_DIR!r})")
     os.environ["TRITON_INTERPRET"] = "1"
     import torch
     import triton
