@@ -102,10 +102,10 @@ def stream_of(t: torch.Tensor) -> int:
 
 # kernels each entry point launches (used by launch accounting)
 # variants writing the GEMM-input outputs in the row-packed f16x3 split layout: same arguments
-# plus an error flag before the stream
+# plus the number of halves written (2: hi and lo, 1: hi only) and an error flag before the stream
 for _name in ("fuma_ln_silu_fwd", "fuma_ln_silu_bwd", "fuma_gather_fwd", "fuma_gather_bwd", "fuma_gating_fwd",
               "fuma_gating_bwd", "fuma_rotate_scatter_bwd", "fuma_init_scatter_bwd"):
-    _SIGS[_name + "_f16x3"] = _SIGS[_name][:-1] + [_P, _P]
+    _SIGS[_name + "_f16x3"] = _SIGS[_name][:-1] + [_I32, _P, _P]   # ..., parts, err_flag, stream
 
 KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3

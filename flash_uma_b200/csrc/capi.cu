@@ -130,7 +130,7 @@ int fuma_edge_vec_to_nodes(const int32_t* src_row_ptr, const int32_t* src_col, c
 }
 
 static int ln_silu_fwd_impl(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
-                     float* out, float* mean, float* rstd, bool split, int* err_flag, void* stream) {
+                     float* out, float* mean, float* rstd, int split, int* err_flag, void* stream) {
   REQUIRE(!split || D % 8 == 0, "ln_silu_fwd_f16x3: the split output needs D %% 8 == 0");
   REQUIRE(M >= 0 && D > 0 && (D & 3) == 0 && D <= 2048, "ln_silu_fwd: D=%d must be a multiple of 4, <= 2048", D);
   if (M == 0) return FUMA_OK;
@@ -147,12 +147,13 @@ int fuma_ln_silu_fwd(const float* x, const float* gamma, const float* beta, floa
 }
 
 int fuma_ln_silu_fwd_f16x3(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
-                     float* out, float* mean, float* rstd, int* err_flag, void* stream) {
-  return ln_silu_fwd_impl(x, gamma, beta, eps, M, D, out, mean, rstd, true, err_flag, stream);
+                     float* out, float* mean, float* rstd, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "ln_silu_fwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
+  return ln_silu_fwd_impl(x, gamma, beta, eps, M, D, out, mean, rstd, parts, err_flag, stream);
 }
 
 static int ln_silu_bwd_impl(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
-                     const float* g_out, int64_t M, int32_t D, float* g_x, bool split, int* err_flag, void* stream) {
+                     const float* g_out, int64_t M, int32_t D, float* g_x, int split, int* err_flag, void* stream) {
   REQUIRE(!split || D % 8 == 0, "ln_silu_bwd_f16x3: the split output needs D %% 8 == 0");
   REQUIRE(M >= 0 && D > 0 && (D & 3) == 0 && D <= 2048, "ln_silu_bwd: D=%d must be a multiple of 4, <= 2048", D);
   if (M == 0) return FUMA_OK;
@@ -169,13 +170,14 @@ int fuma_ln_silu_bwd(const float* x, const float* gamma, const float* beta, cons
 }
 
 int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
-                     const float* g_out, int64_t M, int32_t D, float* g_x, int* err_flag, void* stream) {
-  return ln_silu_bwd_impl(x, gamma, beta, mean, rstd, g_out, M, D, g_x, true, err_flag, stream);
+                     const float* g_out, int64_t M, int32_t D, float* g_x, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "ln_silu_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
+  return ln_silu_bwd_impl(x, gamma, beta, mean, rstd, g_out, M, D, g_x, parts, err_flag, stream);
 }
 
 static int gather_fwd_impl(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                     const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
-                    float* X_m0, float* X_m1, float* X_m2, bool split, int* err_flag, void* stream) {
+                    float* X_m0, float* X_m1, float* X_m2, int split, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gather_fwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "gather_fwd: bad sizes");
@@ -196,8 +198,9 @@ int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, 
 
 int fuma_gather_fwd_f16x3(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                     const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
-                    float* X_m0, float* X_m1, float* X_m2, int* err_flag, void* stream) {
-  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, true, err_flag, stream);
+                    float* X_m0, float* X_m1, float* X_m2, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "gather_fwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
+  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, parts, err_flag, stream);
 }
 
 static int gather_bwd_impl(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
@@ -205,7 +208,7 @@ static int gather_bwd_impl(const float* g_X_m0, const float* g_X_m1, const float
                     const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
                     const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
                     float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
-                    bool split, int* err_flag, void* stream) {
+                    int split, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gather_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "gather_bwd: bad sizes");
@@ -241,13 +244,14 @@ int fuma_gather_bwd_f16x3(const float* g_X_m0, const float* g_X_m1, const float*
                     const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
                     const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
                     float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
-                    int* err_flag, void* stream) {
+                    int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "gather_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
   return gather_bwd_impl(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
-                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, true, err_flag, stream);
+                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, parts, err_flag, stream);
 }
 
 static int gating_fwd_impl(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
-                    float* Z_m1, float* Z_m2, bool split, int* err_flag, void* stream) {
+                    float* Z_m1, float* Z_m2, int split, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gating_fwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(E >= 0, "gating_fwd: bad E");
@@ -266,13 +270,14 @@ int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int
 }
 
 int fuma_gating_fwd_f16x3(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
-                    float* Z_m1, float* Z_m2, int* err_flag, void* stream) {
-  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, true, err_flag, stream);
+                    float* Z_m1, float* Z_m2, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "gating_fwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
+  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, parts, err_flag, stream);
 }
 
 static int gating_bwd_impl(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                     const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
-                    float* g_Y_m2, bool split, int* err_flag, void* stream) {
+                    float* g_Y_m2, int split, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gating_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(E >= 0, "gating_bwd: bad E");
@@ -294,8 +299,9 @@ int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m
 
 int fuma_gating_bwd_f16x3(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                     const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
-                    float* g_Y_m2, int* err_flag, void* stream) {
-  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, true, err_flag, stream);
+                    float* g_Y_m2, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "gating_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
+  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, parts, err_flag, stream);
 }
 
 int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
@@ -316,7 +322,7 @@ int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z
 static int rotate_scatter_bwd_impl(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
                             const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
                             int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
-                            float* g_wigner, float* g_env, bool split, int* err_flag, void* stream) {
+                            float* g_wigner, float* g_env, int split, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "rotate_scatter_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "rotate_scatter_bwd: bad sizes");
@@ -344,9 +350,10 @@ int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* 
 int fuma_rotate_scatter_bwd_f16x3(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
                             const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
                             int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
-                            float* g_wigner, float* g_env, int* err_flag, void* stream) {
+                            float* g_wigner, float* g_env, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "rotate_scatter_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
   return rotate_scatter_bwd_impl(g_out, Z_m0, Z_m1, Z_m2, wigner, env, row_ptr, col_idx, N, E, C, g_Z_m0, g_Z_m1,
-                                 g_Z_m2, g_wigner, g_env, true, err_flag, stream);
+                                 g_Z_m2, g_wigner, g_env, parts, err_flag, stream);
 }
 
 int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* env, const int64_t* Z,
@@ -367,7 +374,7 @@ int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* en
 
 static int init_scatter_bwd_impl(const float* g_out, const float* rad, const float* wigner, const float* env,
                           const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
-                          float* g_rad, float* g_wigner, float* g_env, bool split, int* err_flag, void* stream) {
+                          float* g_rad, float* g_wigner, float* g_env, int split, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "init_scatter_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "init_scatter_bwd: bad sizes");
@@ -390,8 +397,9 @@ int fuma_init_scatter_bwd(const float* g_out, const float* rad, const float* wig
 
 int fuma_init_scatter_bwd_f16x3(const float* g_out, const float* rad, const float* wigner, const float* env,
                           const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
-                          float* g_rad, float* g_wigner, float* g_env, int* err_flag, void* stream) {
-  return init_scatter_bwd_impl(g_out, rad, wigner, env, row_ptr, col_idx, N, E, C, g_rad, g_wigner, g_env, true,
+                          float* g_rad, float* g_wigner, float* g_env, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(parts == 1 || parts == 2, "init_scatter_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
+  return init_scatter_bwd_impl(g_out, rad, wigner, env, row_ptr, col_idx, N, E, C, g_rad, g_wigner, g_env, parts,
                                err_flag, stream);
 }
 

@@ -128,8 +128,10 @@ __device__ __forceinline__ void split_f16x4(float4 v, uint2& hi, uint2& lo, bool
 }
 
 // Store 4 consecutive values at column `col` of the [*, W] output row starting at `row`:
-// plain fp32 (streaming), or the row-packed split when `split`.
-__device__ __forceinline__ void st_out4(float* row, int W, int col, float4 v, bool split, bool& bad) {
+// split = 0: plain fp32 (streaming); 2: the row-packed split (hi and lo halves); 1: only the
+// hi halves of the row-packed split (the operand of the single-product GEMM, which reads
+// nothing else; the lo half of the row is left as it is).
+__device__ __forceinline__ void st_out4(float* row, int W, int col, float4 v, int split, bool& bad) {
   if (!split) {
     st4_stream(row + col, v);
     return;
@@ -138,7 +140,7 @@ __device__ __forceinline__ void st_out4(float* row, int W, int col, float4 v, bo
   split_f16x4(v, hi, lo, bad);
   uint8_t* rb = reinterpret_cast<uint8_t*>(row);
   __stcs(reinterpret_cast<uint2*>(rb + 2 * col), hi);
-  __stcs(reinterpret_cast<uint2*>(rb + 2 * (W + col)), lo);
+  if (split == 2) __stcs(reinterpret_cast<uint2*>(rb + 2 * (W + col)), lo);
 }
 
 __device__ __forceinline__ void report_split_range(bool bad, int* err) {

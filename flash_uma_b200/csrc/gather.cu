@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 4) gather_fwd_kernel(
     const float* __restrict__ x, const int64_t* __restrict__ idx_i, const int64_t* __restrict__ idx_j,
     const float* __restrict__ wig, const float* __restrict__ rad, const float* __restrict__ csd,
     const int64_t* __restrict__ batch, float* __restrict__ X0, float* __restrict__ X1, float* __restrict__ X2,
-    int64_t E, int C, bool split, int* err) {
+    int64_t E, int C, int split, int* err) {
   __shared__ float s_w[kFwdWarps][36];
   bool bad = false;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
     const float* __restrict__ x, const float* __restrict__ wig, const float* __restrict__ rad,
     const float* __restrict__ csd, const int64_t* __restrict__ batch, const int32_t* __restrict__ row_ptr,
     const int32_t* __restrict__ col_idx, float* __restrict__ g_x, float* __restrict__ g_wig,
-    float* __restrict__ g_rad, int64_t N, int C, bool split, int* err) {
+    float* __restrict__ g_rad, int64_t N, int C, int split, int* err) {
   constexpr int s = SIDE;
   constexpr int nrows = PART ? 5 : 4;
   constexpr int nw = PART ? 25 : 9;
@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
 
 void launch_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wig, const float* rad,
                        const float* csd, const int64_t* batch, float* X0, float* X1, float* X2, int64_t E, int C,
-                       bool split, int* err, cudaStream_t s) {
+                       int split, int* err, cudaStream_t s) {
   const int t = kFwdWarps * 32;
   gather_fwd_kernel<0><<<grid_resident(gather_fwd_kernel<0>, t, E, kFwdWarps), t, 0, s>>>(
       x, idx_i, idx_j, wig, rad, csd, batch, X0, X1, X2, E, C, split, err);
@@ -323,7 +323,7 @@ void launch_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_
 void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, const float* x, const int64_t* idx_i,
                        const float* wig, const float* rad, const float* csd, const int64_t* batch,
                        const int32_t* dst_ptr, const int32_t* dst_col, const int32_t* src_ptr, const int32_t* src_col,
-                       float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, bool split, int* err,
+                       float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, int split, int* err,
                        cudaStream_t s) {
   (void)idx_i;
   (void)scratch;   // the two-pass backward needs no scratch rows

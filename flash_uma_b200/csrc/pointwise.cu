@@ -21,7 +21,7 @@ __device__ __forceinline__ float4 sig4(float4 a) {
 __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict__ Y0, const float* __restrict__ Y1,
                                                          const float* __restrict__ Y2, float* __restrict__ Z0,
                                                          float* __restrict__ Z1, float* __restrict__ Z2, int64_t E,
-                                                         int C, bool split, int* err) {
+                                                         int C, int split, int* err) {
   const int C4 = C >> 2;
   bool bad = false;
   const int64_t total = E * C4;
@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict
 __global__ void __launch_bounds__(256) gating_bwd_kernel(
     const float* __restrict__ gZ0, const float* __restrict__ gZ1, const float* __restrict__ gZ2,
     const float* __restrict__ Y0, const float* __restrict__ Y1, const float* __restrict__ Y2,
-    float* __restrict__ gY0, float* __restrict__ gY1, float* __restrict__ gY2, int64_t E, int C, bool split,
+    float* __restrict__ gY0, float* __restrict__ gY1, float* __restrict__ gY2, int64_t E, int C, int split,
     int* err) {
   const int C4 = C >> 2;
   bool bad = false;
@@ -104,7 +104,7 @@ template <int VPL, int ROWS>
 __global__ void __launch_bounds__(256) ln_silu_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta, float* __restrict__ out,
                                                           float* __restrict__ mean_out, float* __restrict__ rstd_out,
-                                                          int64_t M, int D, float eps, bool split, int* err) {
+                                                          int64_t M, int D, float eps, int split, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int D4 = D >> 2;
@@ -164,7 +164,7 @@ template <int VPL, int ROWS>
 __global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta, const float* __restrict__ mean,
                                                           const float* __restrict__ rstd, const float* __restrict__ g_out,
-                                                          float* __restrict__ g_x, int64_t M, int D, bool split,
+                                                          float* __restrict__ g_x, int64_t M, int D, int split,
                                                           int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(256, 4) ln_silu_bwd_row_kernel(const float* __
                                                               const float* __restrict__ mean,
                                                               const float* __restrict__ rstd,
                                                               const float* __restrict__ g_out,
-                                                              float* __restrict__ g_x, int64_t M, int D, bool split,
+                                                              float* __restrict__ g_x, int64_t M, int D, int split,
                                                               int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_short_kernel(const float* __r
                                                                 const float* __restrict__ beta, float* __restrict__ out,
                                                                 float* __restrict__ mean_out,
                                                                 float* __restrict__ rstd_out, int64_t M, int D,
-                                                                float eps, bool split, int* err) {
+                                                                float eps, int split, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int sub = lane >> 3, l8 = lane & 7;
@@ -340,19 +340,19 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_short_kernel(const float* __r
 }
 
 void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,
-                       int C, bool split, int* err, cudaStream_t s) {
+                       int C, int split, int* err, cudaStream_t s) {
   gating_fwd_kernel<<<grid_resident(gating_fwd_kernel, 256, E * (C / 4), 256), 256, 0, s>>>(Y0, Y1, Y2, Z0, Z1, Z2, E, C, split, err);
 }
 
 void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, const float* Y0, const float* Y1,
-                       const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, bool split, int* err,
+                       const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, int split, int* err,
                        cudaStream_t s) {
   gating_bwd_kernel<<<grid_resident(gating_bwd_kernel, 256, E * (C / 4), 256), 256, 0, s>>>(gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C,
                                                                    split, err);
 }
 
 void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float* out, float* mean, float* rstd,
-                        int64_t M, int D, float eps, bool split, int* err, cudaStream_t s) {
+                        int64_t M, int D, float eps, int split, int* err, cudaStream_t s) {
   const int d4 = D / 4;
   // rows of <= 128 values: 8 lanes per row; longer rows: one row per warp (several rows per
   // warp at 32 lanes each raised the register count and measured slower on B200)
@@ -370,7 +370,7 @@ void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, f
 }
 
 void launch_ln_silu_bwd(const float* x, const float* gamma, const float* beta, const float* mean, const float* rstd,
-                        const float* g_out, float* g_x, int64_t M, int D, bool split, int* err, cudaStream_t s) {
+                        const float* g_out, float* g_x, int64_t M, int D, int split, int* err, cudaStream_t s) {
   const int d4 = D / 4;
 #define BWD(V, R)                                                                                                      \
   ln_silu_bwd_kernel<V, R><<<grid_resident(ln_silu_bwd_kernel<V, R>, 256, (M + R - 1) / R, 8), 256, 0, s>>>(x, gamma, beta, mean, rstd, g_out, g_x, M, \

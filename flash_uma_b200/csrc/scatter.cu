@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ Z0, const float* __restrict__ Z1, const float* __restrict__ Z2,
     const float* __restrict__ wig, const float* __restrict__ env, float* __restrict__ gZ0, float* __restrict__ gZ1,
-    float* __restrict__ gZ2, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, bool split,
+    float* __restrict__ gZ2, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, int split,
     int* err) {
   constexpr int kW = PART ? 25 : 9;
   constexpr int kWoff = PART ? 9 : 0;
@@ -396,7 +396,7 @@ template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ rad, const float* __restrict__ wig, const float* __restrict__ env,
-    float* __restrict__ g_rad, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, bool split,
+    float* __restrict__ g_rad, float* __restrict__ g_wig, float* __restrict__ g_env, int64_t N, int C, int split,
     int* err) {
   __shared__ float4 s_stage[WARPS][kRing][3][32];   // radial slots 0-2 of the staged edges
   __shared__ float s_w[WARPS][kRing][12];          // D1 row 1 (0-2), D2 row 2 (3-7), envelope (8)
@@ -510,7 +510,7 @@ void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, c
 
 void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* Z0,
                                const float* Z1, const float* Z2, const float* wig, const float* env, float* gZ0,
-                               float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, bool split,
+                               float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, int split,
                                int* err, cudaStream_t s) {
   const unsigned g = grid_for(N, 8, 2);
   rotate_scatter_bwd_kernel<0><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
@@ -528,7 +528,7 @@ void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, con
 
 void launch_init_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* rad,
                              const float* wig, const float* env, float* g_rad, float* g_wig, float* g_env, int64_t N,
-                             int C, bool split, int* err, cudaStream_t s) {
+                             int C, int split, int* err, cudaStream_t s) {
   init_scatter_bwd_kernel<4><<<grid_resident(init_scatter_bwd_kernel<4>, 128, N, 4), 128, 0, s>>>(row_ptr, col_idx, g_out, rad, wig, env, g_rad, g_wig,
                                                                  g_env, N, C, split, err);
 }

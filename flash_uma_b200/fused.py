@@ -86,19 +86,25 @@ def geometry(pos, Z, idx_i, idx_j, shifts, W_src, W_tgt, offset_g, coeff_g, cuto
 
 # ---- radial MLP on split operands ------------------------------------------------------------
 
-def _ln_silu_split(y, gamma, beta, err):
+def _parts(lin) -> int:
+    """Halves of the split operand a producer writes for the GEMM that reads it: 2 (hi and lo)
+    for the f16x3 products, 1 (hi only) for the single-product "f16" mode."""
+    return 1 if lin.mode == "f16" else 2
+
+
+def _ln_silu_split(y, gamma, beta, err, parts):
     M, D = y.shape
     out, mean, rstd = _empty((M, D), y), _empty((M,), y), _empty((M,), y)
     nat.call("fuma_ln_silu_fwd_f16x3", ptr(y), ptr(gamma), ptr(beta), _EPS_LN, M, D, ptr(out), ptr(mean), ptr(rstd),
-             ptr(err), stream_of(y))
+             parts, ptr(err), stream_of(y))
     return out, mean, rstd
 
 
-def _ln_silu_bwd_split(y, gamma, beta, mean, rstd, g, err):
+def _ln_silu_bwd_split(y, gamma, beta, mean, rstd, g, err, parts):
     M, D = y.shape
     gx = _empty((M, D), y)
     nat.call("fuma_ln_silu_bwd_f16x3", ptr(y), ptr(gamma), ptr(beta), ptr(mean), ptr(rstd), ptr(g), M, D, ptr(gx),
-             ptr(err), stream_of(y))
+             parts, ptr(err), stream_of(y))
     return gx
 
 
@@ -107,10 +113,11 @@ def radial_fwd(rad, xe_p, err):
     fp32 radial output and what the backward needs."""
     Kx = xe_p.shape[1]
     y1 = _gemm16(xe_p, rad.l1.w16, rad.l1.bias_p, Kx)
-    h1, m1, r1 = _ln_silu_split(y1, rad.g1, rad.be1, err)
+    parts = _parts(rad.l1)
+    h1, m1, r1 = _ln_silu_split(y1, rad.g1, rad.be1, err, parts)
     y2 = _gemm16(h1, rad.l2.w16, rad.l2.bias_p, h1.shape[1])
     del h1
-    h2, m2, r2 = _ln_silu_split(y2, rad.g2, rad.be2, err)
+    h2, m2, r2 = _ln_silu_split(y2, rad.g2, rad.be2, err, parts)
     out = _gemm16(h2, rad.l3.w16, rad.l3.bias_p, h2.shape[1])
     return out, (y1, m1, r1, y2, m2, r2)
 
@@ -119,11 +126,12 @@ def radial_bwd(rad, saved, g_out_p, err):
     """Input gradient of :func:`radial_fwd` from the split gradient of its output."""
     y1, m1, r1, y2, m2, r2 = saved
     g_h2 = _gemm16(g_out_p, rad.l3.wt16, None, g_out_p.shape[1])
-    g_y2 = _ln_silu_bwd_split(y2, rad.g2, rad.be2, m2, r2, g_h2, err)
+    parts = _parts(rad.l1)
+    g_y2 = _ln_silu_bwd_split(y2, rad.g2, rad.be2, m2, r2, g_h2, err, parts)
     del g_h2
     g_h1 = _gemm16(g_y2, rad.l2.wt16, None, g_y2.shape[1])
     del g_y2
-    g_y1 = _ln_silu_bwd_split(y1, rad.g1, rad.be1, m1, r1, g_h1, err)
+    g_y1 = _ln_silu_bwd_split(y1, rad.g1, rad.be1, m1, r1, g_h1, err, parts)
     del g_h1
     # only the Gaussian-basis columns of the edge features depend on positions: rows :B of W1^T
     B = rad.n_gauss
@@ -134,8 +142,9 @@ def radial_bwd(rad, saved, g_out_p, err):
 def _conv2(layer, Y0, Y1, Y2, C, err, s):
     """Gating (split outputs) then the three conv2 GEMMs: O0, O1, O2 fp32."""
     E = Y0.shape[0]
+    parts = _parts(layer.conv2_m0)
     Z0, Z1, Z2 = _empty((E, 3 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
-    nat.call("fuma_gating_fwd_f16x3", ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(Z0), ptr(Z1), ptr(Z2), ptr(err), s)
+    nat.call("fuma_gating_fwd_f16x3", ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(Z0), ptr(Z1), ptr(Z2), parts, ptr(err), s)
     O0 = _gemm16(Z0, layer.conv2_m0.w16, layer.conv2_m0.bias_p, 3 * C)
     O1 = _gemm16(Z1, layer.conv2_m1.w16, None, 4 * C)
     O2 = _gemm16(Z2, layer.conv2_m2.w16, None, 2 * C)
@@ -145,10 +154,11 @@ def _conv2(layer, Y0, Y1, Y2, C, err, s):
 def _edge_forward(layer, x_norm, xe_p, wigner, csd, idx_i, idx_j, batch, N, C, err, s):
     """Radial MLP, gather, conv1, gating, conv2 of one block: (rad, radial saved, Y0..2, O0..2)."""
     E = idx_i.shape[0]
+    parts = _parts(layer.conv1_m0)
     rad, rsaved = radial_fwd(layer.rad, xe_p, err)
     X0, X1, X2 = _empty((E, 6 * C), rad), _empty((E, 8 * C), rad), _empty((E, 4 * C), rad)
     nat.call("fuma_gather_fwd_f16x3", ptr(x_norm), ptr(idx_i), ptr(idx_j), ptr(wigner), ptr(rad), ptr(csd),
-             ptr(batch), N, E, C, ptr(X0), ptr(X1), ptr(X2), ptr(err), s)
+             ptr(batch), N, E, C, ptr(X0), ptr(X1), ptr(X2), parts, ptr(err), s)
     Y0 = _gemm16(X0, layer.conv1_m0.w16, layer.conv1_m0.bias_p, 6 * C)
     Y1 = _gemm16(X1, layer.conv1_m1.w16, None, 8 * C)
     Y2 = _gemm16(X2, layer.conv1_m2.w16, None, 4 * C)
@@ -192,6 +202,7 @@ class _MessageBlockFn(torch.autograd.Function):
         E = idx_i.shape[0]
         err = error_flag(x_norm.device)
         s = stream_of(x_norm)
+        parts = _parts(layer.conv1_m0)
         if ctx.lean:
             xe_p, idx_j = saved[6:8]
             rad, rsaved, (Y0, Y1, Y2), (O0, O1, O2) = _edge_forward(layer, x_norm, xe_p, wigner, csd, idx_i, idx_j,
@@ -205,7 +216,7 @@ class _MessageBlockFn(torch.autograd.Function):
         g_env = _empty((E,), Y0)
         nat.call("fuma_rotate_scatter_bwd_f16x3", ptr(g_mid), ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env),
                  ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(gO0), ptr(gO1), ptr(gO2), ptr(g_w),
-                 ptr(g_env), ptr(err), s)
+                 ptr(g_env), parts, ptr(err), s)
         del O0, O1, O2
         gZ0 = _gemm16(gO0, layer.conv2_m0.wt16, None, 3 * C)
         gZ1 = _gemm16(gO1, layer.conv2_m1.wt16, None, 4 * C)
@@ -213,7 +224,7 @@ class _MessageBlockFn(torch.autograd.Function):
         del gO0, gO1, gO2
         gY0, gY1, gY2 = _empty((E, 5 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
         nat.call("fuma_gating_bwd_f16x3", ptr(gZ0), ptr(gZ1), ptr(gZ2), ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(gY0),
-                 ptr(gY1), ptr(gY2), ptr(err), s)
+                 ptr(gY1), ptr(gY2), parts, ptr(err), s)
         del gZ0, gZ1, gZ2, Y0, Y1, Y2
         gX0 = _gemm16(gY0, layer.conv1_m0.wt16, None, 5 * C)
         gX1 = _gemm16(gY1, layer.conv1_m1.wt16, None, 4 * C)
@@ -224,7 +235,7 @@ class _MessageBlockFn(torch.autograd.Function):
         g_rad = torch.empty_like(rad)
         nat.call("fuma_gather_bwd_f16x3", ptr(gX0), ptr(gX1), ptr(gX2), ptr(x_norm), ptr(idx_i), ptr(wigner), ptr(rad),
                  ptr(csd), ptr(batch), ptr(graph.dst_row_ptr), ptr(graph.dst_col), ptr(graph.src_row_ptr),
-                 ptr(graph.src_col), N, E, C, None, 0, ptr(g_x), ptr(g_w2), ptr(g_rad), ptr(err), s)
+                 ptr(graph.src_col), N, E, C, None, 0, ptr(g_x), ptr(g_w2), ptr(g_rad), parts, ptr(err), s)
         del gX0, gX1, gX2, rad
         g_xe = radial_bwd(layer.rad, rsaved, g_rad, err)
         g_w += g_w2
@@ -282,10 +293,11 @@ class _InitBlockFn(torch.autograd.Function):
         g_out = g_out.contiguous()
         E, C = rad.shape[0], model.C
         err = error_flag(rad.device)
+        parts = _parts(model.rad_init.l1)
         g_rad = torch.empty_like(rad)
         g_w, g_env = _empty((E, 34), rad), _empty((E,), rad)
         nat.call("fuma_init_scatter_bwd_f16x3", ptr(g_out), ptr(rad), ptr(wigner), ptr(env), ptr(graph.dst_row_ptr),
-                 ptr(graph.dst_col), N, E, C, ptr(g_rad), ptr(g_w), ptr(g_env), ptr(err), stream_of(rad))
+                 ptr(graph.dst_col), N, E, C, ptr(g_rad), ptr(g_w), ptr(g_env), parts, ptr(err), stream_of(rad))
         g_xe = radial_bwd(model.rad_init, rsaved, g_rad, err)
         return None, g_xe, g_w, g_env, None, None, None, None, None, None
 

@@ -239,35 +239,38 @@ int fuma_split_f16(const float* x, int64_t n, float scale, void* hi, void* lo, v
  *   ln_silu_fwd: out          ln_silu_bwd: g_x              gather_fwd: X_m0, X_m1, X_m2
  *   gather_bwd: g_rad         gating_fwd: Z_m0, Z_m1, Z_m2  gating_bwd: g_Y_m0, g_Y_m1, g_Y_m2
  *   rotate_scatter_bwd: g_Z_m0, g_Z_m1, g_Z_m2              init_scatter_bwd: g_rad
- * All other outputs are unchanged. C (D for ln_silu) must be a multiple of 8. err_flag (device
- * int, may be NULL) receives 16 if a finite value is at or beyond the fp16 limit (65520). */
+ * parts = 2 writes both halves of every split row (the operand of fuma_linear_f16x3); parts = 1
+ * writes only the fp16 hi halves (the operand of the single-product fuma_linear_f16, which reads
+ * nothing else; the lo halves of the rows are left as they are, so the call moves half the
+ * bytes). All other outputs are unchanged. C (D for ln_silu) must be a multiple of 8. err_flag
+ * (device int, may be NULL) receives 16 if a finite value is at or beyond the fp16 limit (65520). */
 int fuma_ln_silu_fwd_f16x3(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
-                           float* out, float* mean, float* rstd, int* err_flag, void* stream);
+                           float* out, float* mean, float* rstd, int32_t parts, int* err_flag, void* stream);
 int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta, const float* mean,
-                           const float* rstd, const float* g_out, int64_t M, int32_t D, float* g_x, int* err_flag,
+                           const float* rstd, const float* g_out, int64_t M, int32_t D, float* g_x, int32_t parts, int* err_flag,
                            void* stream);
 int fuma_gather_fwd_f16x3(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                           const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
-                          float* X_m0, float* X_m1, float* X_m2, int* err_flag, void* stream);
+                          float* X_m0, float* X_m1, float* X_m2, int32_t parts, int* err_flag, void* stream);
 int fuma_gather_bwd_f16x3(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
                           const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
                           const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
                           const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
                           float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
-                          int* err_flag, void* stream);
+                          int32_t parts, int* err_flag, void* stream);
 int fuma_gating_fwd_f16x3(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
-                          float* Z_m1, float* Z_m2, int* err_flag, void* stream);
+                          float* Z_m1, float* Z_m2, int32_t parts, int* err_flag, void* stream);
 int fuma_gating_bwd_f16x3(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                           const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
-                          float* g_Y_m2, int* err_flag, void* stream);
+                          float* g_Y_m2, int32_t parts, int* err_flag, void* stream);
 int fuma_rotate_scatter_bwd_f16x3(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
                                   const float* wigner, const float* env, const int32_t* row_ptr,
                                   const int32_t* col_idx, int64_t N, int64_t E, int32_t C, float* g_Z_m0,
-                                  float* g_Z_m1, float* g_Z_m2, float* g_wigner, float* g_env, int* err_flag,
+                                  float* g_Z_m1, float* g_Z_m2, float* g_wigner, float* g_env, int32_t parts, int* err_flag,
                                   void* stream);
 int fuma_init_scatter_bwd_f16x3(const float* g_out, const float* rad, const float* wigner, const float* env,
                                 const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
-                                float* g_rad, float* g_wigner, float* g_env, int* err_flag, void* stream);
+                                float* g_rad, float* g_wigner, float* g_env, int32_t parts, int* err_flag, void* stream);
 
 /* ---- allocation-free Morton reorder -------------------------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device memory or lend a

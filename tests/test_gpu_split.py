@@ -42,7 +42,7 @@ def test_gating_and_ln_silu_split_outputs():
     plain = [torch.empty(E, k * C, device=DEV) for k in (3, 4, 2)]
     packed = [torch.empty(E, k * C, device=DEV) for k in (3, 4, 2)]
     nat.call("fuma_gating_fwd", *[ptr(t) for t in Y], E, C, *[ptr(t) for t in plain], s)
-    nat.call("fuma_gating_fwd_f16x3", *[ptr(t) for t in Y], E, C, *[ptr(t) for t in packed], ptr(err), s)
+    nat.call("fuma_gating_fwd_f16x3", *[ptr(t) for t in Y], E, C, *[ptr(t) for t in packed], 2, ptr(err), s)
     for a, b in zip(plain, packed):
         _close(a, decode(b))
     gZ = [torch.randn_like(t) for t in plain]
@@ -50,7 +50,7 @@ def test_gating_and_ln_silu_split_outputs():
     packed = [torch.empty_like(t) for t in Y]
     nat.call("fuma_gating_bwd", *[ptr(t) for t in gZ], *[ptr(t) for t in Y], E, C, *[ptr(t) for t in plain], s)
     nat.call("fuma_gating_bwd_f16x3", *[ptr(t) for t in gZ], *[ptr(t) for t in Y], E, C, *[ptr(t) for t in packed],
-             ptr(err), s)
+             2, ptr(err), s)
     for a, b in zip(plain, packed):
         _close(a, decode(b))
     D = 128
@@ -60,13 +60,13 @@ def test_gating_and_ln_silu_split_outputs():
     mean, rstd = torch.empty(E, device=DEV), torch.empty(E, device=DEV)
     nat.call("fuma_ln_silu_fwd", ptr(x), ptr(gam), ptr(bet), 1e-7, E, D, ptr(out), ptr(mean), ptr(rstd), s)
     nat.call("fuma_ln_silu_fwd_f16x3", ptr(x), ptr(gam), ptr(bet), 1e-7, E, D, ptr(out_p), ptr(mean), ptr(rstd),
-             ptr(err), s)
+             2, ptr(err), s)
     _close(out, decode(out_p))
     g = torch.randn_like(x)
     gx, gx_p = torch.empty_like(x), torch.empty_like(x)
     nat.call("fuma_ln_silu_bwd", ptr(x), ptr(gam), ptr(bet), ptr(mean), ptr(rstd), ptr(g), E, D, ptr(gx), s)
     nat.call("fuma_ln_silu_bwd_f16x3", ptr(x), ptr(gam), ptr(bet), ptr(mean), ptr(rstd), ptr(g), E, D, ptr(gx_p),
-             ptr(err), s)
+             2, ptr(err), s)
     _close(gx, decode(gx_p))
     torch.cuda.synchronize()
     check_errors()
@@ -89,3 +89,35 @@ def test_presplit_gemm_matches_fp32_operand(M, N, K):
     assert torch.equal(y_pre, y_in)     # the same split values, the same products, the same order
     y_ref = x.double() @ W.double().t() + b.double()
     assert (y_pre.cpu().double() - y_ref).abs().max() <= (2e-6 + 1e-8 * K) * y_ref.abs().max()
+
+
+def test_hi_only_split_outputs():
+    """parts = 1 (the single-product mode's operands): the hi halves are those of parts = 2, bit
+    for bit, and the lo halves of the rows are not written."""
+    from flash_uma_b200 import _native as nat
+    from flash_uma_b200._native import ptr
+    from flash_uma_b200.linear import check_errors, error_flag
+    E, C = 513, 64
+    s = torch.cuda.current_stream().cuda_stream
+    err = error_flag(DEV)
+    Y = [torch.randn(E, k * C, device=DEV) for k in (5, 4, 2)]
+    both = [torch.empty(E, k * C, device=DEV) for k in (3, 4, 2)]
+    hi = [torch.full((E, k * C), 7.0, device=DEV) for k in (3, 4, 2)]
+    nat.call("fuma_gating_fwd_f16x3", *[ptr(t) for t in Y], E, C, *[ptr(t) for t in both], 2, ptr(err), s)
+    nat.call("fuma_gating_fwd_f16x3", *[ptr(t) for t in Y], E, C, *[ptr(t) for t in hi], 1, ptr(err), s)
+    D = 128
+    x = torch.randn(E, D, device=DEV)
+    gam, bet = torch.rand(D, device=DEV) + 0.5, torch.randn(D, device=DEV)
+    mean, rstd = torch.empty(E, device=DEV), torch.empty(E, device=DEV)
+    o2, o1 = torch.empty_like(x), torch.full_like(x, 7.0)
+    nat.call("fuma_ln_silu_fwd_f16x3", ptr(x), ptr(gam), ptr(bet), 1e-7, E, D, ptr(o2), ptr(mean), ptr(rstd), 2,
+             ptr(err), s)
+    nat.call("fuma_ln_silu_fwd_f16x3", ptr(x), ptr(gam), ptr(bet), 1e-7, E, D, ptr(o1), ptr(mean), ptr(rstd), 1,
+             ptr(err), s)
+    torch.cuda.synchronize()
+    check_errors()
+    for a, b in zip(both + [o2], hi + [o1]):
+        W = a.shape[1]
+        a16, b16 = a.view(torch.int16).view(a.shape[0], 2 * W), b.view(torch.int16).view(b.shape[0], 2 * W)
+        assert torch.equal(a16[:, :W], b16[:, :W])                  # hi halves
+        assert (b.view(b.shape[0], W)[:, W // 2:] == 7.0).all()     # lo halves untouched
