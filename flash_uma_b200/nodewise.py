@@ -126,16 +126,21 @@ def balance_channels_batched(emb, target, natoms, batch, start_idx, end_idx, tar
     equals ``target + target_offset`` (stand-in for FAIRChem's charge/spin
     channel balancing called at ``model.py:213-216``). ``partitioned``: ``emb`` holds this
     rank's atoms of systems spread over the ranks of ``group``; the per-system sums are
-    all-reduced across them (differentiably) before the correction."""
+    all-reduced across them (differentiably) before the correction.
+
+    The per-system sums and the broadcast back to the atoms are one-hot contractions rather
+    than index_add / index_select, whose GPU implementations (and their backward) add with
+    atomics: forces stay bitwise reproducible run to run."""
     chans = emb[:, 0, start_idx:end_idx]
     nsys = natoms.shape[0]
-    sums = torch.zeros(nsys, chans.shape[1], dtype=emb.dtype, device=emb.device).index_add(0, batch, chans)
+    onehot = torch.nn.functional.one_hot(batch, nsys).to(emb.dtype)          # [N, nsys]
+    sums = onehot.t() @ chans
     if partitioned:
         import torch.distributed as dist
         import torch.distributed.nn.functional as dfn
         sums = dfn.all_reduce(sums, op=dist.ReduceOp.SUM, group=group if group is not None else dist.group.WORLD)
     tgt = (target.to(emb.dtype) + target_offset)[:, None]
-    corr = ((tgt - sums) / natoms.to(emb.dtype)[:, None]).index_select(0, batch)
+    corr = onehot @ ((tgt - sums) / natoms.to(emb.dtype)[:, None])
     out = emb.clone()
     out[:, 0, start_idx:end_idx] = chans + corr
     return out
