@@ -37,7 +37,7 @@ _SIGS = {
     "fuma_linear": [_P, _I64, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _P, _P],
     "fuma_split_tf32": [_P, _I64, _P, _P, _P],
     "fuma_linear_f16x3": [_P, _I64, _I32, _P, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _P, _P],
-    "fuma_linear_f16": [_P, _I64, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _P, _P],
+    "fuma_linear_f16": [_P, _I64, _P, _I64, _F32, _P, _I64, _I32, _I32, _P, _I64, _I32, _P, _P],
     "fuma_split_rows_f16": [_P, _I64, _I64, _I32, _P, _I64, _P, _P],
     "fuma_split_f16": [_P, _I64, _F32, _P, _P, _P],
     "fuma_neighbor_list": [_P, _I64, _P, _P, ctypes.c_double, _I32, _P, _I64, _P, _P, _P, _P, _P, _P],
@@ -106,6 +106,10 @@ def stream_of(t: torch.Tensor) -> int:
 for _name in ("fuma_ln_silu_fwd", "fuma_ln_silu_bwd", "fuma_gather_fwd", "fuma_gather_bwd", "fuma_gating_fwd",
               "fuma_gating_bwd", "fuma_rotate_scatter_bwd", "fuma_init_scatter_bwd"):
     _SIGS[_name + "_f16x3"] = _SIGS[_name][:-1] + [_I32, _P, _P]   # ..., parts, err_flag, stream
+for _name in ("fuma_gather_fwd", "fuma_gather_bwd", "fuma_gating_fwd", "fuma_gating_bwd", "fuma_rotate_scatter_bwd"):
+    # ..., parts, act_half (fp16 radial / conv results), err_flag, stream
+    _SIGS[_name + "_f16x3"] = _SIGS[_name][:-1] + [_I32, _I32, _P, _P]
+_SIGS["fuma_rotate_scatter_fwd_f16x3"] = _SIGS["fuma_rotate_scatter_fwd"][:-1] + [_I32, _P]
 
 KERNELS_PER_CALL = {name: 1 for name in _SIGS}
 KERNELS_PER_CALL["fuma_gather_bwd"] = 3
@@ -119,6 +123,7 @@ KERNELS_PER_CALL["fuma_rotate_scatter_fwd"] = 2
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd"] = 2
 KERNELS_PER_CALL["fuma_gather_bwd_f16x3"] = 3
 KERNELS_PER_CALL["fuma_rotate_scatter_bwd_f16x3"] = 2
+KERNELS_PER_CALL["fuma_rotate_scatter_fwd_f16x3"] = 2
 
 
 def launches_of(name: str, args) -> int:

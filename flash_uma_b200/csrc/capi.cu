@@ -177,7 +177,7 @@ int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta
 
 static int gather_fwd_impl(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                     const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
-                    float* X_m0, float* X_m1, float* X_m2, int split, int* err_flag, void* stream) {
+                    float* X_m0, float* X_m1, float* X_m2, int split, bool act_half, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gather_fwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "gather_fwd: bad sizes");
@@ -186,21 +186,21 @@ static int gather_fwd_impl(const float* x, const int64_t* idx_i, const int64_t* 
   REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(rad, "rad"); REQUIRE_ALIGNED(csd, "csd");
   REQUIRE_ALIGNED(X_m0, "X_m0"); REQUIRE_ALIGNED(X_m1, "X_m1"); REQUIRE_ALIGNED(X_m2, "X_m2");
   BIND(x);
-  launch_gather_fwd(x, idx_i, idx_j, wigner, rad, csd, batch, X_m0, X_m1, X_m2, E, C, split, err_flag, (cudaStream_t)stream);
+  launch_gather_fwd(x, idx_i, idx_j, wigner, rad, csd, batch, X_m0, X_m1, X_m2, E, C, split, err_flag, (cudaStream_t)stream, act_half);
   return launched("gather_fwd");
 }
 
 int fuma_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                     const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
                     float* X_m0, float* X_m1, float* X_m2, void* stream) {
-  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, false, nullptr, stream);
+  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, false, false, nullptr, stream);
 }
 
 int fuma_gather_fwd_f16x3(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                     const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
-                    float* X_m0, float* X_m1, float* X_m2, int32_t parts, int* err_flag, void* stream) {
+                    float* X_m0, float* X_m1, float* X_m2, int32_t parts, int32_t act_half, int* err_flag, void* stream) {
   REQUIRE(parts == 1 || parts == 2, "gather_fwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
-  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, parts, err_flag, stream);
+  return gather_fwd_impl(x, idx_i, idx_j, wigner, rad, csd, batch, N, E, C, X_m0, X_m1, X_m2, parts, act_half != 0, err_flag, stream);
 }
 
 static int gather_bwd_impl(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
@@ -208,7 +208,7 @@ static int gather_bwd_impl(const float* g_X_m0, const float* g_X_m1, const float
                     const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
                     const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
                     float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
-                    int split, int* err_flag, void* stream) {
+                    int split, bool act_half, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gather_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "gather_bwd: bad sizes");
@@ -225,7 +225,7 @@ static int gather_bwd_impl(const float* g_X_m0, const float* g_X_m1, const float
   }
   BIND(x);
   launch_gather_bwd(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
-                    src_col, g_x, g_wigner, g_rad, scratch, N, C, split, err_flag, (cudaStream_t)stream);
+                    src_col, g_x, g_wigner, g_rad, scratch, N, C, split, err_flag, (cudaStream_t)stream, act_half);
   return launched("gather_bwd");
 }
 
@@ -236,7 +236,7 @@ int fuma_gather_bwd(const float* g_X_m0, const float* g_X_m1, const float* g_X_m
                     float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
                     void* stream) {
   return gather_bwd_impl(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
-                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, false, nullptr, stream);
+                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, false, false, nullptr, stream);
 }
 
 int fuma_gather_bwd_f16x3(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
@@ -244,14 +244,14 @@ int fuma_gather_bwd_f16x3(const float* g_X_m0, const float* g_X_m1, const float*
                     const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
                     const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
                     float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
-                    int32_t parts, int* err_flag, void* stream) {
+                    int32_t parts, int32_t act_half, int* err_flag, void* stream) {
   REQUIRE(parts == 1 || parts == 2, "gather_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
   return gather_bwd_impl(g_X_m0, g_X_m1, g_X_m2, x, idx_i, wigner, rad, csd, batch, dst_row_ptr, dst_col, src_row_ptr,
-                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, parts, err_flag, stream);
+                         src_col, N, E, C, scratch, scratch_floats, g_x, g_wigner, g_rad, parts, act_half != 0, err_flag, stream);
 }
 
 static int gating_fwd_impl(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
-                    float* Z_m1, float* Z_m2, int split, int* err_flag, void* stream) {
+                    float* Z_m1, float* Z_m2, int split, bool act_half, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gating_fwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(E >= 0, "gating_fwd: bad E");
@@ -260,24 +260,24 @@ static int gating_fwd_impl(const float* Y_m0, const float* Y_m1, const float* Y_
   REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
   REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1"); REQUIRE_ALIGNED(Z_m2, "Z_m2");
   BIND(Y_m0);
-  launch_gating_fwd(Y_m0, Y_m1, Y_m2, Z_m0, Z_m1, Z_m2, E, C, split, err_flag, (cudaStream_t)stream);
+  launch_gating_fwd(Y_m0, Y_m1, Y_m2, Z_m0, Z_m1, Z_m2, E, C, split, err_flag, (cudaStream_t)stream, act_half);
   return launched("gating_fwd");
 }
 
 int fuma_gating_fwd(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
                     float* Z_m1, float* Z_m2, void* stream) {
-  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, false, nullptr, stream);
+  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, false, false, nullptr, stream);
 }
 
 int fuma_gating_fwd_f16x3(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
-                    float* Z_m1, float* Z_m2, int32_t parts, int* err_flag, void* stream) {
+                    float* Z_m1, float* Z_m2, int32_t parts, int32_t act_half, int* err_flag, void* stream) {
   REQUIRE(parts == 1 || parts == 2, "gating_fwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
-  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, parts, err_flag, stream);
+  return gating_fwd_impl(Y_m0, Y_m1, Y_m2, E, C, Z_m0, Z_m1, Z_m2, parts, act_half != 0, err_flag, stream);
 }
 
 static int gating_bwd_impl(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                     const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
-                    float* g_Y_m2, int split, int* err_flag, void* stream) {
+                    float* g_Y_m2, int split, bool act_half, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "gating_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(E >= 0, "gating_bwd: bad E");
@@ -287,26 +287,27 @@ static int gating_bwd_impl(const float* g_Z_m0, const float* g_Z_m1, const float
   REQUIRE_ALIGNED(Y_m0, "Y_m0"); REQUIRE_ALIGNED(Y_m1, "Y_m1"); REQUIRE_ALIGNED(Y_m2, "Y_m2");
   REQUIRE_ALIGNED(g_Y_m0, "g_Y_m0"); REQUIRE_ALIGNED(g_Y_m1, "g_Y_m1"); REQUIRE_ALIGNED(g_Y_m2, "g_Y_m2");
   BIND(Y_m0);
-  launch_gating_bwd(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, g_Y_m0, g_Y_m1, g_Y_m2, E, C, split, err_flag, (cudaStream_t)stream);
+  launch_gating_bwd(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, g_Y_m0, g_Y_m1, g_Y_m2, E, C, split, err_flag, (cudaStream_t)stream, act_half);
   return launched("gating_bwd");
 }
 
 int fuma_gating_bwd(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                     const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
                     float* g_Y_m2, void* stream) {
-  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, false, nullptr, stream);
+  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, false, false, nullptr, stream);
 }
 
 int fuma_gating_bwd_f16x3(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                     const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
-                    float* g_Y_m2, int32_t parts, int* err_flag, void* stream) {
+                    float* g_Y_m2, int32_t parts, int32_t act_half, int* err_flag, void* stream) {
   REQUIRE(parts == 1 || parts == 2, "gating_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
-  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, parts, err_flag, stream);
+  return gating_bwd_impl(g_Z_m0, g_Z_m1, g_Z_m2, Y_m0, Y_m1, Y_m2, E, C, g_Y_m0, g_Y_m1, g_Y_m2, parts, act_half != 0, err_flag, stream);
 }
 
-int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
-                            const float* env, const float* x_res, const int32_t* row_ptr, const int32_t* col_idx,
-                            int64_t N, int64_t E, int32_t C, float* x_out, void* stream) {
+static int rotate_scatter_fwd_impl(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
+                                   const float* env, const float* x_res, const int32_t* row_ptr,
+                                   const int32_t* col_idx, int64_t N, int64_t E, int32_t C, float* x_out,
+                                   int32_t act_half, void* stream) {
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "rotate_scatter_fwd: bad sizes");
   if (N == 0) return FUMA_OK;
@@ -315,14 +316,28 @@ int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z
   REQUIRE_ALIGNED(x_res, "x_res"); REQUIRE_ALIGNED(x_out, "x_out");
   if (E > 0) { REQUIRE_ALIGNED(Z_m0, "Z_m0"); REQUIRE_ALIGNED(Z_m1, "Z_m1"); REQUIRE_ALIGNED(Z_m2, "Z_m2"); }
   BIND(x_res);
-  launch_rotate_scatter_fwd(row_ptr, col_idx, Z_m0, Z_m1, Z_m2, wigner, env, x_res, x_out, N, C, (cudaStream_t)stream);
+  launch_rotate_scatter_fwd(row_ptr, col_idx, Z_m0, Z_m1, Z_m2, wigner, env, x_res, x_out, N, C, (cudaStream_t)stream,
+                            act_half != 0);
   return launched("rotate_scatter_fwd");
+}
+
+int fuma_rotate_scatter_fwd(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
+                            const float* env, const float* x_res, const int32_t* row_ptr, const int32_t* col_idx,
+                            int64_t N, int64_t E, int32_t C, float* x_out, void* stream) {
+  return rotate_scatter_fwd_impl(Z_m0, Z_m1, Z_m2, wigner, env, x_res, row_ptr, col_idx, N, E, C, x_out, 0, stream);
+}
+
+int fuma_rotate_scatter_fwd_f16x3(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
+                                  const float* env, const float* x_res, const int32_t* row_ptr, const int32_t* col_idx,
+                                  int64_t N, int64_t E, int32_t C, float* x_out, int32_t act_half, void* stream) {
+  return rotate_scatter_fwd_impl(Z_m0, Z_m1, Z_m2, wigner, env, x_res, row_ptr, col_idx, N, E, C, x_out, act_half,
+                                 stream);
 }
 
 static int rotate_scatter_bwd_impl(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
                             const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
                             int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
-                            float* g_wigner, float* g_env, int split, int* err_flag, void* stream) {
+                            float* g_wigner, float* g_env, int split, bool act_half, int* err_flag, void* stream) {
   REQUIRE(!split || C % 8 == 0, "rotate_scatter_bwd_f16x3: the split output needs C %% 8 == 0");
   if (int r = check_C(C)) return r;
   REQUIRE(N >= 0 && E >= 0, "rotate_scatter_bwd: bad sizes");
@@ -335,7 +350,7 @@ static int rotate_scatter_bwd_impl(const float* g_out, const float* Z_m0, const 
   REQUIRE_ALIGNED(g_Z_m2, "g_Z_m2");
   BIND(g_out);
   launch_rotate_scatter_bwd(row_ptr, col_idx, g_out, Z_m0, Z_m1, Z_m2, wigner, env, g_Z_m0, g_Z_m1, g_Z_m2, g_wigner,
-                            g_env, N, C, split, err_flag, (cudaStream_t)stream);
+                            g_env, N, C, split, err_flag, (cudaStream_t)stream, act_half);
   return launched("rotate_scatter_bwd");
 }
 
@@ -344,16 +359,16 @@ int fuma_rotate_scatter_bwd(const float* g_out, const float* Z_m0, const float* 
                             int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
                             float* g_wigner, float* g_env, void* stream) {
   return rotate_scatter_bwd_impl(g_out, Z_m0, Z_m1, Z_m2, wigner, env, row_ptr, col_idx, N, E, C, g_Z_m0, g_Z_m1,
-                                 g_Z_m2, g_wigner, g_env, false, nullptr, stream);
+                                 g_Z_m2, g_wigner, g_env, false, false, nullptr, stream);
 }
 
 int fuma_rotate_scatter_bwd_f16x3(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
                             const float* wigner, const float* env, const int32_t* row_ptr, const int32_t* col_idx,
                             int64_t N, int64_t E, int32_t C, float* g_Z_m0, float* g_Z_m1, float* g_Z_m2,
-                            float* g_wigner, float* g_env, int32_t parts, int* err_flag, void* stream) {
+                            float* g_wigner, float* g_env, int32_t parts, int32_t act_half, int* err_flag, void* stream) {
   REQUIRE(parts == 1 || parts == 2, "rotate_scatter_bwd_f16x3: parts=%d must be 1 (hi) or 2 (hi and lo)", parts);
   return rotate_scatter_bwd_impl(g_out, Z_m0, Z_m1, Z_m2, wigner, env, row_ptr, col_idx, N, E, C, g_Z_m0, g_Z_m1,
-                                 g_Z_m2, g_wigner, g_env, parts, err_flag, stream);
+                                 g_Z_m2, g_wigner, g_env, parts, act_half != 0, err_flag, stream);
 }
 
 int fuma_init_scatter_fwd(const float* rad, const float* wigner, const float* env, const int64_t* Z,
@@ -455,11 +470,13 @@ int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* 
 }
 
 int fuma_linear_f16(const float* A, int64_t lda, const void* W_hi, int64_t ldw, float w_scale_inv, const float* bias,
-                    int64_t M, int32_t N, int32_t K, float* C, int64_t ldc, int* err_flag, void* stream) {
+                    int64_t M, int32_t N, int32_t K, void* C, int64_t ldc, int32_t c_half, int* err_flag,
+                    void* stream) {
   REQUIRE(M >= 0 && M < (int64_t(1) << 31), "linear_f16: M=%lld out of range", (long long)M);
   REQUIRE(N > 0 && N % 16 == 0 && N <= 65536 * 16, "linear_f16: N=%d must be a positive multiple of 16", N);
   REQUIRE(K > 0 && K % 8 == 0, "linear_f16: K=%d must be a positive multiple of 8", K);
-  REQUIRE(lda >= K && lda % 8 == 0 && ldc >= N && ldc % 4 == 0, "linear_f16: bad leading dimensions of A or C");
+  REQUIRE(lda >= K && lda % 8 == 0 && ldc >= N && ldc % (c_half ? 8 : 4) == 0,
+          "linear_f16: bad leading dimensions of A or C");
   REQUIRE(ldw >= K && ldw % 8 == 0, "linear_f16: ldw=%lld must be >= K and a multiple of 8", (long long)ldw);
   REQUIRE(w_scale_inv > 0.0f, "linear_f16: w_scale_inv must be positive");
   if (M == 0) return FUMA_OK;
@@ -467,8 +484,8 @@ int fuma_linear_f16(const float* A, int64_t lda, const void* W_hi, int64_t ldw, 
   REQUIRE_ALIGNED(A, "A"); REQUIRE_ALIGNED(W_hi, "W_hi"); REQUIRE_ALIGNED(C, "C");
   if (bias) REQUIRE_ALIGNED(bias, "bias");
   BIND(A);
-  const int r = launch_gemm_f16x3(A, lda, true, W_hi, W_hi, ldw, w_scale_inv, bias, C, ldc, M, N, K, err_flag,
-                                  (cudaStream_t)stream, true);
+  const int r = launch_gemm_f16x3(A, lda, true, W_hi, W_hi, ldw, w_scale_inv, bias, static_cast<float*>(C), ldc, M, N,
+                                  K, err_flag, (cudaStream_t)stream, true, c_half != 0);
   if (r == -1) return fail(FUMA_E_INVALID, "linear_f16: could not encode the TMA tensor maps: %s", gemm_map_error());
   if (r != 0) return fail(r, "linear_f16: launch failed: %s", cudaGetErrorString((cudaError_t)r));
   return launched("linear_f16");

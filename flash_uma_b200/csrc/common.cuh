@@ -143,6 +143,46 @@ __device__ __forceinline__ void st_out4(float* row, int W, int col, float4 v, in
   if (split == 2) __stcs(reinterpret_cast<uint2*>(rb + 2 * (W + col)), lo);
 }
 
+// ---- 16-bit activation storage (the single-product mode) ------------------------------------
+// The single-product GEMMs can write their results as fp16 (radial output, conv1 Y, conv2
+// output); the kernels that read them take the pointer as float* and, with kHalf, treat it as
+// __half* with the same element offsets.
+__device__ __forceinline__ float4 h4_to_f4(uint2 u) {
+  __half2 a, b;
+  memcpy(&a, &u.x, 4);
+  memcpy(&b, &u.y, 4);
+  const float2 fa = __half22float2(a), fb = __half22float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+template <bool kHalf>
+__device__ __forceinline__ float4 ld4_act(const float* base, int64_t idx) {
+  if constexpr (kHalf) {
+    return h4_to_f4(__ldcs(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(base) + idx)));
+  } else {
+    return ld4_stream(base + idx);
+  }
+}
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+// copy 4 activation values into a 16-byte shared-memory slot (fp16: its first 8 bytes)
+template <bool kHalf>
+__device__ __forceinline__ void cp_act(float4* slot, const float* base, int64_t idx) {
+  if constexpr (kHalf) {
+    cp_async8(slot, reinterpret_cast<const __half*>(base) + idx);
+  } else {
+    cp_async16(slot, base + idx);
+  }
+}
+template <bool kHalf>
+__device__ __forceinline__ float4 sm_act(const float4* slot) {
+  if constexpr (kHalf) {
+    return h4_to_f4(*reinterpret_cast<const uint2*>(slot));
+  } else {
+    return *slot;
+  }
+}
+
 __device__ __forceinline__ void report_split_range(bool bad, int* err) {
   if (bad && err) atomicCAS(err, 0, kErrSplitRange);
 }

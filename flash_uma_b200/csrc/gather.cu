@@ -78,7 +78,7 @@ constexpr int kBwdWarps = 8;
 // second read of the indices and Wigner rows, and lowers the live registers of a launch: at 64
 // registers (4 blocks of 8 warps per SM) the pair measured 350 us against 375 us for one
 // 80-register kernel at 3 blocks (E = 120,000, B200).
-template <int PART>
+template <int PART, bool kH>
 __global__ void __launch_bounds__(kFwdWarps * 32, 4) gather_fwd_kernel(
     const float* __restrict__ x, const int64_t* __restrict__ idx_i, const int64_t* __restrict__ idx_j,
     const float* __restrict__ wig, const float* __restrict__ rad, const float* __restrict__ csd,
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 4) gather_fwd_kernel(
     __syncwarp();
     for (int c4 = lane; c4 < C4; c4 += 32) {
       const int co = c4 * 4;
-      const float* rr = rad + e * 12 * (int64_t)C + co;
+      const int64_t rr = e * 12 * (int64_t)C + co;   // element offset of the radial row (fp32 or fp16 rad)
       float* x0 = X0 + e * 6 * (int64_t)C;   // output rows; columns are co + slot * C
       float* x1 = X1 + e * 8 * (int64_t)C;
       float* x2 = X2 + e * 4 * (int64_t)C;
@@ -114,11 +114,11 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 4) gather_fwd_kernel(
         const float* xr = x + node * 9 * (int64_t)C + co;
         if constexpr (PART == 0) {
           const int64_t bsys = s ? bj : bi;
-          const float4 c0 = ld4_keep(xr), cs = ld4_keep(csd + bsys * C + co), r0 = ld4_stream(rr + s * C);
+          const float4 c0 = ld4_keep(xr), cs = ld4_keep(csd + bsys * C + co), r0 = ld4_act<kH>(rad, rr + s * C);
           float4 v[3];
 #pragma unroll
           for (int m = 0; m < 3; ++m) v[m] = ld4_keep(xr + (1 + m) * C);
-          const float4 r2 = ld4_stream(rr + (2 + s) * C), r6 = ld4_stream(rr + (6 + s) * C);
+          const float4 r2 = ld4_act<kH>(rad, rr + (2 + s) * C), r6 = ld4_act<kH>(rad, rr + (6 + s) * C);
           st_out4(x0, 6 * C, s * C + co, (c0 + cs) * r0, split, bad);
           st_out4(x1, 8 * C, (4 + s) * C + co, rot_row<3>(sw, 0, v) * r6, split, bad);
           st_out4(x0, 6 * C, (2 + s) * C + co, rot_row<3>(sw, 1, v) * r2, split, bad);
@@ -127,8 +127,8 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 4) gather_fwd_kernel(
           float4 v[5];
 #pragma unroll
           for (int m = 0; m < 5; ++m) v[m] = ld4_keep(xr + (4 + m) * C);
-          const float4 r4 = ld4_stream(rr + (4 + s) * C), r8 = ld4_stream(rr + (8 + s) * C),
-                       r10 = ld4_stream(rr + (10 + s) * C);
+          const float4 r4 = ld4_act<kH>(rad, rr + (4 + s) * C), r8 = ld4_act<kH>(rad, rr + (8 + s) * C),
+                       r10 = ld4_act<kH>(rad, rr + (10 + s) * C);
           st_out4(x2, 4 * C, (2 + s) * C + co, rot_row<5>(sw, 0, v) * r10, split, bad);
           st_out4(x1, 8 * C, (6 + s) * C + co, rot_row<5>(sw, 1, v) * r8, split, bad);
           st_out4(x0, 6 * C, (4 + s) * C + co, rot_row<5>(sw, 2, v) * r4, split, bad);
@@ -155,7 +155,7 @@ struct BwdSlots {
 // Wigner block are copied into shared memory (cp.async, double-buffered per warp) while the
 // current edge is computed, so two edges' loads are in flight per warp.
 // Dynamic shared memory: kBwdWarps * 2 * BwdSlots<PART>::n * 512 bytes.
-template <int SIDE, int PART>
+template <int SIDE, int PART, bool kH>
 __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
     const float* __restrict__ gX0, const float* __restrict__ gX1, const float* __restrict__ gX2,
     const float* __restrict__ x, const float* __restrict__ wig, const float* __restrict__ rad,
@@ -190,24 +190,24 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
           const float* g0 = gX0 + e * 6 * (int64_t)C + co;
           const float* g1 = gX1 + e * 8 * (int64_t)C + co;
           const float* g2 = gX2 + e * 4 * (int64_t)C + co;
-          const float* rr = rad + e * (int64_t)W + co;
+          const int64_t rr = e * (int64_t)W + co;   // element offset of the radial row
           if constexpr (PART == 0) {
             cp_async16(dst + 0 * 32, g0 + s * C);
             cp_async16(dst + 1 * 32, g0 + (2 + s) * C);
             cp_async16(dst + 2 * 32, g1 + s * C);
             cp_async16(dst + 3 * 32, g1 + (4 + s) * C);
-            cp_async16(dst + 4 * 32, rr + s * C);
-            cp_async16(dst + 5 * 32, rr + (2 + s) * C);
-            cp_async16(dst + 6 * 32, rr + (6 + s) * C);
+            cp_act<kH>(dst + 4 * 32, rad, rr + s * C);
+            cp_act<kH>(dst + 5 * 32, rad, rr + (2 + s) * C);
+            cp_act<kH>(dst + 6 * 32, rad, rr + (6 + s) * C);
           } else {
             cp_async16(dst + 0 * 32, g0 + (4 + s) * C);
             cp_async16(dst + 1 * 32, g1 + (2 + s) * C);
             cp_async16(dst + 2 * 32, g1 + (6 + s) * C);
             cp_async16(dst + 3 * 32, g2 + s * C);
             cp_async16(dst + 4 * 32, g2 + (2 + s) * C);
-            cp_async16(dst + 5 * 32, rr + (4 + s) * C);
-            cp_async16(dst + 6 * 32, rr + (8 + s) * C);
-            cp_async16(dst + 7 * 32, rr + (10 + s) * C);
+            cp_act<kH>(dst + 5 * 32, rad, rr + (4 + s) * C);
+            cp_act<kH>(dst + 6 * 32, rad, rr + (8 + s) * C);
+            cp_act<kH>(dst + 7 * 32, rad, rr + (10 + s) * C);
           }
         }
         if (lane < nw) cp_async4(&s_w[warp][b][lane], wig + e * kWig + woff + lane);
@@ -250,7 +250,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
         if constexpr (PART == 0) {
           const float4 z = f4(0.f);
           const float4 a0 = on ? src[0] : z, a2 = on ? src[32] : z, b0 = on ? src[64] : z, b4 = on ? src[96] : z;
-          const float4 r0 = on ? src[128] : z, r2 = on ? src[160] : z, r6 = on ? src[192] : z;
+          const float4 r0 = on ? sm_act<kH>(src + 128) : z, r2 = on ? sm_act<kH>(src + 160) : z,
+                       r6 = on ? sm_act<kH>(src + 192) : z;
           const float* D1 = sw;
           float4 r1[3];
           rot<3>(D1, v + 1, r1);
@@ -273,7 +274,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
           const float4 z = f4(0.f);
           const float4 a4 = on ? src[0] : z, b2 = on ? src[32] : z, b6 = on ? src[64] : z;
           const float4 c0 = on ? src[96] : z, c2 = on ? src[128] : z;
-          const float4 r4 = on ? src[160] : z, r8 = on ? src[192] : z, r10 = on ? src[224] : z;
+          const float4 r4 = on ? sm_act<kH>(src + 160) : z, r8 = on ? sm_act<kH>(src + 192) : z,
+                       r10 = on ? sm_act<kH>(src + 224) : z;
           const float* D2 = sw;
           float4 rv[5];
           rot<5>(D2, v, rv);
@@ -310,23 +312,31 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
   report_split_range(bad, err);
 }
 
-void launch_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wig, const float* rad,
+template <bool kH>
+void gather_fwd_launch(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wig, const float* rad,
                        const float* csd, const int64_t* batch, float* X0, float* X1, float* X2, int64_t E, int C,
                        int split, int* err, cudaStream_t s) {
   const int t = kFwdWarps * 32;
-  gather_fwd_kernel<0><<<grid_resident(gather_fwd_kernel<0>, t, E, kFwdWarps), t, 0, s>>>(
+  gather_fwd_kernel<0, kH><<<grid_resident(gather_fwd_kernel<0, kH>, t, E, kFwdWarps), t, 0, s>>>(
       x, idx_i, idx_j, wig, rad, csd, batch, X0, X1, X2, E, C, split, err);
-  gather_fwd_kernel<1><<<grid_resident(gather_fwd_kernel<1>, t, E, kFwdWarps), t, 0, s>>>(
+  gather_fwd_kernel<1, kH><<<grid_resident(gather_fwd_kernel<1, kH>, t, E, kFwdWarps), t, 0, s>>>(
       x, idx_i, idx_j, wig, rad, csd, batch, X0, X1, X2, E, C, split, err);
 }
 
-void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, const float* x, const int64_t* idx_i,
-                       const float* wig, const float* rad, const float* csd, const int64_t* batch,
-                       const int32_t* dst_ptr, const int32_t* dst_col, const int32_t* src_ptr, const int32_t* src_col,
-                       float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, int split, int* err,
-                       cudaStream_t s) {
-  (void)idx_i;
-  (void)scratch;   // the two-pass backward needs no scratch rows
+void launch_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wig, const float* rad,
+                       const float* csd, const int64_t* batch, float* X0, float* X1, float* X2, int64_t E, int C,
+                       int split, int* err, cudaStream_t s, bool act_half) {
+  if (act_half)
+    gather_fwd_launch<true>(x, idx_i, idx_j, wig, rad, csd, batch, X0, X1, X2, E, C, split, err, s);
+  else
+    gather_fwd_launch<false>(x, idx_i, idx_j, wig, rad, csd, batch, X0, X1, X2, E, C, split, err, s);
+}
+
+template <bool kH>
+void gather_bwd_launch(const float* gX0, const float* gX1, const float* gX2, const float* x, const float* wig,
+                       const float* rad, const float* csd, const int64_t* batch, const int32_t* dst_ptr,
+                       const int32_t* dst_col, const int32_t* src_ptr, const int32_t* src_col, float* g_x,
+                       float* g_wig, float* g_rad, int64_t N, int C, int split, int* err, cudaStream_t s) {
   const unsigned g = grid_for(N, kBwdWarps, 2);
   const int b = kBwdWarps * 32;
   const size_t sm0 = (size_t)kBwdWarps * 2 * BwdSlots<0>::n * 32 * sizeof(float4);
@@ -335,21 +345,36 @@ void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, con
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured >> (dev & 63) & 1)) {
-    cudaFuncSetAttribute(gather_bwd_side_kernel<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm0);
-    cudaFuncSetAttribute(gather_bwd_side_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
-    cudaFuncSetAttribute(gather_bwd_side_kernel<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm0);
-    cudaFuncSetAttribute(gather_bwd_side_kernel<0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+    cudaFuncSetAttribute(gather_bwd_side_kernel<1, 0, kH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm0);
+    cudaFuncSetAttribute(gather_bwd_side_kernel<1, 1, kH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+    cudaFuncSetAttribute(gather_bwd_side_kernel<0, 0, kH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm0);
+    cudaFuncSetAttribute(gather_bwd_side_kernel<0, 1, kH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
     configured |= uint64_t(1) << (dev & 63);
   }
   // target pass (writes g_x, g_wigner), then source pass (adds to them)
-  gather_bwd_side_kernel<1, 0><<<g, b, sm0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig,
-                                                 g_rad, N, C, split, err);
-  gather_bwd_side_kernel<1, 1><<<g, b, sm1, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x, g_wig,
-                                                 g_rad, N, C, split, err);
-  gather_bwd_side_kernel<0, 0><<<g, b, sm0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x, g_wig,
-                                                 g_rad, N, C, split, err);
-  gather_bwd_side_kernel<0, 1><<<g, b, sm1, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x, g_wig,
-                                                 g_rad, N, C, split, err);
+  gather_bwd_side_kernel<1, 0, kH><<<g, b, sm0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x,
+                                                     g_wig, g_rad, N, C, split, err);
+  gather_bwd_side_kernel<1, 1, kH><<<g, b, sm1, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, g_x,
+                                                     g_wig, g_rad, N, C, split, err);
+  gather_bwd_side_kernel<0, 0, kH><<<g, b, sm0, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x,
+                                                     g_wig, g_rad, N, C, split, err);
+  gather_bwd_side_kernel<0, 1, kH><<<g, b, sm1, s>>>(gX0, gX1, gX2, x, wig, rad, csd, batch, src_ptr, src_col, g_x,
+                                                     g_wig, g_rad, N, C, split, err);
+}
+
+void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, const float* x, const int64_t* idx_i,
+                       const float* wig, const float* rad, const float* csd, const int64_t* batch,
+                       const int32_t* dst_ptr, const int32_t* dst_col, const int32_t* src_ptr, const int32_t* src_col,
+                       float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, int split, int* err,
+                       cudaStream_t s, bool act_half) {
+  (void)idx_i;
+  (void)scratch;   // the two-pass backward needs no scratch rows
+  if (act_half)
+    gather_bwd_launch<true>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, src_ptr, src_col, g_x, g_wig,
+                            g_rad, N, C, split, err, s);
+  else
+    gather_bwd_launch<false>(gX0, gX1, gX2, x, wig, rad, csd, batch, dst_ptr, dst_col, src_ptr, src_col, g_x, g_wig,
+                             g_rad, N, C, split, err, s);
 }
 
 }  // namespace fuma

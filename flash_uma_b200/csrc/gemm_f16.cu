@@ -127,7 +127,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 }  // namespace
 
-template <int BN, int STAGES, bool kPre, bool kX3>
+// kOutHalf (single-product mode only): C is fp16 [M, ldc] (the 16-bit activation storage of
+// the "f16" mode), written through [32 x 32] fp16 boxes with a 64-byte swizzle; a finite result
+// at or beyond the fp16 limit records kErrRange.
+template <int BN, int STAGES, bool kPre, bool kX3, bool kOutHalf = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                  const __grid_constant__ CUtensorMap tmAl,
                                                                  const __grid_constant__ CUtensorMap tmWh,
@@ -137,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
                                                                  float w_scale_inv, int M, int N, int K, int64_t ldc,
                                                                  int* err) {
   static_assert(kX3 || kPre, "the single-product mode takes pre-split operands");
+  static_assert(!kOutHalf || !kX3, "fp16 results belong to the single-product mode");
   using L = F16Smem<BN, STAGES, kPre, kX3>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -299,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
     // ---------------- epilogue (warps 6-9)
     const int q = warp & 3;
     int lt = 0, nbox = 0;
+    bool out_bad = false;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
       const int b = kAcc == 2 ? (lt & 1) : 0;
       bool ok = mbar_wait(&bar_acc_full[b], (lt / kAcc) & 1, abort_flag, err, kErrWaitAcc);
@@ -326,15 +331,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
           uint8_t* box = smem_c + (q * 2 + (nbox & 1)) * 4096;
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           __syncwarp();
+          if constexpr (kOutHalf) {
+            // row = lane, 64 bytes (32 halves); 16-byte chunk j of row r at j ^ ((r >> 1) & 3)
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            float o[4];
+            for (int jj = 0; jj < 4; ++jj) {
+              uint32_t h[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              o[u] = fmaf(__uint_as_float(rc[4 * jj + u]), kLoScaleInv, __uint_as_float(rm[4 * jj + u])) * w_scale_inv;
-            float4 v = make_float4(o[0], o[1], o[2], o[3]);
-            if (bias) v = v + ld4_keep(bias + n0 + c0 + 4 * jj);
-            *reinterpret_cast<float4*>(box + lane * 128 + ((jj ^ (lane & 7)) << 4)) = v;
+              for (int u = 0; u < 4; ++u) {
+                const int c = 8 * jj + 2 * u;
+                float a = __uint_as_float(rm[c]) * w_scale_inv, b = __uint_as_float(rm[c + 1]) * w_scale_inv;
+                if (bias) {
+                  a += bias[n0 + c0 + c];
+                  b += bias[n0 + c0 + c + 1];
+                }
+                const float m = fmaxf(fabsf(a), fabsf(b));
+                out_bad |= (m >= 65520.0f) & (m <= 3.402823466e38f);
+                h[u] = h2_bits(__floats2half2_rn(a, b));
+              }
+              *reinterpret_cast<uint4*>(box + lane * 64 + ((jj ^ ((lane >> 1) & 3)) << 4)) =
+                  make_uint4(h[0], h[1], h[2], h[3]);
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              float o[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                o[u] = fmaf(__uint_as_float(rc[4 * jj + u]), kLoScaleInv, __uint_as_float(rm[4 * jj + u])) * w_scale_inv;
+              float4 v = make_float4(o[0], o[1], o[2], o[3]);
+              if (bias) v = v + ld4_keep(bias + n0 + c0 + 4 * jj);
+              *reinterpret_cast<float4*>(box + lane * 128 + ((jj ^ (lane & 7)) << 4)) = v;
+            }
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
@@ -357,7 +384,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
             for (int u = 0; u < 16; ++u) rc[u] = 0u;
           }
           if (row < M) {
-            float* out = C + (int64_t)row * ldc + n0 + c0;
   #pragma unroll
             for (int jj = 0; jj < 16; jj += 4) {
               float o[4];
@@ -366,7 +392,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
                 o[u] = fmaf(__uint_as_float(rc[jj + u]), kLoScaleInv, __uint_as_float(rm[jj + u])) * w_scale_inv;
               float4 v = make_float4(o[0], o[1], o[2], o[3]);
               if (bias) v = v + ld4_keep(bias + n0 + c0 + jj);
-              st4(out + jj, v);
+              if constexpr (kOutHalf) {
+                const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+                out_bad |= (m >= 65520.0f) & (m <= 3.402823466e38f);
+                __half* out = reinterpret_cast<__half*>(C) + (int64_t)row * ldc + n0 + c0 + jj;
+                *reinterpret_cast<uint2*>(out) =
+                    make_uint2(h2_bits(__floats2half2_rn(v.x, v.y)), h2_bits(__floats2half2_rn(v.z, v.w)));
+              } else {
+                st4(C + (int64_t)row * ldc + n0 + c0 + jj, v);
+              }
             }
           }
         }
@@ -379,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
       if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
       __syncwarp();
     }
+    if (kOutHalf && out_bad && err) atomicCAS(err, 0, (int)kErrRange);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -577,12 +612,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
 
 namespace {
 
-template <int BN, int STAGES, bool kPre, bool kX3>
+template <int BN, int STAGES, bool kPre, bool kX3, bool kOutHalf = false>
 cudaError_t launch_f16(const CUtensorMap& a, const CUtensorMap& al, const CUtensorMap& wh, const CUtensorMap& wl,
                        const CUtensorMap& mc, float* C, const float* bias, float w_scale_inv, int M, int N, int K, int64_t ldc, int* err,
                        cudaStream_t s) {
   using L = F16Smem<BN, STAGES, kPre, kX3>;
-  auto kern = gemm_f16x3_kernel<BN, STAGES, kPre, kX3>;
+  auto kern = gemm_f16x3_kernel<BN, STAGES, kPre, kX3, kOutHalf>;
   static thread_local uint64_t configured = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -631,14 +666,15 @@ cudaError_t launch_f16_t(const CUtensorMap& a, const CUtensorMap& al, const CUte
 }
 
 // single-product mode (pre-split A): half the operand bytes per stage, so deeper rings
+template <bool kOutHalf>
 cudaError_t launch_bn_x1(int BN, const CUtensorMap& a, const CUtensorMap& wh, const CUtensorMap& mc, float* C,
                          const float* bias, float inv, int M, int N, int K, int64_t ldc, int* err, cudaStream_t s) {
   switch (BN) {
-    case 256: return launch_f16<256, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
-    case 128: return launch_f16<128, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
-    case 64: return launch_f16<64, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
-    case 32: return launch_f16<32, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
-    default: return launch_f16<16, 8, true, false>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 256: return launch_f16<256, 8, true, false, kOutHalf>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 128: return launch_f16<128, 8, true, false, kOutHalf>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 64: return launch_f16<64, 8, true, false, kOutHalf>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    case 32: return launch_f16<32, 8, true, false, kOutHalf>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
+    default: return launch_f16<16, 8, true, false, kOutHalf>(a, a, wh, wh, mc, C, bias, inv, M, N, K, ldc, err, s);
   }
 }
 
@@ -668,7 +704,7 @@ bool use_t(int K) {
 
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,
                       float w_scale_inv, const float* bias, float* C, int64_t ldc, int64_t M, int N, int K, int* err,
-                      cudaStream_t s, bool x1) {
+                      cudaStream_t s, bool x1, bool out_half) {
   // single-product mode: one accumulator, so 256-wide tiles stay double-buffered at any K
   const int BN = (N % 256 == 0 && (x1 || K >= g_bn256_min_k)) ? 256
                  : (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : (N % 32 == 0) ? 32 : 16;
@@ -705,14 +741,18 @@ int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_h
     return -1;
   if (!make_map_t(&ml, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, W_lo, N, K, ldw * 2, kBK, BN, CU_TENSOR_MAP_SWIZZLE_64B))
     return -1;
-  // output: fp32 [M, N] rows ldc apart, [32 x 32] boxes with 128-byte swizzle (unused for BN = 16)
+  // output: fp32 [M, N] rows ldc apart, [32 x 32] boxes with 128-byte swizzle, or fp16 [M, N]
+  // (ldc in halves) with 64-byte boxes and a 64-byte swizzle (unused for BN = 16)
   CUtensorMap mc = ma;
-  if (BN >= 32 &&
-      !make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, ldc * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (BN >= 32 && !(out_half ? make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, C, M, N, ldc * 2, 32, 32,
+                                          CU_TENSOR_MAP_SWIZZLE_64B)
+                             : make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, ldc * 4, 32, 32,
+                                          CU_TENSOR_MAP_SWIZZLE_128B)))
     return -1;
   const int m = (int)M;
   const cudaError_t st =
-      x1 ? launch_bn_x1(BN, ma, mh, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s)
+      x1 ? (out_half ? launch_bn_x1<true>(BN, ma, mh, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s)
+                     : launch_bn_x1<false>(BN, ma, mh, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s))
       : a_split ? launch_bn<true>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s)
                 : launch_bn<false>(BN, ma, mal, mh, ml, mc, C, bias, w_scale_inv, m, N, K, ldc, err, s);
   return st == cudaSuccess ? 0 : (int)st;

@@ -18,18 +18,20 @@ void launch_node_vec3_segment(const int32_t* src_ptr, const int32_t* src_col, co
 
 void launch_gather_fwd(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wig, const float* rad,
                        const float* csd, const int64_t* batch, float* X0, float* X1, float* X2, int64_t E, int C,
-                       int split, int* err, cudaStream_t s);
+                       int split, int* err, cudaStream_t s, bool act_half = false);
 void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, const float* x, const int64_t* idx_i,
                        const float* wig, const float* rad, const float* csd, const int64_t* batch,
                        const int32_t* dst_ptr, const int32_t* dst_col, const int32_t* src_ptr, const int32_t* src_col,
                        float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, int split, int* err,
-                       cudaStream_t s);
+                       cudaStream_t s, bool act_half = false);
 
+// act_half (the single-product mode's 16-bit activation storage): Y (gating), rad (gather) and
+// the conv2 output Z (rotate-scatter) are fp16 arrays passed as float*, with the same offsets.
 void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,
-                       int C, int split, int* err, cudaStream_t s);
+                       int C, int split, int* err, cudaStream_t s, bool act_half = false);
 void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, const float* Y0, const float* Y1,
                        const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, int split, int* err,
-                       cudaStream_t s);
+                       cudaStream_t s, bool act_half = false);
 
 void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float* out, float* mean, float* rstd,
                         int64_t M, int D, float eps, int split, int* err, cudaStream_t s);
@@ -38,11 +40,11 @@ void launch_ln_silu_bwd(const float* x, const float* gamma, const float* beta, c
 
 void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* Z0, const float* Z1,
                                const float* Z2, const float* wig, const float* env, const float* x_res, float* x_out,
-                               int64_t N, int C, cudaStream_t s);
+                               int64_t N, int C, cudaStream_t s, bool act_half = false);
 void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* Z0,
                                const float* Z1, const float* Z2, const float* wig, const float* env, float* gZ0,
                                float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, int split,
-                               int* err, cudaStream_t s);
+                               int* err, cudaStream_t s, bool act_half = false);
 void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,
                              const float* env, const int64_t* Z, const int64_t* batch, const float* W_sphere,
                              const float* csd, float* x_out, int64_t N, int C, cudaStream_t s);
@@ -75,7 +77,7 @@ void launch_csr_permute(int ngraphs, const int32_t* const* row_ptr, const int32_
                         int64_t N, int32_t* const* new_row_ptr, int32_t* const* new_col, cudaStream_t s);
 int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_hi, const void* W_lo, int64_t ldw,
                       float w_scale_inv, const float* bias, float* C, int64_t ldc, int64_t M, int N, int K, int* err,
-                      cudaStream_t s, bool x1 = false);
+                      cudaStream_t s, bool x1 = false, bool out_half = false);
 void launch_split_rows_f16(const float* x, int64_t lda, int64_t M, int K, void* out, int64_t ldp, int* err,
                            cudaStream_t s);
 void launch_split_f16(const float* x, void* hi, void* lo, float scale, int64_t n, cudaStream_t s);

@@ -17,7 +17,8 @@ __device__ __forceinline__ float4 sig4(float4 a) {
 }
 }  // namespace
 
-// One thread per (edge, 4 channels).
+// One thread per (edge, 4 channels). kH: Y is stored as fp16 (the single-product mode).
+template <bool kH>
 __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict__ Y0, const float* __restrict__ Y1,
                                                          const float* __restrict__ Y2, float* __restrict__ Z0,
                                                          float* __restrict__ Z1, float* __restrict__ Z2, int64_t E,
@@ -28,14 +29,13 @@ __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = t / C4;
     const int co = (int)(t - e * C4) * 4;
-    const float* y0 = Y0 + e * 5 * (int64_t)C + co;
-    const float* y1 = Y1 + e * 4 * (int64_t)C + co;
-    const float* y2 = Y2 + e * 2 * (int64_t)C + co;
+    const int64_t y0 = e * 5 * (int64_t)C + co, y1 = e * 4 * (int64_t)C + co, y2 = e * 2 * (int64_t)C + co;
     // every load of the row first (11 x 16 bytes in flight per thread), then the arithmetic
-    const float4 p0 = ld4_stream(y0), p1 = ld4_stream(y0 + C), a = ld4_stream(y0 + 2 * C);
-    const float4 y3 = ld4_stream(y0 + 3 * C), y4 = ld4_stream(y0 + 4 * C);
-    const float4 u0 = ld4_stream(y1), u1 = ld4_stream(y1 + C), u2 = ld4_stream(y1 + 2 * C), u3 = ld4_stream(y1 + 3 * C);
-    const float4 w0 = ld4_stream(y2), w1 = ld4_stream(y2 + C);
+    const float4 p0 = ld4_act<kH>(Y0, y0), p1 = ld4_act<kH>(Y0, y0 + C), a = ld4_act<kH>(Y0, y0 + 2 * C);
+    const float4 y3 = ld4_act<kH>(Y0, y0 + 3 * C), y4 = ld4_act<kH>(Y0, y0 + 4 * C);
+    const float4 u0 = ld4_act<kH>(Y1, y1), u1 = ld4_act<kH>(Y1, y1 + C), u2 = ld4_act<kH>(Y1, y1 + 2 * C),
+                 u3 = ld4_act<kH>(Y1, y1 + 3 * C);
+    const float4 w0 = ld4_act<kH>(Y2, y2), w1 = ld4_act<kH>(Y2, y2 + C);
     const float4 g0 = sig4(p0), g1 = sig4(p1);
     float* z0 = Z0 + e * 3 * (int64_t)C;
     float* z1 = Z1 + e * 4 * (int64_t)C;
@@ -53,6 +53,7 @@ __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict
   report_split_range(bad, err);
 }
 
+template <bool kH>
 __global__ void __launch_bounds__(256) gating_bwd_kernel(
     const float* __restrict__ gZ0, const float* __restrict__ gZ1, const float* __restrict__ gZ2,
     const float* __restrict__ Y0, const float* __restrict__ Y1, const float* __restrict__ Y2,
@@ -64,17 +65,16 @@ __global__ void __launch_bounds__(256) gating_bwd_kernel(
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = t / C4;
     const int co = (int)(t - e * C4) * 4;
-    const float* y0 = Y0 + e * 5 * (int64_t)C + co;
-    const float* y1 = Y1 + e * 4 * (int64_t)C + co;
-    const float* y2 = Y2 + e * 2 * (int64_t)C + co;
+    const int64_t y0 = e * 5 * (int64_t)C + co, y1 = e * 4 * (int64_t)C + co, y2 = e * 2 * (int64_t)C + co;
     const float* q0 = gZ0 + e * 3 * (int64_t)C + co;
     const float* q1 = gZ1 + e * 4 * (int64_t)C + co;
     const float* q2 = gZ2 + e * 2 * (int64_t)C + co;
-    const float4 g0 = sig4(ld4_stream(y0)), g1 = sig4(ld4_stream(y0 + C));
-    const float4 a = ld4_stream(y0 + 2 * C), sa = sig4(a);
-    const float4 y3 = ld4_stream(y0 + 3 * C), y4 = ld4_stream(y0 + 4 * C);
-    const float4 u0 = ld4_stream(y1), u1 = ld4_stream(y1 + C), u2 = ld4_stream(y1 + 2 * C), u3 = ld4_stream(y1 + 3 * C);
-    const float4 w0 = ld4_stream(y2), w1 = ld4_stream(y2 + C);
+    const float4 g0 = sig4(ld4_act<kH>(Y0, y0)), g1 = sig4(ld4_act<kH>(Y0, y0 + C));
+    const float4 a = ld4_act<kH>(Y0, y0 + 2 * C), sa = sig4(a);
+    const float4 y3 = ld4_act<kH>(Y0, y0 + 3 * C), y4 = ld4_act<kH>(Y0, y0 + 4 * C);
+    const float4 u0 = ld4_act<kH>(Y1, y1), u1 = ld4_act<kH>(Y1, y1 + C), u2 = ld4_act<kH>(Y1, y1 + 2 * C),
+                 u3 = ld4_act<kH>(Y1, y1 + 3 * C);
+    const float4 w0 = ld4_act<kH>(Y2, y2), w1 = ld4_act<kH>(Y2, y2 + C);
     const float4 ga = ld4_stream(q0), g3 = ld4_stream(q0 + C), g4 = ld4_stream(q0 + 2 * C);
     const float4 h0 = ld4_stream(q1), h1 = ld4_stream(q1 + C), h2 = ld4_stream(q1 + 2 * C), h3 = ld4_stream(q1 + 3 * C);
     const float4 k0 = ld4_stream(q2), k1 = ld4_stream(q2 + C);
@@ -340,15 +340,24 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_short_kernel(const float* __r
 }
 
 void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,
-                       int C, int split, int* err, cudaStream_t s) {
-  gating_fwd_kernel<<<grid_resident(gating_fwd_kernel, 256, E * (C / 4), 256), 256, 0, s>>>(Y0, Y1, Y2, Z0, Z1, Z2, E, C, split, err);
+                       int C, int split, int* err, cudaStream_t s, bool act_half) {
+  if (act_half)
+    gating_fwd_kernel<true><<<grid_resident(gating_fwd_kernel<true>, 256, E * (C / 4), 256), 256, 0, s>>>(
+        Y0, Y1, Y2, Z0, Z1, Z2, E, C, split, err);
+  else
+    gating_fwd_kernel<false><<<grid_resident(gating_fwd_kernel<false>, 256, E * (C / 4), 256), 256, 0, s>>>(
+        Y0, Y1, Y2, Z0, Z1, Z2, E, C, split, err);
 }
 
 void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, const float* Y0, const float* Y1,
                        const float* Y2, float* gY0, float* gY1, float* gY2, int64_t E, int C, int split, int* err,
-                       cudaStream_t s) {
-  gating_bwd_kernel<<<grid_resident(gating_bwd_kernel, 256, E * (C / 4), 256), 256, 0, s>>>(gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C,
-                                                                   split, err);
+                       cudaStream_t s, bool act_half) {
+  if (act_half)
+    gating_bwd_kernel<true><<<grid_resident(gating_bwd_kernel<true>, 256, E * (C / 4), 256), 256, 0, s>>>(
+        gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C, split, err);
+  else
+    gating_bwd_kernel<false><<<grid_resident(gating_bwd_kernel<false>, 256, E * (C / 4), 256), 256, 0, s>>>(
+        gZ0, gZ1, gZ2, Y0, Y1, Y2, gY0, gY1, gY2, E, C, split, err);
 }
 
 void launch_ln_silu_fwd(const float* x, const float* gamma, const float* beta, float* out, float* mean, float* rstd,

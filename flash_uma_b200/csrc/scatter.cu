@@ -31,7 +31,7 @@ constexpr int kRing = 4;       // edges staged per warp (rotate-scatter forward,
 // order into fp64 accumulators; their Z slots, Wigner block and envelope are copied into a
 // per-warp ring of kRing shared-memory buffers with cp.async, kRing - 1 edges ahead of the sum,
 // so a warp waits for memory about once per kRing - 1 edges instead of once per edge.
-template <int PART>
+template <int PART, bool kH>
 __global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ Z0,
     const float* __restrict__ Z1, const float* __restrict__ Z2, const float* __restrict__ wig,
@@ -55,21 +55,20 @@ __global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
       // into ring buffer b, one commit group per edge
       auto issue = [&](int64_t e, int b) {
         if (on) {
-          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+          // element offsets of the edge's rows (fp32, or fp16 with kH)
+          const int64_t z0 = e * 3 * (int64_t)C + co, z1 = e * 4 * (int64_t)C + co, z2 = e * 2 * (int64_t)C + co;
           float4* d = &s_stage[warp][b][0][lane];
           if constexpr (PART == 0) {
-            cp_async16(d + 0 * 32, z0);
-            cp_async16(d + 1 * 32, z1 + 2 * C);
-            cp_async16(d + 2 * 32, z0 + C);
-            cp_async16(d + 3 * 32, z1);
+            cp_act<kH>(d + 0 * 32, Z0, z0);
+            cp_act<kH>(d + 1 * 32, Z1, z1 + 2 * C);
+            cp_act<kH>(d + 2 * 32, Z0, z0 + C);
+            cp_act<kH>(d + 3 * 32, Z1, z1);
           } else {
-            cp_async16(d + 0 * 32, z2 + C);
-            cp_async16(d + 1 * 32, z1 + 3 * C);
-            cp_async16(d + 2 * 32, z0 + 2 * C);
-            cp_async16(d + 3 * 32, z1 + C);
-            cp_async16(d + 4 * 32, z2);
+            cp_act<kH>(d + 0 * 32, Z2, z2 + C);
+            cp_act<kH>(d + 1 * 32, Z1, z1 + 3 * C);
+            cp_act<kH>(d + 2 * 32, Z0, z0 + 2 * C);
+            cp_act<kH>(d + 3 * 32, Z1, z1 + C);
+            cp_act<kH>(d + 4 * 32, Z2, z2);
           }
         }
         if (lane < kW) cp_async4(&s_w[warp][b][lane], wig + e * kWig + kWoff + lane);
@@ -111,8 +110,8 @@ __global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
         const float4* src = &s_stage[warp][b][0][lane];
         if (on) {
           if constexpr (PART == 0) {
-            acc[0] += src[0] * ev;
-            const float4 m0 = src[32], m1 = src[64], m2 = src[96];
+            acc[0] += sm_act<kH>(src) * ev;
+            const float4 m0 = sm_act<kH>(src + 32), m1 = sm_act<kH>(src + 64), m2 = sm_act<kH>(src + 96);
 #pragma unroll
             for (int kk = 0; kk < 3; ++kk) {
               float4 a = D[kk] * m0;
@@ -123,7 +122,7 @@ __global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
           } else {
             float4 m[5];
 #pragma unroll
-            for (int r = 0; r < 5; ++r) m[r] = src[32 * r];
+            for (int r = 0; r < 5; ++r) m[r] = sm_act<kH>(src + 32 * r);
 #pragma unroll
             for (int kk = 0; kk < 5; ++kk) {
               float4 a = D[kk] * m[0];
@@ -152,7 +151,7 @@ __global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
 //   g_env[e] = sum_c g_out[j] . (unscaled message): PART 0 writes its share, PART 1 (launched
 //   after it on the same stream) adds the rest, so the sum has a fixed order.
 // (g_x_res = g_out is returned by the host.)
-template <int PART>
+template <int PART, bool kH>
 __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx, const float* __restrict__ g_out,
     const float* __restrict__ Z0, const float* __restrict__ Z1, const float* __restrict__ Z2,
@@ -181,21 +180,20 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
       // the next edge's copies are in flight while the current edge is computed
       auto issue = [&](int64_t e, int b) {
         if (on) {
-          const float* z0 = Z0 + e * 3 * (int64_t)C + co;
-          const float* z1 = Z1 + e * 4 * (int64_t)C + co;
-          const float* z2 = Z2 + e * 2 * (int64_t)C + co;
+          // element offsets of the edge's rows (fp32, or fp16 with kH)
+          const int64_t z0 = e * 3 * (int64_t)C + co, z1 = e * 4 * (int64_t)C + co, z2 = e * 2 * (int64_t)C + co;
           float4* d = &s_stage[warp][b][0][lane];
           if constexpr (PART == 0) {
-            cp_async16(d + 0 * 32, z0);
-            cp_async16(d + 1 * 32, z1 + 2 * C);
-            cp_async16(d + 2 * 32, z0 + C);
-            cp_async16(d + 3 * 32, z1);
+            cp_act<kH>(d + 0 * 32, Z0, z0);
+            cp_act<kH>(d + 1 * 32, Z1, z1 + 2 * C);
+            cp_act<kH>(d + 2 * 32, Z0, z0 + C);
+            cp_act<kH>(d + 3 * 32, Z1, z1);
           } else {
-            cp_async16(d + 0 * 32, z2 + C);
-            cp_async16(d + 1 * 32, z1 + 3 * C);
-            cp_async16(d + 2 * 32, z0 + 2 * C);
-            cp_async16(d + 3 * 32, z1 + C);
-            cp_async16(d + 4 * 32, z2);
+            cp_act<kH>(d + 0 * 32, Z2, z2 + C);
+            cp_act<kH>(d + 1 * 32, Z1, z1 + 3 * C);
+            cp_act<kH>(d + 2 * 32, Z0, z0 + 2 * C);
+            cp_act<kH>(d + 3 * 32, Z1, z1 + C);
+            cp_act<kH>(d + 4 * 32, Z2, z2);
           }
         }
         if (lane < kW) cp_async4(&s_w[warp][b][lane], wig + e * kWig + kWoff + lane);
@@ -237,8 +235,9 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
 #pragma unroll
         for (int m = 0; m < NV; ++m) part[m] = 0.f;
         if constexpr (PART == 0) {
-          const float4 zl0 = on ? src[0] : zz;
-          const float4 m1[3] = {on ? src[32] : zz, on ? src[64] : zz, on ? src[96] : zz};
+          const float4 zl0 = on ? sm_act<kH>(src) : zz;
+          const float4 m1[3] = {on ? sm_act<kH>(src + 32) : zz, on ? sm_act<kH>(src + 64) : zz,
+                                on ? sm_act<kH>(src + 96) : zz};
           float4 t1[3];
 #pragma unroll
           for (int r = 0; r < 3; ++r) {
@@ -259,8 +258,9 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
             for (int kk = 0; kk < 3; ++kk) part[r * 3 + kk] = dot4(g[1 + kk], m1[r]);
           part[9] = dot4(g[0], zl0);
         } else {
-          const float4 m2[5] = {on ? src[0] : zz, on ? src[32] : zz, on ? src[64] : zz, on ? src[96] : zz,
-                                on ? src[128] : zz};
+          const float4 m2[5] = {on ? sm_act<kH>(src) : zz, on ? sm_act<kH>(src + 32) : zz,
+                                on ? sm_act<kH>(src + 64) : zz, on ? sm_act<kH>(src + 96) : zz,
+                                on ? sm_act<kH>(src + 128) : zz};
           float4 t2[5];
 #pragma unroll
           for (int r = 0; r < 5; ++r) {
@@ -498,25 +498,42 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
   report_split_range(bad, err);
 }
 
+template <bool kH>
+void rs_fwd_launch(const int32_t* row_ptr, const int32_t* col_idx, const float* Z0, const float* Z1, const float* Z2,
+                   const float* wig, const float* env, const float* x_res, float* x_out, int64_t N, int C,
+                   cudaStream_t s) {
+  const int t = kFwdWarps * 32;
+  rotate_scatter_fwd_kernel<0, kH><<<grid_resident(rotate_scatter_fwd_kernel<0, kH>, t, N, kFwdWarps), t, 0, s>>>(
+      row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
+  rotate_scatter_fwd_kernel<1, kH><<<grid_resident(rotate_scatter_fwd_kernel<1, kH>, t, N, kFwdWarps), t, 0, s>>>(
+      row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
+}
+
 void launch_rotate_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* Z0, const float* Z1,
                                const float* Z2, const float* wig, const float* env, const float* x_res, float* x_out,
-                               int64_t N, int C, cudaStream_t s) {
-  const int t = kFwdWarps * 32;
-  rotate_scatter_fwd_kernel<0><<<grid_resident(rotate_scatter_fwd_kernel<0>, t, N, kFwdWarps), t, 0, s>>>(
-      row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
-  rotate_scatter_fwd_kernel<1><<<grid_resident(rotate_scatter_fwd_kernel<1>, t, N, kFwdWarps), t, 0, s>>>(
-      row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C);
+                               int64_t N, int C, cudaStream_t s, bool act_half) {
+  if (act_half)
+    rs_fwd_launch<true>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C, s);
+  else
+    rs_fwd_launch<false>(row_ptr, col_idx, Z0, Z1, Z2, wig, env, x_res, x_out, N, C, s);
 }
 
 void launch_rotate_scatter_bwd(const int32_t* row_ptr, const int32_t* col_idx, const float* g_out, const float* Z0,
                                const float* Z1, const float* Z2, const float* wig, const float* env, float* gZ0,
                                float* gZ1, float* gZ2, float* g_wig, float* g_env, int64_t N, int C, int split,
-                               int* err, cudaStream_t s) {
+                               int* err, cudaStream_t s, bool act_half) {
   const unsigned g = grid_for(N, 8, 2);
-  rotate_scatter_bwd_kernel<0><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
-                                                 g_env, N, C, split, err);
-  rotate_scatter_bwd_kernel<1><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2, g_wig,
-                                                 g_env, N, C, split, err);
+  if (act_half) {
+    rotate_scatter_bwd_kernel<0, true><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2,
+                                                         g_wig, g_env, N, C, split, err);
+    rotate_scatter_bwd_kernel<1, true><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1, gZ2,
+                                                         g_wig, g_env, N, C, split, err);
+  } else {
+    rotate_scatter_bwd_kernel<0, false><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1,
+                                                          gZ2, g_wig, g_env, N, C, split, err);
+    rotate_scatter_bwd_kernel<1, false><<<g, 256, 0, s>>>(row_ptr, col_idx, g_out, Z0, Z1, Z2, wig, env, gZ0, gZ1,
+                                                          gZ2, g_wig, g_env, N, C, split, err);
+  }
 }
 
 void launch_init_scatter_fwd(const int32_t* row_ptr, const int32_t* col_idx, const float* rad, const float* wig,

@@ -108,9 +108,10 @@ def _ln_silu_bwd_split(y, gamma, beta, mean, rstd, g, err, parts):
     return gx
 
 
-def radial_fwd(rad, xe_p, err):
+def radial_fwd(rad, xe_p, err, half_out: bool = False):
     """Linear -> LN-SiLU -> Linear -> LN-SiLU -> Linear on the split edge features; returns the
-    fp32 radial output and what the backward needs."""
+    radial output (fp32; fp16 with ``half_out`` in the single-product mode) and what the
+    backward needs."""
     Kx = xe_p.shape[1]
     y1 = _gemm16(xe_p, rad.l1.w16, rad.l1.bias_p, Kx)
     parts = _parts(rad.l1)
@@ -118,7 +119,7 @@ def radial_fwd(rad, xe_p, err):
     y2 = _gemm16(h1, rad.l2.w16, rad.l2.bias_p, h1.shape[1])
     del h1
     h2, m2, r2 = _ln_silu_split(y2, rad.g2, rad.be2, err, parts)
-    out = _gemm16(h2, rad.l3.w16, rad.l3.bias_p, h2.shape[1])
+    out = _gemm16(h2, rad.l3.w16, rad.l3.bias_p, h2.shape[1], out_half=half_out)
     return out, (y1, m1, r1, y2, m2, r2)
 
 
@@ -144,10 +145,12 @@ def _conv2(layer, Y0, Y1, Y2, C, err, s):
     E = Y0.shape[0]
     parts = _parts(layer.conv2_m0)
     Z0, Z1, Z2 = _empty((E, 3 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
-    nat.call("fuma_gating_fwd_f16x3", ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(Z0), ptr(Z1), ptr(Z2), parts, ptr(err), s)
-    O0 = _gemm16(Z0, layer.conv2_m0.w16, layer.conv2_m0.bias_p, 3 * C)
-    O1 = _gemm16(Z1, layer.conv2_m1.w16, None, 4 * C)
-    O2 = _gemm16(Z2, layer.conv2_m2.w16, None, 2 * C)
+    half = parts == 1   # the single-product mode stores its GEMM results as fp16
+    nat.call("fuma_gating_fwd_f16x3", ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(Z0), ptr(Z1), ptr(Z2), parts, int(half),
+             ptr(err), s)
+    O0 = _gemm16(Z0, layer.conv2_m0.w16, layer.conv2_m0.bias_p, 3 * C, out_half=half)
+    O1 = _gemm16(Z1, layer.conv2_m1.w16, None, 4 * C, out_half=half)
+    O2 = _gemm16(Z2, layer.conv2_m2.w16, None, 2 * C, out_half=half)
     return O0, O1, O2
 
 
@@ -155,13 +158,14 @@ def _edge_forward(layer, x_norm, xe_p, wigner, csd, idx_i, idx_j, batch, N, C, e
     """Radial MLP, gather, conv1, gating, conv2 of one block: (rad, radial saved, Y0..2, O0..2)."""
     E = idx_i.shape[0]
     parts = _parts(layer.conv1_m0)
-    rad, rsaved = radial_fwd(layer.rad, xe_p, err)
-    X0, X1, X2 = _empty((E, 6 * C), rad), _empty((E, 8 * C), rad), _empty((E, 4 * C), rad)
+    half = parts == 1   # the single-product mode: radial and conv results stored as fp16
+    rad, rsaved = radial_fwd(layer.rad, xe_p, err, half_out=half)
+    X0, X1, X2 = _empty((E, 6 * C), x_norm), _empty((E, 8 * C), x_norm), _empty((E, 4 * C), x_norm)
     nat.call("fuma_gather_fwd_f16x3", ptr(x_norm), ptr(idx_i), ptr(idx_j), ptr(wigner), ptr(rad), ptr(csd),
-             ptr(batch), N, E, C, ptr(X0), ptr(X1), ptr(X2), parts, ptr(err), s)
-    Y0 = _gemm16(X0, layer.conv1_m0.w16, layer.conv1_m0.bias_p, 6 * C)
-    Y1 = _gemm16(X1, layer.conv1_m1.w16, None, 8 * C)
-    Y2 = _gemm16(X2, layer.conv1_m2.w16, None, 4 * C)
+             ptr(batch), N, E, C, ptr(X0), ptr(X1), ptr(X2), parts, int(half), ptr(err), s)
+    Y0 = _gemm16(X0, layer.conv1_m0.w16, layer.conv1_m0.bias_p, 6 * C, out_half=half)
+    Y1 = _gemm16(X1, layer.conv1_m1.w16, None, 8 * C, out_half=half)
+    Y2 = _gemm16(X2, layer.conv1_m2.w16, None, 4 * C, out_half=half)
     del X0, X1, X2
     O0, O1, O2 = _conv2(layer, Y0, Y1, Y2, C, err, s)
     return rad, rsaved, (Y0, Y1, Y2), (O0, O1, O2)
@@ -183,8 +187,8 @@ class _MessageBlockFn(torch.autograd.Function):
         rad, rsaved, (Y0, Y1, Y2), (O0, O1, O2) = _edge_forward(layer, x_norm, xe_p, wigner, csd, idx_i, idx_j,
                                                                  batch, N, C, err, s)
         x_mid = _empty((N, 9, C), x_in)
-        nat.call("fuma_rotate_scatter_fwd", ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env), ptr(x_in),
-                 ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(x_mid), s)
+        nat.call("fuma_rotate_scatter_fwd_f16x3", ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env), ptr(x_in),
+                 ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(x_mid), int(O0.dtype == torch.float16), s)
         if lean:
             ctx.save_for_backward(x_norm, wigner, env, csd, idx_i, batch, xe_p, idx_j)
         else:
@@ -211,31 +215,32 @@ class _MessageBlockFn(torch.autograd.Function):
             rad = saved[6]
             rsaved = saved[7:13]
             Y0, Y1, Y2, O0, O1, O2 = saved[13:19]
-        gO0, gO1, gO2 = _empty((E, 3 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
-        g_w = _empty((E, 34), Y0)
-        g_env = _empty((E,), Y0)
+        half = parts == 1   # fp16 radial / conv results in the single-product mode
+        gO0, gO1, gO2 = _empty((E, 3 * C), g_mid), _empty((E, 4 * C), g_mid), _empty((E, 2 * C), g_mid)
+        g_w = _empty((E, 34), g_mid)
+        g_env = _empty((E,), g_mid)
         nat.call("fuma_rotate_scatter_bwd_f16x3", ptr(g_mid), ptr(O0), ptr(O1), ptr(O2), ptr(wigner), ptr(env),
                  ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(gO0), ptr(gO1), ptr(gO2), ptr(g_w),
-                 ptr(g_env), parts, ptr(err), s)
+                 ptr(g_env), parts, int(half), ptr(err), s)
         del O0, O1, O2
         gZ0 = _gemm16(gO0, layer.conv2_m0.wt16, None, 3 * C)
         gZ1 = _gemm16(gO1, layer.conv2_m1.wt16, None, 4 * C)
         gZ2 = _gemm16(gO2, layer.conv2_m2.wt16, None, 2 * C)
         del gO0, gO1, gO2
-        gY0, gY1, gY2 = _empty((E, 5 * C), Y0), _empty((E, 4 * C), Y0), _empty((E, 2 * C), Y0)
+        gY0, gY1, gY2 = _empty((E, 5 * C), g_mid), _empty((E, 4 * C), g_mid), _empty((E, 2 * C), g_mid)
         nat.call("fuma_gating_bwd_f16x3", ptr(gZ0), ptr(gZ1), ptr(gZ2), ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(gY0),
-                 ptr(gY1), ptr(gY2), parts, ptr(err), s)
+                 ptr(gY1), ptr(gY2), parts, int(half), ptr(err), s)
         del gZ0, gZ1, gZ2, Y0, Y1, Y2
         gX0 = _gemm16(gY0, layer.conv1_m0.wt16, None, 5 * C)
         gX1 = _gemm16(gY1, layer.conv1_m1.wt16, None, 4 * C)
         gX2 = _gemm16(gY2, layer.conv1_m2.wt16, None, 2 * C)
         del gY0, gY1, gY2
         g_x = torch.empty_like(x_norm)
-        g_w2 = _empty((E, 34), rad)
-        g_rad = torch.empty_like(rad)
+        g_w2 = _empty((E, 34), g_mid)
+        g_rad = _empty(tuple(rad.shape), g_mid)   # fp32 (split) whatever the radial rows' storage
         nat.call("fuma_gather_bwd_f16x3", ptr(gX0), ptr(gX1), ptr(gX2), ptr(x_norm), ptr(idx_i), ptr(wigner), ptr(rad),
                  ptr(csd), ptr(batch), ptr(graph.dst_row_ptr), ptr(graph.dst_col), ptr(graph.src_row_ptr),
-                 ptr(graph.src_col), N, E, C, None, 0, ptr(g_x), ptr(g_w2), ptr(g_rad), parts, ptr(err), s)
+                 ptr(graph.src_col), N, E, C, None, 0, ptr(g_x), ptr(g_w2), ptr(g_rad), parts, int(half), ptr(err), s)
         del gX0, gX1, gX2, rad
         g_xe = radial_bwd(layer.rad, rsaved, g_rad, err)
         g_w += g_w2

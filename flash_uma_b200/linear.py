@@ -177,10 +177,11 @@ def split_rows(x: torch.Tensor, ldp: int | None = None) -> torch.Tensor:
     return out
 
 
-def _gemm16(a: torch.Tensor, w16, bias: torch.Tensor | None, K: int | None = None):
+def _gemm16(a: torch.Tensor, w16, bias: torch.Tensor | None, K: int | None = None, out_half: bool = False):
     """fp16 tensor-core product with a weight split ``w16 = (hi, lo, scale_inv, x1)`` of W [N, ldw]:
     three products (f16x3) or, with ``x1``, the single hi . hi product. ``K`` given: ``a`` is a
-    row-packed split (:func:`split_rows`) of a [M, K] activation."""
+    row-packed split (:func:`split_rows`) of a [M, K] activation. ``out_half`` (single product
+    only): the result is stored as fp16 (the 16-bit activation storage of the "f16" mode)."""
     hi, lo, inv, x1 = w16
     N, ldw = hi.shape
     if K is None:
@@ -194,10 +195,11 @@ def _gemm16(a: torch.Tensor, w16, bias: torch.Tensor | None, K: int | None = Non
     else:
         M = a.shape[0]
         pre = 1
-    out = torch.empty(M, N, device=a.device, dtype=torch.float32)
+    half = bool(out_half and x1)
+    out = torch.empty(M, N, device=a.device, dtype=torch.float16 if half else torch.float32)
     if x1:
         nat.call("fuma_linear_f16", ptr(a), a.stride(0), ptr(hi), ldw, inv, ptr(bias), M, N, K, ptr(out), N,
-                 ptr(error_flag(a.device)), stream_of(a))
+                 1 if half else 0, ptr(error_flag(a.device)), stream_of(a))
     else:
         nat.call("fuma_linear_f16x3", ptr(a), a.stride(0), pre, ptr(hi), ptr(lo), ldw, inv, ptr(bias), M, N, K,
                  ptr(out), N, ptr(error_flag(a.device)), stream_of(a))

@@ -149,9 +149,12 @@ int fuma_linear_f16x3(const float* A, int64_t lda, int32_t a_split, const void* 
  * (about 11 significant bits per operand, what the reference runs with allow_tf32, its published
  * setting) at a third of the f16x3 tensor work. A is a row-packed split (the layout of
  * fuma_split_rows_f16 and of the *_f16x3 producers; only its hi half is read), W_hi the hi half
- * of fuma_split_f16. K a multiple of 8; lda, ldw multiples of 8. */
+ * of fuma_split_f16. K a multiple of 8; lda, ldw multiples of 8. c_half != 0: C is fp16 [M, ldc]
+ * (ldc in halves, a multiple of 8; the 16-bit activation storage of this mode; a finite result at
+ * or beyond the fp16 limit sets code 16 in err_flag), else fp32. */
 int fuma_linear_f16(const float* A, int64_t lda, const void* W_hi, int64_t ldw, float w_scale_inv, const float* bias,
-                    int64_t M, int32_t N, int32_t K, float* C, int64_t ldc, int* err_flag, void* stream);
+                    int64_t M, int32_t N, int32_t K, void* C, int64_t ldc, int32_t c_half, int* err_flag,
+                    void* stream);
 /* Row-packed f16x3 split of an activation matrix x [M, K] (rows lda floats apart) into out,
  * whose row r spans 4 * ldp bytes: fp16 hi values of x[r, :K] at byte 0, the scaled fp16 lo
  * values at byte 2 * ldp (the same footprint as fp32 [M, ldp]). ldp >= K, a multiple of 8.
@@ -243,7 +246,13 @@ int fuma_split_f16(const float* x, int64_t n, float scale, void* hi, void* lo, v
  * writes only the fp16 hi halves (the operand of the single-product fuma_linear_f16, which reads
  * nothing else; the lo halves of the rows are left as they are, so the call moves half the
  * bytes). All other outputs are unchanged. C (D for ln_silu) must be a multiple of 8. err_flag
- * (device int, may be NULL) receives 16 if a finite value is at or beyond the fp16 limit (65520). */
+ * (device int, may be NULL) receives 16 if a finite value is at or beyond the fp16 limit (65520).
+ * act_half != 0 (gather, gating and rotate-scatter variants; the 16-bit activation storage of the
+ * single-product mode, where fuma_linear_f16 writes its results as fp16 with c_half): the radial
+ * rows `rad` (gather fwd / bwd), the conv1 results Y_m0..2 (gating fwd / bwd) and the conv2
+ * results Z_m0..2 (rotate-scatter fwd / bwd) are fp16 arrays of the same shapes, passed as the
+ * same pointers; everything else stays fp32. fuma_rotate_scatter_fwd_f16x3 is
+ * fuma_rotate_scatter_fwd with that flag. */
 int fuma_ln_silu_fwd_f16x3(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
                            float* out, float* mean, float* rstd, int32_t parts, int* err_flag, void* stream);
 int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta, const float* mean,
@@ -251,22 +260,25 @@ int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta
                            void* stream);
 int fuma_gather_fwd_f16x3(const float* x, const int64_t* idx_i, const int64_t* idx_j, const float* wigner,
                           const float* rad, const float* csd, const int64_t* batch, int64_t N, int64_t E, int32_t C,
-                          float* X_m0, float* X_m1, float* X_m2, int32_t parts, int* err_flag, void* stream);
+                          float* X_m0, float* X_m1, float* X_m2, int32_t parts, int32_t act_half, int* err_flag, void* stream);
 int fuma_gather_bwd_f16x3(const float* g_X_m0, const float* g_X_m1, const float* g_X_m2, const float* x,
                           const int64_t* idx_i, const float* wigner, const float* rad, const float* csd,
                           const int64_t* batch, const int32_t* dst_row_ptr, const int32_t* dst_col,
                           const int32_t* src_row_ptr, const int32_t* src_col, int64_t N, int64_t E, int32_t C,
                           float* scratch, int64_t scratch_floats, float* g_x, float* g_wigner, float* g_rad,
-                          int32_t parts, int* err_flag, void* stream);
+                          int32_t parts, int32_t act_half, int* err_flag, void* stream);
+int fuma_rotate_scatter_fwd_f16x3(const float* Z_m0, const float* Z_m1, const float* Z_m2, const float* wigner,
+                                  const float* env, const float* x_res, const int32_t* row_ptr, const int32_t* col_idx,
+                                  int64_t N, int64_t E, int32_t C, float* x_out, int32_t act_half, void* stream);
 int fuma_gating_fwd_f16x3(const float* Y_m0, const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* Z_m0,
-                          float* Z_m1, float* Z_m2, int32_t parts, int* err_flag, void* stream);
+                          float* Z_m1, float* Z_m2, int32_t parts, int32_t act_half, int* err_flag, void* stream);
 int fuma_gating_bwd_f16x3(const float* g_Z_m0, const float* g_Z_m1, const float* g_Z_m2, const float* Y_m0,
                           const float* Y_m1, const float* Y_m2, int64_t E, int32_t C, float* g_Y_m0, float* g_Y_m1,
-                          float* g_Y_m2, int32_t parts, int* err_flag, void* stream);
+                          float* g_Y_m2, int32_t parts, int32_t act_half, int* err_flag, void* stream);
 int fuma_rotate_scatter_bwd_f16x3(const float* g_out, const float* Z_m0, const float* Z_m1, const float* Z_m2,
                                   const float* wigner, const float* env, const int32_t* row_ptr,
                                   const int32_t* col_idx, int64_t N, int64_t E, int32_t C, float* g_Z_m0,
-                                  float* g_Z_m1, float* g_Z_m2, float* g_wigner, float* g_env, int32_t parts, int* err_flag,
+                                  float* g_Z_m1, float* g_Z_m2, float* g_wigner, float* g_env, int32_t parts, int32_t act_half, int* err_flag,
                                   void* stream);
 int fuma_init_scatter_bwd_f16x3(const float* g_out, const float* rad, const float* wigner, const float* env,
                                 const int32_t* row_ptr, const int32_t* col_idx, int64_t N, int64_t E, int32_t C,
