@@ -46,6 +46,10 @@ _SIGS = {
     "fuma_atomwise_gate_fwd": [_P, _P, _P, _I64, _I32, _P, _P],
     "fuma_atomwise_gate_bwd": [_P, _P, _P, _P, _I64, _I32, _P, _P, _P],
     "fuma_coef_to_node": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
+    "fuma_node_to_coef_f16x3": [_P, _I64, _I32, _P, _I32, _P, _P],
+    "fuma_atomwise_gate_fwd_f16x3": [_P, _P, _P, _I64, _I32, _P, _I32, _P, _P],
+    "fuma_atomwise_gate_bwd_f16x3": [_P, _P, _P, _P, _I64, _I32, _P, _P, _I32, _P, _P],
+    "fuma_coef_to_node_blocked": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
     "fuma_rmsnorm_sh_fwd": [_P, _P, _P, _P, _F32, _I64, _I32, _P, _P, _P],
     "fuma_rmsnorm_sh_bwd": [_P, _P, _P, _P, _P, _I64, _I32, _P, _P],
     "fuma_morton_reorder_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P],

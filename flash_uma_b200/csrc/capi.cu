@@ -536,7 +536,7 @@ int fuma_atomwise_gate_fwd(const float* h, const float* u, const float* b1, int6
   REQUIRE(h && u && b1 && z, "atomwise_gate_fwd: null pointer");
   REQUIRE_ALIGNED(h, "h"); REQUIRE_ALIGNED(u, "u"); REQUIRE_ALIGNED(b1, "b1"); REQUIRE_ALIGNED(z, "z");
   BIND(h);
-  launch_atomwise_gate_fwd(h, u, b1, N, H, z, (cudaStream_t)stream);
+  launch_atomwise_gate_fwd(h, H, false, u, b1, N, H, z, 0, nullptr, (cudaStream_t)stream);
   return launched("atomwise_gate_fwd");
 }
 
@@ -548,7 +548,7 @@ int fuma_atomwise_gate_bwd(const float* gz, const float* h, const float* u, cons
   REQUIRE_ALIGNED(gz, "gz"); REQUIRE_ALIGNED(h, "h"); REQUIRE_ALIGNED(u, "u"); REQUIRE_ALIGNED(b1, "b1");
   REQUIRE_ALIGNED(gh, "gh"); REQUIRE_ALIGNED(gu, "gu");
   BIND(h);
-  launch_atomwise_gate_bwd(gz, h, u, b1, N, H, gh, gu, (cudaStream_t)stream);
+  launch_atomwise_gate_bwd(gz, h, H, false, u, b1, N, H, gh, gu, 0, nullptr, (cudaStream_t)stream);
   return launched("atomwise_gate_bwd");
 }
 
@@ -561,8 +561,58 @@ int fuma_coef_to_node(const float* src, const float* add, const float* row0, int
   if (add) REQUIRE_ALIGNED(add, "add");
   if (row0) REQUIRE_ALIGNED(row0, "row0");
   BIND(src);
-  launch_coef_to_node(src, add, row0, row0_per_node != 0, N, W, out, (cudaStream_t)stream);
+  launch_coef_to_node(src, W, false, add, row0, row0_per_node != 0, N, W, out, (cudaStream_t)stream);
   return launched("coef_to_node");
+}
+
+int fuma_node_to_coef_f16x3(const float* x, int64_t N, int32_t W, float* out, int32_t parts, int* err_flag,
+                            void* stream) {
+  REQUIRE(N >= 0 && W > 0 && W % 8 == 0, "node_to_coef_f16x3: W=%d must be a positive multiple of 8", W);
+  REQUIRE(parts == 1 || parts == 2, "node_to_coef_f16x3: parts=%d must be 1 or 2", parts);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(x && out, "node_to_coef_f16x3: null pointer");
+  REQUIRE_ALIGNED(x, "x"); REQUIRE_ALIGNED(out, "out");
+  BIND(x);
+  launch_node_to_coef(x, N, W, out, parts, err_flag, (cudaStream_t)stream);
+  return launched("node_to_coef_f16x3");
+}
+
+int fuma_atomwise_gate_fwd_f16x3(const float* h, const float* u, const float* b1, int64_t N, int32_t H, float* z,
+                                 int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(N >= 0 && H > 0 && H % 8 == 0, "atomwise_gate_fwd_f16x3: H=%d must be a positive multiple of 8", H);
+  REQUIRE(parts == 1 || parts == 2, "atomwise_gate_fwd_f16x3: parts=%d must be 1 or 2", parts);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(h && u && b1 && z, "atomwise_gate_fwd_f16x3: null pointer");
+  REQUIRE_ALIGNED(h, "h"); REQUIRE_ALIGNED(u, "u"); REQUIRE_ALIGNED(b1, "b1"); REQUIRE_ALIGNED(z, "z");
+  BIND(h);
+  launch_atomwise_gate_fwd(h, 3 * (int64_t)H, true, u, b1, N, H, z, parts, err_flag, (cudaStream_t)stream);
+  return launched("atomwise_gate_fwd_f16x3");
+}
+
+int fuma_atomwise_gate_bwd_f16x3(const float* gz, const float* h, const float* u, const float* b1, int64_t N,
+                                 int32_t H, float* gh, float* gu, int32_t parts, int* err_flag, void* stream) {
+  REQUIRE(N >= 0 && H > 0 && H % 8 == 0, "atomwise_gate_bwd_f16x3: H=%d must be a positive multiple of 8", H);
+  REQUIRE(parts == 1 || parts == 2, "atomwise_gate_bwd_f16x3: parts=%d must be 1 or 2", parts);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(gz && h && u && b1 && gh && gu, "atomwise_gate_bwd_f16x3: null pointer");
+  REQUIRE_ALIGNED(gz, "gz"); REQUIRE_ALIGNED(h, "h"); REQUIRE_ALIGNED(u, "u"); REQUIRE_ALIGNED(b1, "b1");
+  REQUIRE_ALIGNED(gh, "gh"); REQUIRE_ALIGNED(gu, "gu");
+  BIND(h);
+  launch_atomwise_gate_bwd(gz, h, 3 * (int64_t)H, true, u, b1, N, H, gh, gu, parts, err_flag, (cudaStream_t)stream);
+  return launched("atomwise_gate_bwd_f16x3");
+}
+
+int fuma_coef_to_node_blocked(const float* src, const float* add, const float* row0, int32_t row0_per_node,
+                              int64_t N, int32_t W, float* out, void* stream) {
+  REQUIRE(N >= 0 && W > 0 && W % 4 == 0, "coef_to_node_blocked: W=%d must be a positive multiple of 4", W);
+  if (N == 0) return FUMA_OK;
+  REQUIRE(src && out, "coef_to_node_blocked: null pointer");
+  REQUIRE_ALIGNED(src, "src"); REQUIRE_ALIGNED(out, "out");
+  if (add) REQUIRE_ALIGNED(add, "add");
+  if (row0) REQUIRE_ALIGNED(row0, "row0");
+  BIND(src);
+  launch_coef_to_node(src, 3 * (int64_t)W, true, add, row0, row0_per_node != 0, N, W, out, (cudaStream_t)stream);
+  return launched("coef_to_node_blocked");
 }
 
 int64_t fuma_morton_scratch_bytes(int64_t N) { return N < 0 ? 0 : morton_scratch_bytes(N); }

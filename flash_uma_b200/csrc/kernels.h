@@ -60,12 +60,17 @@ void launch_rmsnorm_sh_fwd(const float* x, const float* aw, const float* ab, con
                            int C, float* out, float* rstd, cudaStream_t s);
 void launch_rmsnorm_sh_bwd(const float* x, const float* aw, const float* bal, const float* rstd, const float* g_out,
                            int64_t N, int C, float* g_x, cudaStream_t s);
-void launch_atomwise_gate_fwd(const float* h, const float* u, const float* b1, int64_t N, int H, float* z,
+// Atom-wise block on coefficient rows (row k * N + n = coefficient k of atom n). h / gz: row
+// stride ldh; blocked: the degree-blocked output of one GEMM against the three stacked degree
+// weights (column block deg(k) * H). split 0 writes fp32, 1 / 2 the row-packed split.
+void launch_atomwise_gate_fwd(const float* h, int64_t ldh, bool blocked, const float* u, const float* b1, int64_t N,
+                              int H, float* z, int split, int* err, cudaStream_t s);
+void launch_atomwise_gate_bwd(const float* gz, const float* h, int64_t ldh, bool blocked, const float* u,
+                              const float* b1, int64_t N, int H, float* gh, float* gu, int split, int* err,
                               cudaStream_t s);
-void launch_atomwise_gate_bwd(const float* gz, const float* h, const float* u, const float* b1, int64_t N, int H,
-                              float* gh, float* gu, cudaStream_t s);
-void launch_coef_to_node(const float* src, const float* add, const float* row0, int row0_per_node, int64_t N, int W,
-                         float* out, cudaStream_t s);
+void launch_coef_to_node(const float* src, int64_t lds, bool blocked, const float* add, const float* row0,
+                         int row0_per_node, int64_t N, int W, float* out, cudaStream_t s);
+void launch_node_to_coef(const float* x, int64_t N, int W, float* out, int split, int* err, cudaStream_t s);
 constexpr int kMortonMaxAtoms = 16384;   // up to this many atoms one block sorts them in shared memory
 // scratch bytes of the radix-sort path (0 up to kMortonMaxAtoms atoms)
 int64_t morton_scratch_bytes(int64_t N);

@@ -162,8 +162,8 @@ void launch_rmsnorm_sh_bwd(const float* x, const float* aw, const float* bal, co
 // With h [9, N, H] the per-coefficient output of the first per-degree linear map (no bias) and
 // u [N, 2H] the scalar MLP pre-activation (bias included):
 //   z_0 = SiLU(h_0 + b1),  z_k = h_k * sigmoid(SiLU(u))[l(k) - 1 block]  (k >= 1)
-// Thread per (atom, 4 channels); the 9 coefficient rows of h and z are coefficient-major
-// [9, N, H] (the layout of a batched GEMM over the coefficients).
+// Thread per (atom, 4 channels); h and z are coefficient-major (row k * N + n), the layout in
+// which each degree's map is one GEMM over rows of the same degree.
 namespace {
 
 __device__ __forceinline__ float4 silu4(float4 a) {
@@ -180,93 +180,134 @@ __device__ __forceinline__ float4 sig4n(float4 a) {
 
 }  // namespace
 
-__global__ void __launch_bounds__(256) atomwise_gate_fwd_kernel(const float* __restrict__ h,
-                                                                 const float* __restrict__ u,
+// Coefficient rows of the atom-wise block: row k * N + n of a coefficient-major array holds
+// coefficient k of atom n. The per-degree maps run as one GEMM against the three degree weights
+// stacked ([W_0; W_1; W_2]), whose output is "degree-blocked": row k * N + n, column block
+// deg(k) * width holds the product with the weight of coefficient k's own degree (the other two
+// blocks are not read). Plain layouts: ld = width, block offset 0.
+__device__ __forceinline__ int coef_degree(int k) { return k == 0 ? 0 : (k < 4 ? 1 : 2); }
+
+// z = [silu(h_0 + b1), h_1..3 * sigmoid(silu(u_1)), h_4..8 * sigmoid(silu(u_2))] on coefficient
+// rows (h: row stride ldh, column block deg(k) * H when blocked; u [N, 2H]). z [9N, H] fp32
+// (split 0) or its row-packed split (split 1, 2).
+__global__ void __launch_bounds__(256) atomwise_gate_fwd_kernel(const float* __restrict__ h, int64_t ldh,
+                                                                 int blocked, const float* __restrict__ u,
                                                                  const float* __restrict__ b1, int64_t N, int H,
-                                                                 float* __restrict__ z) {
+                                                                 float* __restrict__ z, int split, int* err) {
   const int H4 = H >> 2;
-  const int64_t plane = N * (int64_t)H;
+  bool bad = false;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * H4; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = t / H4;
     const int c = (int)(t - n * H4) * 4;
-    const int64_t o = n * H + c;
     const float4 g1 = sig4n(silu4(ld4(u + n * 2 * H + c))), g2 = sig4n(silu4(ld4(u + n * 2 * H + H + c)));
-    st4(z + o, silu4(ld4(h + o) + ld4_keep(b1 + c)));
+    st_out4(z + n * H, H, c, silu4(ld4(h + n * ldh + c) + ld4_keep(b1 + c)), split, bad);
 #pragma unroll
-    for (int k = 1; k < 9; ++k) st4(z + k * plane + o, ld4(h + k * plane + o) * (k < 4 ? g1 : g2));
+    for (int k = 1; k < 9; ++k) {
+      const int64_t r = k * N + n;
+      const float4 v = ld4(h + r * ldh + (blocked ? coef_degree(k) * H : 0) + c);
+      st_out4(z + r * H, H, c, v * (k < 4 ? g1 : g2), split, bad);
+    }
   }
+  report_split_range(bad, err);
 }
 
-// Backward of the gating, given gz = dL/dz [9, N, H]: gh = dL/dh [9, N, H], gu = dL/du [N, 2H].
+// Backward of the gating, given gz = dL/dz on coefficient rows (same layout as h): gh = dL/dh
+// [9N, H] and gu = dL/du [N, 2H], fp32 (split 0) or row-packed splits (split 1, 2).
 __global__ void __launch_bounds__(256) atomwise_gate_bwd_kernel(const float* __restrict__ gz,
-                                                                 const float* __restrict__ h,
-                                                                 const float* __restrict__ u,
+                                                                 const float* __restrict__ h, int64_t ldh,
+                                                                 int blocked, const float* __restrict__ u,
                                                                  const float* __restrict__ b1, int64_t N, int H,
-                                                                 float* __restrict__ gh, float* __restrict__ gu) {
+                                                                 float* __restrict__ gh, float* __restrict__ gu,
+                                                                 int split, int* err) {
   const int H4 = H >> 2;
-  const int64_t plane = N * (int64_t)H;
+  bool bad = false;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * H4; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = t / H4;
     const int c = (int)(t - n * H4) * 4;
-    const int64_t o = n * H + c;
     const float4 u1 = ld4(u + n * 2 * H + c), u2 = ld4(u + n * 2 * H + H + c);
     const float4 a1 = silu4(u1), a2 = silu4(u2);
     const float4 g1 = sig4n(a1), g2 = sig4n(a2);
-    st4(gh + o, ld4(gz + o) * dsilu4(ld4(h + o) + ld4_keep(b1 + c)));
+    st_out4(gh + n * H, H, c, ld4(gz + n * ldh + c) * dsilu4(ld4(h + n * ldh + c) + ld4_keep(b1 + c)), split, bad);
     float4 s1 = f4(0.f), s2 = f4(0.f);
 #pragma unroll
     for (int k = 1; k < 9; ++k) {
-      const float4 g = ld4(gz + k * plane + o);
-      st4(gh + k * plane + o, g * (k < 4 ? g1 : g2));
+      const int64_t r = k * N + n;
+      const int64_t o = r * ldh + (blocked ? coef_degree(k) * H : 0) + c;
+      const float4 g = ld4(gz + o);
+      st_out4(gh + r * H, H, c, g * (k < 4 ? g1 : g2), split, bad);
       if (k < 4)
-        s1 += g * ld4(h + k * plane + o);
+        s1 += g * ld4(h + o);
       else
-        s2 += g * ld4(h + k * plane + o);
+        s2 += g * ld4(h + o);
     }
     const float4 one = f4(1.f);
-    st4(gu + n * 2 * H + c, s1 * (g1 * (one - g1)) * dsilu4(u1));
-    st4(gu + n * 2 * H + H + c, s2 * (g2 * (one - g2)) * dsilu4(u2));
+    st_out4(gu + n * 2 * H, 2 * H, c, s1 * (g1 * (one - g1)) * dsilu4(u1), split, bad);
+    st_out4(gu + n * 2 * H, 2 * H, H + c, s2 * (g2 * (one - g2)) * dsilu4(u2), split, bad);
   }
+  report_split_range(bad, err);
 }
 
-// out[n, k, :] = src[k, n, :] (+ add[n, k, :]) (+ row0[n or 0, :] on k = 0): coefficient-major
-// rows back to the node-major [N, 9, W] layout, with the residual and the l = 0 bias (forward) or
-// the scalar-MLP input gradient (backward) folded in.
-__global__ void __launch_bounds__(256) coef_to_node_kernel(const float* __restrict__ src,
+// out[n, k, :] = src[k * N + n, block(k) :] (+ add[n, k, :]) (+ row0[n or 0, :] on k = 0):
+// coefficient rows (row stride lds, column block deg(k) * W when blocked) back to the node-major
+// [N, 9, W] layout, with the residual and the l = 0 bias (forward) or the scalar-MLP input
+// gradient (backward) folded in.
+__global__ void __launch_bounds__(256) coef_to_node_kernel(const float* __restrict__ src, int64_t lds, int blocked,
                                                            const float* __restrict__ add,
                                                            const float* __restrict__ row0, int row0_per_node,
                                                            int64_t N, int W, float* __restrict__ out) {
   const int W4 = W >> 2;
-  const int64_t plane = N * (int64_t)W;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * 9 * W4;
        t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t nk = t / W4;
     const int c = (int)(t - nk * W4) * 4;
     const int64_t n = nk / 9;
     const int k = (int)(nk - n * 9);
-    float4 v = ld4(src + k * plane + n * W + c);
+    float4 v = ld4(src + (k * N + n) * lds + (blocked ? coef_degree(k) * W : 0) + c);
     if (add) v = v + ld4(add + nk * W + c);
     if (k == 0 && row0) v = v + ld4(row0 + (row0_per_node ? n * W : 0) + c);
     st4(out + nk * W + c, v);
   }
 }
 
-void launch_atomwise_gate_fwd(const float* h, const float* u, const float* b1, int64_t N, int H, float* z,
+// The node-major [N, 9, W] array x as coefficient rows (row k * N + n = x[n, k, :]): the
+// row-packed split (split 1, 2) that the tensor-core GEMMs of the atom-wise block read.
+__global__ void __launch_bounds__(256) node_to_coef_kernel(const float* __restrict__ x, int64_t N, int W,
+                                                           float* __restrict__ out, int split, int* err) {
+  const int W4 = W >> 2;
+  bool bad = false;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * 9 * W4;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t nk = t / W4;
+    const int c = (int)(t - nk * W4) * 4;
+    const int64_t n = nk / 9;
+    const int k = (int)(nk - n * 9);
+    st_out4(out + (k * N + n) * W, W, c, ld4_stream(x + nk * W + c), split, bad);
+  }
+  report_split_range(bad, err);
+}
+
+void launch_atomwise_gate_fwd(const float* h, int64_t ldh, bool blocked, const float* u, const float* b1, int64_t N,
+                              int H, float* z, int split, int* err, cudaStream_t s) {
+  atomwise_gate_fwd_kernel<<<grid_resident(atomwise_gate_fwd_kernel, 256, N * (H / 4), 256), 256, 0, s>>>(
+      h, ldh, blocked ? 1 : 0, u, b1, N, H, z, split, err);
+}
+
+void launch_atomwise_gate_bwd(const float* gz, const float* h, int64_t ldh, bool blocked, const float* u,
+                              const float* b1, int64_t N, int H, float* gh, float* gu, int split, int* err,
                               cudaStream_t s) {
-  atomwise_gate_fwd_kernel<<<grid_resident(atomwise_gate_fwd_kernel, 256, N * (H / 4), 256), 256, 0, s>>>(h, u, b1, N,
-                                                                                                         H, z);
-}
-
-void launch_atomwise_gate_bwd(const float* gz, const float* h, const float* u, const float* b1, int64_t N, int H,
-                              float* gh, float* gu, cudaStream_t s) {
   atomwise_gate_bwd_kernel<<<grid_resident(atomwise_gate_bwd_kernel, 256, N * (H / 4), 256), 256, 0, s>>>(
-      gz, h, u, b1, N, H, gh, gu);
+      gz, h, ldh, blocked ? 1 : 0, u, b1, N, H, gh, gu, split, err);
 }
 
-void launch_coef_to_node(const float* src, const float* add, const float* row0, int row0_per_node, int64_t N, int W,
-                         float* out, cudaStream_t s) {
+void launch_coef_to_node(const float* src, int64_t lds, bool blocked, const float* add, const float* row0,
+                         int row0_per_node, int64_t N, int W, float* out, cudaStream_t s) {
   coef_to_node_kernel<<<grid_resident(coef_to_node_kernel, 256, N * 9 * (W / 4), 256), 256, 0, s>>>(
-      src, add, row0, row0_per_node, N, W, out);
+      src, lds, blocked ? 1 : 0, add, row0, row0_per_node, N, W, out);
+}
+
+void launch_node_to_coef(const float* x, int64_t N, int W, float* out, int split, int* err, cudaStream_t s) {
+  node_to_coef_kernel<<<grid_resident(node_to_coef_kernel, 256, N * 9 * (W / 4), 256), 256, 0, s>>>(x, N, W, out,
+                                                                                                   split, err);
 }
 
 }  // namespace fuma

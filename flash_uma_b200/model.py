@@ -136,11 +136,12 @@ def apply_norm(norm, x):
     return norm(x)
 
 
-def apply_atomwise(aw, xn, x_mid):
+def apply_atomwise(aw, xn, x_mid, mode=None):
     """``aw(xn) + x_mid``: the fused CUDA path for the :class:`SpectralAtomwise` modules (the
-    stand-in atom-wise blocks), the module itself for any other atom-wise module."""
+    stand-in atom-wise blocks; its linear maps in the layer's GEMM ``mode``), the module itself
+    for any other atom-wise module."""
     if type(aw) is SpectralAtomwise and xn.is_cuda and aw.lmax == 2:
-        return ops.atomwise_residual(aw, xn, x_mid)
+        return ops.atomwise_residual(aw, xn, x_mid, mode)
     return (aw(xn) + x_mid).contiguous()
 
 
@@ -176,7 +177,7 @@ class PackedLayer(nn.Module):
                                         self.lean)
             if n_out is not None:
                 x_mid = x_mid[:n_out]
-            return apply_atomwise(self.atom_wise, apply_norm(self.norm_2, x_mid), x_mid)
+            return apply_atomwise(self.atom_wise, apply_norm(self.norm_2, x_mid), x_mid, self.conv1_m0.mode)
         rad_out = self.rad(x_edge)
         X0, X1, X2 = ops.gather_wigner_split(x_norm, idx_i, idx_j, wigner, rad_out, csd_emb, batch, graph=graph)
         Z0, Z1, Z2 = ops.fused_gating_split(self.conv1_m0(X0), self.conv1_m1(X1), self.conv1_m2(X2), self.C)
@@ -185,7 +186,7 @@ class PackedLayer(nn.Module):
                                          x_in.shape[0])
         if n_out is not None:
             x_mid = x_mid[:n_out]
-        return apply_atomwise(self.atom_wise, apply_norm(self.norm_2, x_mid), x_mid)
+        return apply_atomwise(self.atom_wise, apply_norm(self.norm_2, x_mid), x_mid, self.conv1_m0.mode)
 
 
 class ESCNInferenceModel(nn.Module):

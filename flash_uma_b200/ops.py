@@ -26,6 +26,7 @@ import torch
 from . import _native as nat
 from . import library  # noqa: F401  (registers the fuma:: custom operators)
 from ._native import ptr, stream_of
+from .linear import _gemm16, error_flag
 
 
 @dataclass
@@ -183,12 +184,100 @@ def atomwise_constants(aw) -> tuple:
     return prm
 
 
-def atomwise_residual(aw, xn: torch.Tensor, x_mid: torch.Tensor) -> torch.Tensor:
-    """``x_mid + aw(xn)`` for a :class:`~flash_uma_b200.nodewise.SpectralAtomwise` (lmax 2): the
-    per-coefficient linear maps as batched fp32 GEMMs on the coefficient-major view, the gating
-    and the layout change (with residual and biases) as CUDA kernels. Frozen parameters."""
+class _AtomwiseResidualTC(torch.autograd.Function):
+    """y = x_mid + atom_wise(xn) with the per-degree maps on the fp16 tensor cores.
+
+    The coefficient rows of xn (row k * N + n = xn[n, k]) are written as the row-packed split
+    the GEMMs read; each per-degree map is one GEMM over all 9N rows against the three degree
+    weights stacked, whose degree-blocked output the next kernel reads at the row's own degree
+    (the unused two thirds of that product cost far less than two more launches)."""
+
+    @staticmethod
+    def forward(ctx, xn, x_mid, tc):
+        nat.require_cuda(xn, x_mid)
+        xn, x_mid = _f32(xn, "xn"), _f32(x_mid, "x_mid")
+        N, _, C = xn.shape
+        H = tc.H
+        s, err, dev = stream_of(xn), ptr(error_flag(xn.device)), xn.device
+        xs = torch.empty(9 * N, C, device=dev)
+        nat.call("fuma_node_to_coef_f16x3", ptr(xn), N, C, ptr(xs), tc.parts, err, s)
+        u = _gemm16(xs[:N], tc.scalar.w16, tc.scalar.bias_p, C)                  # [N, 2H]
+        h = _gemm16(xs, tc.lin1.w16, None, C)                                    # [9N, 3H] degree-blocked
+        zs = torch.empty(9 * N, H, device=dev)
+        nat.call("fuma_atomwise_gate_fwd_f16x3", ptr(h), ptr(u), ptr(tc.b1), N, H, ptr(zs), tc.parts, err, s)
+        o = _gemm16(zs, tc.lin2.w16, None, H)                                    # [9N, 3C] degree-blocked
+        y = torch.empty_like(x_mid)
+        nat.call("fuma_coef_to_node_blocked", ptr(o), ptr(x_mid), ptr(tc.b2), 0, N, C, ptr(y), s)
+        ctx.save_for_backward(h, u)
+        ctx.tc = tc
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        h, u = ctx.saved_tensors
+        tc = ctx.tc
+        gy = _f32(gy, "gy")
+        N, _, C = gy.shape
+        H = tc.H
+        s, err, dev = stream_of(gy), ptr(error_flag(gy.device)), gy.device
+        gs = torch.empty(9 * N, C, device=dev)
+        nat.call("fuma_node_to_coef_f16x3", ptr(gy), N, C, ptr(gs), tc.parts, err, s)
+        gz = _gemm16(gs, tc.lin2t.w16, None, C)                                  # [9N, 3H] degree-blocked
+        ghs, gus = torch.empty(9 * N, H, device=dev), torch.empty(N, 2 * H, device=dev)
+        nat.call("fuma_atomwise_gate_bwd_f16x3", ptr(gz), ptr(h), ptr(u), ptr(tc.b1), N, H, ptr(ghs), ptr(gus),
+                 tc.parts, err, s)
+        gx = _gemm16(ghs, tc.lin1t.w16, None, H)                                 # [9N, 3C] degree-blocked
+        gu_x = _gemm16(gus, tc.scalar.wt16, None, 2 * H)                         # [N, C]
+        gxn = torch.empty_like(gy)
+        nat.call("fuma_coef_to_node_blocked", ptr(gx), None, ptr(gu_x), 1, N, C, ptr(gxn), s)
+        return gxn, gy, None
+
+
+class _AtomwiseTC:
+    """Tensor-core constants of a SpectralAtomwise block for one GEMM mode (cached on it):
+    FrozenLinear splits of the scalar MLP and of the stacked degree weights of both maps and
+    their transposes."""
+
+    def __init__(self, aw, mode: str):
+        from .linear import FrozenLinear
+        f = lambda t: t.detach().float()   # noqa: E731
+        W1, W2 = f(aw.so3_linear_1.weight), f(aw.so3_linear_2.weight)   # [3, H, C], [3, C, H]
+        lin = aw.scalar_mlp[0]
+        self.H = W1.shape[1]
+        self.mode = mode
+        self.parts = 1 if mode == "f16" else 2
+        self.scalar = FrozenLinear(lin.weight, lin.bias, mode)
+        self.lin1 = FrozenLinear(W1.reshape(-1, W1.shape[2]), None, mode)                  # [3H, C]
+        self.lin2 = FrozenLinear(W2.reshape(-1, W2.shape[2]), None, mode)                  # [3C, H]
+        self.lin2t = FrozenLinear(W2.transpose(1, 2).reshape(-1, W2.shape[1]), None, mode)  # [3H, C]
+        self.lin1t = FrozenLinear(W1.transpose(1, 2).reshape(-1, W1.shape[1]), None, mode)  # [3C, H]
+        self.b1 = f(aw.so3_linear_1.bias).contiguous()
+        self.b2 = f(aw.so3_linear_2.bias).contiguous()
+        for m in (self.scalar, self.lin1, self.lin2, self.lin2t, self.lin1t):
+            m.prepare()
+
+
+def _atomwise_tc(aw, mode: str) -> _AtomwiseTC:
+    dev = aw.so3_linear_1.weight.device
+    cache = aw.__dict__.setdefault("_fuma_tc", {})
+    tc = cache.get(mode)
+    if tc is None or tc.b1.device != dev:
+        tc = cache[mode] = _AtomwiseTC(aw, mode)
+    return tc
+
+
+def atomwise_residual(aw, xn: torch.Tensor, x_mid: torch.Tensor, mode: str | None = None) -> torch.Tensor:
+    """``x_mid + aw(xn)`` for a :class:`~flash_uma_b200.nodewise.SpectralAtomwise` (lmax 2), frozen
+    parameters. ``mode`` (default: the ``FUMA_GEMM`` mode) "f16x3" / "f16": the per-degree maps
+    and the scalar MLP on the fp16 tensor cores (fp32 accuracy / single product), gating and the
+    layout changes as CUDA kernels; "tf32x3" / "tf32": batched fp32 GEMMs (cuBLAS) between the
+    same kernels."""
+    from .linear import _F16_MODES, default_mode
     if aw.lmax != 2 or (aw.hidden % 4) or (xn.shape[2] % 4):
         raise ValueError("atomwise_residual: lmax 2 and channel counts that are multiples of 4")
+    mode = mode or default_mode()
+    if mode in _F16_MODES and aw.hidden % 16 == 0 and xn.shape[2] % 16 == 0:   # stacked widths 3H, 3C: GEMM tiles
+        return _AtomwiseResidualTC.apply(xn, x_mid, _atomwise_tc(aw, mode))
     return _AtomwiseResidual.apply(xn, x_mid, atomwise_constants(aw))
 
 

@@ -173,7 +173,7 @@ int fuma_rmsnorm_sh_fwd(const float* x, const float* affine_weight, const float*
 int fuma_rmsnorm_sh_bwd(const float* x, const float* affine_weight, const float* degree_weight, const float* rstd,
                         const float* g_out, int64_t N, int32_t C, float* g_x, void* stream);
 /* Gated atom-wise block (the atom_wise module the reference's layers call, model.py:157; here
- * the stand-in SpectralAtomwise). h [9, N, H]: the per-coefficient output of its first
+ * the stand-in SpectralAtomwise). h [9N, H]: the per-coefficient output of its first
  * per-degree linear map without bias, coefficient-major; u [N, 2H]: its scalar MLP
  * pre-activation (bias included). z_0 = SiLU(h_0 + b1), z_k = h_k sigmoid(SiLU(u))[degree - 1]
  * for k >= 1, written [9, N, H]. The backward returns gh [9, N, H] and gu [N, 2H] from gz.
@@ -187,6 +187,27 @@ int fuma_atomwise_gate_bwd(const float* gz, const float* h, const float* u, cons
  * [N, 9, W] embedding layout. W a multiple of 4. */
 int fuma_coef_to_node(const float* src, const float* add, const float* row0, int32_t row0_per_node, int64_t N,
                       int32_t W, float* out, void* stream);
+/* The same block with its per-degree linear maps on the fp16 tensor cores (fuma_linear_f16x3 /
+ * fuma_linear_f16); no counterpart in the reference, whose atom_wise module is FAIRChem code.
+ * Coefficient rows: row k * N + n holds coefficient k of atom n. Each map is ONE GEMM over all
+ * 9N rows against the three degree weights stacked ([W_0; W_1; W_2]); its output is
+ * "degree-blocked" [9N, 3 * width]: row k * N + n, column block deg(k) * width (deg 0 for k = 0,
+ * 1 for k = 1..3, 2 for k = 4..8) is the product with coefficient k's own weight.
+ * - fuma_node_to_coef_f16x3: x [N, 9, W] -> the row-packed split (parts 1 or 2, as for the
+ *   producer entry points below) of its coefficient rows [9N, W]; W a multiple of 8.
+ * - fuma_atomwise_gate_fwd_f16x3: h degree-blocked [9N, 3H] -> z, the row-packed split [9N, H].
+ * - fuma_atomwise_gate_bwd_f16x3: gz and h degree-blocked [9N, 3H] -> gh split [9N, H] and
+ *   gu split [N, 2H]. H a multiple of 8.
+ * - fuma_coef_to_node_blocked: fuma_coef_to_node with src degree-blocked [9N, 3W].
+ * err_flag receives 16 on a value beyond the fp16 range. */
+int fuma_node_to_coef_f16x3(const float* x, int64_t N, int32_t W, float* out, int32_t parts, int* err_flag,
+                            void* stream);
+int fuma_atomwise_gate_fwd_f16x3(const float* h, const float* u, const float* b1, int64_t N, int32_t H, float* z,
+                                 int32_t parts, int* err_flag, void* stream);
+int fuma_atomwise_gate_bwd_f16x3(const float* gz, const float* h, const float* u, const float* b1, int64_t N,
+                                 int32_t H, float* gh, float* gu, int32_t parts, int* err_flag, void* stream);
+int fuma_coef_to_node_blocked(const float* src, const float* add, const float* row0, int32_t row0_per_node,
+                              int64_t N, int32_t W, float* out, void* stream);
 /* Morton order of the atoms and the renumbered graph (replaces reorder_graph_morton,
  * model.py:47-74): 30-bit codes of the positions quantised to 10 bits per axis over their
  * bounding box, a stable sort by (system << 32 | code), perm [N] (new -> old) and inv_perm [N],

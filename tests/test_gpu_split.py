@@ -160,11 +160,11 @@ def test_fp16_activation_inputs():
 
     f32 = lambda ts: [t.float() for t in ts]   # noqa: E731
     ep = [ptr(d["x"]), ptr(d["idx_i"]), ptr(d["idx_j"]), ptr(wig)]
+    rf = rad_h.float()   # kept alive: the kernels read it after this line
     both("fuma_gather_fwd_f16x3", ep + [ptr(rad_h), ptr(d["csd"]), ptr(d["batch"]), N, E, C],
-         ep + [ptr(rad_h.float()), ptr(d["csd"]), ptr(d["batch"]), N, E, C],
+         ep + [ptr(rf), ptr(d["csd"]), ptr(d["batch"]), N, E, C],
          [(E, 6 * C), (E, 8 * C), (E, 4 * C)], [2, 1, ptr(err), s], [2, 0, ptr(err), s])
     csr = [ptr(g.dst_row_ptr), ptr(g.dst_col), ptr(g.src_row_ptr), ptr(g.src_col)]
-    rf = rad_h.float()
     both("fuma_gather_bwd_f16x3", [ptr(t) for t in gX] + ep[:2] + [ptr(wig), ptr(rad_h), ptr(d["csd"]),
                                                                   ptr(d["batch"])] + csr + [N, E, C, None, 0],
          [ptr(t) for t in gX] + ep[:2] + [ptr(wig), ptr(rf), ptr(d["csd"]), ptr(d["batch"])] + csr + [N, E, C, None, 0],
