@@ -78,66 +78,88 @@ constexpr int kBwdWarps = 8;
 // second read of the indices and Wigner rows, and lowers the live registers of a launch: at 64
 // registers (4 blocks of 8 warps per SM) the pair measured 350 us against 375 us for one
 // 80-register kernel at 3 blocks (E = 120,000, B200).
+// A warp takes chunks of 32 consecutive edges: the lanes load the chunk's edge indices (and, for
+// PART 0, the atoms' system ids) in one coalesced step and the chunk's Wigner blocks into shared
+// memory, so each edge then waits only for its own node and radial rows, not for a chain of
+// index -> system id -> row loads.
 template <int PART, bool kH>
-__global__ void __launch_bounds__(kFwdWarps * 32, 4) gather_fwd_kernel(
+__global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
     const float* __restrict__ x, const int64_t* __restrict__ idx_i, const int64_t* __restrict__ idx_j,
     const float* __restrict__ wig, const float* __restrict__ rad, const float* __restrict__ csd,
     const int64_t* __restrict__ batch, float* __restrict__ X0, float* __restrict__ X1, float* __restrict__ X2,
     int64_t E, int C, int split, int* err) {
-  __shared__ float s_w[kFwdWarps][36];
+  constexpr int nw = PART ? 25 : 9;     // Wigner values of this block per edge
+  constexpr int woff = PART ? 9 : 0;
+  __shared__ float s_w[kFwdWarps][32 * nw];
   bool bad = false;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
-  float* sw = s_w[warp];
-  for (int64_t e = (int64_t)blockIdx.x * kFwdWarps + warp; e < E; e += (int64_t)gridDim.x * kFwdWarps) {
-    if (PART == 0) {
-      if (lane < 9) sw[lane] = __ldg(wig + e * kWig + lane);
-    } else {
-      if (lane < 25) sw[lane] = __ldg(wig + e * kWig + 9 + lane);
+  float* swc = s_w[warp];
+  const int64_t nchunks = (E + 31) >> 5;
+  for (int64_t ch = (int64_t)blockIdx.x * kFwdWarps + warp; ch < nchunks; ch += (int64_t)gridDim.x * kFwdWarps) {
+    const int64_t e0 = ch << 5;
+    const int ne = (int)min((int64_t)32, E - e0);
+    int li = 0, lj = 0, lbi = 0, lbj = 0;   // this lane's edge of the chunk: atoms (and systems)
+    if (lane < ne) {
+      li = (int)idx_i[e0 + lane];
+      lj = (int)idx_j[e0 + lane];
+      if (PART == 0) {
+        lbi = (int)batch[li];
+        lbj = (int)batch[lj];
+      }
     }
-    const int64_t ni = idx_i[e], nj = idx_j[e];
-    int64_t bi = 0, bj = 0;
-    if (PART == 0) {
-      bi = batch[ni];
-      bj = batch[nj];
+    for (int t = lane; t < ne * nw; t += 32) {
+      const int r = t / nw;
+      swc[t] = __ldg(wig + (e0 + r) * kWig + woff + (t - r * nw));
     }
     __syncwarp();
-    for (int c4 = lane; c4 < C4; c4 += 32) {
-      const int co = c4 * 4;
-      const int64_t rr = e * 12 * (int64_t)C + co;   // element offset of the radial row (fp32 or fp16 rad)
-      float* x0 = X0 + e * 6 * (int64_t)C;   // output rows; columns are co + slot * C
-      float* x1 = X1 + e * 8 * (int64_t)C;
-      float* x2 = X2 + e * 4 * (int64_t)C;
 #pragma unroll 1
-      for (int s = 0; s < 2; ++s) {
-        const int64_t node = s ? nj : ni;
-        const float* xr = x + node * 9 * (int64_t)C + co;
-        if constexpr (PART == 0) {
-          const int64_t bsys = s ? bj : bi;
-          const float4 c0 = ld4_keep(xr), cs = ld4_keep(csd + bsys * C + co), r0 = ld4_act<kH>(rad, rr + s * C);
-          float4 v[3];
+    for (int k = 0; k < ne; ++k) {
+      const int64_t e = e0 + k;
+      const int64_t ni = __shfl_sync(kFull, li, k), nj = __shfl_sync(kFull, lj, k);
+      int64_t bi = 0, bj = 0;
+      if (PART == 0) {
+        bi = __shfl_sync(kFull, lbi, k);
+        bj = __shfl_sync(kFull, lbj, k);
+      }
+      const float* sw = swc + k * nw;
+      for (int c4 = lane; c4 < C4; c4 += 32) {
+        const int co = c4 * 4;
+        const int64_t rr = e * 12 * (int64_t)C + co;   // element offset of the radial row (fp32 or fp16 rad)
+        float* x0 = X0 + e * 6 * (int64_t)C;   // output rows; columns are co + slot * C
+        float* x1 = X1 + e * 8 * (int64_t)C;
+        float* x2 = X2 + e * 4 * (int64_t)C;
+#pragma unroll 1
+        for (int s = 0; s < 2; ++s) {
+          const int64_t node = s ? nj : ni;
+          const float* xr = x + node * 9 * (int64_t)C + co;
+          if constexpr (PART == 0) {
+            const int64_t bsys = s ? bj : bi;
+            const float4 c0 = ld4_keep(xr), cs = ld4_keep(csd + bsys * C + co), r0 = ld4_act<kH>(rad, rr + s * C);
+            float4 v[3];
 #pragma unroll
-          for (int m = 0; m < 3; ++m) v[m] = ld4_keep(xr + (1 + m) * C);
-          const float4 r2 = ld4_act<kH>(rad, rr + (2 + s) * C), r6 = ld4_act<kH>(rad, rr + (6 + s) * C);
-          st_out4(x0, 6 * C, s * C + co, (c0 + cs) * r0, split, bad);
-          st_out4(x1, 8 * C, (4 + s) * C + co, rot_row<3>(sw, 0, v) * r6, split, bad);
-          st_out4(x0, 6 * C, (2 + s) * C + co, rot_row<3>(sw, 1, v) * r2, split, bad);
-          st_out4(x1, 8 * C, (0 + s) * C + co, rot_row<3>(sw, 2, v) * r6, split, bad);
-        } else {
-          float4 v[5];
+            for (int m = 0; m < 3; ++m) v[m] = ld4_keep(xr + (1 + m) * C);
+            const float4 r2 = ld4_act<kH>(rad, rr + (2 + s) * C), r6 = ld4_act<kH>(rad, rr + (6 + s) * C);
+            st_out4(x0, 6 * C, s * C + co, (c0 + cs) * r0, split, bad);
+            st_out4(x1, 8 * C, (4 + s) * C + co, rot_row<3>(sw, 0, v) * r6, split, bad);
+            st_out4(x0, 6 * C, (2 + s) * C + co, rot_row<3>(sw, 1, v) * r2, split, bad);
+            st_out4(x1, 8 * C, (0 + s) * C + co, rot_row<3>(sw, 2, v) * r6, split, bad);
+          } else {
+            float4 v[5];
 #pragma unroll
-          for (int m = 0; m < 5; ++m) v[m] = ld4_keep(xr + (4 + m) * C);
-          const float4 r4 = ld4_act<kH>(rad, rr + (4 + s) * C), r8 = ld4_act<kH>(rad, rr + (8 + s) * C),
-                       r10 = ld4_act<kH>(rad, rr + (10 + s) * C);
-          st_out4(x2, 4 * C, (2 + s) * C + co, rot_row<5>(sw, 0, v) * r10, split, bad);
-          st_out4(x1, 8 * C, (6 + s) * C + co, rot_row<5>(sw, 1, v) * r8, split, bad);
-          st_out4(x0, 6 * C, (4 + s) * C + co, rot_row<5>(sw, 2, v) * r4, split, bad);
-          st_out4(x1, 8 * C, (2 + s) * C + co, rot_row<5>(sw, 3, v) * r8, split, bad);
-          st_out4(x2, 4 * C, (0 + s) * C + co, rot_row<5>(sw, 4, v) * r10, split, bad);
+            for (int m = 0; m < 5; ++m) v[m] = ld4_keep(xr + (4 + m) * C);
+            const float4 r4 = ld4_act<kH>(rad, rr + (4 + s) * C), r8 = ld4_act<kH>(rad, rr + (8 + s) * C),
+                         r10 = ld4_act<kH>(rad, rr + (10 + s) * C);
+            st_out4(x2, 4 * C, (2 + s) * C + co, rot_row<5>(sw, 0, v) * r10, split, bad);
+            st_out4(x1, 8 * C, (6 + s) * C + co, rot_row<5>(sw, 1, v) * r8, split, bad);
+            st_out4(x0, 6 * C, (4 + s) * C + co, rot_row<5>(sw, 2, v) * r4, split, bad);
+            st_out4(x1, 8 * C, (2 + s) * C + co, rot_row<5>(sw, 3, v) * r8, split, bad);
+            st_out4(x2, 4 * C, (0 + s) * C + co, rot_row<5>(sw, 4, v) * r10, split, bad);
+          }
         }
       }
     }
-    __syncwarp();
+    __syncwarp();   // the chunk's Wigner blocks are replaced by the next chunk's
   }
   report_split_range(bad, err);
 }
@@ -187,24 +209,23 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
       auto issue = [&](int64_t e, int b) {
         float4* dst = stage + b * kS * 32 + lane;
         if (on) {
-          const float* g0 = gX0 + e * 6 * (int64_t)C + co;
-          const float* g1 = gX1 + e * 8 * (int64_t)C + co;
-          const float* g2 = gX2 + e * 4 * (int64_t)C + co;
-          const int64_t rr = e * (int64_t)W + co;   // element offset of the radial row
+          // element offsets of the edge's gradient and radial rows (fp32, or fp16 with kH)
+          const int64_t g0 = e * 6 * (int64_t)C + co, g1 = e * 8 * (int64_t)C + co, g2 = e * 4 * (int64_t)C + co;
+          const int64_t rr = e * (int64_t)W + co;
           if constexpr (PART == 0) {
-            cp_async16(dst + 0 * 32, g0 + s * C);
-            cp_async16(dst + 1 * 32, g0 + (2 + s) * C);
-            cp_async16(dst + 2 * 32, g1 + s * C);
-            cp_async16(dst + 3 * 32, g1 + (4 + s) * C);
+            cp_act<kH>(dst + 0 * 32, gX0, g0 + s * C);
+            cp_act<kH>(dst + 1 * 32, gX0, g0 + (2 + s) * C);
+            cp_act<kH>(dst + 2 * 32, gX1, g1 + s * C);
+            cp_act<kH>(dst + 3 * 32, gX1, g1 + (4 + s) * C);
             cp_act<kH>(dst + 4 * 32, rad, rr + s * C);
             cp_act<kH>(dst + 5 * 32, rad, rr + (2 + s) * C);
             cp_act<kH>(dst + 6 * 32, rad, rr + (6 + s) * C);
           } else {
-            cp_async16(dst + 0 * 32, g0 + (4 + s) * C);
-            cp_async16(dst + 1 * 32, g1 + (2 + s) * C);
-            cp_async16(dst + 2 * 32, g1 + (6 + s) * C);
-            cp_async16(dst + 3 * 32, g2 + s * C);
-            cp_async16(dst + 4 * 32, g2 + (2 + s) * C);
+            cp_act<kH>(dst + 0 * 32, gX0, g0 + (4 + s) * C);
+            cp_act<kH>(dst + 1 * 32, gX1, g1 + (2 + s) * C);
+            cp_act<kH>(dst + 2 * 32, gX1, g1 + (6 + s) * C);
+            cp_act<kH>(dst + 3 * 32, gX2, g2 + s * C);
+            cp_act<kH>(dst + 4 * 32, gX2, g2 + (2 + s) * C);
             cp_act<kH>(dst + 5 * 32, rad, rr + (4 + s) * C);
             cp_act<kH>(dst + 6 * 32, rad, rr + (8 + s) * C);
             cp_act<kH>(dst + 7 * 32, rad, rr + (10 + s) * C);
@@ -249,7 +270,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
         for (int m = 0; m < NV; ++m) gw[m] = 0.f;
         if constexpr (PART == 0) {
           const float4 z = f4(0.f);
-          const float4 a0 = on ? src[0] : z, a2 = on ? src[32] : z, b0 = on ? src[64] : z, b4 = on ? src[96] : z;
+          const float4 a0 = on ? sm_act<kH>(src) : z, a2 = on ? sm_act<kH>(src + 32) : z,
+                       b0 = on ? sm_act<kH>(src + 64) : z, b4 = on ? sm_act<kH>(src + 96) : z;
           const float4 r0 = on ? sm_act<kH>(src + 128) : z, r2 = on ? sm_act<kH>(src + 160) : z,
                        r6 = on ? sm_act<kH>(src + 192) : z;
           const float* D1 = sw;
@@ -272,8 +294,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
             for (int m = 0; m < 3; ++m) gw[r * 3 + m] = dot4(gi[r], v[1 + m]);
         } else {
           const float4 z = f4(0.f);
-          const float4 a4 = on ? src[0] : z, b2 = on ? src[32] : z, b6 = on ? src[64] : z;
-          const float4 c0 = on ? src[96] : z, c2 = on ? src[128] : z;
+          const float4 a4 = on ? sm_act<kH>(src) : z, b2 = on ? sm_act<kH>(src + 32) : z,
+                       b6 = on ? sm_act<kH>(src + 64) : z;
+          const float4 c0 = on ? sm_act<kH>(src + 96) : z, c2 = on ? sm_act<kH>(src + 128) : z;
           const float4 r4 = on ? sm_act<kH>(src + 160) : z, r8 = on ? sm_act<kH>(src + 192) : z,
                        r10 = on ? sm_act<kH>(src + 224) : z;
           const float* D2 = sw;
@@ -317,9 +340,10 @@ void gather_fwd_launch(const float* x, const int64_t* idx_i, const int64_t* idx_
                        const float* csd, const int64_t* batch, float* X0, float* X1, float* X2, int64_t E, int C,
                        int split, int* err, cudaStream_t s) {
   const int t = kFwdWarps * 32;
-  gather_fwd_kernel<0, kH><<<grid_resident(gather_fwd_kernel<0, kH>, t, E, kFwdWarps), t, 0, s>>>(
+  const int64_t chunks = (E + 31) / 32;   // a warp's unit of work: 32 consecutive edges
+  gather_fwd_kernel<0, kH><<<grid_resident(gather_fwd_kernel<0, kH>, t, chunks, kFwdWarps), t, 0, s>>>(
       x, idx_i, idx_j, wig, rad, csd, batch, X0, X1, X2, E, C, split, err);
-  gather_fwd_kernel<1, kH><<<grid_resident(gather_fwd_kernel<1, kH>, t, E, kFwdWarps), t, 0, s>>>(
+  gather_fwd_kernel<1, kH><<<grid_resident(gather_fwd_kernel<1, kH>, t, chunks, kFwdWarps), t, 0, s>>>(
       x, idx_i, idx_j, wig, rad, csd, batch, X0, X1, X2, E, C, split, err);
 }
 

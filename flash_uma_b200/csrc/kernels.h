@@ -25,8 +25,9 @@ void launch_gather_bwd(const float* gX0, const float* gX1, const float* gX2, con
                        float* g_x, float* g_wig, float* g_rad, float* scratch, int64_t N, int C, int split, int* err,
                        cudaStream_t s, bool act_half = false);
 
-// act_half (the single-product mode's 16-bit activation storage): Y (gating), rad (gather) and
-// the conv2 output Z (rotate-scatter) are fp16 arrays passed as float*, with the same offsets.
+// act_half (the single-product mode's 16-bit storage): the GEMM results these kernels read are
+// fp16 arrays passed as float*, with the same element offsets: Y and gZ (gating), rad and gX
+// (gather), the conv2 output Z (rotate-scatter).
 void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,
                        int C, int split, int* err, cudaStream_t s, bool act_half = false);
 void launch_gating_bwd(const float* gZ0, const float* gZ1, const float* gZ2, const float* Y0, const float* Y1,

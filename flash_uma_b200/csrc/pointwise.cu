@@ -66,18 +66,17 @@ __global__ void __launch_bounds__(256) gating_bwd_kernel(
     const int64_t e = t / C4;
     const int co = (int)(t - e * C4) * 4;
     const int64_t y0 = e * 5 * (int64_t)C + co, y1 = e * 4 * (int64_t)C + co, y2 = e * 2 * (int64_t)C + co;
-    const float* q0 = gZ0 + e * 3 * (int64_t)C + co;
-    const float* q1 = gZ1 + e * 4 * (int64_t)C + co;
-    const float* q2 = gZ2 + e * 2 * (int64_t)C + co;
+    const int64_t q0 = e * 3 * (int64_t)C + co, q1 = e * 4 * (int64_t)C + co, q2 = e * 2 * (int64_t)C + co;
     const float4 g0 = sig4(ld4_act<kH>(Y0, y0)), g1 = sig4(ld4_act<kH>(Y0, y0 + C));
     const float4 a = ld4_act<kH>(Y0, y0 + 2 * C), sa = sig4(a);
     const float4 y3 = ld4_act<kH>(Y0, y0 + 3 * C), y4 = ld4_act<kH>(Y0, y0 + 4 * C);
     const float4 u0 = ld4_act<kH>(Y1, y1), u1 = ld4_act<kH>(Y1, y1 + C), u2 = ld4_act<kH>(Y1, y1 + 2 * C),
                  u3 = ld4_act<kH>(Y1, y1 + 3 * C);
     const float4 w0 = ld4_act<kH>(Y2, y2), w1 = ld4_act<kH>(Y2, y2 + C);
-    const float4 ga = ld4_stream(q0), g3 = ld4_stream(q0 + C), g4 = ld4_stream(q0 + 2 * C);
-    const float4 h0 = ld4_stream(q1), h1 = ld4_stream(q1 + C), h2 = ld4_stream(q1 + 2 * C), h3 = ld4_stream(q1 + 3 * C);
-    const float4 k0 = ld4_stream(q2), k1 = ld4_stream(q2 + C);
+    const float4 ga = ld4_act<kH>(gZ0, q0), g3 = ld4_act<kH>(gZ0, q0 + C), g4 = ld4_act<kH>(gZ0, q0 + 2 * C);
+    const float4 h0 = ld4_act<kH>(gZ1, q1), h1 = ld4_act<kH>(gZ1, q1 + C), h2 = ld4_act<kH>(gZ1, q1 + 2 * C),
+                 h3 = ld4_act<kH>(gZ1, q1 + 3 * C);
+    const float4 k0 = ld4_act<kH>(gZ2, q2), k1 = ld4_act<kH>(gZ2, q2 + C);
     const float4 one = f4(1.f);
     const float4 dg0 = g0 * (one - g0), dg1 = g1 * (one - g1);
     float* p0 = gY0 + e * 5 * (int64_t)C;

@@ -215,7 +215,9 @@ class _MessageBlockFn(torch.autograd.Function):
             rad = saved[6]
             rsaved = saved[7:13]
             Y0, Y1, Y2, O0, O1, O2 = saved[13:19]
-        half = parts == 1   # fp16 radial / conv results in the single-product mode
+        # single-product mode: fp16 radial / conv results, and fp16 results of the two input-gradient
+        # GEMMs read by the gating and gather backward (their operands are fp16 already)
+        half = parts == 1
         gO0, gO1, gO2 = _empty((E, 3 * C), g_mid), _empty((E, 4 * C), g_mid), _empty((E, 2 * C), g_mid)
         g_w = _empty((E, 34), g_mid)
         g_env = _empty((E,), g_mid)
@@ -223,17 +225,17 @@ class _MessageBlockFn(torch.autograd.Function):
                  ptr(graph.dst_row_ptr), ptr(graph.dst_col), N, E, C, ptr(gO0), ptr(gO1), ptr(gO2), ptr(g_w),
                  ptr(g_env), parts, int(half), ptr(err), s)
         del O0, O1, O2
-        gZ0 = _gemm16(gO0, layer.conv2_m0.wt16, None, 3 * C)
-        gZ1 = _gemm16(gO1, layer.conv2_m1.wt16, None, 4 * C)
-        gZ2 = _gemm16(gO2, layer.conv2_m2.wt16, None, 2 * C)
+        gZ0 = _gemm16(gO0, layer.conv2_m0.wt16, None, 3 * C, out_half=half)
+        gZ1 = _gemm16(gO1, layer.conv2_m1.wt16, None, 4 * C, out_half=half)
+        gZ2 = _gemm16(gO2, layer.conv2_m2.wt16, None, 2 * C, out_half=half)
         del gO0, gO1, gO2
         gY0, gY1, gY2 = _empty((E, 5 * C), g_mid), _empty((E, 4 * C), g_mid), _empty((E, 2 * C), g_mid)
         nat.call("fuma_gating_bwd_f16x3", ptr(gZ0), ptr(gZ1), ptr(gZ2), ptr(Y0), ptr(Y1), ptr(Y2), E, C, ptr(gY0),
                  ptr(gY1), ptr(gY2), parts, int(half), ptr(err), s)
         del gZ0, gZ1, gZ2, Y0, Y1, Y2
-        gX0 = _gemm16(gY0, layer.conv1_m0.wt16, None, 5 * C)
-        gX1 = _gemm16(gY1, layer.conv1_m1.wt16, None, 4 * C)
-        gX2 = _gemm16(gY2, layer.conv1_m2.wt16, None, 2 * C)
+        gX0 = _gemm16(gY0, layer.conv1_m0.wt16, None, 5 * C, out_half=half)
+        gX1 = _gemm16(gY1, layer.conv1_m1.wt16, None, 4 * C, out_half=half)
+        gX2 = _gemm16(gY2, layer.conv1_m2.wt16, None, 2 * C, out_half=half)
         del gY0, gY1, gY2
         g_x = torch.empty_like(x_norm)
         g_w2 = _empty((E, 34), g_mid)

@@ -268,12 +268,13 @@ int fuma_split_f16(const float* x, int64_t n, float scale, void* hi, void* lo, v
  * nothing else; the lo halves of the rows are left as they are, so the call moves half the
  * bytes). All other outputs are unchanged. C (D for ln_silu) must be a multiple of 8. err_flag
  * (device int, may be NULL) receives 16 if a finite value is at or beyond the fp16 limit (65520).
- * act_half != 0 (gather, gating and rotate-scatter variants; the 16-bit activation storage of the
+ * act_half != 0 (gather, gating and rotate-scatter variants; the 16-bit storage of the
  * single-product mode, where fuma_linear_f16 writes its results as fp16 with c_half): the radial
- * rows `rad` (gather fwd / bwd), the conv1 results Y_m0..2 (gating fwd / bwd) and the conv2
- * results Z_m0..2 (rotate-scatter fwd / bwd) are fp16 arrays of the same shapes, passed as the
- * same pointers; everything else stays fp32. fuma_rotate_scatter_fwd_f16x3 is
- * fuma_rotate_scatter_fwd with that flag. */
+ * rows `rad` (gather fwd / bwd), the conv1 results Y_m0..2 (gating fwd / bwd), the conv2
+ * results Z_m0..2 (rotate-scatter fwd / bwd) and the input gradients read by the backward
+ * variants, g_X_m0..2 (gather bwd) and g_Z_m0..2 (gating bwd), are fp16 arrays of the same
+ * shapes, passed as the same pointers; everything else stays fp32.
+ * fuma_rotate_scatter_fwd_f16x3 is fuma_rotate_scatter_fwd with that flag. */
 int fuma_ln_silu_fwd_f16x3(const float* x, const float* gamma, const float* beta, float eps, int64_t M, int32_t D,
                            float* out, float* mean, float* rstd, int32_t parts, int* err_flag, void* stream);
 int fuma_ln_silu_bwd_f16x3(const float* x, const float* gamma, const float* beta, const float* mean,

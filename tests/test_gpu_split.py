@@ -124,9 +124,10 @@ def test_hi_only_split_outputs():
 
 
 def test_fp16_activation_inputs():
-    """act_half (the single-product mode's 16-bit storage of the radial, conv1 and conv2 results):
-    gather, gating and rotate-scatter fed fp16 arrays give exactly what they give on the same
-    values in fp32 (the kernels convert each value on load and compute in fp32)."""
+    """act_half (the single-product mode's 16-bit storage of the radial, conv1 and conv2 results
+    and of the input gradients the backward kernels read): gather, gating and rotate-scatter fed
+    fp16 arrays give exactly what they give on the same values in fp32 (the kernels convert each
+    value on load and compute in fp32)."""
     from flash_uma_b200 import _native as nat
     from flash_uma_b200 import ops
     from flash_uma_b200._native import ptr
@@ -144,8 +145,8 @@ def test_fp16_activation_inputs():
     rad_h = torch.randn(E, 12 * C, device=DEV).half()
     Y_h = [torch.randn(E, k * C, device=DEV).half() for k in (5, 4, 2)]
     O_h = [torch.randn(E, k * C, device=DEV).half() for k in (3, 4, 2)]
-    gX = [torch.randn(E, k * C, device=DEV) for k in (6, 8, 4)]
-    gZ = [torch.randn(E, k * C, device=DEV) for k in (3, 4, 2)]
+    gX_h = [torch.randn(E, k * C, device=DEV).half() for k in (6, 8, 4)]
+    gZ_h = [torch.randn(E, k * C, device=DEV).half() for k in (3, 4, 2)]
     gout = torch.randn(N, 9, C, device=DEV)
 
     def both(name, args_h, args_f, outs_shapes, tail_h, tail_f):
@@ -165,15 +166,17 @@ def test_fp16_activation_inputs():
          ep + [ptr(rf), ptr(d["csd"]), ptr(d["batch"]), N, E, C],
          [(E, 6 * C), (E, 8 * C), (E, 4 * C)], [2, 1, ptr(err), s], [2, 0, ptr(err), s])
     csr = [ptr(g.dst_row_ptr), ptr(g.dst_col), ptr(g.src_row_ptr), ptr(g.src_col)]
-    both("fuma_gather_bwd_f16x3", [ptr(t) for t in gX] + ep[:2] + [ptr(wig), ptr(rad_h), ptr(d["csd"]),
-                                                                  ptr(d["batch"])] + csr + [N, E, C, None, 0],
-         [ptr(t) for t in gX] + ep[:2] + [ptr(wig), ptr(rf), ptr(d["csd"]), ptr(d["batch"])] + csr + [N, E, C, None, 0],
+    gXf = f32(gX_h)
+    both("fuma_gather_bwd_f16x3", [ptr(t) for t in gX_h] + ep[:2] + [ptr(wig), ptr(rad_h), ptr(d["csd"]),
+                                                                    ptr(d["batch"])] + csr + [N, E, C, None, 0],
+         [ptr(t) for t in gXf] + ep[:2] + [ptr(wig), ptr(rf), ptr(d["csd"]), ptr(d["batch"])] + csr + [N, E, C, None, 0],
          [(N, 9, C), (E, 34), (E, 12 * C)], [2, 1, ptr(err), s], [2, 0, ptr(err), s])
     Yf = f32(Y_h)
     both("fuma_gating_fwd_f16x3", [ptr(t) for t in Y_h] + [E, C], [ptr(t) for t in Yf] + [E, C],
          [(E, 3 * C), (E, 4 * C), (E, 2 * C)], [2, 1, ptr(err), s], [2, 0, ptr(err), s])
-    both("fuma_gating_bwd_f16x3", [ptr(t) for t in gZ] + [ptr(t) for t in Y_h] + [E, C],
-         [ptr(t) for t in gZ] + [ptr(t) for t in Yf] + [E, C],
+    gZf = f32(gZ_h)
+    both("fuma_gating_bwd_f16x3", [ptr(t) for t in gZ_h] + [ptr(t) for t in Y_h] + [E, C],
+         [ptr(t) for t in gZf] + [ptr(t) for t in Yf] + [E, C],
          [(E, 5 * C), (E, 4 * C), (E, 2 * C)], [2, 1, ptr(err), s], [2, 0, ptr(err), s])
     Of = f32(O_h)
     rs = [ptr(wig), ptr(env), ptr(d["x"]), ptr(g.dst_row_ptr), ptr(g.dst_col), N, E, C]
