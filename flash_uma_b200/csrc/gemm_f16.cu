@@ -436,17 +436,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_kernel(const __grid_co
 constexpr int kTF = 128;   // output features per tile (MMA M)
 constexpr int kTE = 256;   // edges per tile (MMA N)
 
-template <int STAGES>
+template <int STAGES, bool kX3>
 struct F16TSmem {
   static constexpr int kW16 = kTF * kBK * 2;   // 8 KB
   static constexpr int kA16 = kTE * kBK * 2;   // 16 KB
-  static constexpr int kStage = 2 * kW16 + 2 * kA16;
+  static constexpr int kStage = kX3 ? 2 * kW16 + 2 * kA16 : kW16 + kA16;   // the single product loads hi only
   static constexpr int kStaging = 4 * 2 * 4096;
   static constexpr int kBytes = STAGES * kStage + kStaging + 1024 + 1024;
   static_assert(kBytes <= 227 * 1024, "shared memory plan exceeds 227 KB");
 };
 
-template <int STAGES>
+// kX3 = false: the single-product mode (main += W_hi A_hi): one 256-column accumulator per tile,
+// so two of them fill TMEM and the epilogue of one tile overlaps the MMAs of the next; with
+// kOutHalf the results are stored as fp16 (64-byte [32 edges x 32 features] boxes).
+template <int STAGES, bool kX3, bool kOutHalf>
 __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                    const __grid_constant__ CUtensorMap tmAl,
                                                                    const __grid_constant__ CUtensorMap tmWh,
@@ -454,15 +457,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
                                                                    const __grid_constant__ CUtensorMap tmC,
                                                                    const float* __restrict__ bias, float w_scale_inv,
                                                                    int M, int N, int K, int* err) {
-  using L = F16TSmem<STAGES>;
+  static_assert(!kOutHalf || !kX3, "fp16 results belong to the single-product mode");
+  using L = F16TSmem<STAGES, kX3>;
+  constexpr int kAcc = kX3 ? 1 : 2;   // accumulator buffers: main + cross, or two mains
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_c = smem + STAGES * L::kStage;
   uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem_c + L::kStaging);
   uint64_t* bar_empty = bar_full + STAGES;
-  uint64_t* bar_acc_full = bar_empty + STAGES;
-  uint64_t* bar_acc_empty = bar_acc_full + 1;
-  uint64_t* bar_done = bar_acc_empty + 1;
+  uint64_t* bar_acc_full = bar_empty + STAGES;    // [kAcc]
+  uint64_t* bar_acc_empty = bar_acc_full + 2;     // [kAcc]
+  uint64_t* bar_done = bar_acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -470,20 +475,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
   const int num_f = N / kTF;
   const int num_tiles = ((M + kTE - 1) / kTE) * num_f;
   const int num_k = (K + kBK - 1) / kBK;
-  // stage layout: [W_hi | W_lo | A_hi | A_lo]
+  // stage layout: [W_hi | W_lo | A_hi | A_lo] (f16x3) or [W_hi | A_hi] (single product)
   auto stage_Wh = [&](int s) { return smem + s * L::kStage; };
   auto stage_Wl = [&](int s) { return smem + s * L::kStage + L::kW16; };
-  auto stage_Ah = [&](int s) { return smem + s * L::kStage + 2 * L::kW16; };
+  auto stage_Ah = [&](int s) { return smem + s * L::kStage + (kX3 ? 2 : 1) * L::kW16; };
   auto stage_Al = [&](int s) { return smem + s * L::kStage + 2 * L::kW16 + L::kA16; };
-  constexpr uint32_t kTmemCols = 2 * kTE;   // main + cross
+  constexpr uint32_t kTmemCols = 2 * kTE;   // main + cross, or two mains
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(bar_acc_full, 1);
-    mbar_init(bar_acc_empty, 128);
+    for (int b = 0; b < kAcc; ++b) {
+      mbar_init(&bar_acc_full[b], 1);
+      mbar_init(&bar_acc_empty[b], 128);
+    }
     mbar_init(bar_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -501,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
 
   if (warp == kWarpProducer) {
     if (lane == 0) {
-      constexpr uint32_t bytes = 2 * L::kW16 + 2 * L::kA16;
+      constexpr uint32_t bytes = L::kStage;
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         const int e0 = (tile / num_f) * kTE, f0 = (tile % num_f) * kTF;
@@ -511,9 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
             break;
           mbar_expect_tx(&bar_full[s], bytes);
           tma_load_2d(stage_Wh(s), &tmWh, kt * kBK, f0, &bar_full[s]);
-          tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, f0, &bar_full[s]);
+          if constexpr (kX3) tma_load_2d(stage_Wl(s), &tmWl, kt * kBK, f0, &bar_full[s]);
           tma_load_2d(stage_Ah(s), &tmA, kt * kBK, e0, &bar_full[s]);
-          tma_load_2d(stage_Al(s), &tmAl, kt * kBK, e0, &bar_full[s]);
+          if constexpr (kX3) tma_load_2d(stage_Al(s), &tmAl, kt * kBK, e0, &bar_full[s]);
         }
       }
       if (*abort_flag) {
@@ -530,9 +537,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
       int it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++lt) {
-        if (lt >= 1 && !mbar_wait(bar_acc_empty, (lt - 1) & 1, abort_flag, err, kErrWaitAccEmpty)) break;
+        const int b = kAcc == 2 ? (lt & 1) : 0;
+        if (lt >= kAcc && !mbar_wait(&bar_acc_empty[b], ((lt / kAcc) - 1) & 1, abort_flag, err, kErrWaitAccEmpty))
+          break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc_main = tmem, acc_cross = tmem + (uint32_t)kTE;
+        const uint32_t acc_main = tmem + (uint32_t)(b * kTE), acc_cross = tmem + (uint32_t)kTE;
         for (int kt = 0; kt < num_k; ++kt, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&bar_full[s], (it / STAGES) & 1, abort_flag, err, kErrWaitFull)) {
@@ -540,19 +549,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t w_hi = smem_u32(stage_Wh(s)), w_lo = smem_u32(stage_Wl(s));
-          const uint32_t a_hi = smem_u32(stage_Ah(s)), a_lo = smem_u32(stage_Al(s));
+          const uint32_t w_hi = smem_u32(stage_Wh(s)), a_hi = smem_u32(stage_Ah(s));
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint32_t off = kk * 32;
             const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
             mma_f16(acc_main, smem_desc_sw64(w_hi + off), smem_desc_sw64(a_hi + off), idesc, acc);
-            mma_f16(acc_cross, smem_desc_sw64(w_lo + off), smem_desc_sw64(a_hi + off), idesc, acc);
-            mma_f16(acc_cross, smem_desc_sw64(w_hi + off), smem_desc_sw64(a_lo + off), idesc, 1u);
+            if constexpr (kX3) {
+              const uint32_t w_lo = smem_u32(stage_Wl(s)), a_lo = smem_u32(stage_Al(s));
+              mma_f16(acc_cross, smem_desc_sw64(w_lo + off), smem_desc_sw64(a_hi + off), idesc, acc);
+              mma_f16(acc_cross, smem_desc_sw64(w_hi + off), smem_desc_sw64(a_lo + off), idesc, 1u);
+            }
           }
           mma_commit(&bar_empty[s]);
         }
-        if (ok) mma_commit(bar_acc_full);
+        if (ok) mma_commit(&bar_acc_full[b]);
       }
       mma_commit(bar_done);
       for (uint32_t i = 0; i < kWaitLimit && !mbar_try(bar_done, 0); ++i) {
@@ -563,30 +574,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
     // epilogue (warps 6-9): TMEM lane quadrant q = output features f0 + 32q .. f0 + 32q + 31
     const int q = warp & 3;
     int lt = 0, nbox = 0;
+    bool out_bad = false;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
-      bool ok = mbar_wait(bar_acc_full, lt & 1, abort_flag, err, kErrWaitAcc);
+      const int b = kAcc == 2 ? (lt & 1) : 0;
+      bool ok = mbar_wait(&bar_acc_full[b], (lt / kAcc) & 1, abort_flag, err, kErrWaitAcc);
       ok = __all_sync(kFull, ok && !*abort_flag);
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int e0 = (tile / num_f) * kTE, f0 = (tile % num_f) * kTF;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t taddr = tmem + (uint32_t)(b * kTE) + ((uint32_t)(q * 32) << 16);
       const float bv = bias ? bias[f0 + q * 32 + lane] : 0.0f;
 #pragma unroll 1
       for (int c0 = 0; c0 < kTE; c0 += 32) {
         if (e0 + c0 >= M) break;   // whole box beyond the last edge
         uint32_t rm[32], rc[32];
         tmem_ld32(taddr + (uint32_t)c0, rm);
-        tmem_ld32(taddr + (uint32_t)(kTE + c0), rc);
+        if constexpr (kX3) tmem_ld32(taddr + (uint32_t)(kTE + c0), rc);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if constexpr (!kX3) {
+#pragma unroll
+          for (int u = 0; u < 32; ++u) rc[u] = 0u;
+        }
         uint8_t* box = smem_c + (q * 2 + (nbox & 1)) * 4096;
         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
         __syncwarp();
-        // box row j = edge e0 + c0 + j (128 bytes = 32 features), 128-byte swizzle: 16-byte chunk
-        // (lane / 4) of row j at chunk (lane / 4) ^ (j & 7); one row per store instruction
+        if constexpr (kOutHalf) {
+          // box row j = edge e0 + c0 + j (64 bytes = 32 fp16 features), 64-byte swizzle: 16-byte
+          // chunk (lane / 8) of row j at chunk (lane / 8) ^ ((j >> 1) & 3); two lanes share a word
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float v = fmaf(__uint_as_float(rc[j]), kLoScaleInv, __uint_as_float(rm[j])) * w_scale_inv + bv;
-          *reinterpret_cast<float*>(box + j * 128 + ((((lane >> 2) ^ (j & 7))) << 4) + ((lane & 3) << 2)) = v;
+          for (int j = 0; j < 32; ++j) {
+            const float v = __uint_as_float(rm[j]) * w_scale_inv + bv;
+            out_bad |= (fabsf(v) >= 65520.0f) & (fabsf(v) <= 3.402823466e38f);
+            *reinterpret_cast<__half*>(box + j * 64 + (((lane >> 3) ^ ((j >> 1) & 3)) << 4) + ((lane & 7) << 1)) =
+                __float2half_rn(v);
+          }
+        } else {
+          // box row j = edge e0 + c0 + j (128 bytes = 32 features), 128-byte swizzle: 16-byte chunk
+          // (lane / 4) of row j at chunk (lane / 4) ^ (j & 7); one row per store instruction
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float v = fmaf(__uint_as_float(rc[j]), kLoScaleInv, __uint_as_float(rm[j])) * w_scale_inv + bv;
+            *reinterpret_cast<float*>(box + j * 128 + ((((lane >> 2) ^ (j & 7))) << 4) + ((lane & 3) << 2)) = v;
+          }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -597,10 +626,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_f16x3_t_kernel(const __grid_
         ++nbox;
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      mbar_arrive(bar_acc_empty);
+      mbar_arrive(&bar_acc_empty[b]);
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();
+    if (kOutHalf && out_bad && err) atomicCAS(err, 0, (int)kErrRange);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -645,12 +675,12 @@ cudaError_t launch_bn(int BN, const CUtensorMap& a, const CUtensorMap& al, const
   }
 }
 
-template <int STAGES>
+template <int STAGES, bool kX3, bool kOutHalf>
 cudaError_t launch_f16_t(const CUtensorMap& a, const CUtensorMap& al, const CUtensorMap& wh, const CUtensorMap& wl,
                          const CUtensorMap& mc, const float* bias, float w_scale_inv, int M, int N, int K, int* err,
                          cudaStream_t s) {
-  using L = F16TSmem<STAGES>;
-  auto kern = gemm_f16x3_t_kernel<STAGES>;
+  using L = F16TSmem<STAGES, kX3>;
+  auto kern = gemm_f16x3_t_kernel<STAGES, kX3, kOutHalf>;
   static thread_local uint64_t configured = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -690,8 +720,8 @@ const int g_bn256_min_k = [] {
   return e ? atoi(e) : 512;
 }();
 
-// Transposed 128 x 256 tiles (gemm_f16x3_t_kernel) for pre-split f16x3 products whose N is a
-// multiple of 128 that would otherwise run 128-wide tiles, when K >= 384: measured on B200 at
+// Transposed 128 x 256 tiles (gemm_f16x3_t_kernel) for pre-split products (f16x3 and single
+// product) whose N is a multiple of 128 that would otherwise run 128-wide tiles, when K >= 384: measured on B200 at
 // M = 120,000, K = 768, N = 640 0.346 -> 0.290 ms, K = 384, N = 384 0.116 -> 0.109 ms,
 // K = 1536, N = 128 0.179 -> 0.169 ms; shorter K is faster with the double-buffered 128-wide
 // tiles (K = 128: 0.027 -> 0.031 ms). FUMA_GEMM_T=0 / 1 forces them off / on for every
@@ -720,7 +750,23 @@ int launch_gemm_f16x3(const float* A, int64_t lda, bool a_split, const void* W_h
     CUtensorMap mc;
     if (!make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, ldc * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
       return -1;
-    const cudaError_t st = launch_f16_t<4>(ma, mal, mh, ml, mc, bias, w_scale_inv, (int)M, N, K, err, s);
+    const cudaError_t st = launch_f16_t<4, true, false>(ma, mal, mh, ml, mc, bias, w_scale_inv, (int)M, N, K, err, s);
+    return st == cudaSuccess ? 0 : (int)st;
+  }
+  if (a_split && x1 && BN == 128 && N % 128 == 0 && use_t(K)) {
+    // single product: hi halves only, eight stages, two accumulators (overlapped epilogue)
+    const uint8_t* base = reinterpret_cast<const uint8_t*>(A);
+    if (!make_map_t(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, M, K, lda * 4, kBK, kTE, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map_t(&mh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, W_hi, N, K, ldw * 2, kBK, kTF, CU_TENSOR_MAP_SWIZZLE_64B))
+      return -1;
+    CUtensorMap mc;
+    if (!(out_half ? make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, C, M, N, ldc * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+                   : make_map_t(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, ldc * 4, 32, 32,
+                                CU_TENSOR_MAP_SWIZZLE_128B)))
+      return -1;
+    const cudaError_t st =
+        out_half ? launch_f16_t<8, false, true>(ma, ma, mh, mh, mc, bias, w_scale_inv, (int)M, N, K, err, s)
+                 : launch_f16_t<8, false, false>(ma, ma, mh, mh, mc, bias, w_scale_inv, (int)M, N, K, err, s);
     return st == cudaSuccess ? 0 : (int)st;
   }
   if (a_split) {

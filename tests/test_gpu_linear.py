@@ -169,3 +169,33 @@ def test_linear_f16x3_transposed_tiles(M, N, K, monkeypatch):
     ref = x.double() @ W.double().t() + b.double()
     for y in (y0, y1):
         assert (y.double() - ref).abs().max() <= tol(K) * ref.abs().max()
+
+
+@pytest.mark.parametrize("half", [False, True])
+@pytest.mark.parametrize("M,N,K", [(120000, 640, 768), (777, 640, 768), (300, 384, 384), (513, 128, 320),
+                                   (1, 128, 128), (257, 384, 96), (4097, 1536, 128)])
+def test_linear_f16_transposed_tiles(M, N, K, half, monkeypatch):
+    """Single-product mode on the transposed 128 x 256 tiles (two TMEM accumulators, fp32 or fp16
+    results) and on the row-major tiles: both within the accumulation bound of fp64 arithmetic on
+    the same fp16-rounded operands, plus one fp16 rounding of the result when it is stored as
+    fp16 (relative 2^-11)."""
+    from flash_uma_b200.linear import _gemm16, check_errors, split_rows
+    W, b, lin = _lin(N, K, True, "f16", M + 5 * N + K)
+    lin.prepare()
+    g = torch.Generator().manual_seed(M + K)
+    x = torch.randn(M, K, generator=g)
+    xp = split_rows(x.to(DEV))
+    ys = []
+    for t in ("0", "1"):
+        monkeypatch.setenv("FUMA_GEMM_T", t)
+        ys.append(_gemm16(xp, lin.w16, lin.bias_p, K, out_half=half))
+    torch.cuda.synchronize()
+    check_errors()
+    hi, _, inv, x1 = lin.w16
+    assert x1
+    ref = x.half().double() @ (hi[:N, :K].double().cpu() * inv).t() + b.double()
+    for y in ys:
+        assert y.dtype == (torch.float16 if half else torch.float32) and y.shape == (M, N)
+        err = (y[:, :N].cpu().double() - ref).abs()
+        bound = tol(K) * ref.abs().max() + (2.0 ** -11 * ref.abs() if half else 0.0)
+        assert bool((err <= bound).all())
