@@ -130,17 +130,28 @@ __device__ __forceinline__ void split_f16x4(float4 v, uint2& hi, uint2& lo, bool
 // Store 4 consecutive values at column `col` of the [*, W] output row starting at `row`:
 // split = 0: plain fp32 (streaming); 2: the row-packed split (hi and lo halves); 1: only the
 // hi halves of the row-packed split (the operand of the single-product GEMM, which reads
-// nothing else; the lo half of the row is left as it is).
-__device__ __forceinline__ void st_out4(float* row, int W, int col, float4 v, int split, bool& bad) {
+// nothing else; the lo half of the row is left as it is, and no lo value is computed).
+// `amax` keeps the largest magnitude stored as a split; report_split_range checks it once at the
+// end of the kernel (NaN is ignored by fmaxf; an infinity in the data also hides a finite
+// overflow of the same thread, which is then already visible in the results).
+__device__ __forceinline__ void st_out4(float* row, int W, int col, float4 v, int split, float& amax) {
   if (!split) {
     st4_stream(row + col, v);
     return;
   }
-  uint2 hi, lo;
-  split_f16x4(v, hi, lo, bad);
+  const __half2 h01 = __float22half2_rn(make_float2(v.x, v.y));
+  const __half2 h23 = __float22half2_rn(make_float2(v.z, v.w));
   uint8_t* rb = reinterpret_cast<uint8_t*>(row);
-  __stcs(reinterpret_cast<uint2*>(rb + 2 * col), hi);
-  if (split == 2) __stcs(reinterpret_cast<uint2*>(rb + 2 * (W + col)), lo);
+  __stcs(reinterpret_cast<uint2*>(rb + 2 * col), make_uint2(h2_bits(h01), h2_bits(h23)));
+  if (split == 2) {
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 =
+        __float22half2_rn(make_float2((v.x - f01.x) * kSplitLoScale, (v.y - f01.y) * kSplitLoScale));
+    const __half2 l23 =
+        __float22half2_rn(make_float2((v.z - f23.x) * kSplitLoScale, (v.w - f23.y) * kSplitLoScale));
+    __stcs(reinterpret_cast<uint2*>(rb + 2 * (W + col)), make_uint2(h2_bits(l01), h2_bits(l23)));
+  }
+  amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
 }
 
 // ---- 16-bit activation storage (the single-product mode) ------------------------------------
@@ -185,6 +196,9 @@ __device__ __forceinline__ float4 sm_act(const float4* slot) {
 
 __device__ __forceinline__ void report_split_range(bool bad, int* err) {
   if (bad && err) atomicCAS(err, 0, kErrSplitRange);
+}
+__device__ __forceinline__ void report_split_range(float amax, int* err) {
+  if (amax >= 65520.0f && amax <= 3.402823466e38f && err) atomicCAS(err, 0, kErrSplitRange);
 }
 
 // ---- host-side launch helpers ------------------------------------------------------------

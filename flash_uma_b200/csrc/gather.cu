@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
   constexpr int nw = PART ? 25 : 9;     // Wigner values of this block per edge
   constexpr int woff = PART ? 9 : 0;
   __shared__ float s_w[kFwdWarps][32 * nw];
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   float* swc = s_w[warp];
@@ -140,28 +140,28 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 3) gather_fwd_kernel(
 #pragma unroll
             for (int m = 0; m < 3; ++m) v[m] = ld4_keep(xr + (1 + m) * C);
             const float4 r2 = ld4_act<kH>(rad, rr + (2 + s) * C), r6 = ld4_act<kH>(rad, rr + (6 + s) * C);
-            st_out4(x0, 6 * C, s * C + co, (c0 + cs) * r0, split, bad);
-            st_out4(x1, 8 * C, (4 + s) * C + co, rot_row<3>(sw, 0, v) * r6, split, bad);
-            st_out4(x0, 6 * C, (2 + s) * C + co, rot_row<3>(sw, 1, v) * r2, split, bad);
-            st_out4(x1, 8 * C, (0 + s) * C + co, rot_row<3>(sw, 2, v) * r6, split, bad);
+            st_out4(x0, 6 * C, s * C + co, (c0 + cs) * r0, split, amax);
+            st_out4(x1, 8 * C, (4 + s) * C + co, rot_row<3>(sw, 0, v) * r6, split, amax);
+            st_out4(x0, 6 * C, (2 + s) * C + co, rot_row<3>(sw, 1, v) * r2, split, amax);
+            st_out4(x1, 8 * C, (0 + s) * C + co, rot_row<3>(sw, 2, v) * r6, split, amax);
           } else {
             float4 v[5];
 #pragma unroll
             for (int m = 0; m < 5; ++m) v[m] = ld4_keep(xr + (4 + m) * C);
             const float4 r4 = ld4_act<kH>(rad, rr + (4 + s) * C), r8 = ld4_act<kH>(rad, rr + (8 + s) * C),
                          r10 = ld4_act<kH>(rad, rr + (10 + s) * C);
-            st_out4(x2, 4 * C, (2 + s) * C + co, rot_row<5>(sw, 0, v) * r10, split, bad);
-            st_out4(x1, 8 * C, (6 + s) * C + co, rot_row<5>(sw, 1, v) * r8, split, bad);
-            st_out4(x0, 6 * C, (4 + s) * C + co, rot_row<5>(sw, 2, v) * r4, split, bad);
-            st_out4(x1, 8 * C, (2 + s) * C + co, rot_row<5>(sw, 3, v) * r8, split, bad);
-            st_out4(x2, 4 * C, (0 + s) * C + co, rot_row<5>(sw, 4, v) * r10, split, bad);
+            st_out4(x2, 4 * C, (2 + s) * C + co, rot_row<5>(sw, 0, v) * r10, split, amax);
+            st_out4(x1, 8 * C, (6 + s) * C + co, rot_row<5>(sw, 1, v) * r8, split, amax);
+            st_out4(x0, 6 * C, (4 + s) * C + co, rot_row<5>(sw, 2, v) * r4, split, amax);
+            st_out4(x1, 8 * C, (2 + s) * C + co, rot_row<5>(sw, 3, v) * r8, split, amax);
+            st_out4(x2, 4 * C, (0 + s) * C + co, rot_row<5>(sw, 4, v) * r10, split, amax);
           }
         }
       }
     }
     __syncwarp();   // the chunk's Wigner blocks are replaced by the next chunk's
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 template <int PART>
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
   const int C4 = C >> 2;
   const int W = 12 * C;   // g_rad / rad row width
   float4* stage = s_stage + (size_t)warp * 2 * kS * 32;   // [buffer][slot][lane]
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t n = (int64_t)blockIdx.x * kBwdWarps + warp; n < N; n += (int64_t)gridDim.x * kBwdWarps) {
     const int kb = row_ptr[n], ke = row_ptr[n + 1];
     const int64_t bn = batch[n];
@@ -278,9 +278,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
           float4 r1[3];
           rot<3>(D1, v + 1, r1);
           if (on) {
-            st_out4(grow, W, s * C + co, a0 * v[0], split, bad);
-            st_out4(grow, W, (2 + s) * C + co, a2 * r1[1], split, bad);
-            st_out4(grow, W, (6 + s) * C + co, b0 * r1[2] + b4 * r1[0], split, bad);
+            st_out4(grow, W, s * C + co, a0 * v[0], split, amax);
+            st_out4(grow, W, (2 + s) * C + co, a2 * r1[1], split, amax);
+            st_out4(grow, W, (6 + s) * C + co, b0 * r1[2] + b4 * r1[0], split, amax);
           }
           acc[0] += a0 * r0;
           const float4 gi[3] = {b4 * r6, a2 * r2, b0 * r6};
@@ -303,9 +303,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
           float4 rv[5];
           rot<5>(D2, v, rv);
           if (on) {
-            st_out4(grow, W, (4 + s) * C + co, a4 * rv[2], split, bad);
-            st_out4(grow, W, (8 + s) * C + co, b2 * rv[3] + b6 * rv[1], split, bad);
-            st_out4(grow, W, (10 + s) * C + co, c0 * rv[4] + c2 * rv[0], split, bad);
+            st_out4(grow, W, (4 + s) * C + co, a4 * rv[2], split, amax);
+            st_out4(grow, W, (8 + s) * C + co, b2 * rv[3] + b6 * rv[1], split, amax);
+            st_out4(grow, W, (10 + s) * C + co, c0 * rv[4] + c2 * rv[0], split, amax);
           }
           const float4 g[5] = {c2 * r10, b6 * r8, a4 * r4, b2 * r8, c0 * r10};
           float4 t[5];
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
       }
     }
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 template <bool kH>

@@ -195,20 +195,20 @@ __global__ void __launch_bounds__(256) atomwise_gate_fwd_kernel(const float* __r
                                                                  const float* __restrict__ b1, int64_t N, int H,
                                                                  float* __restrict__ z, int split, int* err) {
   const int H4 = H >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * H4; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = t / H4;
     const int c = (int)(t - n * H4) * 4;
     const float4 g1 = sig4n(silu4(ld4(u + n * 2 * H + c))), g2 = sig4n(silu4(ld4(u + n * 2 * H + H + c)));
-    st_out4(z + n * H, H, c, silu4(ld4(h + n * ldh + c) + ld4_keep(b1 + c)), split, bad);
+    st_out4(z + n * H, H, c, silu4(ld4(h + n * ldh + c) + ld4_keep(b1 + c)), split, amax);
 #pragma unroll
     for (int k = 1; k < 9; ++k) {
       const int64_t r = k * N + n;
       const float4 v = ld4(h + r * ldh + (blocked ? coef_degree(k) * H : 0) + c);
-      st_out4(z + r * H, H, c, v * (k < 4 ? g1 : g2), split, bad);
+      st_out4(z + r * H, H, c, v * (k < 4 ? g1 : g2), split, amax);
     }
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 // Backward of the gating, given gz = dL/dz on coefficient rows (same layout as h): gh = dL/dh
@@ -220,31 +220,31 @@ __global__ void __launch_bounds__(256) atomwise_gate_bwd_kernel(const float* __r
                                                                  float* __restrict__ gh, float* __restrict__ gu,
                                                                  int split, int* err) {
   const int H4 = H >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * H4; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = t / H4;
     const int c = (int)(t - n * H4) * 4;
     const float4 u1 = ld4(u + n * 2 * H + c), u2 = ld4(u + n * 2 * H + H + c);
     const float4 a1 = silu4(u1), a2 = silu4(u2);
     const float4 g1 = sig4n(a1), g2 = sig4n(a2);
-    st_out4(gh + n * H, H, c, ld4(gz + n * ldh + c) * dsilu4(ld4(h + n * ldh + c) + ld4_keep(b1 + c)), split, bad);
+    st_out4(gh + n * H, H, c, ld4(gz + n * ldh + c) * dsilu4(ld4(h + n * ldh + c) + ld4_keep(b1 + c)), split, amax);
     float4 s1 = f4(0.f), s2 = f4(0.f);
 #pragma unroll
     for (int k = 1; k < 9; ++k) {
       const int64_t r = k * N + n;
       const int64_t o = r * ldh + (blocked ? coef_degree(k) * H : 0) + c;
       const float4 g = ld4(gz + o);
-      st_out4(gh + r * H, H, c, g * (k < 4 ? g1 : g2), split, bad);
+      st_out4(gh + r * H, H, c, g * (k < 4 ? g1 : g2), split, amax);
       if (k < 4)
         s1 += g * ld4(h + o);
       else
         s2 += g * ld4(h + o);
     }
     const float4 one = f4(1.f);
-    st_out4(gu + n * 2 * H, 2 * H, c, s1 * (g1 * (one - g1)) * dsilu4(u1), split, bad);
-    st_out4(gu + n * 2 * H, 2 * H, H + c, s2 * (g2 * (one - g2)) * dsilu4(u2), split, bad);
+    st_out4(gu + n * 2 * H, 2 * H, c, s1 * (g1 * (one - g1)) * dsilu4(u1), split, amax);
+    st_out4(gu + n * 2 * H, 2 * H, H + c, s2 * (g2 * (one - g2)) * dsilu4(u2), split, amax);
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 // out[n, k, :] = src[k * N + n, block(k) :] (+ add[n, k, :]) (+ row0[n or 0, :] on k = 0):
@@ -274,16 +274,16 @@ __global__ void __launch_bounds__(256) coef_to_node_kernel(const float* __restri
 __global__ void __launch_bounds__(256) node_to_coef_kernel(const float* __restrict__ x, int64_t N, int W,
                                                            float* __restrict__ out, int split, int* err) {
   const int W4 = W >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < N * 9 * W4;
        t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t nk = t / W4;
     const int c = (int)(t - nk * W4) * 4;
     const int64_t n = nk / 9;
     const int k = (int)(nk - n * 9);
-    st_out4(out + (k * N + n) * W, W, c, ld4_stream(x + nk * W + c), split, bad);
+    st_out4(out + (k * N + n) * W, W, c, ld4_stream(x + nk * W + c), split, amax);
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 void launch_atomwise_gate_fwd(const float* h, int64_t ldh, bool blocked, const float* u, const float* b1, int64_t N,

@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict
                                                          float* __restrict__ Z1, float* __restrict__ Z2, int64_t E,
                                                          int C, int split, int* err) {
   const int C4 = C >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   const int64_t total = E * C4;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = t / C4;
@@ -40,17 +40,17 @@ __global__ void __launch_bounds__(256) gating_fwd_kernel(const float* __restrict
     float* z0 = Z0 + e * 3 * (int64_t)C;
     float* z1 = Z1 + e * 4 * (int64_t)C;
     float* z2 = Z2 + e * 2 * (int64_t)C;
-    st_out4(z0, 3 * C, co, a * sig4(a), split, bad);
-    st_out4(z0, 3 * C, C + co, y3 * g0, split, bad);
-    st_out4(z0, 3 * C, 2 * C + co, y4 * g1, split, bad);
-    st_out4(z1, 4 * C, co, u0 * g0, split, bad);
-    st_out4(z1, 4 * C, C + co, u1 * g1, split, bad);
-    st_out4(z1, 4 * C, 2 * C + co, u2 * g0, split, bad);
-    st_out4(z1, 4 * C, 3 * C + co, u3 * g1, split, bad);
-    st_out4(z2, 2 * C, co, w0 * g1, split, bad);
-    st_out4(z2, 2 * C, C + co, w1 * g1, split, bad);
+    st_out4(z0, 3 * C, co, a * sig4(a), split, amax);
+    st_out4(z0, 3 * C, C + co, y3 * g0, split, amax);
+    st_out4(z0, 3 * C, 2 * C + co, y4 * g1, split, amax);
+    st_out4(z1, 4 * C, co, u0 * g0, split, amax);
+    st_out4(z1, 4 * C, C + co, u1 * g1, split, amax);
+    st_out4(z1, 4 * C, 2 * C + co, u2 * g0, split, amax);
+    st_out4(z1, 4 * C, 3 * C + co, u3 * g1, split, amax);
+    st_out4(z2, 2 * C, co, w0 * g1, split, amax);
+    st_out4(z2, 2 * C, C + co, w1 * g1, split, amax);
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 template <bool kH>
@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(256) gating_bwd_kernel(
     float* __restrict__ gY0, float* __restrict__ gY1, float* __restrict__ gY2, int64_t E, int C, int split,
     int* err) {
   const int C4 = C >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   const int64_t total = E * C4;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = t / C4;
@@ -82,19 +82,19 @@ __global__ void __launch_bounds__(256) gating_bwd_kernel(
     float* p0 = gY0 + e * 5 * (int64_t)C;
     float* p1 = gY1 + e * 4 * (int64_t)C;
     float* p2 = gY2 + e * 2 * (int64_t)C;
-    st_out4(p0, 5 * C, co, dg0 * (g3 * y3 + h0 * u0 + h2 * u2), split, bad);
-    st_out4(p0, 5 * C, C + co, dg1 * (g4 * y4 + h1 * u1 + h3 * u3 + k0 * w0 + k1 * w1), split, bad);
-    st_out4(p0, 5 * C, 2 * C + co, ga * (sa + a * (sa * (one - sa))), split, bad);
-    st_out4(p0, 5 * C, 3 * C + co, g3 * g0, split, bad);
-    st_out4(p0, 5 * C, 4 * C + co, g4 * g1, split, bad);
-    st_out4(p1, 4 * C, co, h0 * g0, split, bad);
-    st_out4(p1, 4 * C, C + co, h1 * g1, split, bad);
-    st_out4(p1, 4 * C, 2 * C + co, h2 * g0, split, bad);
-    st_out4(p1, 4 * C, 3 * C + co, h3 * g1, split, bad);
-    st_out4(p2, 2 * C, co, k0 * g1, split, bad);
-    st_out4(p2, 2 * C, C + co, k1 * g1, split, bad);
+    st_out4(p0, 5 * C, co, dg0 * (g3 * y3 + h0 * u0 + h2 * u2), split, amax);
+    st_out4(p0, 5 * C, C + co, dg1 * (g4 * y4 + h1 * u1 + h3 * u3 + k0 * w0 + k1 * w1), split, amax);
+    st_out4(p0, 5 * C, 2 * C + co, ga * (sa + a * (sa * (one - sa))), split, amax);
+    st_out4(p0, 5 * C, 3 * C + co, g3 * g0, split, amax);
+    st_out4(p0, 5 * C, 4 * C + co, g4 * g1, split, amax);
+    st_out4(p1, 4 * C, co, h0 * g0, split, amax);
+    st_out4(p1, 4 * C, C + co, h1 * g1, split, amax);
+    st_out4(p1, 4 * C, 2 * C + co, h2 * g0, split, amax);
+    st_out4(p1, 4 * C, 3 * C + co, h3 * g1, split, amax);
+    st_out4(p2, 2 * C, co, k0 * g1, split, amax);
+    st_out4(p2, 2 * C, C + co, k1 * g1, split, amax);
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 // One warp per group of ROWS rows (their loads in flight together); VPL float4 per lane
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_kernel(const float* __restric
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int D4 = D >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t r0 = ((int64_t)blockIdx.x * wpb + warp) * ROWS; r0 < M; r0 += (int64_t)gridDim.x * wpb * ROWS) {
     float4 v[ROWS][VPL];
     float s[ROWS];
@@ -151,12 +151,12 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_kernel(const float* __restric
         const int d4 = lane + 32 * q;
         if (d4 < D4) {
           const float4 y = (v[i][q] - f4(mean[i])) * rstd[i] * ld4_keep(gamma + d4 * 4) + ld4_keep(beta + d4 * 4);
-          st_out4(orow, D, d4 * 4, y * sig4(y), split, bad);
+          st_out4(orow, D, d4 * 4, y * sig4(y), split, amax);
         }
       }
     }
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 template <int VPL, int ROWS>
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restric
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int D4 = D >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t r0 = ((int64_t)blockIdx.x * wpb + warp) * ROWS; r0 < M; r0 += (int64_t)gridDim.x * wpb * ROWS) {
     float4 xh[ROWS][VPL], gxh[ROWS][VPL];
     float s1[ROWS], s2[ROWS], rs[ROWS];
@@ -212,11 +212,11 @@ __global__ void __launch_bounds__(256) ln_silu_bwd_kernel(const float* __restric
       for (int q = 0; q < VPL; ++q) {
         const int d4 = lane + 32 * q;
         if (d4 < D4)
-          st_out4(g_x + r * D, D, d4 * 4, (gxh[i][q] - (f4(s1[i]) + xh[i][q] * s2[i]) * invD) * rs[i], split, bad);
+          st_out4(g_x + r * D, D, d4 * 4, (gxh[i][q] - (f4(s1[i]) + xh[i][q] * s2[i]) * invD) * rs[i], split, amax);
       }
     }
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 // Backward of rows of at most 128 values, one row per warp per iteration with the next row's
@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(256, 4) ln_silu_bwd_row_kernel(const float* __
   const bool act = lane < D4;
   const float invD = 1.0f / (float)D;
   const float4 gm = act ? ld4_keep(gamma + lane * 4) : f4(0.f), bt = act ? ld4_keep(beta + lane * 4) : f4(0.f);
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
   float4 nx = f4(0.f), ng = f4(0.f);
   float nmu = 0.f, nrs = 0.f;
@@ -271,9 +271,9 @@ __global__ void __launch_bounds__(256, 4) ln_silu_bwd_row_kernel(const float* __
     }
     const float s1 = warp_sum((gxh.x + gxh.y) + (gxh.z + gxh.w));
     const float s2 = warp_sum(dot4(gxh, xh));
-    if (act) st_out4(g_x + r * D, D, lane * 4, (gxh - (f4(s1) + xh * s2) * invD) * rs, split, bad);
+    if (act) st_out4(g_x + r * D, D, lane * 4, (gxh - (f4(s1) + xh * s2) * invD) * rs, split, amax);
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 // (A one-row-per-warp forward with the next row's load in flight, the scheme of
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_short_kernel(const float* __r
   const int wpb = blockDim.x >> 5;
   const int sub = lane >> 3, l8 = lane & 7;
   const int D4 = D >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t r0 = ((int64_t)blockIdx.x * wpb + warp) * 4; r0 < M; r0 += (int64_t)gridDim.x * wpb * 4) {
     const int64_t r = r0 + sub;
     const bool ok = r < M;
@@ -330,12 +330,12 @@ __global__ void __launch_bounds__(256) ln_silu_fwd_short_kernel(const float* __r
         const int d4 = l8 + 8 * q;
         if (d4 < D4) {
           const float4 y = (v[q] - f4(mean)) * rstd * ld4_keep(gamma + d4 * 4) + ld4_keep(beta + d4 * 4);
-          st_out4(out + r * D, D, d4 * 4, y * sig4(y), split, bad);
+          st_out4(out + r * D, D, d4 * 4, y * sig4(y), split, amax);
         }
       }
     }
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 void launch_gating_fwd(const float* Y0, const float* Y1, const float* Y2, float* Z0, float* Z1, float* Z2, int64_t E,

@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     for (int cb = 0; cb < C4; cb += 32) {
@@ -247,10 +247,10 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
             t1[r] = a * ev;
           }
           if (on) {
-            st_out4(q0, 3 * C, co, g[0] * ev, split, bad);
-            st_out4(q0, 3 * C, C + co, t1[1], split, bad);
-            st_out4(q1, 4 * C, co, t1[2], split, bad);
-            st_out4(q1, 4 * C, 2 * C + co, t1[0], split, bad);
+            st_out4(q0, 3 * C, co, g[0] * ev, split, amax);
+            st_out4(q0, 3 * C, C + co, t1[1], split, amax);
+            st_out4(q1, 4 * C, co, t1[2], split, amax);
+            st_out4(q1, 4 * C, 2 * C + co, t1[0], split, amax);
           }
 #pragma unroll
           for (int r = 0; r < 3; ++r)
@@ -270,11 +270,11 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
             t2[r] = a * ev;
           }
           if (on) {
-            st_out4(q0, 3 * C, 2 * C + co, t2[2], split, bad);
-            st_out4(q1, 4 * C, C + co, t2[3], split, bad);
-            st_out4(q1, 4 * C, 3 * C + co, t2[1], split, bad);
-            st_out4(q2, 2 * C, co, t2[4], split, bad);
-            st_out4(q2, 2 * C, C + co, t2[0], split, bad);
+            st_out4(q0, 3 * C, 2 * C + co, t2[2], split, amax);
+            st_out4(q1, 4 * C, C + co, t2[3], split, amax);
+            st_out4(q1, 4 * C, 3 * C + co, t2[1], split, amax);
+            st_out4(q2, 2 * C, co, t2[4], split, amax);
+            st_out4(q2, 2 * C, C + co, t2[0], split, amax);
           }
 #pragma unroll
           for (int r = 0; r < 5; ++r)
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
       }
     }
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 // Initial embedding scatter (the reference's init_node_scatter forward, ops/scatter.py:382-423),
@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
     int* err) {
   __shared__ float4 s_stage[WARPS][kRing][3][32];   // radial slots 0-2 of the staged edges
   __shared__ float s_w[WARPS][kRing][12];          // D1 row 1 (0-2), D2 row 2 (3-7), envelope (8)
-  bool bad = false;
+  float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
@@ -467,9 +467,9 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
         for (int kk = 1; kk < 5; ++kk) fma4(s2, sw[3 + kk], g[4 + kk]);
         if (on) {
           float* gr = g_rad + e * 3 * (int64_t)C;
-          st_out4(gr, 3 * C, co, g[0] * ev, split, bad);
-          st_out4(gr, 3 * C, C + co, s1 * ev, split, bad);
-          st_out4(gr, 3 * C, 2 * C + co, s2 * ev, split, bad);
+          st_out4(gr, 3 * C, co, g[0] * ev, split, amax);
+          st_out4(gr, 3 * C, C + co, s1 * ev, split, amax);
+          st_out4(gr, 3 * C, 2 * C + co, s2 * ev, split, amax);
         }
         float part[16];
 #pragma unroll
@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
       cp_async_wait<0>();
     }
   }
-  report_split_range(bad, err);
+  report_split_range(amax, err);
 }
 
 template <bool kH>
