@@ -816,8 +816,12 @@ def load_reference_gpu():
     # The reference autotunes its Triton kernels on first use (minutes of compiling and timing
     # candidate configurations on a fresh machine). Triton's own on-disk cache, with autotuning
     # results included, is kept next to the installed reference so that a fresh box starts from
-    # the results of an earlier run on the same GPU model; an explicit TRITON_CACHE_DIR wins.
-    os.environ.setdefault("TRITON_CACHE_DIR", os.path.join(REF_DIR, "triton_cache"))
+    # the results of an earlier run on the same GPU model. TRITON_CACHE_DIR is set, not
+    # defaulted: torch.compile points it at inductor's own cache once it has compiled anything in
+    # the process, and the reference would then autotune from scratch (~11 minutes measured in a
+    # test session that compiled a model first). FLASHUMA_REF_TRITON_CACHE_DIR picks another.
+    os.environ["TRITON_CACHE_DIR"] = os.environ.get("FLASHUMA_REF_TRITON_CACHE_DIR",
+                                                    os.path.join(REF_DIR, "triton_cache"))
     os.environ.setdefault("TRITON_CACHE_AUTOTUNING", "1")
     from flash_uma_b200.nodewise import balance_channels_batched
     for name in ["fairchem", "fairchem.core", "fairchem.core.models", "fairchem.core.models.uma",
