@@ -201,7 +201,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) gather_bwd_side_kernel(
   const int W = 12 * C;   // g_rad / rad row width
   float4* stage = s_stage + (size_t)warp * 2 * kS * 32;   // [buffer][slot][lane]
   float amax = 0.f;   // largest magnitude written as a split (range check at the end)
-  for (int64_t n = (int64_t)blockIdx.x * kBwdWarps + warp; n < N; n += (int64_t)gridDim.x * kBwdWarps) {
+  const Share sh = warp_share(N, (int64_t)blockIdx.x * kBwdWarps + warp, (int64_t)gridDim.x * kBwdWarps);
+  for (int64_t n = sh.begin; n < sh.end; ++n) {
     const int kb = row_ptr[n], ke = row_ptr[n + 1];
     const int64_t bn = batch[n];
     for (int cb = 0; cb < C4; cb += 32) {

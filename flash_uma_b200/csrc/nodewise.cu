@@ -33,7 +33,8 @@ __global__ void __launch_bounds__(kNodeWarps * 32) rmsnorm_sh_fwd_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   const float invC = 1.0f / (float)C;
-  for (int64_t n = (int64_t)blockIdx.x * kNodeWarps + warp; n < N; n += (int64_t)gridDim.x * kNodeWarps) {
+  const Share sh = warp_share(N, (int64_t)blockIdx.x * kNodeWarps + warp, (int64_t)gridDim.x * kNodeWarps);
+  for (int64_t n = sh.begin; n < sh.end; ++n) {
     const float* xr = x + n * 9 * (int64_t)C;
     float4 v[9][VPL];
 #pragma unroll
@@ -84,7 +85,8 @@ __global__ void __launch_bounds__(kNodeWarps * 32) rmsnorm_sh_bwd_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
   const float invC = 1.0f / (float)C;
-  for (int64_t n = (int64_t)blockIdx.x * kNodeWarps + warp; n < N; n += (int64_t)gridDim.x * kNodeWarps) {
+  const Share sh = warp_share(N, (int64_t)blockIdx.x * kNodeWarps + warp, (int64_t)gridDim.x * kNodeWarps);
+  for (int64_t n = sh.begin; n < sh.end; ++n) {
     const float* xr = x + n * 9 * (int64_t)C;
     const float* gr = g_out + n * 9 * (int64_t)C;
     float4 f[9][VPL], gw[9][VPL];

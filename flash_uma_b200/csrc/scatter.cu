@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(128, 4) rotate_scatter_fwd_kernel(
   __shared__ float s_w[kFwdWarps][kRing][28];   // Wigner block (0..kW-1) and envelope (27)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
+  // grid-stride over atoms: contiguous even shares (warp_share) measured 4% slower here
   for (int64_t jn = (int64_t)blockIdx.x * kFwdWarps + warp; jn < N; jn += (int64_t)gridDim.x * kFwdWarps) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     for (int cb = 0; cb < C4; cb += 32) {
@@ -170,7 +171,8 @@ __global__ void __launch_bounds__(256, 2) rotate_scatter_bwd_kernel(
   const int wpb = blockDim.x >> 5;
   const int C4 = C >> 2;
   float amax = 0.f;   // largest magnitude written as a split (range check at the end)
-  for (int64_t jn = (int64_t)blockIdx.x * wpb + warp; jn < N; jn += (int64_t)gridDim.x * wpb) {
+  const Share sh = warp_share(N, (int64_t)blockIdx.x * wpb + warp, (int64_t)gridDim.x * wpb);
+  for (int64_t jn = sh.begin; jn < sh.end; ++jn) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     for (int cb = 0; cb < C4; cb += 32) {
       const int c4 = cb + lane;
@@ -314,7 +316,8 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_fwd_kernel(
   __shared__ float s_w[WARPS][kRing][12];          // D1 row 1 (0-2), D2 row 2 (3-7), envelope (8)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
-  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+  const Share sh = warp_share(N, (int64_t)blockIdx.x * WARPS + warp, (int64_t)gridDim.x * WARPS);
+  for (int64_t jn = sh.begin; jn < sh.end; ++jn) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     const int64_t z = Z[jn], b = batch[jn];
     for (int c0 = 0; c0 < C4; c0 += 32) {
@@ -403,7 +406,8 @@ __global__ void __launch_bounds__(WARPS * 32) init_scatter_bwd_kernel(
   float amax = 0.f;   // largest magnitude written as a split (range check at the end)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C4 = C >> 2;
-  for (int64_t jn = (int64_t)blockIdx.x * WARPS + warp; jn < N; jn += (int64_t)gridDim.x * WARPS) {
+  const Share sh = warp_share(N, (int64_t)blockIdx.x * WARPS + warp, (int64_t)gridDim.x * WARPS);
+  for (int64_t jn = sh.begin; jn < sh.end; ++jn) {
     const int kb = row_ptr[jn], ke = row_ptr[jn + 1];
     for (int cb = 0; cb < C4; cb += 32) {
       const int c4 = cb + lane;
