@@ -75,14 +75,18 @@ def alg_bytes(name, N, E, C, B, M_rows=None, D=None):
 # 2*70C^2, conv2 2*29C^2 in the forward; the input-gradient GEMMs of the backward have the same
 # count, except that with gauss_only the first radial layer's gradient covers only the B
 # Gaussian columns (the fused path: the embedding columns do not depend on positions)
-def gemm_flops_per_step(E, C, B, L, H=None, gauss_only=True):
+def gemm_flops_per_step(E, C, B, L, H=None, gauss_only=True, N_atomwise=0):
+    """``N_atomwise``: atoms whose gated atom-wise block runs on the same GEMM kernel (the fp16
+    modes): its scalar MLP and two per-degree maps, 40 N C H forward and 40 N C H for the input
+    gradients per layer (the stacked-degree GEMMs also compute two unused degree blocks, which
+    are not counted)."""
     H = H or C
     rad_layer = 2 * ((B + 2 * C) * H + H * H + H * 12 * C)
     rad_init = 2 * ((B + 2 * C) * H + H * H + H * 3 * C)
     so2 = 2 * 70 * C * C + 2 * 29 * C * C
     fwd = E * (L * (rad_layer + so2) + rad_init)
     bwd = fwd - (E * (L + 1) * 2 * 2 * C * H if gauss_only else 0)
-    return fwd + bwd
+    return fwd + bwd + 80 * N_atomwise * C * H * L
 
 
 GEMM_OPS = ("fuma_linear_f16x3", "fuma_linear", "fuma_linear_f16")
@@ -105,14 +109,15 @@ def gemm_mode(mode, bf16):
             "peak_note": "dense TF32 taken as half the measured dense bf16 rate"}
 
 
-def gemm_summary(per_op, E, C, B, L, mode):
+def gemm_summary(per_op, E, C, B, L, mode, N=0):
     """Dense-contraction share of one step (from the probe pass): fp32-equivalent FLOP rate and the
     tensor-pipe rate (3 products per fp32 product in the split modes)."""
     g = gemm_mode(mode, 0.0)
     ms = per_op.get(g["op"])
     if not ms:
         return None
-    flops = gemm_flops_per_step(E, C, B, L, gauss_only=mode in ("f16x3", "f16"))
+    f16 = mode in ("f16x3", "f16")
+    flops = gemm_flops_per_step(E, C, B, L, gauss_only=f16, N_atomwise=N if f16 else 0)
     return {"flops_per_step": flops, "ms_per_step": ms, "tflops_fp32_equiv": flops / (ms * 1e-3) / 1e12,
             "tflops_pipe": g["passes"] * flops / (ms * 1e-3) / 1e12, "pipe": g["pipe"], "passes": g["passes"]}
 
@@ -397,7 +402,9 @@ def run_flash(args, rank, world, device):
         # FLOPs, 2 x M x N x K per product) over the measured dense bf16 peak; the split modes run
         # ``passes`` tensor-pipe products per fp32 product, reported apart as the pipe utilisation
         launches = gprobe.counts.get(dominant, 1) if graphed else probe.counts.get(dominant, 1) // K
-        flops = gemm_flops_per_step(Ek, C, B, L, gauss_only=args.gemm in ("f16x3", "f16"))
+        f16 = args.gemm in ("f16x3", "f16")
+        n_aw = (len(plan.owned) if world > 1 else N) if f16 else 0   # atom-wise blocks run on owned atoms
+        flops = gemm_flops_per_step(Ek, C, B, L, gauss_only=f16, N_atomwise=n_aw)
         flops_launch = flops / max(1, launches)
         achieved = flops_launch / (avg_ms * 1e-3) / 1e12
         roof = {"kernel": gm["kernel"], "bound": "tensor", "achieved": achieved,
@@ -448,7 +455,7 @@ def run_flash(args, rank, world, device):
         "max_device_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
         "roofline": roof,
         "roofline_top_hbm_kernel": roof_mem,
-        "gemm": gemm_summary(per_op, Ek, C, B, L, args.gemm),
+        "gemm": gemm_summary(per_op, Ek, C, B, L, args.gemm, len(plan.owned) if world > 1 else N),
         "gpu_launches": gpu_launches,
         "per_kernel_ms_one_step": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
         "clocks": clocks,
