@@ -316,3 +316,33 @@ def test_config2_message_block_full_size(cfg2):
     assert _rel(gw[Es.to(DEV)], gw_o[pos]) < 5e-5
     assert _rel(ge[Es.to(DEV)], ge_o[pos]) < 5e-5
     assert _rel(gg[Es.to(DEV)], gg_o[pos]) < 5e-5
+
+
+def test_config3_f16_mode_tf32_accuracy_class():
+    """The single-product "f16" mode (16-bit storage of the per-edge GEMM results, one fp16
+    product per GEMM) on the full config-3 system, against the default f16x3 path (itself held to
+    the fp64 oracle above): within the TF32 accuracy class (energy 1e-3 relative, forces
+    1e-2 eV/A; the reference's own TF32 path deviates 2e-2 eV/A on this system), no fp16 range
+    error at this size, and bitwise reproducible run to run."""
+    from flash_uma_b200.linear import check_errors
+    from flash_uma_b200.predict import Predictor
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone, make_energy_head
+    from flash_uma_b200.systems import config3_system, to_graph
+    from flash_uma_b200.wrapper import ZeroAllocBackbone
+    data = to_graph([config3_system()]).to(DEV)
+    off = SyntheticESCNMDBackbone(seed=0)
+    head = make_energy_head(128, 128, seed=1).to(DEV)
+    out = {}
+    for gemm in ("f16x3", "f16"):
+        bb = ZeroAllocBackbone(copy.deepcopy(off).to(DEV), gemm=gemm)
+        pred = Predictor(bb, head)
+        out[gemm] = [pred(data) for _ in range(2)]
+    torch.cuda.synchronize()
+    check_errors()
+    a, b = out["f16"]
+    assert torch.equal(a["energy"], b["energy"]) and torch.equal(a["forces"], b["forces"])
+    ref = out["f16x3"][0]
+    erel = ((a["energy"].double() - ref["energy"].double()).abs() / ref["energy"].double().abs()).max().item()
+    ferr = (a["forces"].double() - ref["forces"].double()).abs().max().item()
+    assert erel < 1e-3, erel
+    assert ferr < 1e-2, ferr
