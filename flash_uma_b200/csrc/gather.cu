@@ -77,16 +77,16 @@ constexpr int kBwdWarps = 8;
 // D2). The two read disjoint parts of every radial and node row, so splitting costs only the
 // second read of the indices and Wigner rows, and lowers the live registers of a launch: at 64
 // registers (4 blocks of 8 warps per SM) the pair measured 350 us against 375 us for one
-// 80-register kernel at 3 blocks (E = 120,000, B200). With the chunked loop below, PART 0 runs at
-// 64 registers (4 blocks per SM) and PART 1 at 80 (3 blocks): PART 0 at 80 registers measured
-// 8% slower per layer pair at E = 120,000; an L2 evict-last hint on the node-row loads measured
-// 3% slower, and is not used.
+// 80-register kernel at 3 blocks (E = 120,000, B200). With the chunked loop below both parts
+// still run at 64 registers (4 blocks per SM), PART 1 with a few spilled registers: at 80
+// registers (3 blocks) the pair measured 10% slower at E = 120,000; an L2 evict-last hint on the
+// node-row loads measured 3% slower, and is not used.
 // A warp takes chunks of 32 consecutive edges: the lanes load the chunk's edge indices (and, for
 // PART 0, the atoms' system ids) in one coalesced step and the chunk's Wigner blocks into shared
 // memory, so each edge then waits only for its own node and radial rows, not for a chain of
 // index -> system id -> row loads.
 template <int PART, bool kH>
-__global__ void __launch_bounds__(kFwdWarps * 32, PART ? 3 : 4) gather_fwd_kernel(
+__global__ void __launch_bounds__(kFwdWarps * 32, 4) gather_fwd_kernel(
     const float* __restrict__ x, const int64_t* __restrict__ idx_i, const int64_t* __restrict__ idx_j,
     const float* __restrict__ wig, const float* __restrict__ rad, const float* __restrict__ csd,
     const int64_t* __restrict__ batch, float* __restrict__ X0, float* __restrict__ X1, float* __restrict__ X2,
