@@ -68,3 +68,32 @@ def test_fused_module_surface():
     from flash_uma_b200 import fused
     for name in ("geometry", "message_block", "init_block", "fusable", "lean_needed", "radial_fwd", "radial_bwd"):
         assert callable(getattr(fused, name)), name
+
+
+def test_roofline_flops_match_the_model_gemms():
+    """The bench's algorithmic FLOPs (``gemm_flops_per_step``) equal 2 N K per edge of every dense
+    layer the model holds (radial MLPs, conv1 / conv2 m-blocks), forward plus the input
+    gradients, minus the radial layer-1 columns of the embeddings (no position dependence), plus
+    the atom-wise block's maps per atom (scalar MLP 2H x C, per-degree maps on 1 + 3 + 5 rows)."""
+    import bench
+    from flash_uma_b200.linear import FrozenLinear
+    from flash_uma_b200.synthetic import SyntheticESCNMDBackbone
+    from flash_uma_b200.wrapper import ZeroAllocBackbone
+    C, B, L, E, N = 128, 64, 4, 1000, 100
+    bb = ZeroAllocBackbone(SyntheticESCNMDBackbone(num_layers=L, sphere_channels=C, hidden_channels=C,
+                                                   num_distance_basis=B), gemm="f16x3")
+    ce = bb.ce
+    per_edge = 0
+    for mod in [ce.rad_init] + list(ce.layers):
+        for lin in mod.modules():
+            if isinstance(lin, FrozenLinear):
+                per_edge += 2 * lin.N * lin.K
+    fwd = E * per_edge
+    bwd = fwd - E * (L + 1) * 2 * 2 * C * C           # radial layer-1 gradient: Gaussian columns only
+    aw = 0
+    for lay in ce.layers:
+        a = lay.atom_wise
+        H = a.hidden
+        aw += 2 * N * C * 2 * H + 2 * (2 * 9 * N * C * H)   # scalar MLP, two per-degree maps (9 rows each)
+    assert bench.gemm_flops_per_step(E, C, B, L) == fwd + bwd
+    assert bench.gemm_flops_per_step(E, C, B, L, N_atomwise=N) == fwd + bwd + 2 * aw
