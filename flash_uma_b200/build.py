@@ -53,7 +53,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(LIBDIR, exist_ok=True)
     tmp = out + ".tmp"
     # --no-undefined: a launcher declared but not defined fails the build instead of the first dlopen
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-DFUMA_PRECISE",
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17",
            "-Xcompiler", "-fPIC", "-shared", "-Xlinker", "--no-undefined", "-I", os.path.join(ROOT, "include"),
            "-o", tmp, *sources()]
     if verbose:
